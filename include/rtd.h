@@ -1,0 +1,141 @@
+/*
+ * rtd.h -- C ABI of libruntimed_b200, the sm_100a quantized-linear hot path.
+ *
+ * Drop-in boundary for syntropd/runtimed's quantized forward pass.  Every entry
+ * point names the reference interface it replaces (paths relative to the
+ * runtimed project root).  Conventions:
+ *   - plain pointers and sizes only; `stream` is a cudaStream_t passed as void*
+ *     (NULL = the legacy default stream);
+ *   - every call returns an rtd_status; nothing throws across the ABI;
+ *   - weights are uploaded once and owned by the library (opaque handles);
+ *     activations and outputs are caller-owned DEVICE buffers;
+ *   - the compute entry points allocate nothing: scratch comes from the
+ *     context's workspace, reserved by rtd_init.  Calls that share one context
+ *     must not overlap on the GPU (the reference serialises forwards per model
+ *     with Mutex<Session>: crates/runtimed-core/src/model/meta.rs:31-45).
+ */
+#ifndef RTD_H
+#define RTD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; only this ABI is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef int32_t rtd_status;
+
+/* Status codes.  Mapping onto crates/runtimed-model/src/error.rs:6-27 ModelError:
+ *   RTD_ERR_SHAPE -> ModelError::Shape; RTD_ERR_UNSUPPORTED / RTD_ERR_TRUNCATED ->
+ *   ModelError::Gguf(GgufError::{Unsupported, Truncated}); everything else ->
+ *   ModelError::Config(rtd_last_error(ctx)). */
+enum {
+    RTD_OK = 0,
+    RTD_ERR_INVALID = 1,       /* null handle/pointer, bad enum value */
+    RTD_ERR_SHAPE = 2,         /* dimensions inconsistent or not a block multiple */
+    RTD_ERR_UNSUPPORTED = 3,   /* ggml type not on this path */
+    RTD_ERR_TRUNCATED = 4,     /* byte buffer shorter than the tensor needs */
+    RTD_ERR_CUDA = 5,          /* a CUDA runtime call failed */
+    RTD_ERR_OOM = 6,           /* device allocation failed (upload / init only) */
+    RTD_ERR_PEER_TIMEOUT = 7,  /* a bounded cross-GPU wait gave up */
+    RTD_ERR_INDEX = 8,         /* an embedding id was out of range */
+    RTD_ERR_DEVICE = 9,        /* a kernel raised the context's device status word */
+    RTD_ERR_WORKSPACE = 10     /* the call needs more scratch than the context reserved */
+};
+
+/* GGML type ids (crates/runtimed-gguf/src/quant/dtype.rs:27-46). */
+enum { RTD_TYPE_Q8_0 = 8, RTD_TYPE_Q4_K = 12, RTD_TYPE_Q6_K = 14 };
+
+/* Activation / output element types. */
+enum { RTD_DT_F32 = 0, RTD_DT_F16 = 1, RTD_DT_BF16 = 2 };
+
+/* FP8 linear modes.  W8A16: activations stay 16/32-bit (E4M3 -> f16 is exact);
+ * W8A8: activations are first encoded to E4M3 with the reference encoder
+ * (crates/runtimed-model/src/ops/fp8_gemm.rs:96-101), as its cuBLASLt path does. */
+enum { RTD_FP8_W8A16 = 0, RTD_FP8_W8A8 = 1 };
+
+typedef struct rtd_ctx rtd_ctx;
+typedef struct rtd_qweight rtd_qweight;
+typedef struct rtd_fp8weight rtd_fp8weight;
+
+/* ---- context ---------------------------------------------------------------
+ * Replaces the device binding of Weights::ensure_current
+ * (crates/runtimed-model/src/weights/store.rs:128-145): a context binds one CUDA
+ * device and owns the scratch workspace and the device status word. */
+rtd_status rtd_init(int device, rtd_ctx** out);
+rtd_status rtd_destroy(rtd_ctx* ctx);
+/* Last error message recorded on `ctx` (or on the calling thread when ctx is NULL). */
+const char* rtd_last_error(const rtd_ctx* ctx);
+/* Synchronises `stream` and reads then clears the device status word. */
+rtd_status rtd_check_device_status(rtd_ctx* ctx, void* stream);
+/* Block geometry (crates/runtimed-gguf/src/quant/dtype.rs:49-64). */
+rtd_status rtd_block_geometry(uint32_t ggml_type, int64_t* elems, int64_t* bytes);
+
+/* ---- quantized weights -----------------------------------------------------
+ * Replaces load_quantized_tensor (crates/runtimed-model/src/weights/load_gguf.rs:28-38):
+ * raw GGUF superblocks of an [N, K] matrix (N rows of K/elems blocks, the layout
+ * GgufFile::tensor_bytes returns, crates/runtimed-gguf/src/header.rs:191-205) are
+ * copied from host memory to the device once and re-tiled there for the kernels. */
+rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host_blocks,
+                              size_t nbytes, int64_t N, int64_t K, rtd_qweight** out);
+rtd_status rtd_qweight_free(rtd_qweight* w);
+/* raw_bytes = the GGUF byte count (QTensor::storage_size_in_bytes, store.rs:57-76);
+ * device_bytes = what the device copy occupies (rows padded to a tile of 16). */
+rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* N, int64_t* K,
+                            size_t* raw_bytes, size_t* device_bytes);
+
+/* y[M, N] = x[M, K] . W^T (+ bias[N]).  Replaces Weights::linear -> QMatMul::forward
+ * (crates/runtimed-model/src/weights/linear_layer.rs:45-52) and, with a bias,
+ * Weights::linear_bias (linear_layer.rs:107-118).  x rows are `ldx` elements apart
+ * and y rows `ldy` elements apart (pass K and N for dense rows).  bias is f32 on the
+ * device or NULL. */
+rtd_status rtd_qlinear(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype,
+                       int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype,
+                       int64_t ldy, void* stream);
+
+/* y[n, K] (f32) = dequantized rows ids[0..n) of W.  Replaces Weights::embed ->
+ * QMatMul::embedding (crates/runtimed-model/src/weights/embed_layer.rs:16-57).
+ * ids is a device array; an id >= N writes a zero row and raises RTD_ERR_INDEX in
+ * the device status word (read it with rtd_check_device_status). */
+rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n,
+                      float* y, void* stream);
+
+/* y[N, K] (f32) = the whole dequantized matrix, bit-exact with the reference
+ * decoders (crates/runtimed-gguf/src/quant/dequant.rs:83-146).  Replaces
+ * Weights::get on a q_map entry (crates/runtimed-model/src/weights/store.rs:88-97). */
+rtd_status rtd_qdequant(rtd_ctx* ctx, const rtd_qweight* w, float* y, void* stream);
+
+/* ---- FP8 E4M3 --------------------------------------------------------------
+ * Replaces Fp8Weight::new (crates/runtimed-model/src/weights/fp8_weight.rs:17-41):
+ * E4M3 bytes [N, K] row-major and scale[scale_len] (1 = per tensor, N = per output
+ * channel), both host memory. */
+rtd_status rtd_fp8weight_upload(rtd_ctx* ctx, const uint8_t* host_w, const float* host_scale,
+                                int64_t scale_len, int64_t N, int64_t K, rtd_fp8weight** out);
+rtd_status rtd_fp8weight_free(rtd_fp8weight* w);
+
+/* y[M, N] = x . (E4M3(W) * scale)^T.  Replaces SubstratePort::fp8_gemm / ops::fp8_gemm
+ * (crates/runtimed-model/src/substrate/port.rs:73, crates/runtimed-model/src/ops/fp8_gemm.rs:77-191). */
+rtd_status rtd_fp8_linear(rtd_ctx* ctx, const rtd_fp8weight* w, const void* x, uint32_t x_dtype,
+                          int64_t ldx, int64_t M, void* y, uint32_t y_dtype, int64_t ldy,
+                          uint32_t mode, void* stream);
+
+/* out[i] = E4M3 encoding of x[i] (f32, device), ties toward the lower magnitude,
+ * saturating at 448.  Replaces the host loop of f32_to_fp8_e4m3
+ * (crates/runtimed-model/src/weights/load_safetensors.rs:53-69) used at fp8_gemm.rs:98-99. */
+rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RTD_H */

@@ -1,0 +1,396 @@
+// rtd_api.cu -- the C ABI of libruntimed_b200 (declared in include/rtd.h).
+//
+// Host-side operator surface: contexts, weight handles, argument validation and
+// dispatch to the sm_100a kernels.  Weight uploads allocate (once, at load time);
+// the compute entry points never allocate -- their scratch is the context
+// workspace reserved by rtd_init.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/rtd.h"
+#include "rtd_kernels.h"
+#include "rtd_layout.h"
+
+struct rtd_ctx {
+  int device = 0;
+  int sm_count = 148;
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
+  uint32_t* counters = nullptr;
+  int64_t n_counters = 0;
+  int* status = nullptr;
+  std::string err;
+};
+
+struct rtd_qweight {
+  rtd_ctx* ctx = nullptr;
+  int fmt = 0;
+  uint32_t ggml_type = 0;
+  int64_t N = 0, K = 0, G = 0, T = 0;
+  uint8_t* dev = nullptr;
+  size_t dev_bytes = 0, raw_bytes = 0;
+};
+
+struct rtd_fp8weight {
+  rtd_ctx* ctx = nullptr;
+  int64_t N = 0, K = 0, G = 0, T = 0;
+  uint8_t* dev = nullptr;
+  float* scale = nullptr;
+  int64_t scale_len = 0;
+  size_t dev_bytes = 0;
+};
+
+namespace {
+
+constexpr size_t kWorkspaceBytes = 64ull << 20;  // split-K partials
+constexpr int64_t kCounters = 1 << 17;           // per-tile arrival counters
+
+thread_local std::string g_thread_err;
+
+rtd_status fail(rtd_ctx* ctx, rtd_status code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (ctx)
+    ctx->err = buf;
+  else
+    g_thread_err = buf;
+  return code;
+}
+
+rtd_status cuda_fail(rtd_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, RTD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Binds the context's device for the duration of a call and restores the
+// caller's device afterwards (the reference re-binds per call in ensure_current).
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int fmt_of_type(uint32_t t) {
+  switch (t) {
+    case RTD_TYPE_Q4_K: return rtd::FMT_Q4K;
+    case RTD_TYPE_Q6_K: return rtd::FMT_Q6K;
+    case RTD_TYPE_Q8_0: return rtd::FMT_Q80;
+    default: return -1;
+  }
+}
+
+bool valid_dtype(uint32_t d) { return d == RTD_DT_F32 || d == RTD_DT_F16 || d == RTD_DT_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+const char* rtd_last_error(const rtd_ctx* ctx) { return ctx ? ctx->err.c_str() : g_thread_err.c_str(); }
+
+rtd_status rtd_block_geometry(uint32_t ggml_type, int64_t* elems, int64_t* bytes) {
+  int64_t e, b;
+  switch (ggml_type) {
+    case 0: e = 1; b = 4; break;
+    case 1: case 30: e = 1; b = 2; break;
+    case 2: e = 32; b = 18; break;
+    case 6: e = 32; b = 22; break;
+    case 8: e = 32; b = 34; break;
+    case 10: e = 256; b = 84; break;
+    case 11: e = 256; b = 110; break;
+    case 12: e = 256; b = 144; break;
+    case 13: e = 256; b = 176; break;
+    case 14: e = 256; b = 210; break;
+    default: return fail(nullptr, RTD_ERR_UNSUPPORTED, "ggml type %u has no block geometry", ggml_type);
+  }
+  if (elems) *elems = e;
+  if (bytes) *bytes = b;
+  return RTD_OK;
+}
+
+rtd_status rtd_init(int device, rtd_ctx** out) {
+  if (!out) return fail(nullptr, RTD_ERR_INVALID, "rtd_init: out is NULL");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || device < 0 || device >= n)
+    return fail(nullptr, RTD_ERR_CUDA, "rtd_init: device %d not available (%d devices, %s)", device, n,
+                cudaGetErrorString(e));
+  rtd_ctx* c = new (std::nothrow) rtd_ctx();
+  if (!c) return fail(nullptr, RTD_ERR_OOM, "rtd_init: host allocation failed");
+  c->device = device;
+  DeviceGuard g(device);
+  if (g.err != cudaSuccess) {
+    delete c;
+    return fail(nullptr, RTD_ERR_CUDA, "rtd_init: cudaSetDevice: %s", cudaGetErrorString(g.err));
+  }
+  cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if ((e = cudaMalloc(&c->ws, kWorkspaceBytes)) != cudaSuccess ||
+      (e = cudaMalloc(&c->counters, kCounters * sizeof(uint32_t))) != cudaSuccess ||
+      (e = cudaMalloc(&c->status, sizeof(int))) != cudaSuccess ||
+      (e = cudaMemset(c->counters, 0, kCounters * sizeof(uint32_t))) != cudaSuccess ||
+      (e = cudaMemset(c->status, 0, sizeof(int))) != cudaSuccess) {
+    cudaFree(c->ws);
+    cudaFree(c->counters);
+    cudaFree(c->status);
+    delete c;
+    return fail(nullptr, RTD_ERR_OOM, "rtd_init: workspace allocation failed: %s", cudaGetErrorString(e));
+  }
+  c->ws_bytes = kWorkspaceBytes;
+  c->n_counters = kCounters;
+  *out = c;
+  return RTD_OK;
+}
+
+rtd_status rtd_destroy(rtd_ctx* ctx) {
+  if (!ctx) return RTD_OK;
+  DeviceGuard g(ctx->device);
+  cudaFree(ctx->ws);
+  cudaFree(ctx->counters);
+  cudaFree(ctx->status);
+  delete ctx;
+  return RTD_OK;
+}
+
+rtd_status rtd_check_device_status(rtd_ctx* ctx, void* stream) {
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "rtd_check_device_status: ctx is NULL");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "rtd_check_device_status: stream");
+  int v = 0;
+  if ((e = cudaMemcpy(&v, ctx->status, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(ctx, e, "rtd_check_device_status: read");
+  if (v != 0) {
+    cudaMemset(ctx->status, 0, sizeof(int));
+    if (v == RTD_ERR_INDEX) return fail(ctx, RTD_ERR_INDEX, "embedding id out of range");
+    return fail(ctx, RTD_ERR_DEVICE, "device status word raised code %d", v);
+  }
+  return RTD_OK;
+}
+
+rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host_blocks, size_t nbytes,
+                              int64_t N, int64_t K, rtd_qweight** out) {
+  if (!ctx || !out) return fail(ctx, RTD_ERR_INVALID, "rtd_qweight_upload: NULL argument");
+  *out = nullptr;
+  const int fmt = fmt_of_type(ggml_type);
+  if (fmt < 0) return fail(ctx, RTD_ERR_UNSUPPORTED, "rtd_qweight_upload: ggml type %u is not Q4_K/Q6_K/Q8_0", ggml_type);
+  if (N < 0 || K < 0) return fail(ctx, RTD_ERR_SHAPE, "rtd_qweight_upload: negative shape [%lld, %lld]", (long long)N, (long long)K);
+  const rtd::FmtInfo f = rtd::fmt_info(fmt);
+  if (K % f.block_elems != 0)
+    return fail(ctx, RTD_ERR_SHAPE, "rtd_qweight_upload: K=%lld is not a multiple of the block size %d",
+                (long long)K, f.block_elems);
+  const size_t need = (size_t)N * (size_t)(K / f.block_elems) * (size_t)f.block_bytes;
+  if (nbytes < need)
+    return fail(ctx, RTD_ERR_TRUNCATED, "rtd_qweight_upload: %zu bytes given, %zu needed", nbytes, need);
+  if (need > 0 && !host_blocks) return fail(ctx, RTD_ERR_INVALID, "rtd_qweight_upload: host_blocks is NULL");
+  rtd_qweight* w = new (std::nothrow) rtd_qweight();
+  if (!w) return fail(ctx, RTD_ERR_OOM, "rtd_qweight_upload: host allocation failed");
+  w->ctx = ctx;
+  w->fmt = fmt;
+  w->ggml_type = ggml_type;
+  w->N = N;
+  w->K = K;
+  w->T = rtd::tiles_for(N);
+  w->G = rtd::groups_for(fmt, K);
+  w->raw_bytes = need;
+  w->dev_bytes = (size_t)(w->T * w->G) * (size_t)f.gb;
+  if (w->dev_bytes > 0) {
+    std::vector<uint8_t> host;
+    try {
+      host.resize(w->dev_bytes);
+    } catch (...) {
+      delete w;
+      return fail(ctx, RTD_ERR_OOM, "rtd_qweight_upload: host staging allocation failed");
+    }
+    rtd::repack_host(fmt, static_cast<const uint8_t*>(host_blocks), N, K, host.data());
+    DeviceGuard g(ctx->device);
+    cudaError_t e = cudaMalloc(&w->dev, w->dev_bytes);
+    if (e != cudaSuccess) {
+      delete w;
+      return fail(ctx, RTD_ERR_OOM, "rtd_qweight_upload: cudaMalloc(%zu): %s", w->dev_bytes, cudaGetErrorString(e));
+    }
+    if ((e = cudaMemcpy(w->dev, host.data(), w->dev_bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+      cudaFree(w->dev);
+      delete w;
+      return cuda_fail(ctx, e, "rtd_qweight_upload: copy");
+    }
+  }
+  *out = w;
+  return RTD_OK;
+}
+
+rtd_status rtd_qweight_free(rtd_qweight* w) {
+  if (!w) return RTD_OK;
+  if (w->dev) {
+    DeviceGuard g(w->ctx->device);
+    cudaFree(w->dev);
+  }
+  delete w;
+  return RTD_OK;
+}
+
+rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* N, int64_t* K, size_t* raw_bytes,
+                            size_t* device_bytes) {
+  if (!w) return fail(nullptr, RTD_ERR_INVALID, "rtd_qweight_info: NULL handle");
+  if (ggml_type) *ggml_type = w->ggml_type;
+  if (N) *N = w->N;
+  if (K) *K = w->K;
+  if (raw_bytes) *raw_bytes = w->raw_bytes;
+  if (device_bytes) *device_bytes = w->dev_bytes;
+  return RTD_OK;
+}
+
+static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N, int64_t K, int64_t G,
+                           const float* row_scale, int scale_len, const void* x, uint32_t x_dtype, int64_t ldx,
+                           int64_t M, int w8a8, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
+                           void* stream, const char* who) {
+  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (M == 0 || N == 0) return RTD_OK;
+  if ((K > 0 && !x) || !y) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if (ldx < K || ldy < N)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who, (long long)ldx,
+                (long long)ldy, (long long)K, (long long)N);
+  DeviceGuard g(ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(ctx, g.err, who);
+  cudaError_t e;
+  if (K == 0) {
+    e = rtd::launch_fill_rows(bias, y, y_dtype, ldy, M, N, (cudaStream_t)stream);
+    return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+  }
+  rtd::QGemvCall c{};
+  c.fmt = fmt;
+  c.w = wdev;
+  c.N = N;
+  c.K = K;
+  c.G = G;
+  c.row_scale = row_scale;
+  c.scale_len = scale_len;
+  c.x = x;
+  c.x_dtype = (int)x_dtype;
+  c.ldx = ldx;
+  c.M = M;
+  c.w8a8 = w8a8;
+  c.bias = bias;
+  c.y = y;
+  c.y_dtype = (int)y_dtype;
+  c.ldy = ldy;
+  c.ws = ctx->ws;
+  c.ws_bytes = ctx->ws_bytes;
+  c.counters = ctx->counters;
+  c.n_counters = ctx->n_counters;
+  c.status = ctx->status;
+  c.sm_count = ctx->sm_count;
+  c.stream = (cudaStream_t)stream;
+  int plan_err = 0;
+  e = rtd::launch_qgemv(c, &plan_err);
+  if (plan_err) return fail(ctx, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the context workspace", who, (long long)N, (long long)K);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, who);
+  return RTD_OK;
+}
+
+rtd_status rtd_qlinear(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx, int64_t M,
+                       const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qlinear: NULL ctx or weight");
+  return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, nullptr, 0, x, x_dtype, ldx, M, 0, bias, y, y_dtype, ldy,
+                  stream, "rtd_qlinear");
+}
+
+rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n, float* y, void* stream) {
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qembed: NULL ctx or weight");
+  if (n < 0) return fail(ctx, RTD_ERR_SHAPE, "rtd_qembed: n=%lld is negative", (long long)n);
+  if (n == 0 || w->K == 0) return RTD_OK;
+  if (!ids || !y) return fail(ctx, RTD_ERR_INVALID, "rtd_qembed: ids or y is NULL");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_embed(w->fmt, w->dev, w->N, w->K, w->G, ids, n, y, ctx->status, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, "rtd_qembed");
+}
+
+rtd_status rtd_qdequant(rtd_ctx* ctx, const rtd_qweight* w, float* y, void* stream) {
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qdequant: NULL ctx or weight");
+  if (w->N == 0 || w->K == 0) return RTD_OK;
+  if (!y) return fail(ctx, RTD_ERR_INVALID, "rtd_qdequant: y is NULL");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_dequant(w->fmt, w->dev, w->N, w->K, w->G, y, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, "rtd_qdequant");
+}
+
+rtd_status rtd_fp8weight_upload(rtd_ctx* ctx, const uint8_t* host_w, const float* host_scale, int64_t scale_len,
+                                int64_t N, int64_t K, rtd_fp8weight** out) {
+  if (!ctx || !out) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8weight_upload: NULL argument");
+  *out = nullptr;
+  if (N < 0 || K < 0) return fail(ctx, RTD_ERR_SHAPE, "rtd_fp8weight_upload: negative shape");
+  if (!(scale_len == 1 || scale_len == N))
+    return fail(ctx, RTD_ERR_SHAPE, "rtd_fp8weight_upload: scale has %lld elements, expected 1 or N=%lld",
+                (long long)scale_len, (long long)N);
+  if ((N * K > 0 && !host_w) || !host_scale) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8weight_upload: NULL data");
+  rtd_fp8weight* w = new (std::nothrow) rtd_fp8weight();
+  if (!w) return fail(ctx, RTD_ERR_OOM, "rtd_fp8weight_upload: host allocation failed");
+  w->ctx = ctx;
+  w->N = N;
+  w->K = K;
+  w->T = rtd::tiles_for(N);
+  w->G = rtd::groups_for(rtd::FMT_FP8, K);
+  w->scale_len = scale_len;
+  w->dev_bytes = (size_t)(w->T * w->G) * 512u;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaMalloc(&w->scale, (size_t)scale_len * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(w->scale, host_scale, (size_t)scale_len * sizeof(float), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && w->dev_bytes > 0) {
+    std::vector<uint8_t> host(w->dev_bytes);
+    rtd::repack_host(rtd::FMT_FP8, host_w, N, K, host.data());
+    e = cudaMalloc(&w->dev, w->dev_bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(w->dev, host.data(), w->dev_bytes, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) {
+    cudaFree(w->dev);
+    cudaFree(w->scale);
+    delete w;
+    return fail(ctx, RTD_ERR_OOM, "rtd_fp8weight_upload: %s", cudaGetErrorString(e));
+  }
+  *out = w;
+  return RTD_OK;
+}
+
+rtd_status rtd_fp8weight_free(rtd_fp8weight* w) {
+  if (!w) return RTD_OK;
+  DeviceGuard g(w->ctx->device);
+  cudaFree(w->dev);
+  cudaFree(w->scale);
+  delete w;
+  return RTD_OK;
+}
+
+rtd_status rtd_fp8_linear(rtd_ctx* ctx, const rtd_fp8weight* w, const void* x, uint32_t x_dtype, int64_t ldx,
+                          int64_t M, void* y, uint32_t y_dtype, int64_t ldy, uint32_t mode, void* stream) {
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8_linear: NULL ctx or weight");
+  if (mode != RTD_FP8_W8A16 && mode != RTD_FP8_W8A8) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8_linear: bad mode %u", mode);
+  return run_gemv(ctx, rtd::FMT_FP8, w->dev, w->N, w->K, w->G, w->scale, (int)w->scale_len, x, x_dtype, ldx, M,
+                  mode == RTD_FP8_W8A8 ? 1 : 0, nullptr, y, y_dtype, ldy, stream, "rtd_fp8_linear");
+}
+
+rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out, void* stream) {
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "rtd_fp8_encode: ctx is NULL");
+  if (n < 0) return fail(ctx, RTD_ERR_SHAPE, "rtd_fp8_encode: n is negative");
+  if (n == 0) return RTD_OK;
+  if (!x || !out) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8_encode: NULL pointer");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_fp8_encode(x, n, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, "rtd_fp8_encode");
+}
+
+}  // extern "C"

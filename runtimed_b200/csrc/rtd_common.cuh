@@ -1,0 +1,171 @@
+// rtd_common.cuh -- device helpers shared by the sm_100a kernels of libruntimed_b200.
+//
+// Inline PTX for the Blackwell data-movement primitives the kernels use
+// (mbarrier + cp.async.bulk global->shared), the legacy m16n8k16 tensor-core
+// MMA used by the decode GEMV, and bit-exact scalar conversions.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "rtd_layout.h"
+
+namespace rtd {
+
+// Device status word codes (mirrors RTD_ERR_* of include/rtd.h).
+enum : int { kDevOk = 0, kDevIndex = 8, kDevWaitTimeout = 9 };
+
+__device__ __forceinline__ void raise_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: every try_wait suspends for a hardware-defined slice, so the
+// limit is generous; on expiry the device status word records the timeout and
+// the wait continues for a second bounded round so no copy is left in flight
+// towards shared memory of an exited CTA.
+__device__ __forceinline__ void mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
+  for (uint32_t i = 0; i < (1u << 22); ++i)
+    if (mbar_try_wait(bar, parity)) return;
+  raise_status(status, kDevWaitTimeout);
+  for (uint32_t i = 0; i < (1u << 22); ++i)
+    if (mbar_try_wait(bar, parity)) return;
+}
+
+// 1-D bulk copy global -> shared (TMA engine), completion counted in bytes on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- MMA
+// D = A(16x16, f16, row) * B(16x8, f16, col) + C, f32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1, float c0, float c1, float c2, float c3) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
+}
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+  return (a & mask) | orv;  // compiles to one LOP3
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  return __byte_perm(a, b, sel);
+}
+
+// Two E4M3 bytes (low byte -> low half) -> f16x2, exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+
+// ---------------------------------------------------------------- scalar
+// IEEE half bits -> float, bit-exact with the reference decoder for every input
+// (subnormals normalised, NaN payload kept): dequant.rs:11-33.
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits) {
+  uint32_t sign = (bits >> 15) & 1u, exp = (bits >> 10) & 0x1Fu, mant = bits & 0x3FFu, out;
+  if (exp == 0) {
+    if (mant == 0) {
+      out = sign << 31;
+    } else {
+      int sh = __clz(mant) - 21;  // shifts until bit 10 is set
+      uint32_t m = mant << sh;
+      uint32_t e = 113u - (uint32_t)sh;
+      out = (sign << 31) | (e << 23) | ((m & 0x3FFu) << 13);
+    }
+  } else if (exp == 31) {
+    out = (sign << 31) | (0xFFu << 23) | (mant << 13);
+  } else {
+    out = (sign << 31) | ((exp + 112u) << 23) | (mant << 13);
+  }
+  return __uint_as_float(out);
+}
+
+__device__ __forceinline__ float ld_f16(const uint8_t* p) {
+  return f16_bits_to_f32((uint32_t)p[0] | ((uint32_t)p[1] << 8));
+}
+
+// Q4_K scale/min pair j of the 12 packed scale bytes: dequant_k.rs:8-16.
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, uint32_t& sc, uint32_t& m) {
+  if (j < 4) {
+    sc = s[j] & 63u;
+    m = s[j + 4] & 63u;
+  } else {
+    sc = (s[j + 4] & 0xFu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+    m = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+  }
+}
+
+// E4M3 value of the reference encoder (load_safetensors.rs:53-69): nearest grid
+// point, a tie goes to the lower magnitude, |x| >= 448 saturates, NaN stays NaN.
+__device__ __forceinline__ float e4m3_round_ref(float x) {
+  if (isnan(x)) return x;
+  float a = fabsf(x);
+  float v;
+  if (a >= 448.0f) {
+    v = 448.0f;
+  } else if (a == 0.0f) {
+    v = 0.0f;
+  } else {
+    int e = ilogbf(a);
+    if (e < -6) e = -6;
+    float spacing = ldexpf(1.0f, e - 3);
+    float q = a / spacing;  // exact: power-of-two divisor
+    float n = floorf(q);
+    if (q - n > 0.5f) n += 1.0f;
+    v = n * spacing;
+  }
+  return copysignf(v, x);
+}
+
+__device__ __forceinline__ uint8_t e4m3_code_of_value(float v) {
+  if (isnan(v)) return 0x7f;
+  uint8_t sign = signbit(v) ? 0x80 : 0x00;
+  float a = fabsf(v);
+  if (a == 0.0f) return sign;
+  int e = ilogbf(a);
+  if (e < -6) return sign | (uint8_t)(a * 512.0f);  // subnormal: multiples of 2^-9
+  uint32_t mant = (uint32_t)((ldexpf(a, -e) - 1.0f) * 8.0f);
+  return sign | (uint8_t)(((e + 7) << 3) | mant);
+}
+
+}  // namespace rtd

@@ -1,0 +1,884 @@
+// rtd_gemv.cu -- decode GEMV / skinny GEMM on quantized weights, sm_100a.
+//
+//   y[M, N] = x[M, K] . W^T (+ bias)     W in Q4_K / Q6_K / Q8_0 / FP8-E4M3 blocks
+//
+// Replaces QMatMul::forward behind Weights::linear
+// (crates/runtimed-model/src/weights/linear_layer.rs:45-52) for decode-sized M,
+// and the per-call cuBLASLt FP8 GEMM of crates/runtimed-model/src/ops/fp8_gemm.rs:88-191.
+//
+// Every weight byte is read from HBM exactly once per call; the kernels are built
+// to keep HBM busy with as little synchronisation as possible:
+//  * prep kernel, one 8-CTA thread-block cluster per token: each CTA takes 1/8 of
+//    the row, the row's max |x| is combined through distributed shared memory,
+//    and x is scaled by a power of two so that max sits in [2^14, 2^15), split
+//    into f16 hi (+ lo for f32 input: 22 significant bits; bf16 / f16 inputs are
+//    exact in one column) and written group-major to the context workspace with
+//    the per-sub-block column sums the scale algebra needs.  It triggers
+//    programmatic completion at once, so the GEMV grid launches behind it (PDL)
+//    and prefetches weights while x is prepared.
+//  * GEMV kernel: every warp is an independent streaming pipeline.  The flattened
+//    (16-row tile, item of IG groups) space is split evenly over all warps of the
+//    persistent grid; each warp keeps NS items in flight in its own shared-memory
+//    ring with cp.async.bulk (TMA engine) on its own mbarriers -- weights plus the
+//    matching x and column-sum slices, three copies per item -- so no CTA-wide
+//    barrier ever stalls the stream.  In the device layout (rtd_layout.h) an item
+//    is one contiguous 16-byte aligned byte range.
+//  * No dequantized weight is materialised.  Each lane turns its 16-byte vector
+//    of packed codes into exact integer-valued f16 pairs with one LOP3 or PRMT per
+//    pair ((code | 0x6400) is the half 1024 + code) and m16n8k16 tensor-core MMAs
+//    form sum_k x_k * (1024 + code_k) in f32 (A = 16 weight rows, B = up to 8
+//    activation columns per n-tile).  Per sub-block the reference's scale algebra
+//    is applied in f32:
+//      Q4_K  y += (d*sc) * S - (1024*d*sc + dmin*m) * sum(x)    (high nibbles: extra 1/16)
+//      Q6_K  y += (d*sc) * (S - 1056 * sum(x))                  (code - 32, offset 1024)
+//      Q8_0  y += d * (S - 1152 * sum(x))                       (q + 128, offset 1024)
+//      FP8   y += S (E4M3 -> f16 is exact), times the channel scale at the end
+//    so products are exact and only f32 rounding remains.
+//  * A tile finished inside one warp is written straight from the MMA
+//    accumulators; a tile split between warps leaves per-warp partials in the
+//    workspace and the last warp to arrive (per-tile counter) sums them in warp
+//    order, writes y and re-arms the counter, so every call leaves the counters
+//    at zero.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cstdlib>
+
+#include "rtd_common.cuh"
+#include "rtd_kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace rtd {
+
+namespace {
+
+constexpr int kWarps = 8;  // warps per GEMV CTA, each an independent pipeline
+constexpr int kThreads = kWarps * 32;
+constexpr int kPrepThreads = 256;
+constexpr int kPrepCluster = 8;
+constexpr int kMaxStages = 4;
+constexpr int kTblBytes = 1280;  // per-warp scale table: 16 rows x 9 float2 (Q4_K) or 16 x 17 float (Q6_K)
+
+template <int FMT>
+struct FmtC;
+template <>
+struct FmtC<FMT_Q4K> {
+  static constexpr int GK = 256, GB = 2304, SBE = 32, IG = 1;
+  static constexpr float XOFF = 1.0f;  // plain sub-block sums: the min term needs them unscaled
+  static constexpr bool TAB = true;
+};
+template <>
+struct FmtC<FMT_Q6K> {
+  static constexpr int GK = 256, GB = 3360, SBE = 16, IG = 1;
+  static constexpr float XOFF = -1056.0f;
+  static constexpr bool TAB = true;
+};
+template <>
+struct FmtC<FMT_Q80> {
+  static constexpr int GK = 32, GB = 544, SBE = 32, IG = 8;
+  static constexpr float XOFF = -1152.0f;
+  static constexpr bool TAB = true;
+};
+template <>
+struct FmtC<FMT_FP8> {
+  static constexpr int GK = 32, GB = 512, SBE = 32, IG = 8;
+  static constexpr bool TAB = false;
+};
+
+// Bytes one activation column occupies per group in the workspace (and in shared
+// memory): 256-wide groups get 64 bytes of padding so that adjacent columns of the
+// B tile fall on different shared-memory banks.
+__host__ __device__ constexpr int col_stride_bytes(int gk) { return gk * 2 + (gk >= 256 ? 64 : 0); }
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ------------------------------------------------------------------ prep kernel
+struct PrepArgs {
+  const void* x;
+  int x_dtype;
+  int x_vec;
+  int64_t ldx;
+  int64_t K, kp;
+  int M, P, ncol, ncol8;
+  int w8a8;
+  uint8_t* cols;  // [group][ncol][col_stride_bytes(GK)]
+  float* tab;     // [kp / SBE][ncol8]
+  float* tscale;  // [M]
+};
+
+__device__ __forceinline__ void load8(const void* x, int dt, bool vec, int64_t ldx, int64_t K, int t, int64_t k,
+                                      float (&v)[8]) {
+  if (vec && k + 8 <= K) {
+    if (dt == 0) {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (int64_t)t * ldx + k);
+      const float4 u = __ldg(p), w = __ldg(p + 1);
+      v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w; v[4] = w.x; v[5] = w.y; v[6] = w.z; v[7] = w.w;
+    } else {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + (int64_t)t * ldx + k));
+      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const unsigned short lo = (unsigned short)(wd[i] & 0xFFFFu), hi = (unsigned short)(wd[i] >> 16);
+        if (dt == 1) {
+          v[2 * i] = __half2float(__ushort_as_half(lo));
+          v[2 * i + 1] = __half2float(__ushort_as_half(hi));
+        } else {
+          v[2 * i] = __uint_as_float((uint32_t)lo << 16);
+          v[2 * i + 1] = __uint_as_float((uint32_t)hi << 16);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t kk = k + i;
+      float f = 0.0f;
+      if (kk < K) {
+        if (dt == 0) {
+          f = static_cast<const float*>(x)[(int64_t)t * ldx + kk];
+        } else {
+          const unsigned short b = static_cast<const unsigned short*>(x)[(int64_t)t * ldx + kk];
+          f = (dt == 1) ? __half2float(__ushort_as_half(b)) : __uint_as_float((uint32_t)b << 16);
+        }
+      }
+      v[i] = f;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
+template <int FMT>
+__global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThreads)
+    prep_kernel(const PrepArgs a) {
+  using F = FmtC<FMT>;
+  griddep_launch_dependents();  // the GEMV may start streaming weights now
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int t = blockIdx.x / kPrepCluster;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[kPrepThreads / 32];
+  __shared__ float cmax;
+  // this CTA's slice, in whole 32-element windows so sub-block sums never straddle CTAs
+  const int64_t nwin = a.kp / 32;
+  const int64_t w0 = nwin * rank / kPrepCluster, w1 = nwin * (rank + 1) / kPrepCluster;
+  const int64_t c0 = 4 * w0, nch = 4 * (w1 - w0);
+  const bool vec = a.x_vec != 0;
+
+  float m = 0.0f;
+  for (int64_t c = tid; c < nch; c += kPrepThreads) {
+    float v[8];
+    load8(a.x, a.x_dtype, vec, a.ldx, a.K, t, 8 * (c0 + c), v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(a.w8a8 ? e4m3_round_ref(v[i]) : v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = 0.0f;
+    for (int w = 0; w < kPrepThreads / 32; ++w) mm = fmaxf(mm, red[w]);
+    cmax = mm;
+  }
+  cluster.sync();
+  if (tid == 0) {
+    float mm = 0.0f;
+    for (int r = 0; r < kPrepCluster; ++r) mm = fmaxf(mm, *cluster.map_shared_rank(&cmax, r));
+    red[0] = mm;
+  }
+  cluster.sync();  // peers are done reading cmax before any CTA moves on or exits
+  __syncthreads();
+  int e = 0;
+  const float mm = red[0];
+  if (mm > 0.0f && mm <= 3.4e38f) e = min(max(ilogbf(mm) - 14, -110), 110);
+  const float inv = ldexpf(1.0f, -e);
+  if (rank == 0 && tid == 0) a.tscale[t] = ldexpf(1.0f, e);
+
+  constexpr int SBC = F::SBE / 8;
+  constexpr int CSB = col_stride_bytes(F::GK);
+  const int64_t iters = (nch + kPrepThreads - 1) / kPrepThreads;
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t cl = it * kPrepThreads + tid;
+    const bool valid = cl < nch;
+    const int64_t c = c0 + cl;
+    float v[8];
+    if (valid) {
+      load8(a.x, a.x_dtype, vec, a.ldx, a.K, t, 8 * c, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    __half hi[8], lo[8];
+    float shi = 0.0f, slo = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float s = (a.w8a8 ? e4m3_round_ref(v[i]) : v[i]) * inv;
+      hi[i] = __float2half_rn(s);
+      const float hf = __half2float(hi[i]);
+      lo[i] = __float2half_rn(s - hf);
+      shi += hf;
+      slo += __half2float(lo[i]);
+    }
+    if (valid) {
+      const int64_t k = 8 * c;
+      const int64_t grp = k / F::GK;
+      const int within = (int)(k - grp * F::GK);
+      uint8_t* base = a.cols + ((size_t)grp * a.ncol + (size_t)t * a.P) * CSB + within * 2;
+      uint4 u;
+      u.x = pack_h2(hi[0], hi[1]); u.y = pack_h2(hi[2], hi[3]);
+      u.z = pack_h2(hi[4], hi[5]); u.w = pack_h2(hi[6], hi[7]);
+      *reinterpret_cast<uint4*>(base) = u;
+      if (a.P == 2) {
+        u.x = pack_h2(lo[0], lo[1]); u.y = pack_h2(lo[2], lo[3]);
+        u.z = pack_h2(lo[4], lo[5]); u.w = pack_h2(lo[6], lo[7]);
+        *reinterpret_cast<uint4*>(base + CSB) = u;
+      }
+    }
+    if constexpr (F::TAB) {
+      // consecutive chunks sit in consecutive lanes: reduce the SBC chunks of a sub-block
+      shi += __shfl_xor_sync(0xffffffffu, shi, 1);
+      slo += __shfl_xor_sync(0xffffffffu, slo, 1);
+      if constexpr (SBC == 4) {
+        shi += __shfl_xor_sync(0xffffffffu, shi, 2);
+        slo += __shfl_xor_sync(0xffffffffu, slo, 2);
+      }
+      if (valid && (c % SBC) == 0) {
+        const int64_t sb = c / SBC;
+        constexpr float xoff = F::XOFF;
+        a.tab[sb * a.ncol8 + t * a.P] = shi * xoff;
+        if (a.P == 2) a.tab[sb * a.ncol8 + t * a.P + 1] = slo * xoff;
+      }
+    }
+  }
+  if constexpr (F::TAB) {
+    // columns past ncol in the table read as zero; token 0's cluster clears them
+    if (t == 0 && a.ncol < a.ncol8) {
+      const int64_t sb0 = c0 / SBC, nsb = nch / SBC;
+      const int extra = a.ncol8 - a.ncol;
+      for (int64_t i = tid; i < nsb * extra; i += kPrepThreads)
+        a.tab[(sb0 + i / extra) * a.ncol8 + a.ncol + (i % extra)] = 0.0f;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ GEMV kernel
+__device__ __forceinline__ uint4 ld_b16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 ld_b8(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+
+// One group (16 rows x GK k) of one format into the warp's accumulators.
+// xg: this group's x slice (column c at xg + c*xstride); tg: its sub-block table.
+template <int FMT, int NT>
+__device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, int xstride, const float* tg,
+                                         int ncol, int ncol8, uint8_t* tblw, float (&acc)[NT][4], int lane) {
+  const int g = lane >> 2, tq = lane & 3;
+  if constexpr (FMT == FMT_Q4K) {
+    float2* tbl = reinterpret_cast<float2*>(tblw);  // [16 rows][9] (D, -Mo); the 9th pads banks
+    {
+      const int r = lane >> 1, half = lane & 1;
+      const uint4 h = ld_b16(grp + 16 * r);  // d, dmin | scales[0..3] | scales[4..7] | scales[8..11]
+      const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+      const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        uint32_t sc, m;
+        if (half == 0) {  // scale_min_k4, j < 4
+          sc = (h.y >> (8 * jj)) & 63u;
+          m = (h.z >> (8 * jj)) & 63u;
+        } else {  // j = 4 + jj
+          sc = ((h.w >> (8 * jj)) & 0xFu) | (((h.y >> (8 * jj + 6)) & 3u) << 4);
+          m = ((h.w >> (8 * jj + 4)) & 0xFu) | (((h.z >> (8 * jj + 6)) & 3u) << 4);
+        }
+        const int j = 4 * half + jj;
+        float D = d * (float)sc;
+        if (j & 1) D *= 0.0625f;  // high nibbles enter the MMA as 1024 + 16 q
+        tbl[r * 9 + j] = make_float2(D, -fmaf(1024.0f, D, dmin * (float)m));
+      }
+    }
+    __syncwarp();
+    float2 tgv[8], thv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      tgv[j] = tbl[g * 9 + j];
+      thv[j] = tbl[(g + 8) * 9 + j];
+    }
+    const uint4* qv = reinterpret_cast<const uint4*>(grp + 256) + lane;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 q = qv[c * 32];
+      const uint32_t s0 = q.x >> 8, s1 = q.y >> 8, s2 = q.z >> 8, s3 = q.w >> 8;
+#pragma unroll
+      for (int sel = 0; sel < 2; ++sel) {
+        const uint32_t msk = sel ? 0x00F000F0u : 0x000F000Fu;
+        const uint32_t a0 = lop_and_or(q.x, msk, 0x64006400u), a1 = lop_and_or(q.z, msk, 0x64006400u);
+        const uint32_t a2 = lop_and_or(s0, msk, 0x64006400u), a3 = lop_and_or(s2, msk, 0x64006400u);
+        const uint32_t b0 = lop_and_or(q.y, msk, 0x64006400u), b1 = lop_and_or(q.w, msk, 0x64006400u);
+        const uint32_t b2 = lop_and_or(s1, msk, 0x64006400u), b3 = lop_and_or(s3, msk, 0x64006400u);
+        const int sb = 2 * c + sel;
+        const float2 Dg = tgv[sb], Dh = thv[sb];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int col = nt * 8 + g;
+          const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + sb * 64 + tq * 16) : make_uint4(0, 0, 0, 0);
+          float t4[4];
+          mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, 0.f, 0.f, 0.f, 0.f);
+          mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
+          const float2 sv = *reinterpret_cast<const float2*>(tg + sb * ncol8 + nt * 8 + 2 * tq);
+          acc[nt][0] = fmaf(Dg.x, t4[0], fmaf(Dg.y, sv.x, acc[nt][0]));
+          acc[nt][1] = fmaf(Dg.x, t4[1], fmaf(Dg.y, sv.y, acc[nt][1]));
+          acc[nt][2] = fmaf(Dh.x, t4[2], fmaf(Dh.y, sv.x, acc[nt][2]));
+          acc[nt][3] = fmaf(Dh.x, t4[3], fmaf(Dh.y, sv.y, acc[nt][3]));
+        }
+      }
+    }
+    __syncwarp();
+  } else if constexpr (FMT == FMT_Q6K) {
+    float* tbl = reinterpret_cast<float*>(tblw);  // [16 rows][17] d*sc; the 17th pads banks
+    {
+      const int r = lane >> 1, jb = (lane & 1) * 8;
+      const float d = __half2float(*reinterpret_cast<const __half*>(grp + 2 * r));
+      const uint2 sv = ld_b8(grp + 32 + 16 * r + jb);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int8_t sc = (int8_t)(((jj < 4 ? sv.x : sv.y) >> (8 * (jj & 3))) & 0xFFu);
+        tbl[r * 17 + jb + jj] = d * (float)sc;
+      }
+    }
+    __syncwarp();
+    float dg[16], dh[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      dg[j] = tbl[g * 17 + j];
+      dh[j] = tbl[(g + 8) * 17 + j];
+    }
+    uint32_t wv[24];
+#pragma unroll
+    for (int v = 0; v < 6; ++v) {
+      const uint4 u = ld_b16(grp + 288 + v * 512 + lane * 16);
+      wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
+    }
+    constexpr uint32_t C = 0x64006400u, M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const uint32_t X = wv[3 * p], Y = wv[3 * p + 1], Z = wv[3 * p + 2];
+      const uint32_t aa0 = lop_and_or(X, M6, C), aa1 = lop_and_or(Y, M6, C);
+      const uint32_t aa2 = lop_and_or(X >> 6, M6, C), aa3 = lop_and_or(Y >> 6, M6, C);
+      const uint32_t ab0 = lop_and_or(Z, M6, C);
+      const uint32_t ab1 = lop_and_or(X >> 12, M4, C) | ((Z >> 8) & M2);
+      const uint32_t ab2 = lop_and_or(Z >> 6, M6, C);
+      const uint32_t ab3 = lop_and_or(Y >> 12, M4, C) | ((Z >> 10) & M2);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int col = nt * 8 + g;
+        uint2 ba = make_uint2(0, 0), bb = make_uint2(0, 0);
+        if (col < ncol) {
+          ba = ld_b8(xg + col * xstride + p * 64 + tq * 8);
+          bb = ld_b8(xg + col * xstride + p * 64 + 32 + tq * 8);
+        }
+        const float2 xa = *reinterpret_cast<const float2*>(tg + (2 * p) * ncol8 + nt * 8 + 2 * tq);
+        const float2 xb = *reinterpret_cast<const float2*>(tg + (2 * p + 1) * ncol8 + nt * 8 + 2 * tq);
+        float ta[4], tb[4];
+        mma_f16(ta, aa0, aa1, aa2, aa3, ba.x, ba.y, xa.x, xa.y, xa.x, xa.y);
+        mma_f16(tb, ab0, ab1, ab2, ab3, bb.x, bb.y, xb.x, xb.y, xb.x, xb.y);
+        acc[nt][0] = fmaf(dg[2 * p], ta[0], fmaf(dg[2 * p + 1], tb[0], acc[nt][0]));
+        acc[nt][1] = fmaf(dg[2 * p], ta[1], fmaf(dg[2 * p + 1], tb[1], acc[nt][1]));
+        acc[nt][2] = fmaf(dh[2 * p], ta[2], fmaf(dh[2 * p + 1], tb[2], acc[nt][2]));
+        acc[nt][3] = fmaf(dh[2 * p], ta[3], fmaf(dh[2 * p + 1], tb[3], acc[nt][3]));
+      }
+    }
+    __syncwarp();
+  } else if constexpr (FMT == FMT_Q80) {
+    const float dg = __half2float(*reinterpret_cast<const __half*>(grp + 2 * g));
+    const float dh = __half2float(*reinterpret_cast<const __half*>(grp + 2 * (g + 8)));
+    const uint4 q = ld_b16(grp + 32 + lane * 16);
+    const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u, u2 = q.z ^ 0x80808080u,
+                   u3 = q.w ^ 0x80808080u;
+    const uint32_t K64 = 0x64646464u;
+    const uint32_t a0 = prmt(u0, K64, 0x4240), a1 = prmt(u2, K64, 0x4240);
+    const uint32_t a2 = prmt(u0, K64, 0x4341), a3 = prmt(u2, K64, 0x4341);
+    const uint32_t b0 = prmt(u1, K64, 0x4240), b1 = prmt(u3, K64, 0x4240);
+    const uint32_t b2 = prmt(u1, K64, 0x4341), b3 = prmt(u3, K64, 0x4341);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + g;
+      const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + tq * 16) : make_uint4(0, 0, 0, 0);
+      const float2 xo = *reinterpret_cast<const float2*>(tg + nt * 8 + 2 * tq);
+      float t4[4];
+      mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, xo.x, xo.y, xo.x, xo.y);
+      mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
+      acc[nt][0] = fmaf(dg, t4[0], acc[nt][0]);
+      acc[nt][1] = fmaf(dg, t4[1], acc[nt][1]);
+      acc[nt][2] = fmaf(dh, t4[2], acc[nt][2]);
+      acc[nt][3] = fmaf(dh, t4[3], acc[nt][3]);
+    }
+  } else {  // FMT_FP8
+    const uint4 q = ld_b16(grp + lane * 16);
+    const uint32_t p0 = prmt(q.x, 0u, 0x3120), p1 = prmt(q.y, 0u, 0x3120);
+    const uint32_t p2 = prmt(q.z, 0u, 0x3120), p3 = prmt(q.w, 0u, 0x3120);
+    const uint32_t a0 = e4m3x2_to_f16x2((uint16_t)(p0 & 0xFFFFu)), a1 = e4m3x2_to_f16x2((uint16_t)(p2 & 0xFFFFu));
+    const uint32_t a2 = e4m3x2_to_f16x2((uint16_t)(p0 >> 16)), a3 = e4m3x2_to_f16x2((uint16_t)(p2 >> 16));
+    const uint32_t b0 = e4m3x2_to_f16x2((uint16_t)(p1 & 0xFFFFu)), b1 = e4m3x2_to_f16x2((uint16_t)(p3 & 0xFFFFu));
+    const uint32_t b2 = e4m3x2_to_f16x2((uint16_t)(p1 >> 16)), b3 = e4m3x2_to_f16x2((uint16_t)(p3 >> 16));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + g;
+      const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + tq * 16) : make_uint4(0, 0, 0, 0);
+      mma_f16(acc[nt], a0, a1, a2, a3, bx.x, bx.y, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+      mma_f16(acc[nt], b0, b1, b2, b3, bx.z, bx.w, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    }
+  }
+}
+
+
+struct Args {
+  const uint8_t* w;
+  const float* row_scale;  // FP8
+  int scale_len;
+  const uint8_t* cols;
+  const float* tab;
+  const float* tscale;
+  int M, P, ncol, ncol8;
+  const float* bias;
+  void* y;
+  int64_t ldy;
+  int y_dtype;
+  int64_t N;
+  int G, CI;          // groups per row, items per tile
+  int64_t I, WT;      // items in total, warps in the grid
+  int NS;
+  int warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar;
+  float* part;
+  uint32_t* counters;
+  int* status;
+};
+
+__device__ __forceinline__ void store_y(const Args& a, int t, int64_t n, float v) {
+  const int64_t off = (int64_t)t * a.ldy + n;
+  if (a.y_dtype == 0)
+    static_cast<float*>(a.y)[off] = v;
+  else if (a.y_dtype == 1)
+    static_cast<__half*>(a.y)[off] = __float2half_rn(v);
+  else
+    static_cast<__nv_bfloat16*>(a.y)[off] = __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ int64_t item_start(int64_t w, int64_t I, int64_t WT) { return w * I / WT; }
+// The warp whose item range contains item i.
+__device__ __forceinline__ int64_t warp_of(int64_t i, int64_t I, int64_t WT) { return ((i + 1) * WT - 1) / I; }
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(const Args a) {
+  using F = FmtC<FMT>;
+  constexpr int CSB = col_stride_bytes(F::GK);
+  constexpr int NSB = F::GK / F::SBE;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
+  if (gw >= a.WT) return;  // the last CTA may carry warps past the plan; the rest never wait on them
+  const int64_t i0 = item_start(gw, a.I, a.WT), i1 = item_start(gw + 1, a.I, a.WT);
+  const int64_t n_items = i1 - i0;
+  uint8_t* wb = sm + (size_t)warp * a.warp_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(wb + a.off_bar);
+  uint8_t* tblw = wb + a.off_tbl;
+  const int NS = a.NS;
+
+  auto geom = [&](int64_t item, int64_t& tile, int& g0, int& ng) {
+    tile = item / a.CI;
+    g0 = (int)(item - tile * a.CI) * F::IG;
+    ng = min(F::IG, a.G - g0);
+  };
+  auto bytes_of = [&](int ng) -> uint32_t {
+    uint32_t b = (uint32_t)ng * F::GB + (uint32_t)ng * a.ncol * CSB;
+    if constexpr (F::TAB) b += (uint32_t)ng * NSB * a.ncol8 * 4;
+    return b;
+  };
+  auto issue_w = [&](int s, int64_t item) {
+    int64_t tile; int g0, ng;
+    geom(item, tile, g0, ng);
+    mbar_arrive_expect_tx(&bar[s], bytes_of(ng));
+    bulk_g2s(wb + (size_t)s * a.slot_bytes, a.w + ((size_t)tile * a.G + g0) * F::GB, (uint32_t)ng * F::GB, &bar[s]);
+  };
+  auto issue_x = [&](int s, int64_t item) {
+    int64_t tile; int g0, ng;
+    geom(item, tile, g0, ng);
+    uint8_t* slot = wb + (size_t)s * a.slot_bytes;
+    bulk_g2s(slot + a.off_x, a.cols + (size_t)g0 * a.ncol * CSB, (uint32_t)ng * a.ncol * CSB, &bar[s]);
+    if constexpr (F::TAB)
+      bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * NSB * a.ncol8, (uint32_t)ng * NSB * a.ncol8 * 4, &bar[s]);
+  };
+
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const int npro = (int)(n_items < NS ? n_items : NS);
+  if (lane == 0)
+    for (int s = 0; s < npro; ++s) issue_w(s, i0 + s);  // weights go out before x is known to be ready
+  griddep_wait();                                       // the prep kernel's output is visible from here on
+  if (lane == 0)
+    for (int s = 0; s < npro; ++s) issue_x(s, i0 + s);
+
+  // token scales of this lane's accumulator columns
+  float tsr[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int col = nt * 8 + 2 * tq + cc;
+      const int t = col / a.P;
+      tsr[nt][cc] = (col < a.ncol) ? a.tscale[t] : 0.0f;
+    }
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+  float eb[2] = {0.0f, 0.0f}, es[2] = {1.0f, 1.0f};  // bias / channel scale of rows g, g+8
+  const int64_t t_first = i0 / a.CI;
+
+  for (int64_t i = 0; i < n_items; ++i) {
+    const int s = (int)(i % NS);
+    const int64_t item = i0 + i;
+    int64_t tile; int g0, ng;
+    geom(item, tile, g0, ng);
+    const int ci = (int)(item - tile * a.CI);
+    if (ci == 0 || i == 0) {  // a new tile: fetch its epilogue operands early
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int64_t n = tile * 16 + g + 8 * rr;
+        eb[rr] = (a.bias && n < a.N) ? __ldg(a.bias + n) : 0.0f;
+        if constexpr (FMT == FMT_FP8) es[rr] = (n < a.N) ? __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n)) : 1.0f;
+      }
+    }
+    mbar_wait_bounded(&bar[s], (uint32_t)(i / NS) & 1u, a.status);
+    const uint8_t* slot = wb + (size_t)s * a.slot_bytes;
+    for (int gi = 0; gi < ng; ++gi) {
+      const uint8_t* xg = slot + a.off_x + gi * a.ncol * CSB;
+      const float* tg = reinterpret_cast<const float*>(slot + a.off_tab) + gi * NSB * a.ncol8;
+      do_group<FMT, NT>(slot + (size_t)gi * F::GB, xg, CSB, tg, a.ncol, a.ncol8, tblw, acc, lane);
+    }
+    __syncwarp();
+    if (lane == 0 && i + NS < n_items) {
+      issue_w(s, item + NS);
+      issue_x(s, item + NS);
+    }
+    if (ci != a.CI - 1 && i != n_items - 1) continue;
+
+    // ---- tile boundary: write from the accumulators, or hand a partial to the last warp
+    const bool whole = (tile * a.CI >= i0) && (tile * a.CI + a.CI - 1 < i1);
+    const int pslot = (tile == t_first) ? 0 : 1;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = g + 8 * rr;
+        const int64_t n = tile * 16 + r;
+        float v[2];
+        int tt[2], nv;
+        if (a.P == 2) {  // columns 2tq, 2tq+1 are the hi and lo halves of one token
+          tt[0] = nt * 4 + tq;
+          v[0] = (acc[nt][2 * rr] + acc[nt][2 * rr + 1]) * tsr[nt][0];
+          nv = 1;
+        } else {
+          tt[0] = nt * 8 + 2 * tq;
+          tt[1] = tt[0] + 1;
+          v[0] = acc[nt][2 * rr] * tsr[nt][0];
+          v[1] = acc[nt][2 * rr + 1] * tsr[nt][1];
+          nv = 2;
+        }
+        for (int q = 0; q < nv; ++q) {
+          if (tt[q] >= a.M || n >= a.N) continue;
+          float val = v[q];
+          if constexpr (FMT == FMT_FP8) val *= es[rr];
+          if (whole)
+            store_y(a, tt[q], n, val + eb[rr]);
+          else
+            a.part[(((size_t)gw * 2 + pslot) * 16 + r) * a.M + tt[q]] = val;
+        }
+      }
+      acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+    }
+    if (!whole) {
+      __threadfence();
+      __syncwarp();
+      const int64_t wf = warp_of(tile * a.CI, a.I, a.WT), wl = warp_of(tile * a.CI + a.CI - 1, a.I, a.WT);
+      int last = 0;
+      if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (uint32_t)(wl - wf));
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        for (int o = lane; o < 16 * a.M; o += 32) {
+          const int r = o / a.M, t = o - r * a.M;
+          const int64_t n = tile * 16 + r;
+          if (n >= a.N) continue;
+          float sum = 0.0f;
+          for (int64_t ww = wf; ww <= wl; ++ww) {
+            const int ps = (tile == item_start(ww, a.I, a.WT) / a.CI) ? 0 : 1;
+            sum += __ldcg(&a.part[((size_t)(ww * 2 + ps) * 16 + r) * a.M + t]);
+          }
+          store_y(a, t, n, sum + (a.bias ? __ldg(a.bias + n) : 0.0f));
+        }
+        if (lane == 0) a.counters[tile] = 0u;
+      }
+    }
+  }
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Plan {
+  int NS, warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar;
+  size_t smem;
+};
+
+Plan make_plan(int fmt, int ncol, int ncol8, int ns_pref) {
+  const FmtInfo f = fmt_info(fmt);
+  const int IG = (f.gk == 256) ? 1 : 8;
+  const bool tab = fmt != FMT_FP8;
+  const int csb = col_stride_bytes(f.gk);
+  Plan p{};
+  const size_t off_x = align_up((size_t)IG * f.gb, 128);
+  const size_t off_tab = align_up(off_x + (size_t)IG * ncol * csb, 16);
+  const size_t slot = align_up(off_tab + (tab ? (size_t)IG * (f.gk / f.sbe) * ncol8 * 4 : 0), 128);
+  // prefer two CTAs per SM (<= 113 KB each); keep at least two stages in flight
+  int NS = ns_pref;
+  auto warp_bytes = [&](int ns) { return align_up(ns * slot + kTblBytes + kMaxStages * 8, 128); };
+  while (NS > 2 && warp_bytes(NS) * kWarps > 113 * 1024) --NS;
+  p.NS = NS;
+  p.slot_bytes = (int)slot;
+  p.off_x = (int)off_x;
+  p.off_tab = (int)off_tab;
+  p.off_tbl = (int)(NS * slot);
+  p.off_bar = (int)(NS * slot + kTblBytes);
+  p.warp_bytes = (int)warp_bytes(NS);
+  p.smem = (size_t)p.warp_bytes * kWarps;
+  return p;
+}
+
+// Resident CTAs per SM for this instantiation at this shared-memory size (cached per device).
+template <int FMT, int NT>
+int gemv_occupancy(size_t smem) {
+  static size_t last_smem[64] = {0};
+  static int last_occ[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (last_smem[dev & 63] != smem) {
+    cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int occ = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qgemv_kernel<FMT, NT>, kThreads, smem) != cudaSuccess ||
+        occ < 1)
+      occ = 1;
+    last_occ[dev & 63] = occ;
+    last_smem[dev & 63] = smem;
+  }
+  return last_occ[dev & 63];
+}
+
+template <int FMT>
+int occupancy_nt(int NT, size_t smem) {
+  switch (NT) {
+    case 1: return gemv_occupancy<FMT, 1>(smem);
+    case 2: return gemv_occupancy<FMT, 2>(smem);
+    case 3: return gemv_occupancy<FMT, 3>(smem);
+    default: return gemv_occupancy<FMT, 4>(smem);
+  }
+}
+
+int occupancy_of(int fmt, int NT, size_t smem) {
+  switch (fmt) {
+    case FMT_Q4K: return occupancy_nt<FMT_Q4K>(NT, smem);
+    case FMT_Q6K: return occupancy_nt<FMT_Q6K>(NT, smem);
+    case FMT_Q80: return occupancy_nt<FMT_Q80>(NT, smem);
+    default: return occupancy_nt<FMT_FP8>(NT, smem);
+  }
+}
+
+template <int FMT, int NT>
+cudaError_t launch_gemv(const Args& a, unsigned nctas, size_t smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nctas);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qgemv_kernel<FMT, NT>, a);
+}
+
+template <int FMT>
+cudaError_t launch_gemv_nt(const Args& a, int NT, unsigned nctas, size_t smem, cudaStream_t st) {
+  switch (NT) {
+    case 1: return launch_gemv<FMT, 1>(a, nctas, smem, st);
+    case 2: return launch_gemv<FMT, 2>(a, nctas, smem, st);
+    case 3: return launch_gemv<FMT, 3>(a, nctas, smem, st);
+    default: return launch_gemv<FMT, 4>(a, nctas, smem, st);
+  }
+}
+
+template <int FMT>
+cudaError_t launch_prep(const PrepArgs& p, cudaStream_t st) {
+  prep_kernel<FMT><<<p.M * kPrepCluster, kPrepThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+__global__ void fill_rows_kernel(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    const float v = bias ? bias[n] : 0.0f;
+    const int64_t off = m * ldy + n;
+    if (y_dtype == 0)
+      static_cast<float*>(y)[off] = v;
+    else if (y_dtype == 1)
+      static_cast<__half*>(y)[off] = __float2half_rn(v);
+    else
+      static_cast<__nv_bfloat16*>(y)[off] = __float2bfloat16_rn(v);
+  }
+}
+
+cudaError_t launch_fill_rows(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N,
+                             cudaStream_t st) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  int64_t blocks = (M * N + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  fill_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(bias, y, y_dtype, ldy, M, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
+  *plan_error = 0;
+  if (c.M <= 0 || c.N <= 0) return cudaSuccess;
+  const FmtInfo f = fmt_info(c.fmt);
+  const int IG = (f.gk == 256) ? 1 : 8;
+  const int64_t T = tiles_for(c.N);
+  const int64_t G = c.G;
+  const int64_t kp = G * f.gk;
+  const int64_t CI = (G + IG - 1) / IG;
+  const int64_t I = T * CI;
+  const int P = (c.x_dtype == 0 && !c.w8a8) ? 2 : 1;
+  const int max_tokens = 32 / P;
+  static const int env_ns = [] {
+    const char* s = std::getenv("RTD_GEMV_STAGES");
+    const int v = s ? std::atoi(s) : 0;
+    return (v >= 2 && v <= kMaxStages) ? v : kMaxStages;
+  }();
+  static const int env_ctas = [] {
+    const char* s = std::getenv("RTD_GEMV_CTAS_PER_SM");
+    return s ? std::atoi(s) : 0;
+  }();
+  const size_t esz = (c.x_dtype == 0) ? 4 : 2;
+  const bool x_vec = ((uintptr_t)c.x % 16 == 0) && ((c.ldx * (int64_t)esz) % 16 == 0);
+  if (T > c.n_counters) {
+    *plan_error = 1;
+    return cudaSuccess;
+  }
+
+  for (int64_t m0 = 0; m0 < c.M;) {
+    int Mt = (int)std::min<int64_t>(max_tokens, c.M - m0);
+    // fewer tokens per launch when the activation slices would not fit shared memory
+    while (Mt > 1 && make_plan(c.fmt, Mt * P, 8 * ((Mt * P + 7) / 8), env_ns).smem > 220 * 1024) Mt = (Mt + 1) / 2;
+    const int ncol = Mt * P;
+    const int NT = (ncol + 7) / 8;
+    const int ncol8 = 8 * NT;
+    const Plan pl = make_plan(c.fmt, ncol, ncol8, env_ns);
+    int occ = occupancy_of(c.fmt, NT, pl.smem);
+    if (env_ctas > 0) occ = std::min(occ, env_ctas);
+    const int64_t WT = std::min<int64_t>(I, (int64_t)c.sm_count * occ * kWarps);
+    const unsigned nctas = (unsigned)((WT + kWarps - 1) / kWarps);
+    const int64_t WTg = WT;  // WT <= I: every planned warp owns at least one item
+    // workspace carve: cols | tab | tscale | partials
+    const size_t cols_b = align_up((size_t)G * ncol * col_stride_bytes(f.gk), 256);
+    const size_t tab_b = align_up((size_t)(kp / f.sbe) * ncol8 * 4, 256);
+    const size_t ts_b = 256;
+    const size_t part_b = (size_t)WTg * 2 * 16 * Mt * 4;
+    (void)nctas;
+    if (cols_b + tab_b + ts_b + part_b > c.ws_bytes) {
+      *plan_error = 1;
+      return cudaSuccess;
+    }
+    uint8_t* ws = reinterpret_cast<uint8_t*>(c.ws);
+    uint8_t* cols = ws;
+    float* tab = reinterpret_cast<float*>(ws + cols_b);
+    float* tscale = reinterpret_cast<float*>(ws + cols_b + tab_b);
+    float* part = reinterpret_cast<float*>(ws + cols_b + tab_b + ts_b);
+
+    PrepArgs pa{};
+    pa.x = static_cast<const uint8_t*>(c.x) + (size_t)(m0 * c.ldx) * esz;
+    pa.x_dtype = c.x_dtype;
+    pa.x_vec = x_vec ? 1 : 0;
+    pa.ldx = c.ldx;
+    pa.K = c.K;
+    pa.kp = kp;
+    pa.M = Mt;
+    pa.P = P;
+    pa.ncol = ncol;
+    pa.ncol8 = ncol8;
+    pa.w8a8 = c.w8a8;
+    pa.cols = cols;
+    pa.tab = tab;
+    pa.tscale = tscale;
+    cudaError_t e;
+    switch (c.fmt) {
+      case FMT_Q4K: e = launch_prep<FMT_Q4K>(pa, c.stream); break;
+      case FMT_Q6K: e = launch_prep<FMT_Q6K>(pa, c.stream); break;
+      case FMT_Q80: e = launch_prep<FMT_Q80>(pa, c.stream); break;
+      default:      e = launch_prep<FMT_FP8>(pa, c.stream); break;
+    }
+    if (e != cudaSuccess) return e;
+
+    Args a{};
+    a.w = c.w;
+    a.row_scale = c.row_scale;
+    a.scale_len = c.scale_len;
+    a.cols = cols;
+    a.tab = tab;
+    a.tscale = tscale;
+    a.M = Mt;
+    a.P = P;
+    a.ncol = ncol;
+    a.ncol8 = ncol8;
+    a.bias = c.bias;
+    const size_t ysz = (c.y_dtype == 0) ? 4 : 2;
+    a.y = static_cast<uint8_t*>(c.y) + (size_t)(m0 * c.ldy) * ysz;
+    a.ldy = c.ldy;
+    a.y_dtype = c.y_dtype;
+    a.N = c.N;
+    a.G = (int)G;
+    a.CI = (int)CI;
+    a.I = I;
+    a.WT = WTg;
+    a.NS = pl.NS;
+    a.warp_bytes = pl.warp_bytes;
+    a.slot_bytes = pl.slot_bytes;
+    a.off_x = pl.off_x;
+    a.off_tab = pl.off_tab;
+    a.off_tbl = pl.off_tbl;
+    a.off_bar = pl.off_bar;
+    a.part = part;
+    a.counters = c.counters;
+    a.status = c.status;
+    switch (c.fmt) {
+      case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, nctas, pl.smem, c.stream); break;
+      case FMT_Q6K: e = launch_gemv_nt<FMT_Q6K>(a, NT, nctas, pl.smem, c.stream); break;
+      case FMT_Q80: e = launch_gemv_nt<FMT_Q80>(a, NT, nctas, pl.smem, c.stream); break;
+      default:      e = launch_gemv_nt<FMT_FP8>(a, NT, nctas, pl.smem, c.stream); break;
+    }
+    if (e != cudaSuccess) return e;
+    m0 += Mt;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace rtd

@@ -1,0 +1,308 @@
+"""Host-side operator surface: the reference's Weights / QMatMul / Fp8Weight, on the C ABI.
+
+Mirrors, with the same names, argument meaning and error behaviour:
+  * ``QMatMul``  -- candle's QMatMul::QTensor as built by load_quantized_tensor
+                    (crates/runtimed-model/src/weights/load_gguf.rs:28-38): forward,
+                    embedding, dequantize, storage size;
+  * ``Fp8Weight`` -- crates/runtimed-model/src/weights/fp8_weight.rs:9-97;
+  * ``Weights``  -- crates/runtimed-model/src/weights/store.rs:12-101 (map / q_map,
+                    q_matmul, resident_bytes, get) with linear / linear_bias
+                    (linear_layer.rs:45-118) and embed (embed_layer.rs:16-57).
+
+Tensors are torch tensors (device memory, streams); every byte of arithmetic runs
+in libruntimed_b200.so.  There is no CPU path: a CPU tensor handed to a device
+weight is moved to the weight's device first, as the reference does with
+``x.to_device(dev)`` (linear_layer.rs:49).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check
+from .errors import ConfigError, GgufError, MissingWeight, ShapeError
+
+_DT = {torch.float32: _lib.DT_F32, torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}
+_BLOCK = {_lib.TYPE_Q8_0: (32, 34), _lib.TYPE_Q4_K: (256, 144), _lib.TYPE_Q6_K: (256, 210)}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _raise(status: int, ctx_handle) -> None:
+    """Map an rtd_status to the reference's ModelError variants."""
+    if status == _lib.RTD_OK:
+        return
+    msg = _lib.lib().rtd_last_error(ctx_handle)
+    text = msg.decode() if msg else ""
+    if status in (_lib.RTD_ERR_UNSUPPORTED, _lib.RTD_ERR_TRUNCATED):
+        raise GgufError(text)
+    if status == _lib.RTD_ERR_SHAPE:
+        raise ShapeError("rtd", [], [])  # callers check shapes first; this is a backstop
+    raise ConfigError(f"rtd status {status}: {text}")
+
+
+class Context:
+    """One CUDA device bound to the library (rtd_init); owns the kernels' workspace."""
+
+    _by_device: Dict[int, "Context"] = {}
+
+    def __init__(self, device: int = 0):
+        h = ctypes.c_void_p()
+        check(_lib.lib().rtd_init(device, ctypes.byref(h)))
+        self.handle = h
+        self.device = torch.device("cuda", device)
+
+    @classmethod
+    def for_device(cls, device) -> "Context":
+        idx = torch.device(device).index
+        idx = torch.cuda.current_device() if idx is None else idx
+        ctx = cls._by_device.get(idx)
+        if ctx is None:
+            ctx = cls(idx)
+            cls._by_device[idx] = ctx
+        return ctx
+
+    def check_device_status(self, stream: Optional[int] = None) -> None:
+        s = _stream_ptr(self.device) if stream is None else stream
+        _raise(_lib.lib().rtd_check_device_status(self.handle, s), self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.lib().rtd_destroy(self.handle)
+            self.handle = None
+
+
+class QMatMul:
+    """A quantized [N, K] matrix resident on one device (candle QMatMul::QTensor)."""
+
+    def __init__(self, ggml_type: int, raw, n: int, k: int, device="cuda:0"):
+        if ggml_type not in _BLOCK:
+            raise GgufError(f"unsupported ggml type {ggml_type} for QMatMul on this path")
+        self.ctx = Context.for_device(device)
+        self.ggml_type = int(ggml_type)
+        self.n, self.k = int(n), int(k)
+        buf = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
+                                   else np.asarray(raw, dtype=np.uint8).reshape(-1))
+        h = ctypes.c_void_p()
+        st = _lib.lib().rtd_qweight_upload(self.ctx.handle, self.ggml_type, buf.ctypes.data_as(ctypes.c_void_p),
+                                           buf.size, self.n, self.k, ctypes.byref(h))
+        if st == _lib.RTD_ERR_SHAPE:
+            elems = _BLOCK[self.ggml_type][0]
+            raise GgufError(f"{self.k} not a multiple of {elems}")
+        _raise(st, self.ctx.handle)
+        self.handle = h
+        raw_b, dev_b = ctypes.c_size_t(), ctypes.c_size_t()
+        check(_lib.lib().rtd_qweight_info(h, None, None, None, ctypes.byref(raw_b), ctypes.byref(dev_b)))
+        self._raw_bytes, self._dev_bytes = raw_b.value, dev_b.value
+
+    # -- candle QTensor surface
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+    @property
+    def device(self) -> torch.device:
+        return self.ctx.device
+
+    def storage_size_in_bytes(self) -> int:
+        return self._raw_bytes
+
+    def device_bytes(self) -> int:
+        return self._dev_bytes
+
+    def forward(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """y = x . W^T (+ bias); leading dims of x are kept, the last becomes N."""
+        if x.dim() == 0 or x.shape[-1] != self.k:
+            raise ShapeError("qmatmul", [self.k], list(x.shape))
+        if x.dtype not in _DT:
+            x = x.to(torch.float32)
+        if x.device != self.device:
+            x = x.to(self.device)
+        m = 1
+        for d in x.shape[:-1]:
+            m *= int(d)
+        x2 = x.reshape(m, self.k)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        out_dtype = out_dtype or x.dtype
+        y = torch.empty((m, self.n), dtype=out_dtype, device=self.device)
+        b = None
+        if bias is not None:
+            b = bias.to(device=self.device, dtype=torch.float32).contiguous()
+            if b.numel() != self.n:
+                raise ShapeError("bias", [self.n], list(bias.shape))
+        st = _lib.lib().rtd_qlinear(self.ctx.handle, self.handle, x2.data_ptr(), _DT[x2.dtype], self.k, m,
+                                    None if b is None else b.data_ptr(), y.data_ptr(), _DT[out_dtype], self.n,
+                                    _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return y.reshape(*x.shape[:-1], self.n)
+
+    __call__ = forward
+
+    def embedding(self, ids: torch.Tensor) -> torch.Tensor:
+        """f32 rows ids of the dequantized matrix (QMatMul::embedding)."""
+        ids_d = ids.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous()
+        y = torch.empty((ids_d.numel(), self.k), dtype=torch.float32, device=self.device)
+        st = _lib.lib().rtd_qembed(self.ctx.handle, self.handle, ids_d.data_ptr(), ids_d.numel(), y.data_ptr(),
+                                   _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return y
+
+    def dequantize(self) -> torch.Tensor:
+        """The whole matrix as f32 [N, K], bit-exact with the reference decoders."""
+        y = torch.empty((self.n, self.k), dtype=torch.float32, device=self.device)
+        st = _lib.lib().rtd_qdequant(self.ctx.handle, self.handle, y.data_ptr(), _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return y
+
+    def free(self) -> None:
+        if getattr(self, "handle", None):
+            _lib.lib().rtd_qweight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Fp8Weight:
+    """FP8 E4M3 weight [out, in] with a per-channel (or per-tensor) f32 scale."""
+
+    def __init__(self, weight, scale, in_dim: int, out_dim: int, device="cuda:0"):
+        w = np.ascontiguousarray(np.asarray(weight, dtype=np.uint8))
+        s = np.ascontiguousarray(np.asarray(scale, dtype=np.float32))
+        if list(w.shape) != [out_dim, in_dim]:
+            raise ShapeError("fp8_weight", [out_dim, in_dim], list(w.shape))
+        if list(s.shape) not in ([out_dim], [out_dim, 1]) and s.size != 1:
+            raise ShapeError("fp8_scale", [out_dim], list(s.shape))
+        self.in_dim, self.out_dim = int(in_dim), int(out_dim)
+        self.ctx = Context.for_device(device)
+        h = ctypes.c_void_p()
+        s = s.reshape(-1)
+        _raise(_lib.lib().rtd_fp8weight_upload(self.ctx.handle, w.ctypes.data_as(ctypes.c_void_p),
+                                               s.ctypes.data_as(ctypes.c_void_p), s.size, out_dim, in_dim,
+                                               ctypes.byref(h)), self.ctx.handle)
+        self.handle = h
+        self._bytes = w.size + 4 * s.size
+
+    @property
+    def device(self) -> torch.device:
+        return self.ctx.device
+
+    def resident_bytes(self) -> int:
+        return self._bytes
+
+    def forward(self, x: torch.Tensor, mode: str = "w8a16") -> torch.Tensor:
+        """y = x . (E4M3(W) * s)^T.  mode "w8a8" first encodes x to E4M3 like the
+        reference CUDA path; output is f16 for f16 input, else f32 (fp8_gemm.rs:106)."""
+        if x.shape[-1] != self.in_dim:
+            raise ShapeError("fp8_gemm", [self.in_dim], list(x.shape))
+        if x.dtype not in _DT:
+            x = x.to(torch.float32)
+        x = x.to(self.device)
+        m = 1
+        for d in x.shape[:-1]:
+            m *= int(d)
+        x2 = x.reshape(m, self.in_dim).contiguous()
+        out_dtype = torch.float16 if x.dtype == torch.float16 else torch.float32
+        y = torch.empty((x2.shape[0], self.out_dim), dtype=out_dtype, device=self.device)
+        m = {"w8a16": _lib.FP8_W8A16, "w8a8": _lib.FP8_W8A8}[mode]
+        st = _lib.lib().rtd_fp8_linear(self.ctx.handle, self.handle, x2.data_ptr(), _DT[x2.dtype], self.in_dim,
+                                       x2.shape[0], y.data_ptr(), _DT[out_dtype], self.out_dim, m,
+                                       _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return y.reshape(*x.shape[:-1], self.out_dim)
+
+    def free(self) -> None:
+        if getattr(self, "handle", None):
+            _lib.lib().rtd_fp8weight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def fp8_encode(x: torch.Tensor) -> torch.Tensor:
+    """Device E4M3 encoding of f32 x with the reference rounding (uint8 codes)."""
+    x = x.to(torch.float32).contiguous()
+    ctx = Context.for_device(x.device)
+    out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    _raise(_lib.lib().rtd_fp8_encode(ctx.handle, x.data_ptr(), x.numel(), out.data_ptr(), _stream_ptr(x.device)),
+           ctx.handle)
+    return out
+
+
+class Weights:
+    """The reference's weight store: dense tensors in ``map``, quantized in ``q_map``."""
+
+    def __init__(self, device="cuda:0", map: Optional[dict] = None, q_map: Optional[dict] = None,
+                 fp8_map: Optional[dict] = None):
+        self.dev = torch.device(device)
+        self.map: Dict[str, torch.Tensor] = dict(map or {})
+        self.q_map: Dict[str, QMatMul] = dict(q_map or {})
+        self.fp8_map: Dict[str, Fp8Weight] = dict(fp8_map or {})
+
+    def device(self) -> torch.device:
+        return self.dev
+
+    def q_matmul(self, name: str) -> Optional[QMatMul]:
+        return self.q_map.get(name)
+
+    def resident_bytes(self) -> int:
+        dense = sum(t.numel() * t.element_size() for t in self.map.values())
+        seen, quant = set(), 0
+        for qm in self.q_map.values():
+            if id(qm) not in seen:
+                seen.add(id(qm))
+                quant += qm.storage_size_in_bytes()
+        fp8 = sum(w.resident_bytes() for w in {id(w): w for w in self.fp8_map.values()}.values())
+        return dense + quant + fp8
+
+    def get(self, name: str) -> torch.Tensor:
+        if name in self.map:
+            return self.map[name].to(torch.float32)
+        if name in self.q_map:
+            return self.q_map[name].dequantize()
+        raise MissingWeight(name)
+
+    def linear(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        qm = self.q_map.get(name)
+        if qm is not None:
+            return qm.forward(x)
+        fw = self.fp8_map.get(name)
+        if fw is not None:
+            return fw.forward(x).to(x.dtype)
+        raise MissingWeight(name)
+
+    def linear_bias(self, x: torch.Tensor, name: str, bias: Optional[str] = None) -> torch.Tensor:
+        if bias is None:
+            return self.linear(x, name)
+        b = self.get(bias)
+        qm = self.q_map.get(name)
+        if qm is not None:
+            return qm.forward(x, bias=b)
+        y = self.linear(x, name)
+        return y + b.to(device=y.device, dtype=y.dtype)
+
+    def embed(self, name: str, ids) -> torch.Tensor:
+        qm = self.q_map.get(name)
+        if qm is None:
+            raise MissingWeight(name)
+        ids_t = torch.as_tensor(np.asarray(ids, dtype=np.int64) if not torch.is_tensor(ids) else ids)
+        if ids_t.numel() == 0:
+            return torch.zeros((1, 0, qm.k), dtype=torch.float32, device=qm.device)
+        if int(ids_t.max()) >= qm.n or int(ids_t.min()) < 0:
+            raise ConfigError(f"embedding id out of range for {name} with {qm.n} rows")
+        return qm.embedding(ids_t).unsqueeze(0)
