@@ -1,0 +1,370 @@
+"""Benchmark of the quantized decode-GEMV hot path on B200 (driver contract: one JSON line).
+
+Workload (the reference's op-sweep config): y = x . W^T at M = 1 (one decode
+token, bf16 activations) for every feasible (format, shape) of
+  formats Q4_K, Q6_K, Q8_0 (GGUF blocks) and FP8 E4M3 (per-channel scale)
+  shapes (N, K) = (4096, 4096), (14336, 4096), (4096, 14336), (151936, 896)
+(Q4_K / Q6_K need K % 256 == 0, so their K = 896 points are infeasible).
+A "step" is one pass over the 14 GEMVs; every step reads 0.74 GB of distinct
+weights, well above the 126 MB L2, so each weight byte comes from HBM.
+
+Metric: quant-GEMV HBM GB/s from algorithmic bytes (packed weights + x + y (+ FP8
+channel scales)); dequantized weights never count.  value = device-timed
+(weights and x resident in HBM, CUDA graph of the step, CUDA events); e2e = the
+same through the C ABI with the activation copied from pinned host memory and
+the output read back every call.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank its own copy of the sweep
+(weak scaling: independent weight shards), max time over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (151936, 896)]
+FORMATS = [("Q4_K", 12), ("Q6_K", 14), ("Q8_0", 8), ("FP8", 0)]
+METRIC = "quant-GEMV HBM GB/s (decode M=1, config-1 sweep)"
+UNIT = "GB/s"
+
+
+def sweep():
+    out = []
+    for name, t in FORMATS:
+        for (n, k) in SHAPES:
+            if t in (12, 14) and k % 256:
+                continue
+            out.append((name, t, n, k))
+    return out
+
+
+def weight_bytes(t, n, k):
+    if t == 0:
+        return n * k + 4 * n
+    elems, bb = {8: (32, 34), 12: (256, 144), 14: (256, 210)}[t]
+    return n * (k // elems) * bb
+
+
+def alg_bytes(t, n, k, m=1):
+    return weight_bytes(t, n, k) + m * k * 2 + m * n * 2  # bf16 x in, bf16 y out
+
+
+def read_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_tag: str):
+    """dram bytes per launch recorded in profiles/<kernel_tag>.md (line 'dram_bytes_per_launch: N')."""
+    p = os.path.join(ROOT, "profiles", kernel_tag + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"rtd_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(budget_s: float = 20.0):
+    """The restated reference CPU path (oracle/: bit-exact block decode + f32 dot,
+    OpenMP over all host threads) on a bounded row sample of every sweep point."""
+    import oracle
+    from runtimed_b200 import synth
+
+    threads = os.cpu_count() or 1
+    tot_bytes, tot_s = 0.0, 0.0
+    per = budget_s / len(sweep())
+    rows_used = {}
+    for name, t, n, k in sweep():
+        rows = 64
+        x = synth.bf16_round(synth.activations(1, k, seed=0))
+        if t == 0:
+            w, s = synth.fp8_matrix(rows * 64, k, seed=0)
+        else:
+            raw = synth.quant_matrix(t, rows * 64, k, seed=0)
+        spent, done_b = 0.0, 0.0
+        while spent < per and rows <= 64 * 64:
+            t0 = time.perf_counter()
+            if t == 0:
+                oracle.ref_cpu_fp8_linear(x, w[:rows], s[:rows], rows, k, threads=threads)
+            else:
+                row_b = weight_bytes(t, 1, k)
+                oracle.ref_cpu_linear(t, raw[: rows * row_b], rows, k, x, threads=threads)
+            dt = time.perf_counter() - t0
+            spent += dt
+            done_b += alg_bytes(t, rows, k)
+            if dt < 0.25:
+                rows *= 2
+        tot_bytes += done_b
+        tot_s += spent
+        rows_used[f"{name}:{n}x{k}"] = rows
+    return {"value": tot_bytes / tot_s / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"row samples of every sweep point (~{budget_s:.0f} s of CPU work), oracle/rtd_oracle.c "
+                      f"restating the reference block decoders + f32 dot, OpenMP {threads} threads"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = None
+    for _ in range(max(args.warmup, 0)):
+        cpu_baseline(budget_s=2.0)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        base = cpu_baseline(budget_s=max(5.0, 60.0 / max(args.steps, 1)))
+        vals.append(base["value"])
+    wall = time.perf_counter() - t0
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": config_dict(),
+            "cpu_baseline": dict(base, value=value),
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict():
+    return {"workload": "config1 quantized-linear op sweep at decode M=1 (y = x.W^T), one step = 14 GEMVs",
+            "formats": [f for f, _ in FORMATS], "shapes_nk": SHAPES, "m": 1, "activations": "bf16",
+            "weights": "random-init GGUF blocks with the config-1 distributions (seed 0)",
+            "l2": "inputs larger than L2: 0.74 GB of distinct weights per step vs 126 MB L2",
+            "parallelism": "replicas: each rank streams its own weight copy"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.weights import Fp8Weight, QMatMul
+
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    items = []
+    for name, t, n, k in sweep():
+        if t == 0:
+            w, s = synth.fp8_matrix(n, k, seed=rank, stream=k)
+            obj = Fp8Weight(w, s, k, n, device=dev)
+        else:
+            obj = QMatMul(t, synth.quant_matrix(t, n, k, seed=rank, stream=k), n, k, device=dev)
+        x = synth.bf16_round(synth.activations(1, k, seed=rank, stream=n))
+        xd = torch.from_numpy(x).to(torch.bfloat16).to(dev)
+        yd = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+        items.append(dict(name=name, t=t, n=n, k=k, obj=obj, x=xd, y=yd, bytes=alg_bytes(t, n, k)))
+    step_bytes = sum(it["bytes"] for it in items)
+
+    def call(it, x=None, y=None, st=None):
+        x = it["x"] if x is None else x
+        y = it["y"] if y is None else y
+        s = (stream if st is None else st).cuda_stream
+        o = it["obj"]
+        if it["t"] == 0:
+            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, it["k"], 1, y.data_ptr(),
+                                  _lib.DT_BF16, it["n"], _lib.FP8_W8A16, s)
+        else:
+            rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, it["k"], 1, None, y.data_ptr(),
+                               _lib.DT_BF16, it["n"], s)
+        if rc != 0:
+            raise RuntimeError(f"{it['name']} {it['n']}x{it['k']}: status {rc}: {L.rtd_last_error(o.ctx.handle)}")
+
+    for it in items:  # first calls configure kernel attributes outside capture
+        call(it)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for it in items:
+            call(it, st=torch.cuda.current_stream(dev))
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+
+    # ---- timed region (device time, CUDA events, max over ranks)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+
+    # ---- per-GEMV device time (each call preceded by a sleep so only GPU time is measured)
+    reps = 5
+    per = {i: [] for i in range(len(items))}
+    for _ in range(reps):
+        for i, it in enumerate(items):
+            torch.cuda._sleep(200_000)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            call(it)
+            b.record(stream)
+            per[i].append((a, b))
+    torch.cuda.synchronize(dev)
+    per_ms = {i: statistics.mean(a.elapsed_time(b) for a, b in v) for i, v in per.items()}
+    dom = max(per_ms, key=lambda i: per_ms[i])
+    dit = items[dom]
+    peak, peak_kind = read_peaks()
+    achieved = dit["bytes"] / (per_ms[dom] * 1e-3) / 1e9
+    tag = f"qgemv_{dit['name'].lower()}_{dit['n']}x{dit['k']}_m1"
+    traffic = profile_traffic(tag)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": f"prep + qgemv_kernel, {dit['name']} {dit['n']}x{dit['k']} M=1",
+                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                "per_gemv_gbs": {f"{it['name']}:{it['n']}x{it['k']}": round(it["bytes"] / (per_ms[i] * 1e-3) / 1e9, 1)
+                                 for i, it in enumerate(items)}}
+
+    # ---- end to end through the C ABI: pinned host x in, y back to pinned host, every call
+    hx = [torch.empty(it["x"].shape, dtype=torch.bfloat16).pin_memory() for it in items]
+    hy = [torch.empty(it["y"].shape, dtype=torch.bfloat16).pin_memory() for it in items]
+    for i, it in enumerate(items):
+        hx[i].copy_(it["x"].cpu())
+    e2e_steps = max(3, args.steps // 2)
+    h2d = sum(it["k"] * 2 for it in items)
+    d2h = sum(it["n"] * 2 for it in items)
+    for _ in range(2):
+        for i, it in enumerate(items):
+            it["x"].copy_(hx[i], non_blocking=True)
+            call(it)
+            hy[i].copy_(it["y"], non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        for i, it in enumerate(items):
+            it["x"].copy_(hx[i], non_blocking=True)
+            call(it)
+            hy[i].copy_(it["y"], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = world * step_bytes * e2e_steps / (float(e2e_ms.item()) * 1e-3) / 1e9
+
+    cpu = cpu_baseline() if (rank == 0 and world == 1) else None
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 tensor-core products of exact weight codes, f32 accumulate",
+            "data": "synthetic", "config": config_dict(), "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "rtd_qlinear / rtd_fp8_linear per GEMV, eager, pinned-host x in and y out"},
+            "gpu_launches": 2 * len(items) * args.steps,
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -262,6 +262,7 @@ int rtdo_ref_cpu_linear(uint32_t type, const uint8_t* blocks, int64_t N, int64_t
             for (int64_t m = 0; m < M; m++) {
                 const float* xr = x + m * K;
                 float acc = 0.0f;
+#pragma omp simd reduction(+ : acc)
                 for (int64_t k = 0; k < K; k++) acc += xr[k] * row[k];
                 y[m * N + n] = acc;
             }
@@ -381,6 +382,7 @@ void rtdo_ref_cpu_fp8_linear(const float* x, const uint8_t* w, const float* scal
             for (int64_t k = 0; k < K; k++) row[k] = fp8_lut[w[n * K + k]] * s;
             for (int64_t m = 0; m < M; m++) {
                 float acc = 0.0f;
+#pragma omp simd reduction(+ : acc)
                 for (int64_t k = 0; k < K; k++) acc += x[m * K + k] * row[k];
                 y[m * N + n] = acc;
             }

@@ -13,7 +13,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/rtd.h"
+#include "rtd.h"
 #include "rtd_kernels.h"
 #include "rtd_layout.h"
 

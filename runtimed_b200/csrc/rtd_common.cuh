@@ -50,16 +50,47 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: every try_wait suspends for a hardware-defined slice, so the
-// limit is generous; on expiry the device status word records the timeout and
-// the wait continues for a second bounded round so no copy is left in flight
-// towards shared memory of an exited CTA.
+// try_wait with a suspend-time hint: the warp sleeps in hardware until the phase
+// completes (or about `hint_ns` passes) instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase: gives up after `budget_ns` of wall time
+// (read from %globaltimer), records kDevWaitTimeout in the device status word and
+// returns false.  Callers stop issuing copies after a failure and drain what is
+// already in flight with a second bounded wait, so no CTA exits with a copy still
+// heading for its shared memory and no wait can hold the GPU indefinitely.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uint64_t budget_ns, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (global_ns() - t0 > budget_ns) {
+      raise_status(status, kDevWaitTimeout);
+      return false;
+    }
+  }
+}
+
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s: far beyond any legitimate copy latency
+
 __device__ __forceinline__ void mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
-  for (uint32_t i = 0; i < (1u << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return;
-  raise_status(status, kDevWaitTimeout);
-  for (uint32_t i = 0; i < (1u << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return;
+  if (!mbar_wait_ns(bar, parity, kWaitBudgetNs, status)) mbar_wait_ns(bar, parity, kWaitBudgetNs, status);
 }
 
 // 1-D bulk copy global -> shared (TMA engine), completion counted in bytes on `bar`.

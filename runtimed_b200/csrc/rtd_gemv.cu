@@ -64,25 +64,25 @@ template <int FMT>
 struct FmtC;
 template <>
 struct FmtC<FMT_Q4K> {
-  static constexpr int GK = 256, GB = 2304, SBE = 32, IG = 1;
+  static constexpr int GK = 256, GB = 2304, SBE = 32;
   static constexpr float XOFF = 1.0f;  // plain sub-block sums: the min term needs them unscaled
   static constexpr bool TAB = true;
 };
 template <>
 struct FmtC<FMT_Q6K> {
-  static constexpr int GK = 256, GB = 3360, SBE = 16, IG = 1;
+  static constexpr int GK = 256, GB = 3360, SBE = 16;
   static constexpr float XOFF = -1056.0f;
   static constexpr bool TAB = true;
 };
 template <>
 struct FmtC<FMT_Q80> {
-  static constexpr int GK = 32, GB = 544, SBE = 32, IG = 8;
+  static constexpr int GK = 32, GB = 544, SBE = 32;
   static constexpr float XOFF = -1152.0f;
   static constexpr bool TAB = true;
 };
 template <>
 struct FmtC<FMT_FP8> {
-  static constexpr int GK = 32, GB = 512, SBE = 32, IG = 8;
+  static constexpr int GK = 32, GB = 512, SBE = 32;
   static constexpr bool TAB = false;
 };
 
@@ -267,101 +267,186 @@ __global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThre
 }
 
 // ------------------------------------------------------------------ GEMV kernel
-__device__ __forceinline__ uint4 ld_b16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ uint2 ld_b8(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+// 32-bit shared-memory accessors.  They are volatile so no load can be hoisted
+// above the mbarrier wait that publishes the data; ALU work still interleaves.
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 ldsf2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void stsf2(uint32_t a, float x, float y) {
+  asm volatile("st.shared.v2.f32 [%0], {%1,%2};" ::"r"(a), "f"(x), "f"(y) : "memory");
+}
+__device__ __forceinline__ void stsf(uint32_t a, float x) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(x) : "memory");
+}
+__device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+
+// Loads at base + a compile-time offset (folded into the instruction's address).
+template <int OFF>
+__device__ __forceinline__ uint4 lds128o(uint32_t base) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(base), "n"(OFF));
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ float4 ldsf4o(uint32_t base) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4+%5];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(base), "n"(OFF));
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ float2 ldsf2o(uint32_t base) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2+%3];" : "=f"(v.x), "=f"(v.y) : "r"(base), "n"(OFF));
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint2 lds64o(uint32_t base) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(base), "n"(OFF));
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ float ldsfo(uint32_t base) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(base), "n"(OFF));
+  return v;
+}
+
+// (a & b) | c in one LOP3.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+template <int V>
+struct IC {
+  static constexpr int value = V;
+};
+// f(IC<0>{}), ..., f(IC<N-1>{}): a loop whose index is a constant expression.
+template <int I, int N, typename Fn>
+__device__ __forceinline__ void static_for(Fn&& f) {
+  if constexpr (I < N) {
+    f(IC<I>{});
+    static_for<I + 1, N>(f);
+  }
+}
 
 // One group (16 rows x GK k) of one format into the warp's accumulators.
-// xg: this group's x slice (column c at xg + c*xstride); tg: its sub-block table.
+//   gs: the group's bytes; xs: this group's x slice (column c at xs + c*xstride);
+//   ts: its sub-block table [sub-block][ncol8] f32; tb: the warp's scale-table scratch.
+// Activation columns >= ncol read column ncol-1: those MMA output columns are never
+// stored, so no select is needed.
 template <int FMT, int NT>
-__device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, int xstride, const float* tg,
-                                         int ncol, int ncol8, uint8_t* tblw, float (&acc)[NT][4], int lane) {
+__device__ __forceinline__ void do_group(uint32_t gs, uint32_t xs, int xstride, uint32_t ts, int ncol, int ncol8,
+                                         uint32_t tb, float (&acc)[NT][4], int lane) {
   const int g = lane >> 2, tq = lane & 3;
+  uint32_t xcol[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) xcol[nt] = xs + (uint32_t)min(nt * 8 + g, ncol - 1) * xstride;
   if constexpr (FMT == FMT_Q4K) {
-    float2* tbl = reinterpret_cast<float2*>(tblw);  // [16 rows][9] (D, -Mo); the 9th pads banks
+    // per-warp table of (D, -Mo) for 16 rows x 8 sub-blocks; rows are 10 entries
+    // apart so a lane reads two sub-blocks with one 16-byte load, conflict-free
     {
       const int r = lane >> 1, half = lane & 1;
-      const uint4 h = ld_b16(grp + 16 * r);  // d, dmin | scales[0..3] | scales[4..7] | scales[8..11]
-      const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
-      const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+      const uint4 h = lds128(gs + 16 * r);  // d, dmin | scales[0..3] | scales[4..7] | scales[8..11]
+      const float d = h2f(h.x & 0xFFFFu), dmin = h2f(h.x >> 16);
+      // scale_min_k4 for four sub-blocks at once, one byte per sub-block
+      const uint32_t sc4 = half ? and_or(h.w, 0x0F0F0F0Fu, (h.y >> 2) & 0x30303030u) : (h.y & 0x3F3F3F3Fu);
+      const uint32_t m4 = half ? and_or(h.w >> 4, 0x0F0F0F0Fu, (h.z >> 2) & 0x30303030u) : (h.z & 0x3F3F3F3Fu);
+      const uint32_t tr = tb + (uint32_t)(r * 10 + 4 * half) * 8;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        uint32_t sc, m;
-        if (half == 0) {  // scale_min_k4, j < 4
-          sc = (h.y >> (8 * jj)) & 63u;
-          m = (h.z >> (8 * jj)) & 63u;
-        } else {  // j = 4 + jj
-          sc = ((h.w >> (8 * jj)) & 0xFu) | (((h.y >> (8 * jj + 6)) & 3u) << 4);
-          m = ((h.w >> (8 * jj + 4)) & 0xFu) | (((h.z >> (8 * jj + 6)) & 3u) << 4);
-        }
-        const int j = 4 * half + jj;
-        float D = d * (float)sc;
-        if (j & 1) D *= 0.0625f;  // high nibbles enter the MMA as 1024 + 16 q
-        tbl[r * 9 + j] = make_float2(D, -fmaf(1024.0f, D, dmin * (float)m));
+        float D = d * (float)((sc4 >> (8 * jj)) & 0xFFu);
+        if (jj & 1) D *= 0.0625f;  // high nibbles enter the MMA as 1024 + 16 q
+        stsf2(tr + jj * 8, D, -fmaf(1024.0f, D, dmin * (float)((m4 >> (8 * jj)) & 0xFFu)));
       }
     }
     __syncwarp();
-    float2 tgv[8], thv[8];
+    const uint32_t qb = gs + 256 + lane * 16;
+    const uint32_t tg_ = tb + (uint32_t)(g * 10) * 8, th_ = tb + (uint32_t)((g + 8) * 10) * 8;
+    const uint32_t svb = ts + (uint32_t)(2 * tq) * 4;
+    uint32_t xb[NT];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      tgv[j] = tbl[g * 9 + j];
-      thv[j] = tbl[(g + 8) * 9 + j];
-    }
-    const uint4* qv = reinterpret_cast<const uint4*>(grp + 256) + lane;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint4 q = qv[c * 32];
+    for (int nt = 0; nt < NT; ++nt) xb[nt] = xcol[nt] + tq * 16;
+    const uint32_t C64 = 0x64006400u;
+    static_for<0, 4>([&](auto cI) {
+      constexpr int c = decltype(cI)::value;
+      const uint4 q = lds128o<256 * 0 + c * 512>(qb);
+      const float4 Dg = ldsf4o<(2 * c) * 8>(tg_);  // (D, -Mo) of sub-blocks 2c, 2c+1
+      const float4 Dh = ldsf4o<(2 * c) * 8>(th_);
       const uint32_t s0 = q.x >> 8, s1 = q.y >> 8, s2 = q.z >> 8, s3 = q.w >> 8;
-#pragma unroll
-      for (int sel = 0; sel < 2; ++sel) {
+      static_for<0, 2>([&](auto selI) {
+        constexpr int sel = decltype(selI)::value;
+        constexpr int sb = 2 * c + sel;
         const uint32_t msk = sel ? 0x00F000F0u : 0x000F000Fu;
-        const uint32_t a0 = lop_and_or(q.x, msk, 0x64006400u), a1 = lop_and_or(q.z, msk, 0x64006400u);
-        const uint32_t a2 = lop_and_or(s0, msk, 0x64006400u), a3 = lop_and_or(s2, msk, 0x64006400u);
-        const uint32_t b0 = lop_and_or(q.y, msk, 0x64006400u), b1 = lop_and_or(q.w, msk, 0x64006400u);
-        const uint32_t b2 = lop_and_or(s1, msk, 0x64006400u), b3 = lop_and_or(s3, msk, 0x64006400u);
-        const int sb = 2 * c + sel;
-        const float2 Dg = tgv[sb], Dh = thv[sb];
+        const uint32_t a0 = and_or(q.x, msk, C64), a1 = and_or(q.z, msk, C64);
+        const uint32_t a2 = and_or(s0, msk, C64), a3 = and_or(s2, msk, C64);
+        const uint32_t b0 = and_or(q.y, msk, C64), b1 = and_or(q.w, msk, C64);
+        const uint32_t b2 = and_or(s1, msk, C64), b3 = and_or(s3, msk, C64);
+        const float dgx = sel ? Dg.z : Dg.x, dgy = sel ? Dg.w : Dg.y;
+        const float dhx = sel ? Dh.z : Dh.x, dhy = sel ? Dh.w : Dh.y;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const int col = nt * 8 + g;
-          const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + sb * 64 + tq * 16) : make_uint4(0, 0, 0, 0);
+          const uint4 bx = lds128(xb[nt] + sb * 64);
+          const float2 sv = ldsf2(svb + (uint32_t)(sb * 8 * NT + nt * 8) * 4);
           float t4[4];
           mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, 0.f, 0.f, 0.f, 0.f);
           mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
-          const float2 sv = *reinterpret_cast<const float2*>(tg + sb * ncol8 + nt * 8 + 2 * tq);
-          acc[nt][0] = fmaf(Dg.x, t4[0], fmaf(Dg.y, sv.x, acc[nt][0]));
-          acc[nt][1] = fmaf(Dg.x, t4[1], fmaf(Dg.y, sv.y, acc[nt][1]));
-          acc[nt][2] = fmaf(Dh.x, t4[2], fmaf(Dh.y, sv.x, acc[nt][2]));
-          acc[nt][3] = fmaf(Dh.x, t4[3], fmaf(Dh.y, sv.y, acc[nt][3]));
+          acc[nt][0] = fmaf(dgx, t4[0], fmaf(dgy, sv.x, acc[nt][0]));
+          acc[nt][1] = fmaf(dgx, t4[1], fmaf(dgy, sv.y, acc[nt][1]));
+          acc[nt][2] = fmaf(dhx, t4[2], fmaf(dhy, sv.x, acc[nt][2]));
+          acc[nt][3] = fmaf(dhx, t4[3], fmaf(dhy, sv.y, acc[nt][3]));
         }
-      }
-    }
+      });
+    });
     __syncwarp();
   } else if constexpr (FMT == FMT_Q6K) {
-    float* tbl = reinterpret_cast<float*>(tblw);  // [16 rows][17] d*sc; the 17th pads banks
+    // per-warp table of d*sc for 16 rows x 16 sub-blocks, rows padded to 17 floats
     {
       const int r = lane >> 1, jb = (lane & 1) * 8;
-      const float d = __half2float(*reinterpret_cast<const __half*>(grp + 2 * r));
-      const uint2 sv = ld_b8(grp + 32 + 16 * r + jb);
+      const float d = h2f(lds16(gs + 2 * r));
+      const uint2 sv = lds64(gs + 32 + 16 * r + jb);
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
         const int8_t sc = (int8_t)(((jj < 4 ? sv.x : sv.y) >> (8 * (jj & 3))) & 0xFFu);
-        tbl[r * 17 + jb + jj] = d * (float)sc;
+        stsf(tb + (uint32_t)(r * 17 + jb + jj) * 4, d * (float)sc);
       }
     }
     __syncwarp();
-    float dg[16], dh[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      dg[j] = tbl[g * 17 + j];
-      dh[j] = tbl[(g + 8) * 17 + j];
-    }
+    constexpr uint32_t C = 0x64006400u, M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
     uint32_t wv[24];
 #pragma unroll
     for (int v = 0; v < 6; ++v) {
-      const uint4 u = ld_b16(grp + 288 + v * 512 + lane * 16);
+      const uint4 u = lds128(gs + 288 + v * 512 + lane * 16);
       wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
     }
-    constexpr uint32_t C = 0x64006400u, M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
       const uint32_t X = wv[3 * p], Y = wv[3 * p + 1], Z = wv[3 * p + 2];
@@ -371,30 +456,27 @@ __device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, 
       const uint32_t ab1 = lop_and_or(X >> 12, M4, C) | ((Z >> 8) & M2);
       const uint32_t ab2 = lop_and_or(Z >> 6, M6, C);
       const uint32_t ab3 = lop_and_or(Y >> 12, M4, C) | ((Z >> 10) & M2);
+      const float dga = ldsf(tb + (uint32_t)(g * 17 + 2 * p) * 4), dgb = ldsf(tb + (uint32_t)(g * 17 + 2 * p + 1) * 4);
+      const float dha = ldsf(tb + (uint32_t)((g + 8) * 17 + 2 * p) * 4);
+      const float dhb = ldsf(tb + (uint32_t)((g + 8) * 17 + 2 * p + 1) * 4);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const int col = nt * 8 + g;
-        uint2 ba = make_uint2(0, 0), bb = make_uint2(0, 0);
-        if (col < ncol) {
-          ba = ld_b8(xg + col * xstride + p * 64 + tq * 8);
-          bb = ld_b8(xg + col * xstride + p * 64 + 32 + tq * 8);
-        }
-        const float2 xa = *reinterpret_cast<const float2*>(tg + (2 * p) * ncol8 + nt * 8 + 2 * tq);
-        const float2 xb = *reinterpret_cast<const float2*>(tg + (2 * p + 1) * ncol8 + nt * 8 + 2 * tq);
-        float ta[4], tb[4];
+        const uint2 ba = lds64(xcol[nt] + p * 64 + tq * 8), bb = lds64(xcol[nt] + p * 64 + 32 + tq * 8);
+        const float2 xa = ldsf2(ts + (uint32_t)((2 * p) * ncol8 + nt * 8 + 2 * tq) * 4);
+        const float2 xb = ldsf2(ts + (uint32_t)((2 * p + 1) * ncol8 + nt * 8 + 2 * tq) * 4);
+        float ta[4], tbv[4];
         mma_f16(ta, aa0, aa1, aa2, aa3, ba.x, ba.y, xa.x, xa.y, xa.x, xa.y);
-        mma_f16(tb, ab0, ab1, ab2, ab3, bb.x, bb.y, xb.x, xb.y, xb.x, xb.y);
-        acc[nt][0] = fmaf(dg[2 * p], ta[0], fmaf(dg[2 * p + 1], tb[0], acc[nt][0]));
-        acc[nt][1] = fmaf(dg[2 * p], ta[1], fmaf(dg[2 * p + 1], tb[1], acc[nt][1]));
-        acc[nt][2] = fmaf(dh[2 * p], ta[2], fmaf(dh[2 * p + 1], tb[2], acc[nt][2]));
-        acc[nt][3] = fmaf(dh[2 * p], ta[3], fmaf(dh[2 * p + 1], tb[3], acc[nt][3]));
+        mma_f16(tbv, ab0, ab1, ab2, ab3, bb.x, bb.y, xb.x, xb.y, xb.x, xb.y);
+        acc[nt][0] = fmaf(dga, ta[0], fmaf(dgb, tbv[0], acc[nt][0]));
+        acc[nt][1] = fmaf(dga, ta[1], fmaf(dgb, tbv[1], acc[nt][1]));
+        acc[nt][2] = fmaf(dha, ta[2], fmaf(dhb, tbv[2], acc[nt][2]));
+        acc[nt][3] = fmaf(dha, ta[3], fmaf(dhb, tbv[3], acc[nt][3]));
       }
     }
     __syncwarp();
   } else if constexpr (FMT == FMT_Q80) {
-    const float dg = __half2float(*reinterpret_cast<const __half*>(grp + 2 * g));
-    const float dh = __half2float(*reinterpret_cast<const __half*>(grp + 2 * (g + 8)));
-    const uint4 q = ld_b16(grp + 32 + lane * 16);
+    const float dg = h2f(lds16(gs + 2 * g)), dh = h2f(lds16(gs + 2 * (g + 8)));
+    const uint4 q = lds128(gs + 32 + lane * 16);
     const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u, u2 = q.z ^ 0x80808080u,
                    u3 = q.w ^ 0x80808080u;
     const uint32_t K64 = 0x64646464u;
@@ -404,9 +486,8 @@ __device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, 
     const uint32_t b2 = prmt(u1, K64, 0x4341), b3 = prmt(u3, K64, 0x4341);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int col = nt * 8 + g;
-      const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + tq * 16) : make_uint4(0, 0, 0, 0);
-      const float2 xo = *reinterpret_cast<const float2*>(tg + nt * 8 + 2 * tq);
+      const uint4 bx = lds128(xcol[nt] + tq * 16);
+      const float2 xo = ldsf2(ts + (uint32_t)(nt * 8 + 2 * tq) * 4);
       float t4[4];
       mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, xo.x, xo.y, xo.x, xo.y);
       mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
@@ -416,7 +497,7 @@ __device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, 
       acc[nt][3] = fmaf(dh, t4[3], acc[nt][3]);
     }
   } else {  // FMT_FP8
-    const uint4 q = ld_b16(grp + lane * 16);
+    const uint4 q = lds128(gs + lane * 16);
     const uint32_t p0 = prmt(q.x, 0u, 0x3120), p1 = prmt(q.y, 0u, 0x3120);
     const uint32_t p2 = prmt(q.z, 0u, 0x3120), p3 = prmt(q.w, 0u, 0x3120);
     const uint32_t a0 = e4m3x2_to_f16x2((uint16_t)(p0 & 0xFFFFu)), a1 = e4m3x2_to_f16x2((uint16_t)(p2 & 0xFFFFu));
@@ -425,14 +506,12 @@ __device__ __forceinline__ void do_group(const uint8_t* grp, const uint8_t* xg, 
     const uint32_t b2 = e4m3x2_to_f16x2((uint16_t)(p1 >> 16)), b3 = e4m3x2_to_f16x2((uint16_t)(p3 >> 16));
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int col = nt * 8 + g;
-      const uint4 bx = col < ncol ? ld_b16(xg + col * xstride + tq * 16) : make_uint4(0, 0, 0, 0);
+      const uint4 bx = lds128(xcol[nt] + tq * 16);
       mma_f16(acc[nt], a0, a1, a2, a3, bx.x, bx.y, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
       mma_f16(acc[nt], b0, b1, b2, b3, bx.z, bx.w, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
     }
   }
 }
-
 
 struct Args {
   const uint8_t* w;
@@ -447,12 +526,10 @@ struct Args {
   int64_t ldy;
   int y_dtype;
   int64_t N;
-  int G, CI;          // groups per row, items per tile
-  int64_t I, WT;      // items in total, warps in the grid
-  int NS;
-  int warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar;
-  float* part;
-  uint32_t* counters;
+  int G, IG, CI, T;   // groups per row, groups per item, items per tile, tiles
+  int nctas, NS;
+  int whole;          // 1: every warp owns whole tiles (no cross-warp reduction)
+  int warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar, off_red;
   int* status;
 };
 
@@ -466,10 +543,19 @@ __device__ __forceinline__ void store_y(const Args& a, int t, int64_t n, float v
     static_cast<__nv_bfloat16*>(a.y)[off] = __float2bfloat16_rn(v);
 }
 
-__device__ __forceinline__ int64_t item_start(int64_t w, int64_t I, int64_t WT) { return w * I / WT; }
-// The warp whose item range contains item i.
-__device__ __forceinline__ int64_t warp_of(int64_t i, int64_t I, int64_t WT) { return ((i + 1) * WT - 1) / I; }
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
+__device__ __forceinline__ void named_bar_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Each CTA owns a contiguous run of whole 16-row tiles; inside a tile, warp w
+// takes items w, w+8, ... (an item = IG groups).  Every warp streams its own
+// item sequence through a private ring of NS shared-memory stages, so warps only
+// meet once per tile: to add their partial sums in shared memory (double
+// buffered), after which one warp (tile index mod 8) writes the tile's outputs.
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(const Args a) {
   using F = FmtC<FMT>;
@@ -478,153 +564,202 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
-  if (gw >= a.WT) return;  // the last CTA may carry warps past the plan; the rest never wait on them
-  const int64_t i0 = item_start(gw, a.I, a.WT), i1 = item_start(gw + 1, a.I, a.WT);
-  const int64_t n_items = i1 - i0;
+  const int CI = a.CI;
+  const bool whole = a.whole != 0;
+  int t0, t1, per_tile;
+  if (whole) {  // this warp's own run of tiles, all items of each
+    const int64_t gw = (int64_t)blockIdx.x * kWarps + warp, WT = (int64_t)a.nctas * kWarps;
+    t0 = (int)(gw * a.T / WT);
+    t1 = (int)((gw + 1) * a.T / WT);
+    per_tile = CI;
+  } else {  // the CTA's run of tiles, items warp, warp+8, ... of each
+    t0 = (int)((int64_t)blockIdx.x * a.T / a.nctas);
+    t1 = (int)((int64_t)(blockIdx.x + 1) * a.T / a.nctas);
+    per_tile = (CI > warp) ? (CI - warp + kWarps - 1) / kWarps : 0;
+  }
+  const int n_items = per_tile * (t1 - t0);
   uint8_t* wb = sm + (size_t)warp * a.warp_bytes;
   uint64_t* bar = reinterpret_cast<uint64_t*>(wb + a.off_bar);
   uint8_t* tblw = wb + a.off_tbl;
+  const uint32_t wb_s = smem_u32(wb), tb_s = smem_u32(tblw);
+  float* red = reinterpret_cast<float*>(sm + a.off_red);  // [2][8 warps][16][ncol8]
+  float* ts_s = red + 2 * kWarps * 16 * a.ncol8;          // [32] token scales
   const int NS = a.NS;
 
-  auto geom = [&](int64_t item, int64_t& tile, int& g0, int& ng) {
-    tile = item / a.CI;
-    g0 = (int)(item - tile * a.CI) * F::IG;
-    ng = min(F::IG, a.G - g0);
-  };
+  // the issue side walks its own cursor over (tile, group) a few items ahead
   auto bytes_of = [&](int ng) -> uint32_t {
     uint32_t b = (uint32_t)ng * F::GB + (uint32_t)ng * a.ncol * CSB;
     if constexpr (F::TAB) b += (uint32_t)ng * NSB * a.ncol8 * 4;
     return b;
   };
-  auto issue_w = [&](int s, int64_t item) {
-    int64_t tile; int g0, ng;
-    geom(item, tile, g0, ng);
+  auto issue_w = [&](int s, int tile, int g0, int ng) {
     mbar_arrive_expect_tx(&bar[s], bytes_of(ng));
     bulk_g2s(wb + (size_t)s * a.slot_bytes, a.w + ((size_t)tile * a.G + g0) * F::GB, (uint32_t)ng * F::GB, &bar[s]);
   };
-  auto issue_x = [&](int s, int64_t item) {
-    int64_t tile; int g0, ng;
-    geom(item, tile, g0, ng);
+  auto issue_x = [&](int s, int g0, int ng) {
     uint8_t* slot = wb + (size_t)s * a.slot_bytes;
     bulk_g2s(slot + a.off_x, a.cols + (size_t)g0 * a.ncol * CSB, (uint32_t)ng * a.ncol * CSB, &bar[s]);
     if constexpr (F::TAB)
       bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * NSB * a.ncol8, (uint32_t)ng * NSB * a.ncol8 * 4, &bar[s]);
   };
+  const int gstep = (whole ? 1 : kWarps) * a.IG;  // group stride between a warp's items in a tile
+  const int gfirst = (whole ? 0 : warp) * a.IG;
 
   if (lane == 0) {
     for (int s = 0; s < NS; ++s) mbar_init(&bar[s], 1);
     fence_mbar_init();
   }
   __syncwarp();
-  const int npro = (int)(n_items < NS ? n_items : NS);
-  if (lane == 0)
-    for (int s = 0; s < npro; ++s) issue_w(s, i0 + s);  // weights go out before x is known to be ready
-  griddep_wait();                                       // the prep kernel's output is visible from here on
-  if (lane == 0)
-    for (int s = 0; s < npro; ++s) issue_x(s, i0 + s);
-
-  // token scales of this lane's accumulator columns
-  float tsr[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int col = nt * 8 + 2 * tq + cc;
-      const int t = col / a.P;
-      tsr[nt][cc] = (col < a.ncol) ? a.tscale[t] : 0.0f;
+  const int npro = n_items < NS ? n_items : NS;
+  // issue cursor: (tile, group) of the next item to issue
+  int it_tile = t0, it_g0 = gfirst, it_k = 0;
+  auto advance = [&]() {
+    if (++it_k == per_tile) {
+      it_k = 0;
+      ++it_tile;
+      it_g0 = gfirst;
+    } else {
+      it_g0 += gstep;
     }
+  };
+  if (lane == 0) {
+    int tt = t0, gg = gfirst, kk = 0;
+    for (int s = 0; s < npro; ++s) {  // weights go out before x is known to be ready
+      issue_w(s, tt, gg, min(a.IG, a.G - gg));
+      if (++kk == per_tile) { kk = 0; ++tt; gg = gfirst; } else { gg += gstep; }
+    }
+  }
+  griddep_wait();  // the prep kernel's output is visible from here on
+  for (int s = 0; s < npro; ++s) {
+    if (lane == 0) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
+    advance();
+  }
+  if (tid < a.M) ts_s[tid] = a.tscale[tid];
+  __syncthreads();
 
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-  float eb[2] = {0.0f, 0.0f}, es[2] = {1.0f, 1.0f};  // bias / channel scale of rows g, g+8
-  const int64_t t_first = i0 / a.CI;
-
-  for (int64_t i = 0; i < n_items; ++i) {
-    const int s = (int)(i % NS);
-    const int64_t item = i0 + i;
-    int64_t tile; int g0, ng;
-    geom(item, tile, g0, ng);
-    const int ci = (int)(item - tile * a.CI);
-    if (ci == 0 || i == 0) {  // a new tile: fetch its epilogue operands early
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int64_t n = tile * 16 + g + 8 * rr;
-        eb[rr] = (a.bias && n < a.N) ? __ldg(a.bias + n) : 0.0f;
-        if constexpr (FMT == FMT_FP8) es[rr] = (n < a.N) ? __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n)) : 1.0f;
+  int i = 0;
+  int slot_i = 0;         // ring slot of item i
+  uint32_t phase = 0;     // its mbarrier phase parity
+  int next_issue = npro;  // items [0, next_issue) have had their copies issued
+  bool aborted = false;   // a bounded wait gave up: stop issuing and computing, keep the barriers
+  for (int tile = t0; tile < t1; ++tile) {
+    // the warp that will write this tile prefetches its epilogue operands
+    // (split mode: lane r < 16 holds row r; whole mode: each lane its rows g and g+8)
+    const bool writer = whole || (warp == (tile & (kWarps - 1)));
+    float eb = 0.0f, es = 1.0f, eb2 = 0.0f, es2 = 1.0f;
+    if (writer && (whole || lane < 16)) {
+      const int64_t n = (int64_t)tile * 16 + (whole ? g : lane), n2 = n + 8;
+      if (n < a.N) {
+        if (a.bias) eb = __ldg(a.bias + n);
+        if constexpr (FMT == FMT_FP8) es = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n));
+      }
+      if (whole && n2 < a.N) {
+        if (a.bias) eb2 = __ldg(a.bias + n2);
+        if constexpr (FMT == FMT_FP8) es2 = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n2));
       }
     }
-    mbar_wait_bounded(&bar[s], (uint32_t)(i / NS) & 1u, a.status);
-    const uint8_t* slot = wb + (size_t)s * a.slot_bytes;
-    for (int gi = 0; gi < ng; ++gi) {
-      const uint8_t* xg = slot + a.off_x + gi * a.ncol * CSB;
-      const float* tg = reinterpret_cast<const float*>(slot + a.off_tab) + gi * NSB * a.ncol8;
-      do_group<FMT, NT>(slot + (size_t)gi * F::GB, xg, CSB, tg, a.ncol, a.ncol8, tblw, acc, lane);
+    for (int k = 0; k < per_tile; ++k, ++i) {
+      if (aborted) continue;
+      const int g0 = gfirst + k * gstep;
+      const int ng = min(a.IG, a.G - g0);
+      if (!mbar_wait_ns(&bar[slot_i], phase, kWaitBudgetNs, a.status)) {
+        aborted = true;
+        continue;
+      }
+      const uint32_t slot = wb_s + (uint32_t)(slot_i * a.slot_bytes);
+#pragma unroll 2
+      for (int gi = 0; gi < ng; ++gi)
+        do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB,
+                          slot + a.off_tab + gi * NSB * a.ncol8 * 4, a.ncol, a.ncol8, tb_s, acc, lane);
+      __syncwarp();
+      if (i + NS < n_items) {
+        if (lane == 0) {
+          const int ng2 = min(a.IG, a.G - it_g0);
+          issue_w(slot_i, it_tile, it_g0, ng2);
+          issue_x(slot_i, it_g0, ng2);
+        }
+        advance();
+        next_issue = i + NS + 1;
+      }
+      if (++slot_i == NS) {
+        slot_i = 0;
+        phase ^= 1u;
+      }
     }
-    __syncwarp();
-    if (lane == 0 && i + NS < n_items) {
-      issue_w(s, item + NS);
-      issue_x(s, item + NS);
+    if (whole) {  // ---- tile end, whole mode: write straight from the accumulators
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int64_t n = (int64_t)tile * 16 + g + 8 * rr;
+          const float bias = rr ? eb2 : eb, cs = rr ? es2 : es;
+          if (a.P == 2) {  // columns 2tq, 2tq+1: hi and lo halves of token nt*4 + tq
+            const int t = nt * 4 + tq;
+            if (t < a.M && n < a.N)
+              store_y(a, t, n, (acc[nt][2 * rr] + acc[nt][2 * rr + 1]) * ts_s[t] * cs + bias);
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int t = nt * 8 + 2 * tq + cc;
+              if (t < a.M && n < a.N) store_y(a, t, n, acc[nt][2 * rr + cc] * ts_s[t] * cs + bias);
+            }
+          }
+        }
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+      }
+      continue;
     }
-    if (ci != a.CI - 1 && i != n_items - 1) continue;
-
-    // ---- tile boundary: write from the accumulators, or hand a partial to the last warp
-    const bool whole = (tile * a.CI >= i0) && (tile * a.CI + a.CI - 1 < i1);
-    const int pslot = (tile == t_first) ? 0 : 1;
+    // ---- tile end: the 8 partial sums meet in shared memory (double buffered).
+    // Only the writer of the tile waits for them (bar.sync on FULL[b]); the others
+    // arrive and move on.  A buffer is reused two tiles later, after its previous
+    // writer has released it on EMPTY[b] (every warp but that writer syncs there).
+    const int b = tile & 1;
+    const int lt = tile - t0;
+    if (lt >= 2) {
+      const int prev_writer = (tile - 2) & (kWarps - 1);
+      if (warp != prev_writer) named_bar_sync(3 + b, kThreads);
+    }
+    float* rb = red + (size_t)b * kWarps * 16 * a.ncol8;
+    float* rw = rb + (size_t)warp * 16 * a.ncol8;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int r = g + 8 * rr;
-        const int64_t n = tile * 16 + r;
-        float v[2];
-        int tt[2], nv;
-        if (a.P == 2) {  // columns 2tq, 2tq+1 are the hi and lo halves of one token
-          tt[0] = nt * 4 + tq;
-          v[0] = (acc[nt][2 * rr] + acc[nt][2 * rr + 1]) * tsr[nt][0];
-          nv = 1;
-        } else {
-          tt[0] = nt * 8 + 2 * tq;
-          tt[1] = tt[0] + 1;
-          v[0] = acc[nt][2 * rr] * tsr[nt][0];
-          v[1] = acc[nt][2 * rr + 1] * tsr[nt][1];
-          nv = 2;
-        }
-        for (int q = 0; q < nv; ++q) {
-          if (tt[q] >= a.M || n >= a.N) continue;
-          float val = v[q];
-          if constexpr (FMT == FMT_FP8) val *= es[rr];
-          if (whole)
-            store_y(a, tt[q], n, val + eb[rr]);
-          else
-            a.part[(((size_t)gw * 2 + pslot) * 16 + r) * a.M + tt[q]] = val;
-        }
-      }
+      rw[g * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][0];
+      rw[g * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][1];
+      rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][2];
+      rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][3];
       acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
     }
-    if (!whole) {
-      __threadfence();
-      __syncwarp();
-      const int64_t wf = warp_of(tile * a.CI, a.I, a.WT), wl = warp_of(tile * a.CI + a.CI - 1, a.I, a.WT);
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(&a.counters[tile], 1u) == (uint32_t)(wl - wf));
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        for (int o = lane; o < 16 * a.M; o += 32) {
-          const int r = o / a.M, t = o - r * a.M;
-          const int64_t n = tile * 16 + r;
-          if (n >= a.N) continue;
-          float sum = 0.0f;
-          for (int64_t ww = wf; ww <= wl; ++ww) {
-            const int ps = (tile == item_start(ww, a.I, a.WT) / a.CI) ? 0 : 1;
-            sum += __ldcg(&a.part[((size_t)(ww * 2 + ps) * 16 + r) * a.M + t]);
-          }
-          store_y(a, t, n, sum + (a.bias ? __ldg(a.bias + n) : 0.0f));
-        }
-        if (lane == 0) a.counters[tile] = 0u;
+    if (!writer) {
+      named_bar_arrive(1 + b, kThreads);
+    } else {
+      named_bar_sync(1 + b, kThreads);
+      float* ep = reinterpret_cast<float*>(tblw);  // the scale table is idle between groups
+      if (lane < 16) {
+        ep[lane] = eb;
+        ep[16 + lane] = es;
       }
+      __syncwarp();
+      for (int o = lane; o < 16 * a.M; o += 32) {
+        const int r = o / a.M, t = o - r * a.M;
+        const int64_t n = (int64_t)tile * 16 + r;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w)
+          for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
+        if (n < a.N) store_y(a, t, n, sum * ts_s[t] * ep[16 + r] + ep[r]);
+      }
+      __syncwarp();
+      if (tile + 2 < t1) named_bar_arrive(3 + b, kThreads);  // hand the buffer back
+    }
+  }
+  // after a failed wait, drain the copies already issued before leaving
+  if (aborted) {
+    for (int s = 0; s < NS && s < next_issue; ++s) {
+      const int last = s + ((next_issue - 1 - s) / NS) * NS;  // the last item issued into slot s
+      mbar_wait_ns(&bar[s], (uint32_t)(last / NS) & 1u, kWaitBudgetNs, a.status);
     }
   }
 }
@@ -632,23 +767,23 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Plan {
-  int NS, warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar;
+  int NS, warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar, off_red;
   size_t smem;
 };
 
-Plan make_plan(int fmt, int ncol, int ncol8, int ns_pref) {
+Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref) {
   const FmtInfo f = fmt_info(fmt);
-  const int IG = (f.gk == 256) ? 1 : 8;
   const bool tab = fmt != FMT_FP8;
   const int csb = col_stride_bytes(f.gk);
   Plan p{};
   const size_t off_x = align_up((size_t)IG * f.gb, 128);
   const size_t off_tab = align_up(off_x + (size_t)IG * ncol * csb, 16);
   const size_t slot = align_up(off_tab + (tab ? (size_t)IG * (f.gk / f.sbe) * ncol8 * 4 : 0), 128);
+  const size_t red = (size_t)2 * kWarps * 16 * ncol8 * 4 + 32 * 4;
   // prefer two CTAs per SM (<= 113 KB each); keep at least two stages in flight
   int NS = ns_pref;
   auto warp_bytes = [&](int ns) { return align_up(ns * slot + kTblBytes + kMaxStages * 8, 128); };
-  while (NS > 2 && warp_bytes(NS) * kWarps > 113 * 1024) --NS;
+  while (NS > 2 && warp_bytes(NS) * kWarps + red > 113 * 1024) --NS;
   p.NS = NS;
   p.slot_bytes = (int)slot;
   p.off_x = (int)off_x;
@@ -656,8 +791,27 @@ Plan make_plan(int fmt, int ncol, int ncol8, int ns_pref) {
   p.off_tbl = (int)(NS * slot);
   p.off_bar = (int)(NS * slot + kTblBytes);
   p.warp_bytes = (int)warp_bytes(NS);
-  p.smem = (size_t)p.warp_bytes * kWarps;
+  p.off_red = (int)((size_t)p.warp_bytes * kWarps);
+  p.smem = (size_t)p.off_red + red;
   return p;
+}
+
+// Groups per item: one 256-wide group for Q4_K / Q6_K; for the 32-wide Q8_0 / FP8
+// groups the largest of 8, 4, 2, 1 that still spreads a tile evenly over the warps.
+int items_group(int fmt, int64_t G) {
+  if (fmt_info(fmt).gk == 256) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int ig : {8, 4, 2, 1}) {
+    const int64_t ci = (G + ig - 1) / ig;
+    const double eff = (double)G / ((double)ig * kWarps * ((ci + kWarps - 1) / kWarps));
+    if (eff >= 0.85) return ig;
+    if (eff > best_eff) {
+      best_eff = eff;
+      best = ig;
+    }
+  }
+  return best;
 }
 
 // Resident CTAs per SM for this instantiation at this shared-memory size (cached per device).
@@ -761,12 +915,11 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   *plan_error = 0;
   if (c.M <= 0 || c.N <= 0) return cudaSuccess;
   const FmtInfo f = fmt_info(c.fmt);
-  const int IG = (f.gk == 256) ? 1 : 8;
   const int64_t T = tiles_for(c.N);
   const int64_t G = c.G;
   const int64_t kp = G * f.gk;
+  const int IG = items_group(c.fmt, G);
   const int64_t CI = (G + IG - 1) / IG;
-  const int64_t I = T * CI;
   const int P = (c.x_dtype == 0 && !c.w8a8) ? 2 : 1;
   const int max_tokens = 32 / P;
   static const int env_ns = [] {
@@ -774,13 +927,9 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     const int v = s ? std::atoi(s) : 0;
     return (v >= 2 && v <= kMaxStages) ? v : kMaxStages;
   }();
-  static const int env_ctas = [] {
-    const char* s = std::getenv("RTD_GEMV_CTAS_PER_SM");
-    return s ? std::atoi(s) : 0;
-  }();
   const size_t esz = (c.x_dtype == 0) ? 4 : 2;
   const bool x_vec = ((uintptr_t)c.x % 16 == 0) && ((c.ldx * (int64_t)esz) % 16 == 0);
-  if (T > c.n_counters) {
+  if (T >= (1LL << 31) || G >= (1LL << 31)) {
     *plan_error = 1;
     return cudaSuccess;
   }
@@ -788,23 +937,22 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   for (int64_t m0 = 0; m0 < c.M;) {
     int Mt = (int)std::min<int64_t>(max_tokens, c.M - m0);
     // fewer tokens per launch when the activation slices would not fit shared memory
-    while (Mt > 1 && make_plan(c.fmt, Mt * P, 8 * ((Mt * P + 7) / 8), env_ns).smem > 220 * 1024) Mt = (Mt + 1) / 2;
+    while (Mt > 1 && make_plan(c.fmt, IG, Mt * P, 8 * ((Mt * P + 7) / 8), env_ns).smem > 220 * 1024)
+      Mt = (Mt + 1) / 2;
     const int ncol = Mt * P;
     const int NT = (ncol + 7) / 8;
     const int ncol8 = 8 * NT;
-    const Plan pl = make_plan(c.fmt, ncol, ncol8, env_ns);
-    int occ = occupancy_of(c.fmt, NT, pl.smem);
-    if (env_ctas > 0) occ = std::min(occ, env_ctas);
-    const int64_t WT = std::min<int64_t>(I, (int64_t)c.sm_count * occ * kWarps);
-    const unsigned nctas = (unsigned)((WT + kWarps - 1) / kWarps);
-    const int64_t WTg = WT;  // WT <= I: every planned warp owns at least one item
-    // workspace carve: cols | tab | tscale | partials
+    const Plan pl = make_plan(c.fmt, IG, ncol, ncol8, env_ns);
+    const int occ = occupancy_of(c.fmt, NT, pl.smem);
+    const int64_t slots = (int64_t)c.sm_count * occ;
+    // Enough tiles for every warp to own at least two whole ones: no cross-warp
+    // reduction at all.  Otherwise the warps of a CTA split each tile's groups.
+    const bool whole = T >= 2 * slots * kWarps;
+    const int nctas = (int)(whole ? slots : std::min<int64_t>(T, slots));
+    // workspace carve: cols | tab | tscale
     const size_t cols_b = align_up((size_t)G * ncol * col_stride_bytes(f.gk), 256);
     const size_t tab_b = align_up((size_t)(kp / f.sbe) * ncol8 * 4, 256);
-    const size_t ts_b = 256;
-    const size_t part_b = (size_t)WTg * 2 * 16 * Mt * 4;
-    (void)nctas;
-    if (cols_b + tab_b + ts_b + part_b > c.ws_bytes) {
+    if (cols_b + tab_b + 256 > c.ws_bytes) {
       *plan_error = 1;
       return cudaSuccess;
     }
@@ -812,7 +960,6 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     uint8_t* cols = ws;
     float* tab = reinterpret_cast<float*>(ws + cols_b);
     float* tscale = reinterpret_cast<float*>(ws + cols_b + tab_b);
-    float* part = reinterpret_cast<float*>(ws + cols_b + tab_b + ts_b);
 
     PrepArgs pa{};
     pa.x = static_cast<const uint8_t*>(c.x) + (size_t)(m0 * c.ldx) * esz;
@@ -856,9 +1003,11 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.y_dtype = c.y_dtype;
     a.N = c.N;
     a.G = (int)G;
+    a.IG = IG;
     a.CI = (int)CI;
-    a.I = I;
-    a.WT = WTg;
+    a.T = (int)T;
+    a.nctas = nctas;
+    a.whole = whole ? 1 : 0;
     a.NS = pl.NS;
     a.warp_bytes = pl.warp_bytes;
     a.slot_bytes = pl.slot_bytes;
@@ -866,14 +1015,13 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_tab = pl.off_tab;
     a.off_tbl = pl.off_tbl;
     a.off_bar = pl.off_bar;
-    a.part = part;
-    a.counters = c.counters;
+    a.off_red = pl.off_red;
     a.status = c.status;
     switch (c.fmt) {
-      case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, nctas, pl.smem, c.stream); break;
-      case FMT_Q6K: e = launch_gemv_nt<FMT_Q6K>(a, NT, nctas, pl.smem, c.stream); break;
-      case FMT_Q80: e = launch_gemv_nt<FMT_Q80>(a, NT, nctas, pl.smem, c.stream); break;
-      default:      e = launch_gemv_nt<FMT_FP8>(a, NT, nctas, pl.smem, c.stream); break;
+      case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;
+      case FMT_Q6K: e = launch_gemv_nt<FMT_Q6K>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;
+      case FMT_Q80: e = launch_gemv_nt<FMT_Q80>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;
+      default:      e = launch_gemv_nt<FMT_FP8>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;
     }
     if (e != cudaSuccess) return e;
     m0 += Mt;
