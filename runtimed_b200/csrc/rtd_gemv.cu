@@ -156,7 +156,11 @@ template <int FMT>
 __global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThreads)
     prep_kernel(const PrepArgs a) {
   using F = FmtC<FMT>;
-  griddep_launch_dependents();  // the GEMV may start streaming weights now
+  // The GEMV behind this kernel may launch and start streaming weights at once;
+  // this kernel itself waits for whatever ran before it (which may be producing x,
+  // or a previous GEMV still reading the workspace this kernel overwrites).
+  griddep_launch_dependents();
+  griddep_wait();
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int t = blockIdx.x / kPrepCluster;
@@ -530,6 +534,12 @@ struct Args {
   int nctas, NS;
   int whole;          // 1: every warp owns whole tiles (no cross-warp reduction)
   int warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar, off_red;
+  // local-x mode: every CTA stages the raw bf16/f16 activations itself (no prep kernel)
+  int local_x;
+  const void* xraw;
+  int64_t ldx, K, kp;
+  int x_dtype, w8a8;
+  int off_xloc, xcs, off_tabloc;
   int* status;
 };
 
@@ -549,6 +559,100 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 
 __device__ __forceinline__ void named_bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Local-x mode: the CTA copies the raw bf16 / f16 activation rows into shared
+// memory (one bulk copy per token), finds each token's max |x|, and rewrites the
+// rows in place as power-of-two-scaled f16 plus the per-sub-block column sums --
+// exactly what the prep kernel would have produced, without a second launch.
+// Every CTA sees the whole row, so every CTA derives the same scale.
+template <int FMT>
+__device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float* ts_s, int* status) {
+  using F = FmtC<FMT>;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint8_t* xloc = sm + a.off_xloc;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + a.off_tabloc - 16);
+  float* red = reinterpret_cast<float*>(sm + a.off_tabloc - 16 - 32 * kWarps * 4);  // [8 warps][32 tokens]
+  const uint32_t row_bytes = (uint32_t)(a.K * 2);
+  if (tid == 0) {
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(xbar, row_bytes * (uint32_t)a.M);
+    for (int t = 0; t < a.M; ++t)
+      bulk_g2s(xloc + (size_t)t * a.xcs, static_cast<const uint8_t*>(a.xraw) + (size_t)t * a.ldx * 2, row_bytes, xbar);
+  }
+  // zero the padding past K (only FP8 rows can be ragged)
+  for (int64_t i = a.K + tid; i < a.kp; i += kThreads)
+    for (int t = 0; t < a.M; ++t) reinterpret_cast<uint16_t*>(xloc + (size_t)t * a.xcs)[i] = 0;
+  __syncthreads();  // the barrier init is visible before anyone waits on it
+  mbar_wait_bounded(xbar, 0, status);
+  const int nchunk = (int)(a.kp / 8);
+  for (int t = 0; t < a.M; ++t) {
+    const uint4* row = reinterpret_cast<const uint4*>(xloc + (size_t)t * a.xcs);
+    float m = 0.0f;
+    for (int c = tid; c < nchunk; c += kThreads) {
+      const uint4 u = row[c];
+      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t b16 = (wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+        float v = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
+        if (a.w8a8) v = e4m3_round_ref(v);
+        m = fmaxf(m, fabsf(v));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp * 32 + t] = m;
+  }
+  __syncthreads();
+  if (tid < a.M) {
+    float mm = 0.0f;
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, red[w * 32 + tid]);
+    int e = 0;
+    if (mm > 0.0f && mm <= 3.4e38f) e = min(max(ilogbf(mm) - 14, -110), 110);
+    ts_s[tid] = ldexpf(1.0f, e);
+    red[tid] = ldexpf(1.0f, -e);  // every warp has read its maxima above (barrier)
+  }
+  __syncthreads();
+  float* tab = reinterpret_cast<float*>(sm + a.off_tabloc);
+  constexpr int SBC = F::SBE / 8;
+  const int iters = (nchunk + kThreads - 1) / kThreads;
+  for (int t = 0; t < a.M; ++t) {
+    uint4* row = reinterpret_cast<uint4*>(xloc + (size_t)t * a.xcs);
+    const float inv = red[t];
+    for (int it = 0; it < iters; ++it) {
+      const int c = it * kThreads + tid;
+      const bool valid = c < nchunk;
+      float sum = 0.0f;
+      if (valid) {
+        const uint4 u = row[c];
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+        uint32_t out[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __half h2v[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const uint32_t b16 = (wd[i] >> (16 * k)) & 0xFFFFu;
+            float v = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
+            if (a.w8a8) v = e4m3_round_ref(v);
+            h2v[k] = __float2half_rn(v * inv);
+            sum += __half2float(h2v[k]);
+          }
+          out[i] = pack_h2(h2v[0], h2v[1]);
+        }
+        row[c] = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+      if constexpr (F::TAB) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if constexpr (SBC == 4) sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        constexpr float xoff = F::XOFF;
+        if (valid && (c % SBC) == 0) tab[(c / SBC) * a.ncol8 + t] = sum * xoff;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 // Each CTA owns a contiguous run of whole 16-row tiles; inside a tile, warp w
@@ -587,9 +691,13 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   const int NS = a.NS;
 
   // the issue side walks its own cursor over (tile, group) a few items ahead
+  const bool local_x = a.local_x != 0;
   auto bytes_of = [&](int ng) -> uint32_t {
-    uint32_t b = (uint32_t)ng * F::GB + (uint32_t)ng * a.ncol * CSB;
-    if constexpr (F::TAB) b += (uint32_t)ng * NSB * a.ncol8 * 4;
+    uint32_t b = (uint32_t)ng * F::GB;
+    if (!local_x) {
+      b += (uint32_t)ng * a.ncol * CSB;
+      if constexpr (F::TAB) b += (uint32_t)ng * NSB * a.ncol8 * 4;
+    }
     return b;
   };
   auto issue_w = [&](int s, int tile, int g0, int ng) {
@@ -629,13 +737,19 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       if (++kk == per_tile) { kk = 0; ++tt; gg = gfirst; } else { gg += gstep; }
     }
   }
-  griddep_wait();  // the prep kernel's output is visible from here on
+  griddep_wait();  // earlier work in the stream (x, the prep kernel's output) is visible from here on
+  griddep_launch_dependents();  // the next call may launch; it waits for this grid before touching x
   for (int s = 0; s < npro; ++s) {
-    if (lane == 0) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
+    if (lane == 0 && !local_x) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
     advance();
   }
-  if (tid < a.M) ts_s[tid] = a.tscale[tid];
-  __syncthreads();
+  if (local_x) {
+    stage_local_x<FMT>(a, sm, ts_s, &a.status[0]);
+  } else {
+    if (tid < a.M) ts_s[tid] = a.tscale[tid];
+    __syncthreads();
+  }
+  const uint32_t xloc_s = smem_u32(sm + a.off_xloc), tabloc_s = smem_u32(sm + a.off_tabloc);
 
   float acc[NT][4];
 #pragma unroll
@@ -670,16 +784,24 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         continue;
       }
       const uint32_t slot = wb_s + (uint32_t)(slot_i * a.slot_bytes);
+      if (local_x) {
 #pragma unroll 2
-      for (int gi = 0; gi < ng; ++gi)
-        do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB,
-                          slot + a.off_tab + gi * NSB * a.ncol8 * 4, a.ncol, a.ncol8, tb_s, acc, lane);
+        for (int gi = 0; gi < ng; ++gi)
+          do_group<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, a.xcs,
+                            tabloc_s + (uint32_t)((g0 + gi) * NSB * a.ncol8) * 4, a.ncol, a.ncol8, tb_s, acc,
+                            lane);
+      } else {
+#pragma unroll 2
+        for (int gi = 0; gi < ng; ++gi)
+          do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB,
+                            slot + a.off_tab + gi * NSB * a.ncol8 * 4, a.ncol, a.ncol8, tb_s, acc, lane);
+      }
       __syncwarp();
       if (i + NS < n_items) {
         if (lane == 0) {
           const int ng2 = min(a.IG, a.G - it_g0);
           issue_w(slot_i, it_tile, it_g0, ng2);
-          issue_x(slot_i, it_g0, ng2);
+          if (!local_x) issue_x(slot_i, it_g0, ng2);
         }
         advance();
         next_issue = i + NS + 1;
@@ -768,22 +890,33 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Plan {
   int NS, warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar, off_red;
+  int off_xloc = 0, xcs = 0, off_tabloc = 0;
   size_t smem;
 };
 
-Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref) {
+// local_kp > 0 asks for the local-x region (activations staged by every CTA).
+Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref, int64_t local_kp = 0) {
   const FmtInfo f = fmt_info(fmt);
   const bool tab = fmt != FMT_FP8;
   const int csb = col_stride_bytes(f.gk);
+  const bool local = local_kp > 0;
   Plan p{};
   const size_t off_x = align_up((size_t)IG * f.gb, 128);
-  const size_t off_tab = align_up(off_x + (size_t)IG * ncol * csb, 16);
-  const size_t slot = align_up(off_tab + (tab ? (size_t)IG * (f.gk / f.sbe) * ncol8 * 4 : 0), 128);
+  const size_t off_tab = align_up(off_x + (local ? 0 : (size_t)IG * ncol * csb), 16);
+  const size_t slot = align_up(off_tab + ((tab && !local) ? (size_t)IG * (f.gk / f.sbe) * ncol8 * 4 : 0), 128);
   const size_t red = (size_t)2 * kWarps * 16 * ncol8 * 4 + 32 * 4;
+  size_t loc = 0;
+  if (local) {
+    int xcs = (int)align_up((size_t)local_kp * 2, 16);
+    if (xcs % 128 == 0) xcs += 64;  // columns of the B tile on alternating bank halves
+    p.xcs = xcs;
+    loc = align_up((size_t)ncol * xcs, 16) + (size_t)32 * kWarps * 4 + 16 +
+          (size_t)(local_kp / f.sbe) * ncol8 * 4 + 16;
+  }
   // prefer two CTAs per SM (<= 113 KB each); keep at least two stages in flight
   int NS = ns_pref;
   auto warp_bytes = [&](int ns) { return align_up(ns * slot + kTblBytes + kMaxStages * 8, 128); };
-  while (NS > 2 && warp_bytes(NS) * kWarps + red > 113 * 1024) --NS;
+  while (NS > 2 && warp_bytes(NS) * kWarps + red + loc > 113 * 1024) --NS;
   p.NS = NS;
   p.slot_bytes = (int)slot;
   p.off_x = (int)off_x;
@@ -792,7 +925,13 @@ Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref) {
   p.off_bar = (int)(NS * slot + kTblBytes);
   p.warp_bytes = (int)warp_bytes(NS);
   p.off_red = (int)((size_t)p.warp_bytes * kWarps);
-  p.smem = (size_t)p.off_red + red;
+  size_t end = (size_t)p.off_red + red;
+  if (local) {
+    p.off_xloc = (int)align_up(end, 128);
+    p.off_tabloc = (int)align_up((size_t)p.off_xloc + (size_t)ncol * p.xcs, 16) + 32 * kWarps * 4 + 16;
+    end = (size_t)p.off_tabloc + (size_t)(local_kp / f.sbe) * ncol8 * 4;
+  }
+  p.smem = align_up(end, 16);
   return p;
 }
 
@@ -881,8 +1020,17 @@ cudaError_t launch_gemv_nt(const Args& a, int NT, unsigned nctas, size_t smem, c
 
 template <int FMT>
 cudaError_t launch_prep(const PrepArgs& p, cudaStream_t st) {
-  prep_kernel<FMT><<<p.M * kPrepCluster, kPrepThreads, 0, st>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.M * kPrepCluster));
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prep_kernel<FMT>, p);
 }
 
 }  // namespace
@@ -929,6 +1077,7 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   }();
   const size_t esz = (c.x_dtype == 0) ? 4 : 2;
   const bool x_vec = ((uintptr_t)c.x % 16 == 0) && ((c.ldx * (int64_t)esz) % 16 == 0);
+  static const bool env_no_local = std::getenv("RTD_GEMV_NO_LOCAL_X") != nullptr;
   if (T >= (1LL << 31) || G >= (1LL << 31)) {
     *plan_error = 1;
     return cudaSuccess;
@@ -942,7 +1091,11 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     const int ncol = Mt * P;
     const int NT = (ncol + 7) / 8;
     const int ncol8 = 8 * NT;
-    const Plan pl = make_plan(c.fmt, IG, ncol, ncol8, env_ns);
+    // bf16 / f16 activations whose rows are bulk-copyable: every CTA stages x itself
+    // (no prep kernel) when the staged rows and sums stay small.
+    const bool local_ok = P == 1 && x_vec && (c.K % 8 == 0) && !env_no_local &&
+                          (size_t)ncol * kp * 2 + (size_t)(kp / f.sbe) * ncol8 * 4 <= 48 * 1024;
+    const Plan pl = make_plan(c.fmt, IG, ncol, ncol8, env_ns, local_ok ? kp : 0);
     const int occ = occupancy_of(c.fmt, NT, pl.smem);
     const int64_t slots = (int64_t)c.sm_count * occ;
     // Enough tiles for every warp to own at least two whole ones: no cross-warp
@@ -976,14 +1129,16 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     pa.cols = cols;
     pa.tab = tab;
     pa.tscale = tscale;
-    cudaError_t e;
-    switch (c.fmt) {
-      case FMT_Q4K: e = launch_prep<FMT_Q4K>(pa, c.stream); break;
-      case FMT_Q6K: e = launch_prep<FMT_Q6K>(pa, c.stream); break;
-      case FMT_Q80: e = launch_prep<FMT_Q80>(pa, c.stream); break;
-      default:      e = launch_prep<FMT_FP8>(pa, c.stream); break;
+    cudaError_t e = cudaSuccess;
+    if (!local_ok) {
+      switch (c.fmt) {
+        case FMT_Q4K: e = launch_prep<FMT_Q4K>(pa, c.stream); break;
+        case FMT_Q6K: e = launch_prep<FMT_Q6K>(pa, c.stream); break;
+        case FMT_Q80: e = launch_prep<FMT_Q80>(pa, c.stream); break;
+        default:      e = launch_prep<FMT_FP8>(pa, c.stream); break;
+      }
+      if (e != cudaSuccess) return e;
     }
-    if (e != cudaSuccess) return e;
 
     Args a{};
     a.w = c.w;
@@ -1016,6 +1171,16 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_tbl = pl.off_tbl;
     a.off_bar = pl.off_bar;
     a.off_red = pl.off_red;
+    a.local_x = local_ok ? 1 : 0;
+    a.xraw = pa.x;
+    a.ldx = c.ldx;
+    a.K = c.K;
+    a.kp = kp;
+    a.x_dtype = c.x_dtype;
+    a.w8a8 = c.w8a8;
+    a.off_xloc = pl.off_xloc;
+    a.xcs = pl.xcs;
+    a.off_tabloc = pl.off_tabloc;
     a.status = c.status;
     switch (c.fmt) {
       case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;
