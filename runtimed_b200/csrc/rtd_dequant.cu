@@ -12,63 +12,62 @@
 
 namespace rtd {
 
-// Position of natural byte `off` (0..7) inside a lane's 8-byte run: bytes 1 and 2
-// of every 4-byte word are swapped by the repack (rtd_repack.cpp).
+// Position of natural byte `off` (0..7) inside an FP8 lane's 8-byte run: bytes 1
+// and 2 of every 4-byte word are swapped by the repack (rtd_repack.cpp).
 __device__ __forceinline__ int swz(int off) {
   const int b = off & 3;
   return (off & 4) | (b == 1 ? 2 : b == 2 ? 1 : b);
 }
 
-// Decode element (row r in 0..15, element e in 0..gk-1) of one group.
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t* a) {
+  return (uint32_t)a[0] | ((uint32_t)a[1] << 8) | ((uint32_t)a[2] << 16) | ((uint32_t)a[3] << 24);
+}
+
+// Decode element (row r in 0..15, element e in 0..gk-1) of one group (layouts in
+// rtd_layout.h: lane 4g+t owns whole sub-blocks of rows g and g+8).
 template <int FMT>
 __device__ __forceinline__ float decode_elem(const uint8_t* grp, int r, int e) {
-  const int g = r & 7, half = r >> 3;
+  const int g = r & 7, rr = r >> 3;
   if constexpr (FMT == FMT_Q4K) {
     const uint8_t* hdr = grp + 16 * r;
     const float d = ld_f16(hdr), dmin = ld_f16(hdr + 2);
-    const int c = e >> 6, rem = e & 63, l = rem & 31;
+    const int c = e >> 6, rem = e & 63, j = rem & 31;
     const bool low = rem < 32;
-    const int j = 2 * c + (low ? 0 : 1);
     uint32_t sc, m;
-    scale_min_k4(j, hdr + 4, sc, m);
+    scale_min_k4(2 * c + (low ? 0 : 1), hdr + 4, sc, m);
     const float d1 = __fmul_rn(d, (float)sc);
     const float m1 = __fmul_rn(dmin, (float)m);
-    const int tg = l >> 3, off = l & 7;
-    const uint8_t byte = grp[256 + c * 512 + (4 * g + tg) * 16 + half * 8 + swz(off)];
+    const uint8_t byte = grp[256 + (2 * rr + (j >> 4)) * 512 + (4 * g + c) * 16 + (j & 15)];
     const float q = (float)(low ? (byte & 0xF) : (byte >> 4));
     return __fsub_rn(__fmul_rn(d1, q), m1);
   } else if constexpr (FMT == FMT_Q6K) {
-    const float d = ld_f16(grp + 2 * r);
-    const int sb = e >> 4, i = e & 15, tg = i >> 2, j = i & 3;
-    const int8_t sc = (int8_t)grp[32 + 16 * r + sb];
-    const int p = sb >> 1, which = sb & 1;
-    const int lane = 4 * g + tg;
-    auto word = [&](int w) -> uint32_t {
-      const uint8_t* a = grp + 288 + (w >> 2) * 512 + lane * 16 + (w & 3) * 4;
-      return (uint32_t)a[0] | ((uint32_t)a[1] << 8) | ((uint32_t)a[2] << 16) | ((uint32_t)a[3] << 24);
-    };
+    const float d = ld_f16(grp + 4 * g + 2 * rr);
+    const int sb = e >> 4, i = e & 15;
+    const int h = sb >> 3, t = (sb & 7) >> 1, side = sb & 1;
+    const int lane = 4 * g + t;
+    const int8_t sc = (int8_t)grp[32 + lane * 8 + 4 * rr + 2 * h + side];
+    const int w0 = 12 * h + 3 * (2 * side + rr);  // first word of this (row, sub-block) triple
+    auto word = [&](int w) -> uint32_t { return ld_u32(grp + 288 + (w >> 2) * 512 + lane * 16 + (w & 3) * 4); };
     const int shift[4] = {0, 16, 6, 22};
     uint32_t code;
-    if (which == 0) {
-      code = (word(3 * p + half) >> shift[j]) & 63u;
-    } else if (half == 0) {
-      code = (word(3 * p + 2) >> shift[j]) & 63u;
+    if (i < 12) {
+      code = (word(w0 + (i >> 2)) >> shift[i & 3]) & 63u;
     } else {
-      const uint32_t X = word(3 * p), Y = word(3 * p + 1), Z = word(3 * p + 2);
-      const uint32_t lo = (j == 0) ? (X >> 12) : (j == 1) ? (X >> 28) : (j == 2) ? (Y >> 12) : (Y >> 28);
-      const uint32_t hi = (j == 0) ? (Z >> 12) : (j == 1) ? (Z >> 28) : (j == 2) ? (Z >> 14) : (Z >> 30);
+      const uint32_t X = word(w0), Y = word(w0 + 1), Z = word(w0 + 2);
+      const uint32_t lo = (i == 12) ? (X >> 12) : (i == 13) ? (X >> 28) : (i == 14) ? (Y >> 12) : (Y >> 28);
+      const uint32_t hi = (i == 12) ? (Z >> 12) : (i == 13) ? (Z >> 28) : (i == 14) ? (Z >> 14) : (Z >> 30);
       code = (lo & 0xFu) | ((hi & 3u) << 4);
     }
     const float v = (float)(int)code - 32.0f;
     return __fmul_rn(__fmul_rn(d, (float)sc), v);
   } else if constexpr (FMT == FMT_Q80) {
-    const float d = ld_f16(grp + 2 * r);
-    const int tg = e >> 3, off = e & 7;
-    const int8_t q = (int8_t)grp[32 + (4 * g + tg) * 16 + half * 8 + swz(off)];
+    const int blk = e >> 5, i = e & 31, lane = 4 * g + blk;
+    const float d = ld_f16(grp + 4 * lane + 2 * rr);
+    const int8_t q = (int8_t)grp[128 + (2 * rr + (i >> 4)) * 512 + lane * 16 + (i & 15)];
     return __fmul_rn(d, (float)q);
   } else {
     const int tg = e >> 3, off = e & 7;
-    const uint8_t b = grp[(4 * g + tg) * 16 + half * 8 + swz(off)];
+    const uint8_t b = grp[(4 * g + tg) * 16 + rr * 8 + swz(off)];
     const uint32_t h = e4m3x2_to_f16x2((uint16_t)b) & 0xFFFFu;
     return __half2float(__ushort_as_half((unsigned short)h));
   }
@@ -77,8 +76,8 @@ __device__ __forceinline__ float decode_elem(const uint8_t* grp, int r, int e) {
 // One thread per output element of row `n` (global row), k in [0, K).
 template <int FMT>
 __device__ __forceinline__ float decode_row_elem(const uint8_t* w, int64_t G, int64_t n, int64_t k) {
-  constexpr int GK = (FMT == FMT_Q4K || FMT == FMT_Q6K) ? 256 : 32;
-  constexpr int GB = (FMT == FMT_Q4K) ? 2304 : (FMT == FMT_Q6K) ? 3360 : (FMT == FMT_Q80) ? 544 : 512;
+  constexpr int GK = (FMT == FMT_Q4K || FMT == FMT_Q6K) ? 256 : (FMT == FMT_Q80) ? 128 : 32;
+  constexpr int GB = (FMT == FMT_Q4K) ? 2304 : (FMT == FMT_Q6K) ? 3360 : (FMT == FMT_Q80) ? 2176 : 512;
   const int64_t t = n >> 4, s = k / GK;
   const uint8_t* grp = w + (size_t)(t * G + s) * GB;
   return decode_elem<FMT>(grp, (int)(n & 15), (int)(k - s * GK));

@@ -58,38 +58,61 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kPrepThreads = 256;
 constexpr int kPrepCluster = 8;
 constexpr int kMaxStages = 4;
-constexpr int kTblBytes = 1280;  // per-warp scale table: 16 rows x 9 float2 (Q4_K) or 16 x 17 float (Q6_K)
+constexpr int kTblBytes = 1280;
+constexpr int kZeroPage = 512;  // zero B-fragment source for DIAG lanes that own no column  // per-warp scale table: 16 rows x 9 float2 (Q4_K) or 16 x 17 float (Q6_K)
 
 template <int FMT>
 struct FmtC;
+// DIAG formats (the K-quants and Q8_0) use the lane-owned group layouts of
+// rtd_layout.h and the sub-block-per-MMA-column decoder (do_group_diag); FP8 keeps
+// the token-per-column decoder.  DIAG codes enter the MMA as f16 subnormals (code
+// bits in the mantissa, exponent 0: value = code * 2^-24, exact).  XOFF: the
+// column-sum table holds XOFF * sum(x) per sub-block -- plain sums for Q4_K's min
+// term, and for Q6_K / Q8_0 the C-init that removes the code bias (32, 128) at the
+// same 2^-24 scale.
 template <>
 struct FmtC<FMT_Q4K> {
   static constexpr int GK = 256, GB = 2304, SBE = 32;
-  static constexpr float XOFF = 1.0f;  // plain sub-block sums: the min term needs them unscaled
-  static constexpr bool TAB = true;
+  static constexpr float XOFF = 1.0f;
+  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_Q6K> {
   static constexpr int GK = 256, GB = 3360, SBE = 16;
-  static constexpr float XOFF = -1056.0f;
-  static constexpr bool TAB = true;
+  static constexpr float XOFF = -0x1p-19f;  // -32 * 2^-24
+  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_Q80> {
-  static constexpr int GK = 32, GB = 544, SBE = 32;
-  static constexpr float XOFF = -1152.0f;
-  static constexpr bool TAB = true;
+  static constexpr int GK = 128, GB = 2176, SBE = 32;
+  static constexpr float XOFF = -0x1p-17f;  // -128 * 2^-24
+  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_FP8> {
   static constexpr int GK = 32, GB = 512, SBE = 32;
-  static constexpr bool TAB = false;
+  static constexpr bool TAB = false, DIAG = false;
 };
 
 // Bytes one activation column occupies per group in the workspace (and in shared
-// memory): 256-wide groups get 64 bytes of padding so that adjacent columns of the
-// B tile fall on different shared-memory banks.
-__host__ __device__ constexpr int col_stride_bytes(int gk) { return gk * 2 + (gk >= 256 ? 64 : 0); }
+// memory).  FP8 keeps its natural order; DIAG formats store a group's x as 16-byte
+// units (8 elements) transposed to [unit-in-sub-block j][sub-block], so that the
+// lanes supplying different sub-blocks in one load hit different banks.
+__host__ __device__ constexpr int col_stride_bytes(int gk) { return gk * 2; }
+
+// Destination of natural unit n (elements 8n..8n+7) of a group in the DIAG x order.
+template <int FMT>
+__host__ __device__ constexpr int diag_unit_offset(int n) {
+  constexpr int UPS = FmtC<FMT>::SBE / 8, NSB = FmtC<FMT>::GK / FmtC<FMT>::SBE;
+  return (n % UPS) * (NSB * 16) + 16 * (n / UPS);
+}
+
+// Q4_K's MMA pairs take elements (4u, 4u+2) and (4u+1, 4u+3) of a sub-block (the two
+// 16-bit halves of one 4-byte code word); x is staged in that order.
+__device__ __forceinline__ uint4 q4k_quad_order(uint4 u) {
+  return make_uint4(__byte_perm(u.x, u.y, 0x5410), __byte_perm(u.x, u.y, 0x7632), __byte_perm(u.z, u.w, 0x5410),
+                    __byte_perm(u.z, u.w, 0x7632));
+}
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
@@ -104,7 +127,7 @@ struct PrepArgs {
   int M, P, ncol, ncol8;
   int w8a8;
   uint8_t* cols;  // [group][ncol][col_stride_bytes(GK)]
-  float* tab;     // [kp / SBE][ncol8]
+  float* tab;     // [group][ncol][GK / SBE]
   float* tscale;  // [M]
 };
 
@@ -232,14 +255,17 @@ __global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThre
       const int64_t k = 8 * c;
       const int64_t grp = k / F::GK;
       const int within = (int)(k - grp * F::GK);
-      uint8_t* base = a.cols + ((size_t)grp * a.ncol + (size_t)t * a.P) * CSB + within * 2;
+      const int off = F::DIAG ? diag_unit_offset<FMT>(within / 8) : within * 2;
+      uint8_t* base = a.cols + ((size_t)grp * a.ncol + (size_t)t * a.P) * CSB + off;
       uint4 u;
       u.x = pack_h2(hi[0], hi[1]); u.y = pack_h2(hi[2], hi[3]);
       u.z = pack_h2(hi[4], hi[5]); u.w = pack_h2(hi[6], hi[7]);
+      if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
       *reinterpret_cast<uint4*>(base) = u;
       if (a.P == 2) {
         u.x = pack_h2(lo[0], lo[1]); u.y = pack_h2(lo[2], lo[3]);
         u.z = pack_h2(lo[4], lo[5]); u.w = pack_h2(lo[6], lo[7]);
+        if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
         *reinterpret_cast<uint4*>(base + CSB) = u;
       }
     }
@@ -252,20 +278,15 @@ __global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThre
         slo += __shfl_xor_sync(0xffffffffu, slo, 2);
       }
       if (valid && (c % SBC) == 0) {
-        const int64_t sb = c / SBC;
+        // table [group][column][sub-block]
+        constexpr int NSB = F::GK / F::SBE;
+        const int64_t sb = c / SBC, grp = sb / NSB;
+        const int sbi = (int)(sb - grp * NSB);
+        float* tp = a.tab + ((size_t)grp * a.ncol + (size_t)t * a.P) * NSB + sbi;
         constexpr float xoff = F::XOFF;
-        a.tab[sb * a.ncol8 + t * a.P] = shi * xoff;
-        if (a.P == 2) a.tab[sb * a.ncol8 + t * a.P + 1] = slo * xoff;
+        tp[0] = shi * xoff;
+        if (a.P == 2) tp[NSB] = slo * xoff;
       }
-    }
-  }
-  if constexpr (F::TAB) {
-    // columns past ncol in the table read as zero; token 0's cluster clears them
-    if (t == 0 && a.ncol < a.ncol8) {
-      const int64_t sb0 = c0 / SBC, nsb = nch / SBC;
-      const int extra = a.ncol8 - a.ncol;
-      for (int64_t i = tid; i < nsb * extra; i += kPrepThreads)
-        a.tab[(sb0 + i / extra) * a.ncol8 + a.ncol + (i % extra)] = 0.0f;
     }
   }
 }
@@ -292,17 +313,6 @@ __device__ __forceinline__ float ldsf(uint32_t a) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-  unsigned short v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ void stsf2(uint32_t a, float x, float y) {
-  asm volatile("st.shared.v2.f32 [%0], {%1,%2};" ::"r"(a), "f"(x), "f"(y) : "memory");
-}
-__device__ __forceinline__ void stsf(uint32_t a, float x) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(x) : "memory");
 }
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 
@@ -362,145 +372,20 @@ __device__ __forceinline__ void static_for(Fn&& f) {
   }
 }
 
-// One group (16 rows x GK k) of one format into the warp's accumulators.
-//   gs: the group's bytes; xs: this group's x slice (column c at xs + c*xstride);
-//   ts: its sub-block table [sub-block][ncol8] f32; tb: the warp's scale-table scratch.
+// One FP8 group (16 rows x 32 k) into the warp's accumulators, tokens as MMA
+// columns: acc[nt] is the m16n8 C fragment of activation columns 8nt .. 8nt+7.
+//   gs: the group's bytes; xs: this group's x slice (column c at xs + c*xstride).
 // Activation columns >= ncol read column ncol-1: those MMA output columns are never
 // stored, so no select is needed.
 template <int FMT, int NT>
-__device__ __forceinline__ void do_group(uint32_t gs, uint32_t xs, int xstride, uint32_t ts, int ncol, int ncol8,
-                                         uint32_t tb, float (&acc)[NT][4], int lane) {
+__device__ __forceinline__ void do_group(uint32_t gs, uint32_t xs, int xstride, int ncol, float (&acc)[NT][4],
+                                         int lane) {
+  static_assert(FMT == FMT_FP8, "the token-per-column decoder serves FP8 groups");
   const int g = lane >> 2, tq = lane & 3;
-  uint32_t xcol[NT];
+  uint32_t xcol[NT];  // this lane's B column (clamped)
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) xcol[nt] = xs + (uint32_t)min(nt * 8 + g, ncol - 1) * xstride;
-  if constexpr (FMT == FMT_Q4K) {
-    // per-warp table of (D, -Mo) for 16 rows x 8 sub-blocks; rows are 10 entries
-    // apart so a lane reads two sub-blocks with one 16-byte load, conflict-free
-    {
-      const int r = lane >> 1, half = lane & 1;
-      const uint4 h = lds128(gs + 16 * r);  // d, dmin | scales[0..3] | scales[4..7] | scales[8..11]
-      const float d = h2f(h.x & 0xFFFFu), dmin = h2f(h.x >> 16);
-      // scale_min_k4 for four sub-blocks at once, one byte per sub-block
-      const uint32_t sc4 = half ? and_or(h.w, 0x0F0F0F0Fu, (h.y >> 2) & 0x30303030u) : (h.y & 0x3F3F3F3Fu);
-      const uint32_t m4 = half ? and_or(h.w >> 4, 0x0F0F0F0Fu, (h.z >> 2) & 0x30303030u) : (h.z & 0x3F3F3F3Fu);
-      const uint32_t tr = tb + (uint32_t)(r * 10 + 4 * half) * 8;
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        float D = d * (float)((sc4 >> (8 * jj)) & 0xFFu);
-        if (jj & 1) D *= 0.0625f;  // high nibbles enter the MMA as 1024 + 16 q
-        stsf2(tr + jj * 8, D, -fmaf(1024.0f, D, dmin * (float)((m4 >> (8 * jj)) & 0xFFu)));
-      }
-    }
-    __syncwarp();
-    const uint32_t qb = gs + 256 + lane * 16;
-    const uint32_t tg_ = tb + (uint32_t)(g * 10) * 8, th_ = tb + (uint32_t)((g + 8) * 10) * 8;
-    const uint32_t svb = ts + (uint32_t)(2 * tq) * 4;
-    uint32_t xb[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) xb[nt] = xcol[nt] + tq * 16;
-    const uint32_t C64 = 0x64006400u;
-    static_for<0, 4>([&](auto cI) {
-      constexpr int c = decltype(cI)::value;
-      const uint4 q = lds128o<256 * 0 + c * 512>(qb);
-      const float4 Dg = ldsf4o<(2 * c) * 8>(tg_);  // (D, -Mo) of sub-blocks 2c, 2c+1
-      const float4 Dh = ldsf4o<(2 * c) * 8>(th_);
-      const uint32_t s0 = q.x >> 8, s1 = q.y >> 8, s2 = q.z >> 8, s3 = q.w >> 8;
-      static_for<0, 2>([&](auto selI) {
-        constexpr int sel = decltype(selI)::value;
-        constexpr int sb = 2 * c + sel;
-        const uint32_t msk = sel ? 0x00F000F0u : 0x000F000Fu;
-        const uint32_t a0 = and_or(q.x, msk, C64), a1 = and_or(q.z, msk, C64);
-        const uint32_t a2 = and_or(s0, msk, C64), a3 = and_or(s2, msk, C64);
-        const uint32_t b0 = and_or(q.y, msk, C64), b1 = and_or(q.w, msk, C64);
-        const uint32_t b2 = and_or(s1, msk, C64), b3 = and_or(s3, msk, C64);
-        const float dgx = sel ? Dg.z : Dg.x, dgy = sel ? Dg.w : Dg.y;
-        const float dhx = sel ? Dh.z : Dh.x, dhy = sel ? Dh.w : Dh.y;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const uint4 bx = lds128(xb[nt] + sb * 64);
-          const float2 sv = ldsf2(svb + (uint32_t)(sb * 8 * NT + nt * 8) * 4);
-          float t4[4];
-          mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, 0.f, 0.f, 0.f, 0.f);
-          mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
-          acc[nt][0] = fmaf(dgx, t4[0], fmaf(dgy, sv.x, acc[nt][0]));
-          acc[nt][1] = fmaf(dgx, t4[1], fmaf(dgy, sv.y, acc[nt][1]));
-          acc[nt][2] = fmaf(dhx, t4[2], fmaf(dhy, sv.x, acc[nt][2]));
-          acc[nt][3] = fmaf(dhx, t4[3], fmaf(dhy, sv.y, acc[nt][3]));
-        }
-      });
-    });
-    __syncwarp();
-  } else if constexpr (FMT == FMT_Q6K) {
-    // per-warp table of d*sc for 16 rows x 16 sub-blocks, rows padded to 17 floats
-    {
-      const int r = lane >> 1, jb = (lane & 1) * 8;
-      const float d = h2f(lds16(gs + 2 * r));
-      const uint2 sv = lds64(gs + 32 + 16 * r + jb);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int8_t sc = (int8_t)(((jj < 4 ? sv.x : sv.y) >> (8 * (jj & 3))) & 0xFFu);
-        stsf(tb + (uint32_t)(r * 17 + jb + jj) * 4, d * (float)sc);
-      }
-    }
-    __syncwarp();
-    constexpr uint32_t C = 0x64006400u, M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
-    uint32_t wv[24];
-#pragma unroll
-    for (int v = 0; v < 6; ++v) {
-      const uint4 u = lds128(gs + 288 + v * 512 + lane * 16);
-      wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
-    }
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const uint32_t X = wv[3 * p], Y = wv[3 * p + 1], Z = wv[3 * p + 2];
-      const uint32_t aa0 = lop_and_or(X, M6, C), aa1 = lop_and_or(Y, M6, C);
-      const uint32_t aa2 = lop_and_or(X >> 6, M6, C), aa3 = lop_and_or(Y >> 6, M6, C);
-      const uint32_t ab0 = lop_and_or(Z, M6, C);
-      const uint32_t ab1 = lop_and_or(X >> 12, M4, C) | ((Z >> 8) & M2);
-      const uint32_t ab2 = lop_and_or(Z >> 6, M6, C);
-      const uint32_t ab3 = lop_and_or(Y >> 12, M4, C) | ((Z >> 10) & M2);
-      const float dga = ldsf(tb + (uint32_t)(g * 17 + 2 * p) * 4), dgb = ldsf(tb + (uint32_t)(g * 17 + 2 * p + 1) * 4);
-      const float dha = ldsf(tb + (uint32_t)((g + 8) * 17 + 2 * p) * 4);
-      const float dhb = ldsf(tb + (uint32_t)((g + 8) * 17 + 2 * p + 1) * 4);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint2 ba = lds64(xcol[nt] + p * 64 + tq * 8), bb = lds64(xcol[nt] + p * 64 + 32 + tq * 8);
-        const float2 xa = ldsf2(ts + (uint32_t)((2 * p) * ncol8 + nt * 8 + 2 * tq) * 4);
-        const float2 xb = ldsf2(ts + (uint32_t)((2 * p + 1) * ncol8 + nt * 8 + 2 * tq) * 4);
-        float ta[4], tbv[4];
-        mma_f16(ta, aa0, aa1, aa2, aa3, ba.x, ba.y, xa.x, xa.y, xa.x, xa.y);
-        mma_f16(tbv, ab0, ab1, ab2, ab3, bb.x, bb.y, xb.x, xb.y, xb.x, xb.y);
-        acc[nt][0] = fmaf(dga, ta[0], fmaf(dgb, tbv[0], acc[nt][0]));
-        acc[nt][1] = fmaf(dga, ta[1], fmaf(dgb, tbv[1], acc[nt][1]));
-        acc[nt][2] = fmaf(dha, ta[2], fmaf(dhb, tbv[2], acc[nt][2]));
-        acc[nt][3] = fmaf(dha, ta[3], fmaf(dhb, tbv[3], acc[nt][3]));
-      }
-    }
-    __syncwarp();
-  } else if constexpr (FMT == FMT_Q80) {
-    const float dg = h2f(lds16(gs + 2 * g)), dh = h2f(lds16(gs + 2 * (g + 8)));
-    const uint4 q = lds128(gs + 32 + lane * 16);
-    const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u, u2 = q.z ^ 0x80808080u,
-                   u3 = q.w ^ 0x80808080u;
-    const uint32_t K64 = 0x64646464u;
-    const uint32_t a0 = prmt(u0, K64, 0x4240), a1 = prmt(u2, K64, 0x4240);
-    const uint32_t a2 = prmt(u0, K64, 0x4341), a3 = prmt(u2, K64, 0x4341);
-    const uint32_t b0 = prmt(u1, K64, 0x4240), b1 = prmt(u3, K64, 0x4240);
-    const uint32_t b2 = prmt(u1, K64, 0x4341), b3 = prmt(u3, K64, 0x4341);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint4 bx = lds128(xcol[nt] + tq * 16);
-      const float2 xo = ldsf2(ts + (uint32_t)(nt * 8 + 2 * tq) * 4);
-      float t4[4];
-      mma_f16(t4, a0, a1, a2, a3, bx.x, bx.y, xo.x, xo.y, xo.x, xo.y);
-      mma_f16(t4, b0, b1, b2, b3, bx.z, bx.w, t4[0], t4[1], t4[2], t4[3]);
-      acc[nt][0] = fmaf(dg, t4[0], acc[nt][0]);
-      acc[nt][1] = fmaf(dg, t4[1], acc[nt][1]);
-      acc[nt][2] = fmaf(dh, t4[2], acc[nt][2]);
-      acc[nt][3] = fmaf(dh, t4[3], acc[nt][3]);
-    }
-  } else {  // FMT_FP8
+  {
     const uint4 q = lds128(gs + lane * 16);
     const uint32_t p0 = prmt(q.x, 0u, 0x3120), p1 = prmt(q.y, 0u, 0x3120);
     const uint32_t p2 = prmt(q.z, 0u, 0x3120), p3 = prmt(q.w, 0u, 0x3120);
@@ -513,6 +398,211 @@ __device__ __forceinline__ void do_group(uint32_t gs, uint32_t xs, int xstride, 
       const uint4 bx = lds128(xcol[nt] + tq * 16);
       mma_f16(acc[nt], a0, a1, a2, a3, bx.x, bx.y, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
       mma_f16(acc[nt], b0, b1, b2, b3, bx.z, bx.w, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
+// The float with bits 0x4B0000XX is 2^23 + XX.  Used through an FMA the 2^23 drops
+// out exactly: fmaf(s, 2^23 + XX, -2^23 * s) == s * XX, rounded once.
+__device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(bits); }
+constexpr float kMagic = 8388608.0f;  // 2^23
+
+// Sub-block factors of one Q4_K row for the two sub-blocks a lane owns (2t, 2t+1):
+// Ea = d*sc_a*2^24 (low nibbles enter the MMA as q * 2^-24), Eb = d*sc_b*2^20 (high
+// nibbles as 16q * 2^-24), Fa/b = -dmin*m (times the plain column sums).
+// Header h = (d | dmin << 16, scales[0..3], scales[4..7], scales[8..11]), dequant_k.rs:8-16.
+__device__ __forceinline__ void q4k_row_factors(uint4 h, bool hiq, uint32_t selA, uint32_t selB, float& Ea,
+                                                float& Eb, float& Fa, float& Fb) {
+  const uint32_t sc4 = hiq ? and_or(h.w, 0x0F0F0F0Fu, (h.y >> 2) & 0x30303030u) : (h.y & 0x3F3F3F3Fu);
+  const uint32_t m4 = hiq ? and_or(h.w >> 4, 0x0F0F0F0Fu, (h.z >> 2) & 0x30303030u) : (h.z & 0x3F3F3F3Fu);
+  const float D = h2f(h.x & 0xFFFFu), Dm = h2f(h.x >> 16);
+  const float Da = D * 0x1p24f, Db = D * 0x1p20f;
+  constexpr uint32_t MG = 0x4B000000u;
+  Ea = fmaf(Da, magic_f(prmt(sc4, MG, selA)), -kMagic * Da);
+  Eb = fmaf(Db, magic_f(prmt(sc4, MG, selB)), -kMagic * Db);
+  Fa = fmaf(-Dm, magic_f(prmt(m4, MG, selA)), kMagic * Dm);
+  Fb = fmaf(-Dm, magic_f(prmt(m4, MG, selB)), kMagic * Dm);
+}
+
+// One group of a DIAG format for NC activation columns.
+//
+// The 8 columns of each m16n8k16 MMA are SUB-BLOCKS, not tokens: lane (g, t) holds
+// the A fragments of the sub-blocks it owns (k-slots 2t,2t+1 = its first sub-block,
+// 2t+8,2t+9 = its second), and the B fragment of column n is the activation slice of
+// sub-block n, supplied only by the lane whose MMA column is n (g == 2t or 2t+1);
+// every other lane feeds zeros from a zero page.  After all MMAs of the group,
+// C[row][n] is the code-weighted dot product of sub-block n alone (times 2^-24),
+// so each lane applies the scales of exactly its own (row, sub-block) pairs -- no
+// per-sub-block MMA chains and no shared scale table.
+//   gs: group bytes; xs: column 0's x units of this group (column c at xs + c*xcs);
+//   ts: table of this group, [column][sub-block] f32; z0 / z1: zero-page pointers for
+//   idle b0 / b1 lanes; acc[c][0 / 1]: this lane's partial sums of rows g / g+8.
+template <int FMT, int NC>
+__device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t xcs, uint32_t ts, uint32_t z0,
+                                              uint32_t z1, bool act0, bool act1, float (&acc)[NC][4], int lane) {
+  const int g = lane >> 2, tq = lane & 3;
+  if constexpr (FMT == FMT_Q4K) {
+    constexpr int NSB = 8;
+    const uint4 hg = lds128(gs + 16 * g), hh = lds128(gs + 16 * (g + 8));
+    const uint32_t qb = gs + 256 + lane * 16;
+    const uint4 q0 = lds128o<0>(qb), q1 = lds128o<512>(qb), q2 = lds128o<1024>(qb), q3 = lds128o<1536>(qb);
+    const bool hiq = tq >= 2;
+    const uint32_t selA = 0x7440u | (uint32_t)(2 * (tq & 1)), selB = selA + 1;
+    float Ea0, Eb0, Fa0, Fb0, Ea1, Eb1, Fa1, Fb1;
+    q4k_row_factors(hg, hiq, selA, selB, Ea0, Eb0, Fa0, Fb0);
+    q4k_row_factors(hh, hiq, selA, selB, Ea1, Eb1, Fa1, Fb1);
+    const uint32_t wg[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t wh[8] = {q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    uint32_t p0[NC], p1[NC];
+    float2 T[NC];
+    float C[NC][4];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const uint32_t xc = xs + c * xcs + 32 * tq;
+      p0[c] = act0 ? xc : z0;
+      p1[c] = act1 ? xc + 16 : z1;
+      T[c] = ldsf2(ts + (uint32_t)(c * NSB + 2 * tq) * 4);
+      C[c][0] = C[c][1] = C[c][2] = C[c][3] = 0.0f;
+    }
+    static_for<0, 4>([&](auto jI) {
+      constexpr int j = decltype(jI)::value;
+      uint4 B0[NC], B1[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        B0[c] = lds128o<128 * j>(p0[c]);
+        B1[c] = lds128o<128 * j>(p1[c]);
+      }
+      static_for<0, 4>([&](auto eI) {
+        constexpr int e4 = decltype(eI)::value;
+        constexpr int u = 2 * j + (e4 >> 1);
+        const uint32_t vg = (e4 & 1) ? (wg[u] >> 8) : wg[u];
+        const uint32_t vh = (e4 & 1) ? (wh[u] >> 8) : wh[u];
+        const uint32_t a0 = vg & 0x000F000Fu, a1 = vh & 0x000F000Fu;
+        const uint32_t a2 = vg & 0x00F000F0u, a3 = vh & 0x00F000F0u;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const uint32_t b0 = e4 == 0 ? B0[c].x : e4 == 1 ? B0[c].y : e4 == 2 ? B0[c].z : B0[c].w;
+          const uint32_t b1 = e4 == 0 ? B1[c].x : e4 == 1 ? B1[c].y : e4 == 2 ? B1[c].z : B1[c].w;
+          mma_f16(C[c], a0, a1, a2, a3, b0, b1, C[c][0], C[c][1], C[c][2], C[c][3]);
+        }
+      });
+    });
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      acc[c][0] = fmaf(Ea0, C[c][0], fmaf(Eb0, C[c][1], fmaf(Fa0, T[c].x, fmaf(Fb0, T[c].y, acc[c][0]))));
+      acc[c][1] = fmaf(Ea1, C[c][2], fmaf(Eb1, C[c][3], fmaf(Fa1, T[c].x, fmaf(Fb1, T[c].y, acc[c][1]))));
+    }
+  } else if constexpr (FMT == FMT_Q6K) {
+    constexpr int NSB = 16;
+    const uint32_t dd = lds32(gs + 4 * g);
+    const uint2 scw = lds64(gs + 32 + lane * 8);
+    const float dg = h2f(dd & 0xFFFFu) * 0x1p24f, dh = h2f(dd >> 16) * 0x1p24f;
+    const uint32_t cb = gs + 288 + lane * 16;
+    constexpr uint32_t M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
+    // code pair i (elements 2i, 2i+1 of the sub-block) of one (X, Y, Z) triple
+    auto pair = [&](uint32_t X, uint32_t Y, uint32_t Z, int i) -> uint32_t {
+      switch (i) {
+        case 0: return X & M6;
+        case 1: return (X >> 6) & M6;
+        case 2: return Y & M6;
+        case 3: return (Y >> 6) & M6;
+        case 4: return Z & M6;
+        case 5: return (Z >> 6) & M6;
+        case 6: return lop_and_or(X >> 12, M4, (Z >> 8) & M2);
+        default: return lop_and_or(Y >> 12, M4, (Z >> 10) & M2);
+      }
+    };
+    static_for<0, 2>([&](auto hI) {
+      constexpr int h = decltype(hI)::value;
+      const uint4 v0 = lds128o<(3 * h) * 512>(cb), v1 = lds128o<(3 * h + 1) * 512>(cb),
+                  v2 = lds128o<(3 * h + 2) * 512>(cb);
+      // triples: (g, a) = v0.xyz, (g+8, a) = v0.w v1.xy, (g, b) = v1.zw v2.x, (g+8, b) = v2.yzw
+      const float Ega = dg * (float)(int8_t)((scw.x >> (16 * h)) & 0xFFu);
+      const float Egb = dg * (float)(int8_t)((scw.x >> (16 * h + 8)) & 0xFFu);
+      const float Eha = dh * (float)(int8_t)((scw.y >> (16 * h)) & 0xFFu);
+      const float Ehb = dh * (float)(int8_t)((scw.y >> (16 * h + 8)) & 0xFFu);
+      uint32_t p0[NC], p1[NC];
+      float Cc[NC][4];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const uint32_t xc = xs + c * xcs + 128 * h + 32 * tq;
+        p0[c] = act0 ? xc : z0 + 128 * h;
+        p1[c] = act1 ? xc + 16 : z1 + 128 * h;
+        const float2 T = ldsf2(ts + (uint32_t)(c * NSB + 8 * h + 2 * tq) * 4);
+        Cc[c][0] = T.x; Cc[c][1] = T.y; Cc[c][2] = T.x; Cc[c][3] = T.y;
+      }
+      static_for<0, 2>([&](auto jI) {
+        constexpr int j = decltype(jI)::value;
+        uint4 B0[NC], B1[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          B0[c] = lds128o<256 * j>(p0[c]);
+          B1[c] = lds128o<256 * j>(p1[c]);
+        }
+        static_for<0, 4>([&](auto eI) {
+          constexpr int e4 = decltype(eI)::value;
+          constexpr int i = 4 * j + e4;
+          const uint32_t a0 = pair(v0.x, v0.y, v0.z, i), a1 = pair(v0.w, v1.x, v1.y, i);
+          const uint32_t a2 = pair(v1.z, v1.w, v2.x, i), a3 = pair(v2.y, v2.z, v2.w, i);
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            const uint32_t b0 = e4 == 0 ? B0[c].x : e4 == 1 ? B0[c].y : e4 == 2 ? B0[c].z : B0[c].w;
+            const uint32_t b1 = e4 == 0 ? B1[c].x : e4 == 1 ? B1[c].y : e4 == 2 ? B1[c].z : B1[c].w;
+            mma_f16(Cc[c], a0, a1, a2, a3, b0, b1, Cc[c][0], Cc[c][1], Cc[c][2], Cc[c][3]);
+          }
+        });
+      });
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        acc[c][0] = fmaf(Ega, Cc[c][0], fmaf(Egb, Cc[c][1], acc[c][0]));
+        acc[c][1] = fmaf(Eha, Cc[c][2], fmaf(Ehb, Cc[c][3], acc[c][1]));
+      }
+    });
+  } else {  // FMT_Q80: lane t owns block t; both k-slot pairs feed MMA column 2t
+    constexpr int NSB = 4;
+    const uint32_t dd = lds32(gs + 4 * lane);
+    const float dg = h2f(dd & 0xFFFFu) * 0x1p24f, dh = h2f(dd >> 16) * 0x1p24f;
+    const uint32_t qb = gs + 128 + lane * 16;
+    const uint4 q0 = lds128o<0>(qb), q1 = lds128o<512>(qb), q2 = lds128o<1024>(qb), q3 = lds128o<1536>(qb);
+    const uint32_t wg[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t wh[8] = {q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    uint32_t p[NC];
+    float T[NC];
+    float C[NC][4];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      p[c] = act0 ? xs + c * xcs + 16 * tq : z0;
+      T[c] = ldsf(ts + (uint32_t)(c * NSB + tq) * 4);
+      C[c][0] = T[c]; C[c][1] = 0.0f; C[c][2] = T[c]; C[c][3] = 0.0f;
+    }
+    static_for<0, 4>([&](auto jI) {
+      constexpr int j = decltype(jI)::value;
+      uint4 B[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) B[c] = lds128o<64 * j>(p[c]);
+      static_for<0, 2>([&](auto eI) {
+        constexpr int e = decltype(eI)::value;
+        constexpr int t = 2 * j + e;
+        const uint32_t ug = wg[t] ^ 0x80808080u, uh = wh[t] ^ 0x80808080u;
+        const uint32_t a0 = prmt(ug, 0u, 0x4140), a1 = prmt(uh, 0u, 0x4140);
+        const uint32_t a2 = prmt(ug, 0u, 0x4342), a3 = prmt(uh, 0u, 0x4342);
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const uint32_t b0 = e ? B[c].z : B[c].x, b1 = e ? B[c].w : B[c].y;
+          mma_f16(C[c], a0, a1, a2, a3, b0, b1, C[c][0], C[c][1], C[c][2], C[c][3]);
+        }
+      });
+    });
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      acc[c][0] = fmaf(dg, C[c][0], acc[c][0]);
+      acc[c][1] = fmaf(dh, C[c][2], acc[c][1]);
     }
   }
 }
@@ -540,6 +630,9 @@ struct Args {
   int64_t ldx, K, kp;
   int x_dtype, w8a8;
   int off_xloc, xcs, off_tabloc;
+  int tstride;  // floats per sub-block row of the column-sum table (FP8-style decoder)
+  int tabw;     // table floats per group: ncol * (GK / SBE) for DIAG formats
+  int off_zero; // DIAG: kZeroPage bytes of zeros
   int* status;
 };
 
@@ -581,7 +674,7 @@ __device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float*
     for (int t = 0; t < a.M; ++t)
       bulk_g2s(xloc + (size_t)t * a.xcs, static_cast<const uint8_t*>(a.xraw) + (size_t)t * a.ldx * 2, row_bytes, xbar);
   }
-  // zero the padding past K (only FP8 rows can be ragged)
+  // zero the padding past K (FP8 rows and trailing partial Q8_0 groups)
   for (int64_t i = a.K + tid; i < a.kp; i += kThreads)
     for (int t = 0; t < a.M; ++t) reinterpret_cast<uint16_t*>(xloc + (size_t)t * a.xcs)[i] = 0;
   __syncthreads();  // the barrier init is visible before anyone waits on it
@@ -625,6 +718,7 @@ __device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float*
       const int c = it * kThreads + tid;
       const bool valid = c < nchunk;
       float sum = 0.0f;
+      uint4 cv = make_uint4(0u, 0u, 0u, 0u);
       if (valid) {
         const uint4 u = row[c];
         const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
@@ -642,13 +736,29 @@ __device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float*
           }
           out[i] = pack_h2(h2v[0], h2v[1]);
         }
-        row[c] = make_uint4(out[0], out[1], out[2], out[3]);
+        if constexpr (!F::DIAG) row[c] = make_uint4(out[0], out[1], out[2], out[3]);
+        cv = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+      if constexpr (F::DIAG) {
+        // a warp converts whole groups (32 or 16 units): all of its lanes have read
+        // their unit before any lane stores into the group's transposed order
+        __syncwarp();
+        constexpr int UPG = F::GK / 8;
+        if (valid) {
+          if constexpr (FMT == FMT_Q4K) cv = q4k_quad_order(cv);
+          *reinterpret_cast<uint4*>(xloc + (size_t)t * a.xcs + (size_t)(c / UPG) * F::GK * 2 +
+                                    diag_unit_offset<FMT>(c % UPG)) = cv;
+        }
       }
       if constexpr (F::TAB) {
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         if constexpr (SBC == 4) sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         constexpr float xoff = F::XOFF;
-        if (valid && (c % SBC) == 0) tab[(c / SBC) * a.ncol8 + t] = sum * xoff;
+        if (valid && (c % SBC) == 0) {
+          constexpr int NSB = F::GK / F::SBE;
+          const int sb = c / SBC, grp = sb / NSB;
+          tab[(grp * a.ncol + t) * NSB + (sb - grp * NSB)] = sum * xoff;
+        }
       }
     }
   }
@@ -696,7 +806,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     uint32_t b = (uint32_t)ng * F::GB;
     if (!local_x) {
       b += (uint32_t)ng * a.ncol * CSB;
-      if constexpr (F::TAB) b += (uint32_t)ng * NSB * a.ncol8 * 4;
+      if constexpr (F::TAB) b += (uint32_t)ng * a.tabw * 4;
     }
     return b;
   };
@@ -708,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     uint8_t* slot = wb + (size_t)s * a.slot_bytes;
     bulk_g2s(slot + a.off_x, a.cols + (size_t)g0 * a.ncol * CSB, (uint32_t)ng * a.ncol * CSB, &bar[s]);
     if constexpr (F::TAB)
-      bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * NSB * a.ncol8, (uint32_t)ng * NSB * a.ncol8 * 4, &bar[s]);
+      bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * a.tabw, (uint32_t)ng * a.tabw * 4, &bar[s]);
   };
   const int gstep = (whole ? 1 : kWarps) * a.IG;  // group stride between a warp's items in a tile
   const int gfirst = (whole ? 0 : warp) * a.IG;
@@ -743,6 +853,9 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     if (lane == 0 && !local_x) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
     advance();
   }
+  if constexpr (F::DIAG) {  // the zero page idle B-fragment lanes read (published by the barrier below)
+    for (int i = tid; i < kZeroPage / 4; i += kThreads) reinterpret_cast<uint32_t*>(sm + a.off_zero)[i] = 0u;
+  }
   if (local_x) {
     stage_local_x<FMT>(a, sm, ts_s, &a.status[0]);
   } else {
@@ -750,6 +863,10 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     __syncthreads();
   }
   const uint32_t xloc_s = smem_u32(sm + a.off_xloc), tabloc_s = smem_u32(sm + a.off_tabloc);
+  // DIAG: idle lanes point at the zero page, on banks no active lane of the same load uses
+  const uint32_t zero_s = smem_u32(sm + a.off_zero);
+  const uint32_t z0 = zero_s + (FMT == FMT_Q80 ? 112u : 16u), z1 = zero_s;
+  const bool act0 = g == 2 * tq, act1 = g == 2 * tq + 1;
 
   float acc[NT][4];
 #pragma unroll
@@ -779,22 +896,32 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       if (aborted) continue;
       const int g0 = gfirst + k * gstep;
       const int ng = min(a.IG, a.G - g0);
-      if (!mbar_wait_ns(&bar[slot_i], phase, kWaitBudgetNs, a.status)) {
+      // every lane observes the phase itself; the verdict is made warp-uniform
+      if (!__all_sync(0xffffffffu, mbar_wait_ns(&bar[slot_i], phase, kWaitBudgetNs, a.status))) {
         aborted = true;
         continue;
       }
       const uint32_t slot = wb_s + (uint32_t)(slot_i * a.slot_bytes);
-      if (local_x) {
+      if constexpr (F::DIAG) {
+        if (local_x) {
+#pragma unroll 1
+          for (int gi = 0; gi < ng; ++gi)
+            do_group_diag<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, (uint32_t)a.xcs,
+                                   tabloc_s + (uint32_t)((g0 + gi) * a.tabw) * 4, z0, z1, act0, act1, acc, lane);
+        } else {
+#pragma unroll 1
+          for (int gi = 0; gi < ng; ++gi)
+            do_group_diag<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, (uint32_t)CSB,
+                                   slot + a.off_tab + gi * a.tabw * 4, z0, z1, act0, act1, acc, lane);
+        }
+      } else if (local_x) {
 #pragma unroll 2
         for (int gi = 0; gi < ng; ++gi)
-          do_group<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, a.xcs,
-                            tabloc_s + (uint32_t)((g0 + gi) * NSB * a.ncol8) * 4, a.ncol, a.ncol8, tb_s, acc,
-                            lane);
+          do_group<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, a.xcs, a.ncol, acc, lane);
       } else {
 #pragma unroll 2
         for (int gi = 0; gi < ng; ++gi)
-          do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB,
-                            slot + a.off_tab + gi * NSB * a.ncol8 * 4, a.ncol, a.ncol8, tb_s, acc, lane);
+          do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB, a.ncol, acc, lane);
       }
       __syncwarp();
       if (i + NS < n_items) {
@@ -811,7 +938,39 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         phase ^= 1u;
       }
     }
-    if (whole) {  // ---- tile end, whole mode: write straight from the accumulators
+    if constexpr (F::DIAG) {
+      // each lane holds partial sums over its own sub-blocks: add the 4 lanes of a row
+#pragma unroll
+      for (int c = 0; c < NT; ++c)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          float v = acc[c][r];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[c][r] = v;
+        }
+      if (whole) {  // lane t writes token t of rows g and g+8
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int64_t n = (int64_t)tile * 16 + g + 8 * rr;
+          const float bias = rr ? eb2 : eb, cs = rr ? es2 : es;
+#pragma unroll
+          for (int c = 0; c < NT; ++c) {
+            if (a.P == 2) {
+              const int t = c >> 1;
+              if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N)
+                store_y(a, t, n, (acc[c][rr] + acc[c + 1][rr]) * ts_s[t] * cs + bias);
+            } else if (tq == c && c < a.M && n < a.N) {
+              store_y(a, c, n, acc[c][rr] * ts_s[c] * cs + bias);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
+        continue;
+      }
+    }
+    if (!F::DIAG && whole) {  // ---- tile end, whole mode: write straight from the accumulators
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -846,13 +1005,25 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     }
     float* rb = red + (size_t)b * kWarps * 16 * a.ncol8;
     float* rw = rb + (size_t)warp * 16 * a.ncol8;
+    if constexpr (F::DIAG) {
+      if (tq == 0) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      rw[g * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][0];
-      rw[g * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][1];
-      rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][2];
-      rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][3];
-      acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+        for (int c = 0; c < NT; ++c) {
+          rw[g * a.ncol8 + c] = acc[c][0];
+          rw[(g + 8) * a.ncol8 + c] = acc[c][1];
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        rw[g * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][0];
+        rw[g * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][1];
+        rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][2];
+        rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][3];
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+      }
     }
     if (!writer) {
       named_bar_arrive(1 + b, kThreads);
@@ -890,33 +1061,47 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Plan {
   int NS, warp_bytes, slot_bytes, off_x, off_tab, off_tbl, off_bar, off_red;
-  int off_xloc = 0, xcs = 0, off_tabloc = 0;
+  int off_xloc = 0, xcs = 0, off_tabloc = 0, off_zero = 0;
   size_t smem;
 };
 
-// local_kp > 0 asks for the local-x region (activations staged by every CTA).
+inline bool is_diag(int fmt) { return fmt != FMT_FP8; }
+
+// Floats per sub-block row of the column-sum table staged by the CTA itself (FP8-style decoder).
+inline int local_tstride(int ncol) { return std::max(2, (ncol + 1) & ~1); }
+
+// Column-sum table floats for `kp` elements and `ncol` columns.
+inline size_t tab_floats(int fmt, int64_t kp, int ncol, int ncol8) {
+  const FmtInfo f = fmt_info(fmt);
+  if (fmt == FMT_FP8) return 0;
+  return (size_t)(kp / f.sbe) * (is_diag(fmt) ? (size_t)ncol : (size_t)ncol8);
+}
+
+// Shared-memory plan of one GEMV launch.  local_kp > 0 asks for the local-x region
+// (activations staged by every CTA).
 Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref, int64_t local_kp = 0) {
   const FmtInfo f = fmt_info(fmt);
-  const bool tab = fmt != FMT_FP8;
   const int csb = col_stride_bytes(f.gk);
-  const bool local = local_kp > 0;
+  const bool local = local_kp > 0, diag = is_diag(fmt);
   Plan p{};
   const size_t off_x = align_up((size_t)IG * f.gb, 128);
   const size_t off_tab = align_up(off_x + (local ? 0 : (size_t)IG * ncol * csb), 16);
-  const size_t slot = align_up(off_tab + ((tab && !local) ? (size_t)IG * (f.gk / f.sbe) * ncol8 * 4 : 0), 128);
+  const size_t slot = align_up(off_tab + (local ? 0 : tab_floats(fmt, (int64_t)IG * f.gk, ncol, ncol8) * 4), 128);
   const size_t red = (size_t)2 * kWarps * 16 * ncol8 * 4 + 32 * 4;
+  const size_t zero = diag ? (size_t)kZeroPage : 0;
   size_t loc = 0;
   if (local) {
-    int xcs = (int)align_up((size_t)local_kp * 2, 16);
-    if (xcs % 128 == 0) xcs += 64;  // columns of the B tile on alternating bank halves
+    int xcs = (int)align_up((size_t)local_kp * 2, diag ? 128 : 16);
+    if (!diag && xcs % 128 == 0) xcs += 64;  // columns of the B tile on alternating bank halves
     p.xcs = xcs;
-    loc = align_up((size_t)ncol * xcs, 16) + (size_t)32 * kWarps * 4 + 16 +
-          (size_t)(local_kp / f.sbe) * ncol8 * 4 + 16;
+    loc = 128 + (size_t)ncol * xcs + (size_t)32 * kWarps * 4 + 16 + tab_floats(fmt, local_kp, ncol, 0) * 4;
+    if (!diag) loc = 128 + (size_t)ncol * xcs + (size_t)32 * kWarps * 4 + 16 +
+                     (size_t)(local_kp / f.sbe) * local_tstride(ncol) * 4;
   }
   // prefer two CTAs per SM (<= 113 KB each); keep at least two stages in flight
   int NS = ns_pref;
   auto warp_bytes = [&](int ns) { return align_up(ns * slot + kTblBytes + kMaxStages * 8, 128); };
-  while (NS > 2 && warp_bytes(NS) * kWarps + red + loc > 113 * 1024) --NS;
+  while (NS > 2 && warp_bytes(NS) * kWarps + red + loc + zero + 128 > 113 * 1024) --NS;
   p.NS = NS;
   p.slot_bytes = (int)slot;
   p.off_x = (int)off_x;
@@ -926,22 +1111,37 @@ Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref, int64_t local_
   p.warp_bytes = (int)warp_bytes(NS);
   p.off_red = (int)((size_t)p.warp_bytes * kWarps);
   size_t end = (size_t)p.off_red + red;
+  if (diag) {
+    p.off_zero = (int)align_up(end, 128);
+    end = (size_t)p.off_zero + zero;
+  }
   if (local) {
     p.off_xloc = (int)align_up(end, 128);
     p.off_tabloc = (int)align_up((size_t)p.off_xloc + (size_t)ncol * p.xcs, 16) + 32 * kWarps * 4 + 16;
-    end = (size_t)p.off_tabloc + (size_t)(local_kp / f.sbe) * ncol8 * 4;
+    end = (size_t)p.off_tabloc +
+          (diag ? tab_floats(fmt, local_kp, ncol, 0) : (size_t)(local_kp / f.sbe) * local_tstride(ncol)) * 4;
   }
   p.smem = align_up(end, 16);
   return p;
 }
 
-// Groups per item: one 256-wide group for Q4_K / Q6_K; for the 32-wide Q8_0 / FP8
-// groups the largest of 8, 4, 2, 1 that still spreads a tile evenly over the warps.
+// Groups per item (one bulk copy): two 256-wide Q4_K groups when a row has enough of
+// them, one Q6_K group (two would halve the CTAs per SM); for Q8_0 (128-wide) and
+// FP8 (32-wide) the largest candidate that still spreads a tile evenly over the warps.
 int items_group(int fmt, int64_t G) {
-  if (fmt_info(fmt).gk == 256) return 1;
+  static const int env_ig = [] {  // tuning override: RTD_GEMV_IG=1|2|4|8
+    const char* s = std::getenv("RTD_GEMV_IG");
+    const int v = s ? std::atoi(s) : 0;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }();
+  if (env_ig) return (int)std::min<int64_t>(env_ig, std::max<int64_t>(1, G / kWarps));
+  if (fmt == FMT_Q4K) return G >= 2 * kWarps ? 2 : 1;
+  if (fmt == FMT_Q6K) return 1;
   int best = 1;
   double best_eff = 0.0;
-  for (int ig : {8, 4, 2, 1}) {
+  const int cands[4] = {8, 4, 2, 1};
+  for (int ig : cands) {
+    if (fmt == FMT_Q80 && ig > 4) continue;
     const int64_t ci = (G + ig - 1) / ig;
     const double eff = (double)G / ((double)ig * kWarps * ((ci + kWarps - 1) / kWarps));
     if (eff >= 0.85) return ig;
@@ -1069,7 +1269,9 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   const int IG = items_group(c.fmt, G);
   const int64_t CI = (G + IG - 1) / IG;
   const int P = (c.x_dtype == 0 && !c.w8a8) ? 2 : 1;
-  const int max_tokens = 32 / P;
+  const bool diag = is_diag(c.fmt);
+  // DIAG decoders run one MMA chain per activation column: at most 4 columns a launch
+  const int max_tokens = (diag ? 4 : 32) / P;
   static const int env_ns = [] {
     const char* s = std::getenv("RTD_GEMV_STAGES");
     const int v = s ? std::atoi(s) : 0;
@@ -1089,12 +1291,14 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     while (Mt > 1 && make_plan(c.fmt, IG, Mt * P, 8 * ((Mt * P + 7) / 8), env_ns).smem > 220 * 1024)
       Mt = (Mt + 1) / 2;
     const int ncol = Mt * P;
-    const int NT = (ncol + 7) / 8;
-    const int ncol8 = 8 * NT;
+    // template width: activation columns (DIAG) or 8-column MMA tiles (FP8)
+    const int NT = diag ? ncol : (ncol + 7) / 8;
+    const int ncol8 = 8 * ((ncol + 7) / 8);
     // bf16 / f16 activations whose rows are bulk-copyable: every CTA stages x itself
     // (no prep kernel) when the staged rows and sums stay small.
+    const size_t local_tab = diag ? tab_floats(c.fmt, kp, ncol, 0) : (size_t)(kp / f.sbe) * local_tstride(ncol);
     const bool local_ok = P == 1 && x_vec && (c.K % 8 == 0) && !env_no_local &&
-                          (size_t)ncol * kp * 2 + (size_t)(kp / f.sbe) * ncol8 * 4 <= 48 * 1024;
+                          (size_t)ncol * kp * 2 + local_tab * 4 <= 40 * 1024;
     const Plan pl = make_plan(c.fmt, IG, ncol, ncol8, env_ns, local_ok ? kp : 0);
     const int occ = occupancy_of(c.fmt, NT, pl.smem);
     const int64_t slots = (int64_t)c.sm_count * occ;
@@ -1104,7 +1308,7 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     const int nctas = (int)(whole ? slots : std::min<int64_t>(T, slots));
     // workspace carve: cols | tab | tscale
     const size_t cols_b = align_up((size_t)G * ncol * col_stride_bytes(f.gk), 256);
-    const size_t tab_b = align_up((size_t)(kp / f.sbe) * ncol8 * 4, 256);
+    const size_t tab_b = align_up(tab_floats(c.fmt, kp, ncol, ncol8) * 4 + 4, 256);
     if (cols_b + tab_b + 256 > c.ws_bytes) {
       *plan_error = 1;
       return cudaSuccess;
@@ -1181,6 +1385,9 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_xloc = pl.off_xloc;
     a.xcs = pl.xcs;
     a.off_tabloc = pl.off_tabloc;
+    a.tstride = local_ok ? local_tstride(ncol) : ncol8;
+    a.tabw = diag ? ncol * (f.gk / f.sbe) : (f.gk / f.sbe) * ncol8;
+    a.off_zero = pl.off_zero;
     a.status = c.status;
     switch (c.fmt) {
       case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;

@@ -9,25 +9,41 @@
 //   device buffer            = [tile][column][group bytes], rows past N zero-filled
 //
 // so that one unit of GEMV work (a tile x a run of columns) is ONE contiguous,
-// 16-byte aligned byte range -- a single cp.async.bulk -- and, inside a group,
-// every warp lane finds the bytes of its m16n8k16 A fragment in one 16-byte
-// vector (lane = 4*g + t holds rows g and g+8).
+// 16-byte aligned byte range -- a single cp.async.bulk.
 //
-//   Q4_K  GK=256 GB=2304: [16 rows x (d, dmin, scales[12]) = 256 B]
-//                         [qs: chunk c(4) x lane(32) x 16 B]
-//                         lane 16 B = row g qs[32c+8t .. +8] ++ row g+8 qs[32c+8t .. +8]
-//   Q6_K  GK=256 GB=3360: [d: 16 x 2 B][scales: 16 x 16 B]
-//                         [codes: vec v(6) x lane(32) x 16 B]  (24 words per lane, see below)
-//   Q8_0  GK=32  GB=544:  [d: 16 x 2 B][qs: lane(32) x 16 B, row g bytes 8t..8t+7 ++ row g+8]
+// Inside a K-quant group every warp lane (lane = 4*g + t) owns WHOLE sub-blocks
+// of rows g and g+8: the m16n8k16 decode GEMV then sums each sub-block in its own
+// MMA output column (see rtd_gemv.cu), and a lane only ever needs the scales of
+// the sub-blocks it owns.  A lane's bytes sit in 16-byte vectors, one per "pass":
+// pass p occupies bytes [p*512, p*512+512) of the code region, lane L at L*16.
+//
+//   Q4_K  GK=256 GB=2304: [16 rows x (d, dmin, scales[12]) = 256 B, GGUF order]
+//                         [qs: pass(4) x lane(32) x 16 B]
+//         lane t owns qs chunk t (bytes 32t..32t+31: sub-blocks 2t (low nibbles)
+//         and 2t+1 (high nibbles)); passes 0,1 = row g bytes 0-15, 16-31;
+//         passes 2,3 = row g+8.
+//   Q6_K  GK=256 GB=3360: [d: 8 x (row g, row g+8) f16 = 32 B]
+//                         [scales: lane(32) x (row g 4 B, row g+8 4 B)]
+//                         [codes: pass(6) x lane(32) x 16 B]
+//         lane t owns sub-blocks 2t, 2t+1, 8+2t, 9+2t; its scale bytes are
+//         sc[2t], sc[2t+1], sc[8+2t], sc[9+2t] of each row.  Codes: one 3-word
+//         triple per (row, sub-block) -- see below -- ordered half h (passes
+//         3h..3h+2): (row g, 8h+2t), (row g+8, 8h+2t), (row g, 8h+2t+1),
+//         (row g+8, 8h+2t+1).
+//   Q8_0  GK=128 GB=2176: [d: lane(32) x (row g, row g+8) f16 = 128 B]
+//                         [qs: pass(4) x lane(32) x 16 B]
+//         lane t owns block t of the group (32 int8); passes as for Q4_K.
+//         K is a multiple of 32; a trailing partial group is zero-filled.
 //   FP8   GK=32  GB=512:  [lane(32) x 16 B, row g bytes 8t..8t+7 ++ row g+8]
+//         (bytes 1 and 2 of every 4-byte word swapped).
 //
-// Q6_K code words.  The 6-bit code of element e of a superblock row is
-// (ql nibble | 2 qh bits << 4), dequant_k.rs:87-111.  Sub-block sb (16 elements,
-// scale index sb) is split 4 codes per lane: lane t holds elements 16*sb+4t+{0..3}.
-// Window p (sub-blocks a=2p, b=2p+1) uses lane words 3p..3p+2 (X, Y, Z):
-//   X = codes (a, row g):   c0@0 c1@6 c2@16 c3@22 ; spare 12-15, 28-31 = low nibbles of (b, g+8) c0, c2
-//   Y = codes (a, row g+8): same ; spare = low nibbles of (b, g+8) c1, c3
-//   Z = codes (b, row g):   same ; spare 12-13/14-15/28-29/30-31 = high 2 bits of (b, g+8) c0/c1/c2/c3
+// Q6_K code triples.  The 6-bit code of element e of a superblock row is
+// (ql nibble | 2 qh bits << 4), dequant_k.rs:87-111.  The 16 codes c0..c15 of one
+// (row, sub-block) fill three words:
+//   X = c0@0 c1@16 c2@6 c3@22,  Y = c4..c7 likewise,  Z = c8..c11 likewise,
+//   spare bits: X 12-15 / 28-31 = low nibbles of c12 / c13, Y 12-15 / 28-31 = low
+//   nibbles of c14 / c15, Z 12-13 / 28-29 / 14-15 / 30-31 = high 2 bits of c12 /
+//   c13 / c14 / c15.
 #pragma once
 
 #include <stddef.h>
@@ -55,7 +71,7 @@ RTD_HD inline FmtInfo fmt_info(int fmt) {
   switch (fmt) {
     case FMT_Q4K: return FmtInfo{256, 2304, 32, 256, 144};
     case FMT_Q6K: return FmtInfo{256, 3360, 16, 256, 210};
-    case FMT_Q80: return FmtInfo{32, 544, 32, 32, 34};
+    case FMT_Q80: return FmtInfo{128, 2176, 32, 32, 34};
     default:      return FmtInfo{32, 512, 32, 1, 1};
   }
 }
@@ -65,7 +81,7 @@ RTD_HD inline int group_payload_offset(int fmt) {
   switch (fmt) {
     case FMT_Q4K: return 256;
     case FMT_Q6K: return 288;
-    case FMT_Q80: return 32;
+    case FMT_Q80: return 128;
     default:      return 0;
   }
 }

@@ -29,7 +29,7 @@ inline uint32_t pack4(const uint32_t c[4]) {
 }
 
 // Copy 8 bytes swapping bytes 1 and 2 of each 4-byte word, so that the halves
-// of (word & 0x000F000F) are two consecutive elements.
+// of a 16-bit pair extraction are two consecutive elements (FP8 groups).
 inline void copy8_swapped(uint8_t* dst, const uint8_t* src) {
   for (int w = 0; w < 2; ++w) {
     dst[4 * w + 0] = src[4 * w + 0];
@@ -63,20 +63,25 @@ void repack_host(int fmt, const uint8_t* raw, int64_t N, int64_t K, uint8_t* out
       };
       if (fmt == FMT_Q4K) {
         for (int r = 0; r < 16; ++r) std::memcpy(grp + 16 * r, src(r), 16);
-        for (int c = 0; c < 4; ++c)
-          for (int lane = 0; lane < 32; ++lane) {
-            int g = lane >> 2, tg = lane & 3;
-            uint8_t* v = grp + 256 + c * 512 + lane * 16;
-            copy8_swapped(v, src(g) + 16 + 32 * c + 8 * tg);
-            copy8_swapped(v + 8, src(g + 8) + 16 + 32 * c + 8 * tg);
-          }
-      } else if (fmt == FMT_Q80) {
-        for (int r = 0; r < 16; ++r) std::memcpy(grp + 2 * r, src(r), 2);
         for (int lane = 0; lane < 32; ++lane) {
-          int g = lane >> 2, tg = lane & 3;
-          uint8_t* v = grp + 32 + lane * 16;
-          copy8_swapped(v, src(g) + 2 + 8 * tg);
-          copy8_swapped(v + 8, src(g + 8) + 2 + 8 * tg);
+          const int g = lane >> 2, tg = lane & 3;
+          for (int p = 0; p < 4; ++p)  // row g / g+8, chunk tg bytes 0-15 / 16-31
+            std::memcpy(grp + 256 + p * 512 + lane * 16, src(g + 8 * (p >> 1)) + 16 + 32 * tg + 16 * (p & 1), 16);
+        }
+      } else if (fmt == FMT_Q80) {
+        // blocks 4s .. 4s+3 of each row; blocks past K/32 stay zero (d = 0, q = 0)
+        const int64_t nblk = K / 32;
+        auto blk = [&](int r, int b) -> const uint8_t* {
+          const int64_t n = t * 16 + r, bi = 4 * s + b;
+          if (n >= N || bi >= nblk) return zero_block;
+          return raw + (size_t)n * row_bytes + (size_t)bi * 34;
+        };
+        for (int lane = 0; lane < 32; ++lane) {
+          const int g = lane >> 2, tg = lane & 3;
+          std::memcpy(grp + 4 * lane, blk(g, tg), 2);
+          std::memcpy(grp + 4 * lane + 2, blk(g + 8, tg), 2);
+          for (int p = 0; p < 4; ++p)
+            std::memcpy(grp + 128 + p * 512 + lane * 16, blk(g + 8 * (p >> 1), tg) + 2 + 16 * (p & 1), 16);
         }
       } else if (fmt == FMT_FP8) {
         for (int lane = 0; lane < 32; ++lane) {
@@ -93,31 +98,34 @@ void repack_host(int fmt, const uint8_t* raw, int64_t N, int64_t K, uint8_t* out
           }
         }
       } else {  // FMT_Q6K
-        for (int r = 0; r < 16; ++r) {
-          std::memcpy(grp + 2 * r, src(r) + 208, 2);
-          std::memcpy(grp + 32 + 16 * r, src(r) + 192, 16);
+        for (int g = 0; g < 8; ++g) {
+          std::memcpy(grp + 4 * g, src(g) + 208, 2);
+          std::memcpy(grp + 4 * g + 2, src(g + 8) + 208, 2);
         }
         for (int lane = 0; lane < 32; ++lane) {
-          int g = lane >> 2, tg = lane & 3;
-          uint32_t words[24];
-          for (int p = 0; p < 8; ++p) {
-            uint32_t ca_g[4], ca_h[4], cb_g[4], cb_h[4];
-            for (int j = 0; j < 4; ++j) {
-              int ea = 16 * (2 * p) + 4 * tg + j, eb = 16 * (2 * p + 1) + 4 * tg + j;
-              ca_g[j] = q6k_code(src(g), ea);
-              ca_h[j] = q6k_code(src(g + 8), ea);
-              cb_g[j] = q6k_code(src(g), eb);
-              cb_h[j] = q6k_code(src(g + 8), eb);
-            }
-            uint32_t X = pack4(ca_g), Y = pack4(ca_h), Z = pack4(cb_g);
-            X |= ((cb_h[0] & 0xFu) << 12) | ((cb_h[1] & 0xFu) << 28);
-            Y |= ((cb_h[2] & 0xFu) << 12) | ((cb_h[3] & 0xFu) << 28);
-            Z |= ((cb_h[0] >> 4) << 12) | ((cb_h[1] >> 4) << 28) | ((cb_h[2] >> 4) << 14) |
-                 ((cb_h[3] >> 4) << 30);
-            words[3 * p + 0] = X;
-            words[3 * p + 1] = Y;
-            words[3 * p + 2] = Z;
+          const int g = lane >> 2, tg = lane & 3;
+          for (int rr = 0; rr < 2; ++rr) {
+            const uint8_t* sc = src(g + 8 * rr) + 192;
+            uint8_t* d = grp + 32 + lane * 8 + 4 * rr;
+            d[0] = sc[2 * tg];
+            d[1] = sc[2 * tg + 1];
+            d[2] = sc[8 + 2 * tg];
+            d[3] = sc[9 + 2 * tg];
           }
+          uint32_t words[24];
+          for (int h = 0; h < 2; ++h)
+            for (int tr = 0; tr < 4; ++tr) {  // (g, a), (g+8, a), (g, b), (g+8, b)
+              const int row = g + 8 * (tr & 1), sb = 8 * h + 2 * tg + (tr >> 1);
+              uint32_t c[16];
+              for (int i = 0; i < 16; ++i) c[i] = q6k_code(src(row), 16 * sb + i);
+              uint32_t X = pack4(c), Y = pack4(c + 4), Z = pack4(c + 8);
+              X |= ((c[12] & 0xFu) << 12) | ((c[13] & 0xFu) << 28);
+              Y |= ((c[14] & 0xFu) << 12) | ((c[15] & 0xFu) << 28);
+              Z |= ((c[12] >> 4) << 12) | ((c[13] >> 4) << 28) | ((c[14] >> 4) << 14) | ((c[15] >> 4) << 30);
+              words[12 * h + 3 * tr + 0] = X;
+              words[12 * h + 3 * tr + 1] = Y;
+              words[12 * h + 3 * tr + 2] = Z;
+            }
           for (int w = 0; w < 24; ++w)
             std::memcpy(grp + 288 + (w / 4) * 512 + lane * 16 + (w % 4) * 4, &words[w], 4);
         }
