@@ -114,6 +114,22 @@ __device__ __forceinline__ uint4 q4k_quad_order(uint4 u) {
                     __byte_perm(u.z, u.w, 0x7632));
 }
 
+// Column-sum table of DIAG formats: per (group, column) TW = GK/SBE + 4 floats --
+// XOFF * sum(x) for every sub-block, then the group's activation scale (2^e) at
+// index GK/SBE; rows stay 16-byte aligned.
+template <int FMT>
+__host__ __device__ constexpr int tab_row_floats() {
+  return FmtC<FMT>::GK / FmtC<FMT>::SBE + 4;
+}
+
+// Power-of-two exponent that maps a group's max |x| into [2^14, 2^15): the staged f16
+// values then keep 11 significant bits without overflow; 0 for all-zero or
+// non-finite groups (non-finite values then propagate as in the reference).
+__device__ __forceinline__ int group_exponent(float amax) {
+  if (!(amax > 0.0f) || !(amax <= 3.4e38f)) return 0;
+  return min(max(ilogbf(amax) - 14, -110), 110);
+}
+
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
@@ -291,6 +307,77 @@ __global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThre
   }
 }
 
+// Prep for DIAG formats: one warp per (token, group) -- the group's own max |x| sets
+// its scale, so no cross-CTA reduction is needed.  Writes the transposed f16 units
+// (hi, and for f32 inputs the lo remainder as a second column) and the table rows.
+template <int FMT>
+__global__ void __launch_bounds__(kPrepThreads) prep_diag_kernel(const PrepArgs a) {
+  using F = FmtC<FMT>;
+  constexpr int UPG = F::GK / 8, NSB = F::GK / F::SBE, SBC = F::SBE / 8, TW = tab_row_floats<FMT>();
+  constexpr int CSB = col_stride_bytes(F::GK);
+  griddep_launch_dependents();
+  griddep_wait();
+  const int t = blockIdx.y;
+  const int64_t c = (int64_t)blockIdx.x * kPrepThreads + threadIdx.x;  // chunk of 8 elements
+  const int64_t nch = a.kp / 8;
+  const bool valid = c < nch;  // kp / 8 is a multiple of UPG: groups never straddle warps
+  float v[8];
+  if (valid) {
+    load8(a.x, a.x_dtype, a.x_vec != 0, a.ldx, a.K, t, 8 * c, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+  for (int o = 1; o < UPG; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int e = group_exponent(m);
+  const float inv = ldexpf(1.0f, -e);
+  __half hi[8], lo[8];
+  float shi = 0.0f, slo = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float sv = v[i] * inv;
+    hi[i] = __float2half_rn(sv);
+    const float hf = __half2float(hi[i]);
+    lo[i] = __float2half_rn(sv - hf);
+    shi += hf;
+    slo += __half2float(lo[i]);
+  }
+#pragma unroll
+  for (int o = 1; o < SBC; o <<= 1) {
+    shi += __shfl_xor_sync(0xffffffffu, shi, o);
+    slo += __shfl_xor_sync(0xffffffffu, slo, o);
+  }
+  if (!valid) return;
+  const int64_t grp = c / UPG;
+  const int n = (int)(c - grp * UPG);
+  uint8_t* base = a.cols + ((size_t)grp * a.ncol + (size_t)t * a.P) * CSB + diag_unit_offset<FMT>(n);
+  uint4 u;
+  u.x = pack_h2(hi[0], hi[1]); u.y = pack_h2(hi[2], hi[3]);
+  u.z = pack_h2(hi[4], hi[5]); u.w = pack_h2(hi[6], hi[7]);
+  if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
+  *reinterpret_cast<uint4*>(base) = u;
+  if (a.P == 2) {
+    u.x = pack_h2(lo[0], lo[1]); u.y = pack_h2(lo[2], lo[3]);
+    u.z = pack_h2(lo[4], lo[5]); u.w = pack_h2(lo[6], lo[7]);
+    if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
+    *reinterpret_cast<uint4*>(base + CSB) = u;
+  }
+  float* tp = a.tab + ((size_t)grp * a.ncol + (size_t)t * a.P) * TW;
+  if (n % SBC == 0) {
+    tp[n / SBC] = shi * F::XOFF;
+    if (a.P == 2) tp[TW + n / SBC] = slo * F::XOFF;
+  }
+  if (n == 0) {
+    const float sc = ldexpf(1.0f, e);
+    tp[NSB] = sc;
+    if (a.P == 2) tp[TW + NSB] = sc;
+  }
+}
+
 // ------------------------------------------------------------------ GEMV kernel
 // 32-bit shared-memory accessors.  They are volatile so no load can be hoisted
 // above the mbarrier wait that publishes the data; ALU work still interleaves.
@@ -447,6 +534,7 @@ template <int FMT, int NC>
 __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t xcs, uint32_t ts, uint32_t z0,
                                               uint32_t z1, bool act0, bool act1, float (&acc)[NC][4], int lane) {
   const int g = lane >> 2, tq = lane & 3;
+  constexpr int TW = tab_row_floats<FMT>();
   if constexpr (FMT == FMT_Q4K) {
     constexpr int NSB = 8;
     const uint4 hg = lds128(gs + 16 * g), hh = lds128(gs + 16 * (g + 8));
@@ -461,15 +549,21 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
     const uint32_t wh[8] = {q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
     uint32_t p0[NC], p1[NC];
     float2 T[NC];
+    float S[NC];
     float C[NC][4];
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const uint32_t xc = xs + c * xcs + 32 * tq;
       p0[c] = act0 ? xc : z0;
       p1[c] = act1 ? xc + 16 : z1;
-      T[c] = ldsf2(ts + (uint32_t)(c * NSB + 2 * tq) * 4);
+      T[c] = ldsf2(ts + (uint32_t)(c * TW + 2 * tq) * 4);
+      S[c] = ldsf(ts + (uint32_t)(c * TW + NSB) * 4);
       C[c][0] = C[c][1] = C[c][2] = C[c][3] = 0.0f;
     }
+    // MMA pairs per 4-byte code word u: the low nibbles (sub-block 2t, elements
+    // (4u, 4u+2) | (4u+1, 4u+3)) feed MMA column 2t from the b0-lane (g == 2t); the high
+    // nibbles (sub-block 2t+1) feed column 2t+1 from the b1-lane.  Each MMA takes both
+    // B registers from one 16-byte load.
     static_for<0, 4>([&](auto jI) {
       constexpr int j = decltype(jI)::value;
       uint4 B0[NC], B1[NC];
@@ -478,25 +572,29 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
         B0[c] = lds128o<128 * j>(p0[c]);
         B1[c] = lds128o<128 * j>(p1[c]);
       }
-      static_for<0, 4>([&](auto eI) {
-        constexpr int e4 = decltype(eI)::value;
-        constexpr int u = 2 * j + (e4 >> 1);
-        const uint32_t vg = (e4 & 1) ? (wg[u] >> 8) : wg[u];
-        const uint32_t vh = (e4 & 1) ? (wh[u] >> 8) : wh[u];
-        const uint32_t a0 = vg & 0x000F000Fu, a1 = vh & 0x000F000Fu;
-        const uint32_t a2 = vg & 0x00F000F0u, a3 = vh & 0x00F000F0u;
+      static_for<0, 2>([&](auto hI) {
+        constexpr int hh = decltype(hI)::value;
+        constexpr int u = 2 * j + hh;
+        const uint32_t sg = wg[u] >> 8, sh = wh[u] >> 8;
+        const uint32_t l0 = wg[u] & 0x000F000Fu, l1 = wh[u] & 0x000F000Fu;
+        const uint32_t l2 = sg & 0x000F000Fu, l3 = sh & 0x000F000Fu;
+        const uint32_t h0 = wg[u] & 0x00F000F0u, h1 = wh[u] & 0x00F000F0u;
+        const uint32_t h2 = sg & 0x00F000F0u, h3 = sh & 0x00F000F0u;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
-          const uint32_t b0 = e4 == 0 ? B0[c].x : e4 == 1 ? B0[c].y : e4 == 2 ? B0[c].z : B0[c].w;
-          const uint32_t b1 = e4 == 0 ? B1[c].x : e4 == 1 ? B1[c].y : e4 == 2 ? B1[c].z : B1[c].w;
-          mma_f16(C[c], a0, a1, a2, a3, b0, b1, C[c][0], C[c][1], C[c][2], C[c][3]);
+          const uint32_t x0 = hh ? B0[c].z : B0[c].x, x1 = hh ? B0[c].w : B0[c].y;
+          const uint32_t y0 = hh ? B1[c].z : B1[c].x, y1 = hh ? B1[c].w : B1[c].y;
+          mma_f16_acc(C[c], l0, l1, l2, l3, x0, x1);
+          mma_f16_acc(C[c], h0, h1, h2, h3, y0, y1);
         }
       });
     });
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      acc[c][0] = fmaf(Ea0, C[c][0], fmaf(Eb0, C[c][1], fmaf(Fa0, T[c].x, fmaf(Fb0, T[c].y, acc[c][0]))));
-      acc[c][1] = fmaf(Ea1, C[c][2], fmaf(Eb1, C[c][3], fmaf(Fa1, T[c].x, fmaf(Fb1, T[c].y, acc[c][1]))));
+      const float v0 = fmaf(Ea0, C[c][0], fmaf(Eb0, C[c][1], fmaf(Fa0, T[c].x, Fb0 * T[c].y)));
+      const float v1 = fmaf(Ea1, C[c][2], fmaf(Eb1, C[c][3], fmaf(Fa1, T[c].x, Fb1 * T[c].y)));
+      acc[c][0] = fmaf(S[c], v0, acc[c][0]);
+      acc[c][1] = fmaf(S[c], v1, acc[c][1]);
     }
   } else if constexpr (FMT == FMT_Q6K) {
     constexpr int NSB = 16;
@@ -504,6 +602,12 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
     const uint2 scw = lds64(gs + 32 + lane * 8);
     const float dg = h2f(dd & 0xFFFFu) * 0x1p24f, dh = h2f(dd >> 16) * 0x1p24f;
     const uint32_t cb = gs + 288 + lane * 16;
+    float V[NC][2], S[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      V[c][0] = V[c][1] = 0.0f;
+      S[c] = ldsf(ts + (uint32_t)(c * TW + NSB) * 4);
+    }
     constexpr uint32_t M6 = 0x003F003Fu, M4 = 0x000F000Fu, M2 = 0x00300030u;
     // code pair i (elements 2i, 2i+1 of the sub-block) of one (X, Y, Z) triple
     auto pair = [&](uint32_t X, uint32_t Y, uint32_t Z, int i) -> uint32_t {
@@ -534,9 +638,11 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
         const uint32_t xc = xs + c * xcs + 128 * h + 32 * tq;
         p0[c] = act0 ? xc : z0 + 128 * h;
         p1[c] = act1 ? xc + 16 : z1 + 128 * h;
-        const float2 T = ldsf2(ts + (uint32_t)(c * NSB + 8 * h + 2 * tq) * 4);
+        const float2 T = ldsf2(ts + (uint32_t)(c * TW + 8 * h + 2 * tq) * 4);
         Cc[c][0] = T.x; Cc[c][1] = T.y; Cc[c][2] = T.x; Cc[c][3] = T.y;
       }
+      // sub-block a (pairs 2m, 2m+1 of triples (g,a), (g+8,a)) feeds column 2t from the
+      // b0-lane, sub-block b feeds column 2t+1 from the b1-lane; one load per MMA's B
       static_for<0, 2>([&](auto jI) {
         constexpr int j = decltype(jI)::value;
         uint4 B0[NC], B1[NC];
@@ -545,25 +651,33 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
           B0[c] = lds128o<256 * j>(p0[c]);
           B1[c] = lds128o<256 * j>(p1[c]);
         }
-        static_for<0, 4>([&](auto eI) {
-          constexpr int e4 = decltype(eI)::value;
-          constexpr int i = 4 * j + e4;
-          const uint32_t a0 = pair(v0.x, v0.y, v0.z, i), a1 = pair(v0.w, v1.x, v1.y, i);
-          const uint32_t a2 = pair(v1.z, v1.w, v2.x, i), a3 = pair(v2.y, v2.z, v2.w, i);
+        static_for<0, 2>([&](auto mI) {
+          constexpr int m = 2 * j + decltype(mI)::value;  // pairs 2m, 2m+1
+          const uint32_t a0 = pair(v0.x, v0.y, v0.z, 2 * m), a1 = pair(v0.w, v1.x, v1.y, 2 * m);
+          const uint32_t a2 = pair(v0.x, v0.y, v0.z, 2 * m + 1), a3 = pair(v0.w, v1.x, v1.y, 2 * m + 1);
+          const uint32_t e0 = pair(v1.z, v1.w, v2.x, 2 * m), e1 = pair(v2.y, v2.z, v2.w, 2 * m);
+          const uint32_t e2 = pair(v1.z, v1.w, v2.x, 2 * m + 1), e3 = pair(v2.y, v2.z, v2.w, 2 * m + 1);
 #pragma unroll
           for (int c = 0; c < NC; ++c) {
-            const uint32_t b0 = e4 == 0 ? B0[c].x : e4 == 1 ? B0[c].y : e4 == 2 ? B0[c].z : B0[c].w;
-            const uint32_t b1 = e4 == 0 ? B1[c].x : e4 == 1 ? B1[c].y : e4 == 2 ? B1[c].z : B1[c].w;
-            mma_f16(Cc[c], a0, a1, a2, a3, b0, b1, Cc[c][0], Cc[c][1], Cc[c][2], Cc[c][3]);
+            const bool odd = (m & 1) != 0;
+            const uint32_t x0 = odd ? B0[c].z : B0[c].x, x1 = odd ? B0[c].w : B0[c].y;
+            const uint32_t y0 = odd ? B1[c].z : B1[c].x, y1 = odd ? B1[c].w : B1[c].y;
+            mma_f16_acc(Cc[c], a0, a1, a2, a3, x0, x1);
+            mma_f16_acc(Cc[c], e0, e1, e2, e3, y0, y1);
           }
         });
       });
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
-        acc[c][0] = fmaf(Ega, Cc[c][0], fmaf(Egb, Cc[c][1], acc[c][0]));
-        acc[c][1] = fmaf(Eha, Cc[c][2], fmaf(Ehb, Cc[c][3], acc[c][1]));
+        V[c][0] = fmaf(Ega, Cc[c][0], fmaf(Egb, Cc[c][1], V[c][0]));
+        V[c][1] = fmaf(Eha, Cc[c][2], fmaf(Ehb, Cc[c][3], V[c][1]));
       }
     });
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      acc[c][0] = fmaf(S[c], V[c][0], acc[c][0]);
+      acc[c][1] = fmaf(S[c], V[c][1], acc[c][1]);
+    }
   } else {  // FMT_Q80: lane t owns block t; both k-slot pairs feed MMA column 2t
     constexpr int NSB = 4;
     const uint32_t dd = lds32(gs + 4 * lane);
@@ -573,12 +687,13 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
     const uint32_t wg[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint32_t wh[8] = {q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
     uint32_t p[NC];
-    float T[NC];
+    float T[NC], S[NC];
     float C[NC][4];
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       p[c] = act0 ? xs + c * xcs + 16 * tq : z0;
-      T[c] = ldsf(ts + (uint32_t)(c * NSB + tq) * 4);
+      T[c] = ldsf(ts + (uint32_t)(c * TW + tq) * 4);
+      S[c] = ldsf(ts + (uint32_t)(c * TW + NSB) * 4);
       C[c][0] = T[c]; C[c][1] = 0.0f; C[c][2] = T[c]; C[c][3] = 0.0f;
     }
     static_for<0, 4>([&](auto jI) {
@@ -595,14 +710,14 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
           const uint32_t b0 = e ? B[c].z : B[c].x, b1 = e ? B[c].w : B[c].y;
-          mma_f16(C[c], a0, a1, a2, a3, b0, b1, C[c][0], C[c][1], C[c][2], C[c][3]);
+          mma_f16_acc(C[c], a0, a1, a2, a3, b0, b1);
         }
       });
     });
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      acc[c][0] = fmaf(dg, C[c][0], acc[c][0]);
-      acc[c][1] = fmaf(dh, C[c][2], acc[c][1]);
+      acc[c][0] = fmaf(dg * S[c], C[c][0], acc[c][0]);
+      acc[c][1] = fmaf(dh * S[c], C[c][2], acc[c][1]);
     }
   }
 }
@@ -765,6 +880,98 @@ __device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float*
   __syncthreads();
 }
 
+// Local-x staging for DIAG formats.  The CTA copies the raw bf16 / f16 rows into
+// shared memory (one bulk copy per token); then every warp converts groups on its
+// own: a group's max |x| (warp shuffles) sets its power-of-two scale, the scaled f16
+// units are rewritten in place in the transposed DIAG order, and the table row gets
+// the sub-block sums and the scale.  In split mode a warp converts exactly the groups
+// it will consume, so no block-wide barrier follows; in whole mode the warps share
+// the work and meet once.
+template <int FMT>
+__device__ __forceinline__ void stage_local_diag(const Args& a, uint8_t* sm, bool whole, int* status) {
+  using F = FmtC<FMT>;
+  constexpr int UPG = F::GK / 8, GPI = 32 / UPG, SBC = F::SBE / 8, NSB = F::GK / F::SBE;
+  constexpr int TW = tab_row_floats<FMT>();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint8_t* xloc = sm + a.off_xloc;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + a.off_tabloc - 16);
+  float* tab = reinterpret_cast<float*>(sm + a.off_tabloc);
+  const uint32_t row_bytes = (uint32_t)(a.K * 2);
+  if (tid == 0) {
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(xbar, row_bytes * (uint32_t)a.M);
+    for (int t = 0; t < a.M; ++t)
+      bulk_g2s(xloc + (size_t)t * a.xcs, static_cast<const uint8_t*>(a.xraw) + (size_t)t * a.ldx * 2, row_bytes, xbar);
+  }
+  // zero the padding past K (trailing partial Q8_0 groups)
+  for (int64_t i = a.K + tid; i < a.kp; i += kThreads)
+    for (int t = 0; t < a.M; ++t) reinterpret_cast<uint16_t*>(xloc + (size_t)t * a.xcs)[i] = 0;
+  __syncthreads();  // barrier init, zero page and padding visible to every warp
+  mbar_wait_bounded(xbar, 0, status);
+  // this warp's groups: split mode -> those of items warp, warp+8, ...; whole -> warp, warp+8, ...
+  const int sub = lane / UPG, n = lane % UPG;  // GPI groups side by side in the warp
+  const int per = whole ? (a.G - warp + kWarps - 1) / kWarps
+                        : ((a.CI > warp) ? (a.CI - warp + kWarps - 1) / kWarps : 0) * a.IG;
+  for (int q0 = 0; q0 < per; q0 += GPI) {
+    const int q = q0 + sub;
+    int gi = -1;
+    if (q < per) {
+      if (whole) {
+        gi = warp + kWarps * q;
+      } else {
+        const int it = warp + kWarps * (q / a.IG);
+        gi = it * a.IG + q % a.IG;
+        if (gi >= a.G) gi = -1;
+      }
+    }
+    for (int t = 0; t < a.M; ++t) {
+      uint8_t* gbase = xloc + (size_t)t * a.xcs + (size_t)(gi < 0 ? 0 : gi) * F::GK * 2;
+      float v[8];
+      if (gi >= 0) {
+        const uint4 u = reinterpret_cast<const uint4*>(gbase)[n];
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t b16 = (wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+          v[i] = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+      }
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+      for (int o = 1; o < UPG; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int e = group_exponent(m);
+      const float inv = ldexpf(1.0f, -e);
+      __half h[8];
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        h[i] = __float2half_rn(v[i] * inv);
+        sum += __half2float(h[i]);
+      }
+#pragma unroll
+      for (int o = 1; o < SBC; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      uint4 cv = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
+      if constexpr (FMT == FMT_Q4K) cv = q4k_quad_order(cv);
+      __syncwarp();  // every lane has read its unit before the group is rewritten in place
+      if (gi >= 0) {
+        *reinterpret_cast<uint4*>(gbase + diag_unit_offset<FMT>(n)) = cv;
+        float* tp = tab + ((size_t)gi * a.ncol + t) * TW;
+        if (n % SBC == 0) tp[n / SBC] = sum * F::XOFF;
+        if (n == 0) tp[NSB] = ldexpf(1.0f, e);
+      }
+      __syncwarp();
+    }
+  }
+  if (whole) __syncthreads();
+  else __syncwarp();
+}
+
 // Each CTA owns a contiguous run of whole 16-row tiles; inside a tile, warp w
 // takes items w, w+8, ... (an item = IG groups).  Every warp streams its own
 // item sequence through a private ring of NS shared-memory stages, so warps only
@@ -853,10 +1060,17 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     if (lane == 0 && !local_x) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
     advance();
   }
-  if constexpr (F::DIAG) {  // the zero page idle B-fragment lanes read (published by the barrier below)
+  if constexpr (F::DIAG) {
+    // the zero page idle B-fragment lanes read (published by the barrier below);
+    // activation scales travel per group in the table, so token scales are 1
     for (int i = tid; i < kZeroPage / 4; i += kThreads) reinterpret_cast<uint32_t*>(sm + a.off_zero)[i] = 0u;
-  }
-  if (local_x) {
+    if (tid < 32) ts_s[tid] = 1.0f;
+    if (local_x) {
+      stage_local_diag<FMT>(a, sm, whole, &a.status[0]);
+    } else {
+      __syncthreads();
+    }
+  } else if (local_x) {
     stage_local_x<FMT>(a, sm, ts_s, &a.status[0]);
   } else {
     if (tid < a.M) ts_s[tid] = a.tscale[tid];
@@ -1074,7 +1288,8 @@ inline int local_tstride(int ncol) { return std::max(2, (ncol + 1) & ~1); }
 inline size_t tab_floats(int fmt, int64_t kp, int ncol, int ncol8) {
   const FmtInfo f = fmt_info(fmt);
   if (fmt == FMT_FP8) return 0;
-  return (size_t)(kp / f.sbe) * (is_diag(fmt) ? (size_t)ncol : (size_t)ncol8);
+  if (is_diag(fmt)) return (size_t)(kp / f.gk) * (size_t)ncol * (size_t)(f.gk / f.sbe + 4);
+  return (size_t)(kp / f.sbe) * (size_t)ncol8;
 }
 
 // Shared-memory plan of one GEMV launch.  local_kp > 0 asks for the local-x region
@@ -1233,6 +1448,21 @@ cudaError_t launch_prep(const PrepArgs& p, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, prep_kernel<FMT>, p);
 }
 
+template <int FMT>
+cudaError_t launch_prep_diag(const PrepArgs& p, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((p.kp / 8 + kPrepThreads - 1) / kPrepThreads), (unsigned)p.M);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prep_diag_kernel<FMT>, p);
+}
+
 }  // namespace
 
 __global__ void fill_rows_kernel(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N) {
@@ -1336,9 +1566,9 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     cudaError_t e = cudaSuccess;
     if (!local_ok) {
       switch (c.fmt) {
-        case FMT_Q4K: e = launch_prep<FMT_Q4K>(pa, c.stream); break;
-        case FMT_Q6K: e = launch_prep<FMT_Q6K>(pa, c.stream); break;
-        case FMT_Q80: e = launch_prep<FMT_Q80>(pa, c.stream); break;
+        case FMT_Q4K: e = launch_prep_diag<FMT_Q4K>(pa, c.stream); break;
+        case FMT_Q6K: e = launch_prep_diag<FMT_Q6K>(pa, c.stream); break;
+        case FMT_Q80: e = launch_prep_diag<FMT_Q80>(pa, c.stream); break;
         default:      e = launch_prep<FMT_FP8>(pa, c.stream); break;
       }
       if (e != cudaSuccess) return e;
@@ -1386,7 +1616,7 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.xcs = pl.xcs;
     a.off_tabloc = pl.off_tabloc;
     a.tstride = local_ok ? local_tstride(ncol) : ncol8;
-    a.tabw = diag ? ncol * (f.gk / f.sbe) : (f.gk / f.sbe) * ncol8;
+    a.tabw = diag ? ncol * (f.gk / f.sbe + 4) : (f.gk / f.sbe) * ncol8;
     a.off_zero = pl.off_zero;
     a.status = c.status;
     switch (c.fmt) {
