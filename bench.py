@@ -106,6 +106,15 @@ class Clocks:
             self.proc = None
         return self
 
+    def wait_first_sample(self, timeout_s: float = 5.0) -> None:
+        """Block until the sampler has written its first line (nvidia-smi start-up)."""
+        t0 = time.perf_counter()
+        while self.proc is not None and time.perf_counter() - t0 < timeout_s:
+            self.f.flush()
+            if os.path.exists(self.path) and os.path.getsize(self.path) > 0:
+                return
+            time.sleep(0.05)
+
     def __exit__(self, *a):
         if self.proc is not None:
             self.proc.terminate()
@@ -195,6 +204,16 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def launches_per_gemv(t: int, k: int) -> int:
+    """Kernels one M=1 bf16 call launches: the GEMV alone when every CTA can stage the
+    activation row itself (rtd_gemv.cu launch_qgemv: K % 8 == 0 and the staged row plus
+    its column-sum table within 40 KB), else a prep kernel as well."""
+    gk, sbe = {0: (32, 32), 8: (128, 32), 12: (256, 32), 14: (256, 16)}[t]
+    kp = -(-k // gk) * gk
+    tab = (kp // gk) * (gk // sbe + 4) if t else 0
+    return 1 if (k % 8 == 0 and kp * 2 + tab * 4 <= 40 * 1024) else 2
+
+
 def config_dict():
     return {"workload": "config1 quantized-linear op sweep at decode M=1 (y = x.W^T), one step = 14 GEMVs",
             "formats": [f for f, _ in FORMATS], "shapes_nk": SHAPES, "m": 1, "activations": "bf16",
@@ -203,13 +222,64 @@ def config_dict():
             "parallelism": "replicas: each rank streams its own weight copy"}
 
 
+def _time_steps(graph, stream, dev, n: int) -> float:
+    import torch
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) * 1e-3
+
+
+def profile_one(spec: str, calls: int) -> int:
+    """Run `calls` M=1 bf16 calls of one sweep GEMV (FMT:N:K) and exit: the target of
+    the ncu captures summarised under profiles/."""
+    import torch
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.weights import Fp8Weight, QMatMul
+
+    name, n, k = spec.split(":")
+    n, k = int(n), int(k)
+    t = dict(FORMATS)[name]
+    dev = torch.device("cuda", 0)
+    x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=0))).to(torch.bfloat16).to(dev)
+    y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    if t == 0:
+        w, s = synth.fp8_matrix(n, k, seed=0, stream=k)
+        o = Fp8Weight(w, s, k, n, device=dev)
+    else:
+        o = QMatMul(t, synth.quant_matrix(t, n, k, seed=0, stream=k), n, k, device=dev)
+    L = _lib.lib()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(calls):
+        if t == 0:
+            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, y.data_ptr(),
+                                  _lib.DT_BF16, n, _lib.FP8_W8A16, st)
+        else:
+            rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, None, y.data_ptr(),
+                               _lib.DT_BF16, n, st)
+        if rc != 0:
+            raise RuntimeError(f"status {rc}")
+    torch.cuda.synchronize(dev)
+    print(f"profile-one {spec}: {calls} calls ok")
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K",
+                    help="only run a few calls of one sweep GEMV (ncu target), no JSON line")
+    ap.add_argument("--calls", type=int, default=4)
     args = ap.parse_args()
+    if args.profile_one:
+        return profile_one(args.profile_one, args.calls)
     if args.impl == "reference":
         run_reference(args)
         return 0
@@ -275,11 +345,21 @@ def main() -> int:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # nvidia-smi samples every 200 ms: the timed K steps sit inside a window of the same
+    # load (an untimed pre-roll of about a second and a short post-roll), so the clock
+    # samples are taken while the GPU runs exactly this work.
+    step_s = max(1e-5, _time_steps(graph, stream, dev, 5) / 5)
+    roll = max(1, int(1.0 / step_s))
     with Clocks(local) as clk:
+        clk.wait_first_sample()
+        for _ in range(roll):
+            graph.replay()
         e0.record(stream)
         for _ in range(args.steps):
             graph.replay()
         e1.record(stream)
+        for _ in range(roll // 2):
+            graph.replay()
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -310,7 +390,7 @@ def main() -> int:
     tag = f"qgemv_{dit['name'].lower()}_{dit['n']}x{dit['k']}_m1"
     traffic = profile_traffic(tag)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": f"prep + qgemv_kernel, {dit['name']} {dit['n']}x{dit['k']} M=1",
+                "traffic": traffic, "kernel": f"qgemv_kernel, {dit['name']} {dit['n']}x{dit['k']} M=1",
                 "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                 "per_gemv_gbs": {f"{it['name']}:{it['n']}x{it['k']}": round(it["bytes"] / (per_ms[i] * 1e-3) / 1e9, 1)
                                  for i, it in enumerate(items)}}
@@ -360,7 +440,7 @@ def main() -> int:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "rtd_qlinear / rtd_fp8_linear per GEMV, eager, pinned-host x in and y out"},
-            "gpu_launches": 2 * len(items) * args.steps,
+            "gpu_launches": sum(launches_per_gemv(it["t"], it["k"]) for it in items) * args.steps,
             "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
