@@ -130,6 +130,28 @@ rtd_status rtd_fp8_linear(rtd_ctx* ctx, const rtd_fp8weight* w, const void* x, u
  * (crates/runtimed-model/src/weights/load_safetensors.rs:53-69) used at fp8_gemm.rs:98-99. */
 rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out, void* stream);
 
+/* ---- tensor-parallel row reduction -----------------------------------------
+ * Replaces RowParallelLinear::forward + ring_all_reduce
+ * (crates/runtimed-model/src/tp/row_linear.rs:20-66, crates/runtimed-model/src/tp/ring_reduce.rs:7-65)
+ * for one process per GPU: each rank holds the [N, K/world] column shard of a
+ * quantized matrix (rtd_qweight_upload of the shard's blocks) and its slice of x; the
+ * GEMV's epilogue exchanges the tile partials over NVLink and every rank writes the
+ * full, reduced y[M, N] (+ bias once).  Set-up:
+ *   1. rtd_tp_comm_create on every rank -> RTD_IPC_HANDLE_BYTES of handle bytes;
+ *   2. the caller exchanges the handles (rank order) by its own means;
+ *   3. rtd_tp_comm_open with all handles.
+ * Every rank must issue the same sequence of rtd_tp_qlinear_row calls; a rank that
+ * does not arrive within 2 s makes the others finish with RTD_ERR_PEER_TIMEOUT in
+ * the device status word (rtd_check_device_status). */
+#define RTD_IPC_HANDLE_BYTES 64
+typedef struct rtd_comm rtd_comm;
+rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, rtd_comm** out, void* handle_out);
+rtd_status rtd_tp_comm_open(rtd_comm* comm, const void* handles);
+rtd_status rtd_tp_comm_destroy(rtd_comm* comm);
+rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const void* x, uint32_t x_dtype,
+                              int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
+                              void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -48,7 +48,7 @@ struct rtd_fp8weight {
 
 namespace {
 
-constexpr size_t kWorkspaceBytes = 64ull << 20;  // split-K partials
+constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging of prep-mode GEMV calls
 constexpr int64_t kCounters = 1 << 17;           // per-tile arrival counters
 
 thread_local std::string g_thread_err;
@@ -177,6 +177,8 @@ rtd_status rtd_check_device_status(rtd_ctx* ctx, void* stream) {
   if (v != 0) {
     cudaMemset(ctx->status, 0, sizeof(int));
     if (v == RTD_ERR_INDEX) return fail(ctx, RTD_ERR_INDEX, "embedding id out of range");
+    if (v == RTD_ERR_PEER_TIMEOUT)
+      return fail(ctx, RTD_ERR_PEER_TIMEOUT, "a tensor-parallel peer did not arrive within the wait budget");
     return fail(ctx, RTD_ERR_DEVICE, "device status word raised code %d", v);
   }
   return RTD_OK;
@@ -346,7 +348,7 @@ rtd_status rtd_fp8weight_upload(rtd_ctx* ctx, const uint8_t* host_w, const float
   w->T = rtd::tiles_for(N);
   w->G = rtd::groups_for(rtd::FMT_FP8, K);
   w->scale_len = scale_len;
-  w->dev_bytes = (size_t)(w->T * w->G) * 512u;
+  w->dev_bytes = (size_t)(w->T * w->G) * (size_t)rtd::fmt_info(rtd::FMT_FP8).gb;
   DeviceGuard g(ctx->device);
   cudaError_t e = cudaMalloc(&w->scale, (size_t)scale_len * sizeof(float));
   if (e == cudaSuccess) e = cudaMemcpy(w->scale, host_scale, (size_t)scale_len * sizeof(float), cudaMemcpyHostToDevice);
@@ -394,3 +396,143 @@ rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out,
 }
 
 }  // extern "C"
+
+
+// ---- tensor-parallel row reduction ------------------------------------------
+// One communicator per rank (one process per GPU).  Its device buffer holds, for
+// both call parities, a receive slot per rank ([world][4 * max_n] f32, up to four
+// activation columns per launch) and a flag per (rank, tile); peers map it through
+// CUDA IPC and store into it over NVLink.
+struct rtd_comm {
+  rtd_ctx* ctx = nullptr;
+  int world = 1, rank = 0;
+  int64_t max_n = 0, max_tiles = 0;
+  unsigned char* base = nullptr;  // this rank's buffer (cudaMalloc, exported by IPC)
+  size_t recv_bytes = 0, bytes = 0;
+  unsigned char* peer[rtd::kMaxTpWorld] = {};  // mapped peer buffers (peer[rank] = base)
+  bool opened = false;
+  uint32_t epoch = 0;
+  rtd::TpReduce tp{};
+};
+
+rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, rtd_comm** out, void* handle_out) {
+  const char* who = "rtd_tp_comm_create";
+  if (!ctx || !out || !handle_out) return fail(ctx, RTD_ERR_INVALID, "%s: NULL argument", who);
+  if (world < 1 || world > rtd::kMaxTpWorld || rank < 0 || rank >= world)
+    return fail(ctx, RTD_ERR_INVALID, "%s: rank %d of world %d (1..%d ranks)", who, rank, world, rtd::kMaxTpWorld);
+  if (max_n <= 0) return fail(ctx, RTD_ERR_SHAPE, "%s: max_n=%lld", who, (long long)max_n);
+  DeviceGuard g(ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(ctx, g.err, who);
+  rtd_comm* c = new (std::nothrow) rtd_comm();
+  if (!c) return fail(ctx, RTD_ERR_OOM, "%s: host allocation failed", who);
+  c->ctx = ctx;
+  c->world = world;
+  c->rank = rank;
+  c->max_n = max_n;
+  c->max_tiles = (max_n + 15) / 16;
+  c->recv_bytes = (size_t)2 * world * 4 * (size_t)max_n * sizeof(float);
+  c->bytes = c->recv_bytes + (size_t)2 * world * (size_t)c->max_tiles * sizeof(uint32_t);
+  cudaError_t e = cudaMalloc(&c->base, c->bytes);
+  if (e != cudaSuccess) {
+    delete c;
+    return fail(ctx, RTD_ERR_OOM, "%s: cudaMalloc(%zu): %s", who, c->bytes, cudaGetErrorString(e));
+  }
+  if ((e = cudaMemset(c->base, 0, c->bytes)) != cudaSuccess ||
+      (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), c->base)) != cudaSuccess) {
+    cudaFree(c->base);
+    delete c;
+    return cuda_fail(ctx, e, who);
+  }
+  c->peer[rank] = c->base;
+  *out = c;
+  return RTD_OK;
+}
+
+rtd_status rtd_tp_comm_open(rtd_comm* c, const void* handles) {
+  const char* who = "rtd_tp_comm_open";
+  if (!c || !handles) return fail(nullptr, RTD_ERR_INVALID, "%s: NULL argument", who);
+  if (c->opened) return RTD_OK;
+  DeviceGuard g(c->ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(c->ctx, g.err, who);
+  const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int p = 0; p < c->world; ++p) {
+    if (p == c->rank) continue;
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h[p], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < p; ++q)
+        if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
+      return fail(c->ctx, RTD_ERR_CUDA, "%s: mapping rank %d: %s", who, p, cudaGetErrorString(e));
+    }
+    c->peer[p] = static_cast<unsigned char*>(ptr);
+  }
+  c->tp.world = c->world;
+  c->tp.rank = c->rank;
+  c->tp.max_n = c->max_n;
+  c->tp.max_tiles = c->max_tiles;
+  c->tp.epoch = &c->epoch;
+  for (int p = 0; p < c->world; ++p) {
+    c->tp.recv[p] = reinterpret_cast<float*>(c->peer[p]);
+    c->tp.flags[p] = reinterpret_cast<uint32_t*>(c->peer[p] + c->recv_bytes);
+  }
+  c->opened = true;
+  return RTD_OK;
+}
+
+rtd_status rtd_tp_comm_destroy(rtd_comm* c) {
+  if (!c) return RTD_OK;
+  DeviceGuard g(c->ctx->device);
+  for (int p = 0; p < c->world; ++p)
+    if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
+  cudaFree(c->base);
+  delete c;
+  return RTD_OK;
+}
+
+rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const void* x, uint32_t x_dtype, int64_t ldx,
+                              int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
+  const char* who = "rtd_tp_qlinear_row";
+  if (!comm || !shard) return fail(nullptr, RTD_ERR_INVALID, "%s: NULL comm or weight", who);
+  rtd_ctx* ctx = comm->ctx;
+  if (comm->world > 1 && !comm->opened) return fail(ctx, RTD_ERR_INVALID, "%s: communicator not opened", who);
+  if (shard->ctx != ctx) return fail(ctx, RTD_ERR_INVALID, "%s: weight and communicator on different contexts", who);
+  if (shard->N > comm->max_n)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: N=%lld above the communicator's max_n=%lld", who, (long long)shard->N,
+                (long long)comm->max_n);
+  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (M == 0 || shard->N == 0) return RTD_OK;
+  if ((shard->K > 0 && !x) || !y) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if (shard->K == 0) return fail(ctx, RTD_ERR_SHAPE, "%s: empty K shard", who);
+  if (ldx < shard->K || ldy < shard->N)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who, (long long)ldx,
+                (long long)ldy, (long long)shard->K, (long long)shard->N);
+  DeviceGuard g(ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(ctx, g.err, who);
+  rtd::QGemvCall c{};
+  c.fmt = shard->fmt;
+  c.w = shard->dev;
+  c.N = shard->N;
+  c.K = shard->K;
+  c.G = shard->G;
+  c.x = x;
+  c.x_dtype = (int)x_dtype;
+  c.ldx = ldx;
+  c.M = M;
+  c.bias = bias;
+  c.y = y;
+  c.y_dtype = (int)y_dtype;
+  c.ldy = ldy;
+  c.ws = ctx->ws;
+  c.ws_bytes = ctx->ws_bytes;
+  c.status = ctx->status;
+  c.sm_count = ctx->sm_count;
+  c.stream = (cudaStream_t)stream;
+  c.tp = comm->world > 1 ? &comm->tp : nullptr;
+  int plan_err = 0;
+  cudaError_t e = rtd::launch_qgemv(c, &plan_err);
+  if (plan_err) return fail(ctx, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the workspace", who,
+                            (long long)shard->N, (long long)shard->K);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, who);
+  return RTD_OK;
+}

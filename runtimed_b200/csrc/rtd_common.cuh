@@ -14,7 +14,7 @@
 namespace rtd {
 
 // Device status word codes (mirrors RTD_ERR_* of include/rtd.h).
-enum : int { kDevOk = 0, kDevIndex = 8, kDevWaitTimeout = 9 };
+enum : int { kDevOk = 0, kDevPeerTimeout = 7, kDevIndex = 8, kDevWaitTimeout = 9 };
 
 __device__ __forceinline__ void raise_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
@@ -101,6 +101,35 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// ---------------------------------------------------------------- cross-GPU flags
+// System-scope release store / acquire load: pair a peer's data stores (made
+// visible by __threadfence_system before the release) with the reader's loads.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *p has reached `epoch` (wrap-safe) for at most `budget_ns`; on
+// timeout records kDevPeerTimeout and returns false, so no wait outlives a peer
+// that never arrives.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t epoch, uint64_t budget_ns, int* status) {
+  if ((int32_t)(ld_acquire_sys(p) - epoch) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    __nanosleep(64);
+    if ((int32_t)(ld_acquire_sys(p) - epoch) >= 0) return true;
+    if (global_ns() - t0 > budget_ns) {
+      raise_status(status, kDevPeerTimeout);
+      return false;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- MMA

@@ -12,13 +12,6 @@
 
 namespace rtd {
 
-// Position of natural byte `off` (0..7) inside an FP8 lane's 8-byte run: bytes 1
-// and 2 of every 4-byte word are swapped by the repack (rtd_repack.cpp).
-__device__ __forceinline__ int swz(int off) {
-  const int b = off & 3;
-  return (off & 4) | (b == 1 ? 2 : b == 2 ? 1 : b);
-}
-
 __device__ __forceinline__ uint32_t ld_u32(const uint8_t* a) {
   return (uint32_t)a[0] | ((uint32_t)a[1] << 8) | ((uint32_t)a[2] << 16) | ((uint32_t)a[3] << 24);
 }
@@ -66,8 +59,8 @@ __device__ __forceinline__ float decode_elem(const uint8_t* grp, int r, int e) {
     const int8_t q = (int8_t)grp[128 + (2 * rr + (i >> 4)) * 512 + lane * 16 + (i & 15)];
     return __fmul_rn(d, (float)q);
   } else {
-    const int tg = e >> 3, off = e & 7;
-    const uint8_t b = grp[(4 * g + tg) * 16 + rr * 8 + swz(off)];
+    const int blk = e >> 5, i = e & 31, lane = 4 * g + blk;
+    const uint8_t b = grp[(2 * rr + (i >> 4)) * 512 + lane * 16 + (i & 15)];
     const uint32_t h = e4m3x2_to_f16x2((uint16_t)b) & 0xFFFFu;
     return __half2float(__ushort_as_half((unsigned short)h));
   }
@@ -76,8 +69,8 @@ __device__ __forceinline__ float decode_elem(const uint8_t* grp, int r, int e) {
 // One thread per output element of row `n` (global row), k in [0, K).
 template <int FMT>
 __device__ __forceinline__ float decode_row_elem(const uint8_t* w, int64_t G, int64_t n, int64_t k) {
-  constexpr int GK = (FMT == FMT_Q4K || FMT == FMT_Q6K) ? 256 : (FMT == FMT_Q80) ? 128 : 32;
-  constexpr int GB = (FMT == FMT_Q4K) ? 2304 : (FMT == FMT_Q6K) ? 3360 : (FMT == FMT_Q80) ? 2176 : 512;
+  constexpr int GK = (FMT == FMT_Q4K || FMT == FMT_Q6K) ? 256 : 128;
+  constexpr int GB = (FMT == FMT_Q4K) ? 2304 : (FMT == FMT_Q6K) ? 3360 : (FMT == FMT_Q80) ? 2176 : 2048;
   const int64_t t = n >> 4, s = k / GK;
   const uint8_t* grp = w + (size_t)(t * G + s) * GB;
   return decode_elem<FMT>(grp, (int)(n & 15), (int)(k - s * GK));

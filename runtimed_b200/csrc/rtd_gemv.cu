@@ -39,7 +39,6 @@
 //    workspace and the last warp to arrive (per-tile counter) sums them in warp
 //    order, writes y and re-arms the counter, so every call leaves the counters
 //    at zero.
-#include <cooperative_groups.h>
 
 #include <algorithm>
 #include <cstdlib>
@@ -47,7 +46,6 @@
 #include "rtd_common.cuh"
 #include "rtd_kernels.h"
 
-namespace cg = cooperative_groups;
 
 namespace rtd {
 
@@ -56,10 +54,9 @@ namespace {
 constexpr int kWarps = 8;  // warps per GEMV CTA, each an independent pipeline
 constexpr int kThreads = kWarps * 32;
 constexpr int kPrepThreads = 256;
-constexpr int kPrepCluster = 8;
 constexpr int kMaxStages = 4;
-constexpr int kTblBytes = 1280;
-constexpr int kZeroPage = 512;  // zero B-fragment source for DIAG lanes that own no column  // per-warp scale table: 16 rows x 9 float2 (Q4_K) or 16 x 17 float (Q6_K)
+constexpr int kTblBytes = 128;   // per-warp epilogue scratch (bias and row scale of a tile)
+constexpr int kZeroPage = 512;   // zero B-fragment source for lanes that own no MMA column
 
 template <int FMT>
 struct FmtC;
@@ -74,24 +71,21 @@ template <>
 struct FmtC<FMT_Q4K> {
   static constexpr int GK = 256, GB = 2304, SBE = 32;
   static constexpr float XOFF = 1.0f;
-  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_Q6K> {
   static constexpr int GK = 256, GB = 3360, SBE = 16;
   static constexpr float XOFF = -0x1p-19f;  // -32 * 2^-24
-  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_Q80> {
   static constexpr int GK = 128, GB = 2176, SBE = 32;
   static constexpr float XOFF = -0x1p-17f;  // -128 * 2^-24
-  static constexpr bool TAB = true, DIAG = true;
 };
 template <>
 struct FmtC<FMT_FP8> {
-  static constexpr int GK = 32, GB = 512, SBE = 32;
-  static constexpr bool TAB = false, DIAG = false;
+  static constexpr int GK = 128, GB = 2048, SBE = 32;
+  static constexpr float XOFF = 0.0f;  // signed E4M3 codes carry no bias; the sums go unused
 };
 
 // Bytes one activation column occupies per group in the workspace (and in shared
@@ -191,122 +185,6 @@ __device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
   return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
-template <int FMT>
-__global__ void __cluster_dims__(kPrepCluster, 1, 1) __launch_bounds__(kPrepThreads)
-    prep_kernel(const PrepArgs a) {
-  using F = FmtC<FMT>;
-  // The GEMV behind this kernel may launch and start streaming weights at once;
-  // this kernel itself waits for whatever ran before it (which may be producing x,
-  // or a previous GEMV still reading the workspace this kernel overwrites).
-  griddep_launch_dependents();
-  griddep_wait();
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int t = blockIdx.x / kPrepCluster;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float red[kPrepThreads / 32];
-  __shared__ float cmax;
-  // this CTA's slice, in whole 32-element windows so sub-block sums never straddle CTAs
-  const int64_t nwin = a.kp / 32;
-  const int64_t w0 = nwin * rank / kPrepCluster, w1 = nwin * (rank + 1) / kPrepCluster;
-  const int64_t c0 = 4 * w0, nch = 4 * (w1 - w0);
-  const bool vec = a.x_vec != 0;
-
-  float m = 0.0f;
-  for (int64_t c = tid; c < nch; c += kPrepThreads) {
-    float v[8];
-    load8(a.x, a.x_dtype, vec, a.ldx, a.K, t, 8 * (c0 + c), v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(a.w8a8 ? e4m3_round_ref(v[i]) : v[i]));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  if (tid == 0) {
-    float mm = 0.0f;
-    for (int w = 0; w < kPrepThreads / 32; ++w) mm = fmaxf(mm, red[w]);
-    cmax = mm;
-  }
-  cluster.sync();
-  if (tid == 0) {
-    float mm = 0.0f;
-    for (int r = 0; r < kPrepCluster; ++r) mm = fmaxf(mm, *cluster.map_shared_rank(&cmax, r));
-    red[0] = mm;
-  }
-  cluster.sync();  // peers are done reading cmax before any CTA moves on or exits
-  __syncthreads();
-  int e = 0;
-  const float mm = red[0];
-  if (mm > 0.0f && mm <= 3.4e38f) e = min(max(ilogbf(mm) - 14, -110), 110);
-  const float inv = ldexpf(1.0f, -e);
-  if (rank == 0 && tid == 0) a.tscale[t] = ldexpf(1.0f, e);
-
-  constexpr int SBC = F::SBE / 8;
-  constexpr int CSB = col_stride_bytes(F::GK);
-  const int64_t iters = (nch + kPrepThreads - 1) / kPrepThreads;
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t cl = it * kPrepThreads + tid;
-    const bool valid = cl < nch;
-    const int64_t c = c0 + cl;
-    float v[8];
-    if (valid) {
-      load8(a.x, a.x_dtype, vec, a.ldx, a.K, t, 8 * c, v);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-    }
-    __half hi[8], lo[8];
-    float shi = 0.0f, slo = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s = (a.w8a8 ? e4m3_round_ref(v[i]) : v[i]) * inv;
-      hi[i] = __float2half_rn(s);
-      const float hf = __half2float(hi[i]);
-      lo[i] = __float2half_rn(s - hf);
-      shi += hf;
-      slo += __half2float(lo[i]);
-    }
-    if (valid) {
-      const int64_t k = 8 * c;
-      const int64_t grp = k / F::GK;
-      const int within = (int)(k - grp * F::GK);
-      const int off = F::DIAG ? diag_unit_offset<FMT>(within / 8) : within * 2;
-      uint8_t* base = a.cols + ((size_t)grp * a.ncol + (size_t)t * a.P) * CSB + off;
-      uint4 u;
-      u.x = pack_h2(hi[0], hi[1]); u.y = pack_h2(hi[2], hi[3]);
-      u.z = pack_h2(hi[4], hi[5]); u.w = pack_h2(hi[6], hi[7]);
-      if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
-      *reinterpret_cast<uint4*>(base) = u;
-      if (a.P == 2) {
-        u.x = pack_h2(lo[0], lo[1]); u.y = pack_h2(lo[2], lo[3]);
-        u.z = pack_h2(lo[4], lo[5]); u.w = pack_h2(lo[6], lo[7]);
-        if constexpr (FMT == FMT_Q4K) u = q4k_quad_order(u);
-        *reinterpret_cast<uint4*>(base + CSB) = u;
-      }
-    }
-    if constexpr (F::TAB) {
-      // consecutive chunks sit in consecutive lanes: reduce the SBC chunks of a sub-block
-      shi += __shfl_xor_sync(0xffffffffu, shi, 1);
-      slo += __shfl_xor_sync(0xffffffffu, slo, 1);
-      if constexpr (SBC == 4) {
-        shi += __shfl_xor_sync(0xffffffffu, shi, 2);
-        slo += __shfl_xor_sync(0xffffffffu, slo, 2);
-      }
-      if (valid && (c % SBC) == 0) {
-        // table [group][column][sub-block]
-        constexpr int NSB = F::GK / F::SBE;
-        const int64_t sb = c / SBC, grp = sb / NSB;
-        const int sbi = (int)(sb - grp * NSB);
-        float* tp = a.tab + ((size_t)grp * a.ncol + (size_t)t * a.P) * NSB + sbi;
-        constexpr float xoff = F::XOFF;
-        tp[0] = shi * xoff;
-        if (a.P == 2) tp[NSB] = slo * xoff;
-      }
-    }
-  }
-}
-
 // Prep for DIAG formats: one warp per (token, group) -- the group's own max |x| sets
 // its scale, so no cross-CTA reduction is needed.  Writes the transposed f16 units
 // (hi, and for f32 inputs the lo remainder as a second column) and the table rows.
@@ -324,6 +202,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_diag_kernel(const PrepArgs 
   float v[8];
   if (valid) {
     load8(a.x, a.x_dtype, a.x_vec != 0, a.ldx, a.K, t, 8 * c, v);
+    if (a.w8a8) {  // W8A8: activations take the reference E4M3 rounding first
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = e4m3_round_ref(v[i]);
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
@@ -456,36 +338,6 @@ __device__ __forceinline__ void static_for(Fn&& f) {
   if constexpr (I < N) {
     f(IC<I>{});
     static_for<I + 1, N>(f);
-  }
-}
-
-// One FP8 group (16 rows x 32 k) into the warp's accumulators, tokens as MMA
-// columns: acc[nt] is the m16n8 C fragment of activation columns 8nt .. 8nt+7.
-//   gs: the group's bytes; xs: this group's x slice (column c at xs + c*xstride).
-// Activation columns >= ncol read column ncol-1: those MMA output columns are never
-// stored, so no select is needed.
-template <int FMT, int NT>
-__device__ __forceinline__ void do_group(uint32_t gs, uint32_t xs, int xstride, int ncol, float (&acc)[NT][4],
-                                         int lane) {
-  static_assert(FMT == FMT_FP8, "the token-per-column decoder serves FP8 groups");
-  const int g = lane >> 2, tq = lane & 3;
-  uint32_t xcol[NT];  // this lane's B column (clamped)
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) xcol[nt] = xs + (uint32_t)min(nt * 8 + g, ncol - 1) * xstride;
-  {
-    const uint4 q = lds128(gs + lane * 16);
-    const uint32_t p0 = prmt(q.x, 0u, 0x3120), p1 = prmt(q.y, 0u, 0x3120);
-    const uint32_t p2 = prmt(q.z, 0u, 0x3120), p3 = prmt(q.w, 0u, 0x3120);
-    const uint32_t a0 = e4m3x2_to_f16x2((uint16_t)(p0 & 0xFFFFu)), a1 = e4m3x2_to_f16x2((uint16_t)(p2 & 0xFFFFu));
-    const uint32_t a2 = e4m3x2_to_f16x2((uint16_t)(p0 >> 16)), a3 = e4m3x2_to_f16x2((uint16_t)(p2 >> 16));
-    const uint32_t b0 = e4m3x2_to_f16x2((uint16_t)(p1 & 0xFFFFu)), b1 = e4m3x2_to_f16x2((uint16_t)(p3 & 0xFFFFu));
-    const uint32_t b2 = e4m3x2_to_f16x2((uint16_t)(p1 >> 16)), b3 = e4m3x2_to_f16x2((uint16_t)(p3 >> 16));
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint4 bx = lds128(xcol[nt] + tq * 16);
-      mma_f16(acc[nt], a0, a1, a2, a3, bx.x, bx.y, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-      mma_f16(acc[nt], b0, b1, b2, b3, bx.z, bx.w, acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    }
   }
 }
 
@@ -678,6 +530,45 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
       acc[c][0] = fmaf(S[c], V[c][0], acc[c][0]);
       acc[c][1] = fmaf(S[c], V[c][1], acc[c][1]);
     }
+  } else if constexpr (FMT == FMT_FP8) {
+    // lane t owns codes 32t..32t+31 of the group; E4M3 -> f16 is exact, and the
+    // per-row scale is applied when the tile is written.  Column 2t as for Q8_0.
+    constexpr int NSB = 4;
+    const uint32_t qb = gs + lane * 16;
+    const uint4 q0 = lds128o<0>(qb), q1 = lds128o<512>(qb), q2 = lds128o<1024>(qb), q3 = lds128o<1536>(qb);
+    const uint32_t wg[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t wh[8] = {q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    uint32_t p[NC];
+    float S[NC];
+    float C[NC][4];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      p[c] = act0 ? xs + c * xcs + 16 * tq : z0;
+      S[c] = ldsf(ts + (uint32_t)(c * TW + NSB) * 4);
+      C[c][0] = C[c][1] = C[c][2] = C[c][3] = 0.0f;
+    }
+    static_for<0, 4>([&](auto jI) {
+      constexpr int j = decltype(jI)::value;
+      uint4 B[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) B[c] = lds128o<64 * j>(p[c]);
+      static_for<0, 2>([&](auto eI) {
+        constexpr int e = decltype(eI)::value;
+        constexpr int t = 2 * j + e;
+        const uint32_t a0 = e4m3x2_to_f16x2((uint16_t)(wg[t] & 0xFFFFu)), a1 = e4m3x2_to_f16x2((uint16_t)(wh[t] & 0xFFFFu));
+        const uint32_t a2 = e4m3x2_to_f16x2((uint16_t)(wg[t] >> 16)), a3 = e4m3x2_to_f16x2((uint16_t)(wh[t] >> 16));
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const uint32_t b0 = e ? B[c].z : B[c].x, b1 = e ? B[c].w : B[c].y;
+          mma_f16_acc(C[c], a0, a1, a2, a3, b0, b1);
+        }
+      });
+    });
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      acc[c][0] = fmaf(S[c], C[c][0], acc[c][0]);
+      acc[c][1] = fmaf(S[c], C[c][2], acc[c][1]);
+    }
   } else {  // FMT_Q80: lane t owns block t; both k-slot pairs feed MMA column 2t
     constexpr int NSB = 4;
     const uint32_t dd = lds32(gs + 4 * lane);
@@ -745,9 +636,15 @@ struct Args {
   int64_t ldx, K, kp;
   int x_dtype, w8a8;
   int off_xloc, xcs, off_tabloc;
-  int tstride;  // floats per sub-block row of the column-sum table (FP8-style decoder)
-  int tabw;     // table floats per group: ncol * (GK / SBE) for DIAG formats
-  int off_zero; // DIAG: kZeroPage bytes of zeros
+  int tabw;      // table floats per group: ncol * (GK / SBE + 4)
+  int off_zero;  // kZeroPage bytes of zeros
+  // row-parallel reduction (tp_world > 1): this launch's parity half of every rank's
+  // receive slots [world][4 * max_n] and arrival flags [world][max_tiles]
+  int tp_world, tp_rank;
+  float* tp_recv[kMaxTpWorld];
+  uint32_t* tp_flags[kMaxTpWorld];
+  int64_t tp_max_n, tp_max_tiles;
+  uint32_t tp_epoch;
   int* status;
 };
 
@@ -769,115 +666,49 @@ __device__ __forceinline__ void named_bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// Local-x mode: the CTA copies the raw bf16 / f16 activation rows into shared
-// memory (one bulk copy per token), finds each token's max |x|, and rewrites the
-// rows in place as power-of-two-scaled f16 plus the per-sub-block column sums --
-// exactly what the prep kernel would have produced, without a second launch.
-// Every CTA sees the whole row, so every CTA derives the same scale.
-template <int FMT>
-__device__ __forceinline__ void stage_local_x(const Args& a, uint8_t* sm, float* ts_s, int* status) {
-  using F = FmtC<FMT>;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint8_t* xloc = sm + a.off_xloc;
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + a.off_tabloc - 16);
-  float* red = reinterpret_cast<float*>(sm + a.off_tabloc - 16 - 32 * kWarps * 4);  // [8 warps][32 tokens]
-  const uint32_t row_bytes = (uint32_t)(a.K * 2);
-  if (tid == 0) {
-    mbar_init(xbar, 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(xbar, row_bytes * (uint32_t)a.M);
-    for (int t = 0; t < a.M; ++t)
-      bulk_g2s(xloc + (size_t)t * a.xcs, static_cast<const uint8_t*>(a.xraw) + (size_t)t * a.ldx * 2, row_bytes, xbar);
-  }
-  // zero the padding past K (FP8 rows and trailing partial Q8_0 groups)
-  for (int64_t i = a.K + tid; i < a.kp; i += kThreads)
-    for (int t = 0; t < a.M; ++t) reinterpret_cast<uint16_t*>(xloc + (size_t)t * a.xcs)[i] = 0;
-  __syncthreads();  // the barrier init is visible before anyone waits on it
-  mbar_wait_bounded(xbar, 0, status);
-  const int nchunk = (int)(a.kp / 8);
-  for (int t = 0; t < a.M; ++t) {
-    const uint4* row = reinterpret_cast<const uint4*>(xloc + (size_t)t * a.xcs);
-    float m = 0.0f;
-    for (int c = tid; c < nchunk; c += kThreads) {
-      const uint4 u = row[c];
-      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+// Row-parallel tile exchange, run by the tile's writer warp in place of the plain
+// store.  rb holds the 8 warps' partial sums of the tile, ep the bias (full, added
+// once after the reduction) and the row scale.  The rank's partials go to its slot on
+// every rank (peer stores over NVLink), are published with a system-scope release,
+// and the tile is written once every rank's partial has arrived -- in rank order, so
+// every rank writes the same bits.  A peer that never arrives ends the wait after
+// kWaitBudgetNs with RTD_ERR_PEER_TIMEOUT in the status word.
+__device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const float* rb, const float* ep,
+                                                 int lane) {
+  const int W = a.tp_world, R = a.tp_rank;
+  const int64_t slot_elems = 4 * a.tp_max_n;
+  for (int o = lane; o < 16 * a.M; o += 32) {
+    const int r = o / a.M, t = o - r * a.M;
+    const int64_t n = (int64_t)tile * 16 + r;
+    float sum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t b16 = (wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
-        float v = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
-        if (a.w8a8) v = e4m3_round_ref(v);
-        m = fmaxf(m, fabsf(v));
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp * 32 + t] = m;
-  }
-  __syncthreads();
-  if (tid < a.M) {
-    float mm = 0.0f;
-    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, red[w * 32 + tid]);
-    int e = 0;
-    if (mm > 0.0f && mm <= 3.4e38f) e = min(max(ilogbf(mm) - 14, -110), 110);
-    ts_s[tid] = ldexpf(1.0f, e);
-    red[tid] = ldexpf(1.0f, -e);  // every warp has read its maxima above (barrier)
-  }
-  __syncthreads();
-  float* tab = reinterpret_cast<float*>(sm + a.off_tabloc);
-  constexpr int SBC = F::SBE / 8;
-  const int iters = (nchunk + kThreads - 1) / kThreads;
-  for (int t = 0; t < a.M; ++t) {
-    uint4* row = reinterpret_cast<uint4*>(xloc + (size_t)t * a.xcs);
-    const float inv = red[t];
-    for (int it = 0; it < iters; ++it) {
-      const int c = it * kThreads + tid;
-      const bool valid = c < nchunk;
-      float sum = 0.0f;
-      uint4 cv = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) {
-        const uint4 u = row[c];
-        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-        uint32_t out[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __half h2v[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const uint32_t b16 = (wd[i] >> (16 * k)) & 0xFFFFu;
-            float v = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
-            if (a.w8a8) v = e4m3_round_ref(v);
-            h2v[k] = __float2half_rn(v * inv);
-            sum += __half2float(h2v[k]);
-          }
-          out[i] = pack_h2(h2v[0], h2v[1]);
-        }
-        if constexpr (!F::DIAG) row[c] = make_uint4(out[0], out[1], out[2], out[3]);
-        cv = make_uint4(out[0], out[1], out[2], out[3]);
-      }
-      if constexpr (F::DIAG) {
-        // a warp converts whole groups (32 or 16 units): all of its lanes have read
-        // their unit before any lane stores into the group's transposed order
-        __syncwarp();
-        constexpr int UPG = F::GK / 8;
-        if (valid) {
-          if constexpr (FMT == FMT_Q4K) cv = q4k_quad_order(cv);
-          *reinterpret_cast<uint4*>(xloc + (size_t)t * a.xcs + (size_t)(c / UPG) * F::GK * 2 +
-                                    diag_unit_offset<FMT>(c % UPG)) = cv;
-        }
-      }
-      if constexpr (F::TAB) {
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        if constexpr (SBC == 4) sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        constexpr float xoff = F::XOFF;
-        if (valid && (c % SBC) == 0) {
-          constexpr int NSB = F::GK / F::SBE;
-          const int sb = c / SBC, grp = sb / NSB;
-          tab[(grp * a.ncol + t) * NSB + (sb - grp * NSB)] = sum * xoff;
-        }
-      }
+    for (int w = 0; w < kWarps; ++w)
+      for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
+    if (n < a.N) {
+      const int64_t off = (int64_t)R * slot_elems + (int64_t)t * a.N + n;
+      for (int p = 0; p < W; ++p) a.tp_recv[p][off] = sum * ep[16 + r];
     }
   }
-  __syncthreads();
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_system();
+    for (int p = 0; p < W; ++p) st_release_sys(a.tp_flags[p] + (int64_t)R * a.tp_max_tiles + tile, a.tp_epoch);
+  }
+  if (lane < W && lane != R)
+    wait_flag_sys(a.tp_flags[R] + (int64_t)lane * a.tp_max_tiles + tile, a.tp_epoch, kWaitBudgetNs, a.status);
+  __syncwarp();
+  for (int q = 0; q < W; ++q)  // every reading lane acquires the arrivals itself
+    if (q != R) (void)ld_acquire_sys(a.tp_flags[R] + (int64_t)q * a.tp_max_tiles + tile);
+  for (int o = lane; o < 16 * a.M; o += 32) {
+    const int r = o / a.M, t = o - r * a.M;
+    const int64_t n = (int64_t)tile * 16 + r;
+    if (n < a.N) {
+      const volatile float* src = a.tp_recv[R] + (int64_t)t * a.N + n;
+      float v = 0.0f;
+      for (int q = 0; q < W; ++q) v += src[(int64_t)q * slot_elems];
+      store_y(a, t, n, v + ep[r]);
+    }
+  }
 }
 
 // Local-x staging for DIAG formats.  The CTA copies the raw bf16 / f16 rows into
@@ -935,6 +766,7 @@ __device__ __forceinline__ void stage_local_diag(const Args& a, uint8_t* sm, boo
         for (int i = 0; i < 8; ++i) {
           const uint32_t b16 = (wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
           v[i] = (a.x_dtype == 1) ? h2f(b16) : __uint_as_float(b16 << 16);
+          if (a.w8a8) v[i] = e4m3_round_ref(v[i]);  // W8A8: the reference E4M3 rounding first
         }
       } else {
 #pragma unroll
@@ -1004,7 +836,6 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   uint8_t* tblw = wb + a.off_tbl;
   const uint32_t wb_s = smem_u32(wb), tb_s = smem_u32(tblw);
   float* red = reinterpret_cast<float*>(sm + a.off_red);  // [2][8 warps][16][ncol8]
-  float* ts_s = red + 2 * kWarps * 16 * a.ncol8;          // [32] token scales
   const int NS = a.NS;
 
   // the issue side walks its own cursor over (tile, group) a few items ahead
@@ -1013,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     uint32_t b = (uint32_t)ng * F::GB;
     if (!local_x) {
       b += (uint32_t)ng * a.ncol * CSB;
-      if constexpr (F::TAB) b += (uint32_t)ng * a.tabw * 4;
+      b += (uint32_t)ng * a.tabw * 4;
     }
     return b;
   };
@@ -1024,8 +855,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   auto issue_x = [&](int s, int g0, int ng) {
     uint8_t* slot = wb + (size_t)s * a.slot_bytes;
     bulk_g2s(slot + a.off_x, a.cols + (size_t)g0 * a.ncol * CSB, (uint32_t)ng * a.ncol * CSB, &bar[s]);
-    if constexpr (F::TAB)
-      bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * a.tabw, (uint32_t)ng * a.tabw * 4, &bar[s]);
+    bulk_g2s(slot + a.off_tab, a.tab + (size_t)g0 * a.tabw, (uint32_t)ng * a.tabw * 4, &bar[s]);
   };
   const int gstep = (whole ? 1 : kWarps) * a.IG;  // group stride between a warp's items in a tile
   const int gfirst = (whole ? 0 : warp) * a.IG;
@@ -1060,26 +890,17 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     if (lane == 0 && !local_x) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
     advance();
   }
-  if constexpr (F::DIAG) {
-    // the zero page idle B-fragment lanes read (published by the barrier below);
-    // activation scales travel per group in the table, so token scales are 1
-    for (int i = tid; i < kZeroPage / 4; i += kThreads) reinterpret_cast<uint32_t*>(sm + a.off_zero)[i] = 0u;
-    if (tid < 32) ts_s[tid] = 1.0f;
-    if (local_x) {
-      stage_local_diag<FMT>(a, sm, whole, &a.status[0]);
-    } else {
-      __syncthreads();
-    }
-  } else if (local_x) {
-    stage_local_x<FMT>(a, sm, ts_s, &a.status[0]);
+  // the zero page idle B-fragment lanes read (published by the barrier below)
+  for (int i = tid; i < kZeroPage / 4; i += kThreads) reinterpret_cast<uint32_t*>(sm + a.off_zero)[i] = 0u;
+  if (local_x) {
+    stage_local_diag<FMT>(a, sm, whole, &a.status[0]);
   } else {
-    if (tid < a.M) ts_s[tid] = a.tscale[tid];
     __syncthreads();
   }
   const uint32_t xloc_s = smem_u32(sm + a.off_xloc), tabloc_s = smem_u32(sm + a.off_tabloc);
-  // DIAG: idle lanes point at the zero page, on banks no active lane of the same load uses
+  // idle lanes point at the zero page, on banks no active lane of the same load uses
   const uint32_t zero_s = smem_u32(sm + a.off_zero);
-  const uint32_t z0 = zero_s + (FMT == FMT_Q80 ? 112u : 16u), z1 = zero_s;
+  const uint32_t z0 = zero_s + ((FMT == FMT_Q80 || FMT == FMT_FP8) ? 112u : 16u), z1 = zero_s;
   const bool act0 = g == 2 * tq, act1 = g == 2 * tq + 1;
 
   float acc[NT][4];
@@ -1116,26 +937,16 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         continue;
       }
       const uint32_t slot = wb_s + (uint32_t)(slot_i * a.slot_bytes);
-      if constexpr (F::DIAG) {
-        if (local_x) {
+      if (local_x) {
 #pragma unroll 1
-          for (int gi = 0; gi < ng; ++gi)
-            do_group_diag<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, (uint32_t)a.xcs,
-                                   tabloc_s + (uint32_t)((g0 + gi) * a.tabw) * 4, z0, z1, act0, act1, acc, lane);
-        } else {
-#pragma unroll 1
-          for (int gi = 0; gi < ng; ++gi)
-            do_group_diag<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, (uint32_t)CSB,
-                                   slot + a.off_tab + gi * a.tabw * 4, z0, z1, act0, act1, acc, lane);
-        }
-      } else if (local_x) {
-#pragma unroll 2
         for (int gi = 0; gi < ng; ++gi)
-          do_group<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, a.xcs, a.ncol, acc, lane);
+          do_group_diag<FMT, NT>(slot + gi * F::GB, xloc_s + (uint32_t)(g0 + gi) * F::GK * 2, (uint32_t)a.xcs,
+                                 tabloc_s + (uint32_t)((g0 + gi) * a.tabw) * 4, z0, z1, act0, act1, acc, lane);
       } else {
-#pragma unroll 2
+#pragma unroll 1
         for (int gi = 0; gi < ng; ++gi)
-          do_group<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, CSB, a.ncol, acc, lane);
+          do_group_diag<FMT, NT>(slot + gi * F::GB, slot + a.off_x + gi * a.ncol * CSB, (uint32_t)CSB,
+                                 slot + a.off_tab + gi * a.tabw * 4, z0, z1, act0, act1, acc, lane);
       }
       __syncwarp();
       if (i + NS < n_items) {
@@ -1152,7 +963,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         phase ^= 1u;
       }
     }
-    if constexpr (F::DIAG) {
+    {
       // each lane holds partial sums over its own sub-blocks: add the 4 lanes of a row
 #pragma unroll
       for (int c = 0; c < NT; ++c)
@@ -1173,9 +984,9 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
             if (a.P == 2) {
               const int t = c >> 1;
               if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N)
-                store_y(a, t, n, (acc[c][rr] + acc[c + 1][rr]) * ts_s[t] * cs + bias);
+                store_y(a, t, n, (acc[c][rr] + acc[c + 1][rr]) * cs + bias);
             } else if (tq == c && c < a.M && n < a.N) {
-              store_y(a, c, n, acc[c][rr] * ts_s[c] * cs + bias);
+              store_y(a, c, n, acc[c][rr] * cs + bias);
             }
           }
         }
@@ -1183,29 +994,6 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
         continue;
       }
-    }
-    if (!F::DIAG && whole) {  // ---- tile end, whole mode: write straight from the accumulators
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int64_t n = (int64_t)tile * 16 + g + 8 * rr;
-          const float bias = rr ? eb2 : eb, cs = rr ? es2 : es;
-          if (a.P == 2) {  // columns 2tq, 2tq+1: hi and lo halves of token nt*4 + tq
-            const int t = nt * 4 + tq;
-            if (t < a.M && n < a.N)
-              store_y(a, t, n, (acc[nt][2 * rr] + acc[nt][2 * rr + 1]) * ts_s[t] * cs + bias);
-          } else {
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-              const int t = nt * 8 + 2 * tq + cc;
-              if (t < a.M && n < a.N) store_y(a, t, n, acc[nt][2 * rr + cc] * ts_s[t] * cs + bias);
-            }
-          }
-        }
-        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-      }
-      continue;
     }
     // ---- tile end: the 8 partial sums meet in shared memory (double buffered).
     // Only the writer of the tile waits for them (bar.sync on FULL[b]); the others
@@ -1219,26 +1007,15 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     }
     float* rb = red + (size_t)b * kWarps * 16 * a.ncol8;
     float* rw = rb + (size_t)warp * 16 * a.ncol8;
-    if constexpr (F::DIAG) {
-      if (tq == 0) {
+    if (tq == 0) {
 #pragma unroll
-        for (int c = 0; c < NT; ++c) {
-          rw[g * a.ncol8 + c] = acc[c][0];
-          rw[(g + 8) * a.ncol8 + c] = acc[c][1];
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
-    } else {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        rw[g * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][0];
-        rw[g * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][1];
-        rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq] = acc[nt][2];
-        rw[(g + 8) * a.ncol8 + nt * 8 + 2 * tq + 1] = acc[nt][3];
-        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+      for (int c = 0; c < NT; ++c) {
+        rw[g * a.ncol8 + c] = acc[c][0];
+        rw[(g + 8) * a.ncol8 + c] = acc[c][1];
       }
     }
+#pragma unroll
+    for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
     if (!writer) {
       named_bar_arrive(1 + b, kThreads);
     } else {
@@ -1249,14 +1026,18 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         ep[16 + lane] = es;
       }
       __syncwarp();
-      for (int o = lane; o < 16 * a.M; o += 32) {
-        const int r = o / a.M, t = o - r * a.M;
-        const int64_t n = (int64_t)tile * 16 + r;
-        float sum = 0.0f;
+      if (a.tp_world > 1) {
+        tp_exchange_tile(a, tile, rb, ep, lane);
+      } else {
+        for (int o = lane; o < 16 * a.M; o += 32) {
+          const int r = o / a.M, t = o - r * a.M;
+          const int64_t n = (int64_t)tile * 16 + r;
+          float sum = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w)
-          for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
-        if (n < a.N) store_y(a, t, n, sum * ts_s[t] * ep[16 + r] + ep[r]);
+          for (int w = 0; w < kWarps; ++w)
+            for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
+          if (n < a.N) store_y(a, t, n, sum * ep[16 + r] + ep[r]);
+        }
       }
       __syncwarp();
       if (tile + 2 < t1) named_bar_arrive(3 + b, kThreads);  // hand the buffer back
@@ -1279,44 +1060,36 @@ struct Plan {
   size_t smem;
 };
 
-inline bool is_diag(int fmt) { return fmt != FMT_FP8; }
-
-// Floats per sub-block row of the column-sum table staged by the CTA itself (FP8-style decoder).
-inline int local_tstride(int ncol) { return std::max(2, (ncol + 1) & ~1); }
-
 // Column-sum table floats for `kp` elements and `ncol` columns.
-inline size_t tab_floats(int fmt, int64_t kp, int ncol, int ncol8) {
+inline size_t tab_floats(int fmt, int64_t kp, int ncol) {
   const FmtInfo f = fmt_info(fmt);
-  if (fmt == FMT_FP8) return 0;
-  if (is_diag(fmt)) return (size_t)(kp / f.gk) * (size_t)ncol * (size_t)(f.gk / f.sbe + 4);
-  return (size_t)(kp / f.sbe) * (size_t)ncol8;
+  return (size_t)(kp / f.gk) * (size_t)ncol * (size_t)(f.gk / f.sbe + 4);
 }
 
 // Shared-memory plan of one GEMV launch.  local_kp > 0 asks for the local-x region
 // (activations staged by every CTA).
+//   per warp : NS ring slots (weights [+ x units + table rows when not local]),
+//              a 128-byte epilogue scratch, NS mbarriers
+//   per CTA  : the double-buffered split-mode reduction, the token scales, the zero
+//              page, and (local) the staged rows, amax scratch, x barrier, table
 Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref, int64_t local_kp = 0) {
   const FmtInfo f = fmt_info(fmt);
   const int csb = col_stride_bytes(f.gk);
-  const bool local = local_kp > 0, diag = is_diag(fmt);
+  const bool local = local_kp > 0;
   Plan p{};
   const size_t off_x = align_up((size_t)IG * f.gb, 128);
   const size_t off_tab = align_up(off_x + (local ? 0 : (size_t)IG * ncol * csb), 16);
-  const size_t slot = align_up(off_tab + (local ? 0 : tab_floats(fmt, (int64_t)IG * f.gk, ncol, ncol8) * 4), 128);
+  const size_t slot = align_up(off_tab + (local ? 0 : tab_floats(fmt, (int64_t)IG * f.gk, ncol) * 4), 128);
   const size_t red = (size_t)2 * kWarps * 16 * ncol8 * 4 + 32 * 4;
-  const size_t zero = diag ? (size_t)kZeroPage : 0;
   size_t loc = 0;
   if (local) {
-    int xcs = (int)align_up((size_t)local_kp * 2, diag ? 128 : 16);
-    if (!diag && xcs % 128 == 0) xcs += 64;  // columns of the B tile on alternating bank halves
-    p.xcs = xcs;
-    loc = 128 + (size_t)ncol * xcs + (size_t)32 * kWarps * 4 + 16 + tab_floats(fmt, local_kp, ncol, 0) * 4;
-    if (!diag) loc = 128 + (size_t)ncol * xcs + (size_t)32 * kWarps * 4 + 16 +
-                     (size_t)(local_kp / f.sbe) * local_tstride(ncol) * 4;
+    p.xcs = (int)align_up((size_t)local_kp * 2, 128);
+    loc = 128 + (size_t)ncol * p.xcs + (size_t)32 * kWarps * 4 + 16 + tab_floats(fmt, local_kp, ncol) * 4;
   }
   // prefer two CTAs per SM (<= 113 KB each); keep at least two stages in flight
   int NS = ns_pref;
   auto warp_bytes = [&](int ns) { return align_up(ns * slot + kTblBytes + kMaxStages * 8, 128); };
-  while (NS > 2 && warp_bytes(NS) * kWarps + red + loc + zero + 128 > 113 * 1024) --NS;
+  while (NS > 2 && warp_bytes(NS) * kWarps + red + kZeroPage + 128 + loc > 113 * 1024) --NS;
   p.NS = NS;
   p.slot_bytes = (int)slot;
   p.off_x = (int)off_x;
@@ -1326,23 +1099,21 @@ Plan make_plan(int fmt, int IG, int ncol, int ncol8, int ns_pref, int64_t local_
   p.warp_bytes = (int)warp_bytes(NS);
   p.off_red = (int)((size_t)p.warp_bytes * kWarps);
   size_t end = (size_t)p.off_red + red;
-  if (diag) {
-    p.off_zero = (int)align_up(end, 128);
-    end = (size_t)p.off_zero + zero;
-  }
+  p.off_zero = (int)align_up(end, 128);
+  end = (size_t)p.off_zero + kZeroPage;
   if (local) {
     p.off_xloc = (int)align_up(end, 128);
     p.off_tabloc = (int)align_up((size_t)p.off_xloc + (size_t)ncol * p.xcs, 16) + 32 * kWarps * 4 + 16;
-    end = (size_t)p.off_tabloc +
-          (diag ? tab_floats(fmt, local_kp, ncol, 0) : (size_t)(local_kp / f.sbe) * local_tstride(ncol)) * 4;
+    end = (size_t)p.off_tabloc + tab_floats(fmt, local_kp, ncol) * 4;
   }
   p.smem = align_up(end, 16);
   return p;
 }
 
 // Groups per item (one bulk copy): two 256-wide Q4_K groups when a row has enough of
-// them, one Q6_K group (two would halve the CTAs per SM); for Q8_0 (128-wide) and
-// FP8 (32-wide) the largest candidate that still spreads a tile evenly over the warps.
+// them, one Q6_K group (two would halve the CTAs per SM); for the 128-wide Q8_0 and
+// FP8 groups the largest candidate up to ~6 KB that still spreads a tile evenly over
+// the warps.
 int items_group(int fmt, int64_t G) {
   static const int env_ig = [] {  // tuning override: RTD_GEMV_IG=1|2|4|8
     const char* s = std::getenv("RTD_GEMV_IG");
@@ -1352,11 +1123,13 @@ int items_group(int fmt, int64_t G) {
   if (env_ig) return (int)std::min<int64_t>(env_ig, std::max<int64_t>(1, G / kWarps));
   if (fmt == FMT_Q4K) return G >= 2 * kWarps ? 2 : 1;
   if (fmt == FMT_Q6K) return 1;
+  // items of at most ~6 KB keep a two-stage ring of 8 warps within shared memory
+  const int cap = std::max(1, 6144 / fmt_info(fmt).gb);
   int best = 1;
   double best_eff = 0.0;
   const int cands[4] = {8, 4, 2, 1};
   for (int ig : cands) {
-    if (fmt == FMT_Q80 && ig > 4) continue;
+    if (ig > cap) continue;
     const int64_t ci = (G + ig - 1) / ig;
     const double eff = (double)G / ((double)ig * kWarps * ((ci + kWarps - 1) / kWarps));
     if (eff >= 0.85) return ig;
@@ -1434,21 +1207,6 @@ cudaError_t launch_gemv_nt(const Args& a, int NT, unsigned nctas, size_t smem, c
 }
 
 template <int FMT>
-cudaError_t launch_prep(const PrepArgs& p, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.M * kPrepCluster));
-  cfg.blockDim = dim3(kPrepThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prep_kernel<FMT>, p);
-}
-
-template <int FMT>
 cudaError_t launch_prep_diag(const PrepArgs& p, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((p.kp / 8 + kPrepThreads - 1) / kPrepThreads), (unsigned)p.M);
@@ -1499,9 +1257,8 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   const int IG = items_group(c.fmt, G);
   const int64_t CI = (G + IG - 1) / IG;
   const int P = (c.x_dtype == 0 && !c.w8a8) ? 2 : 1;
-  const bool diag = is_diag(c.fmt);
-  // DIAG decoders run one MMA chain per activation column: at most 4 columns a launch
-  const int max_tokens = (diag ? 4 : 32) / P;
+  // the decoders run one MMA chain per activation column: at most 4 columns a launch
+  const int max_tokens = 4 / P;
   static const int env_ns = [] {
     const char* s = std::getenv("RTD_GEMV_STAGES");
     const int v = s ? std::atoi(s) : 0;
@@ -1521,24 +1278,23 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     while (Mt > 1 && make_plan(c.fmt, IG, Mt * P, 8 * ((Mt * P + 7) / 8), env_ns).smem > 220 * 1024)
       Mt = (Mt + 1) / 2;
     const int ncol = Mt * P;
-    // template width: activation columns (DIAG) or 8-column MMA tiles (FP8)
-    const int NT = diag ? ncol : (ncol + 7) / 8;
-    const int ncol8 = 8 * ((ncol + 7) / 8);
+    const int NT = ncol;  // template width: activation columns of this launch
+    const int ncol8 = 8;  // row stride of the split-mode reduction buffer
     // bf16 / f16 activations whose rows are bulk-copyable: every CTA stages x itself
     // (no prep kernel) when the staged rows and sums stay small.
-    const size_t local_tab = diag ? tab_floats(c.fmt, kp, ncol, 0) : (size_t)(kp / f.sbe) * local_tstride(ncol);
-    const bool local_ok = P == 1 && x_vec && (c.K % 8 == 0) && !env_no_local &&
+    const size_t local_tab = tab_floats(c.fmt, kp, ncol);
+    const bool local_ok = c.x_dtype != 0 && x_vec && (c.K % 8 == 0) && !env_no_local &&
                           (size_t)ncol * kp * 2 + local_tab * 4 <= 40 * 1024;
     const Plan pl = make_plan(c.fmt, IG, ncol, ncol8, env_ns, local_ok ? kp : 0);
     const int occ = occupancy_of(c.fmt, NT, pl.smem);
     const int64_t slots = (int64_t)c.sm_count * occ;
     // Enough tiles for every warp to own at least two whole ones: no cross-warp
     // reduction at all.  Otherwise the warps of a CTA split each tile's groups.
-    const bool whole = T >= 2 * slots * kWarps;
+    const bool whole = !c.tp && T >= 2 * slots * kWarps;  // the row-parallel exchange runs in split mode
     const int nctas = (int)(whole ? slots : std::min<int64_t>(T, slots));
     // workspace carve: cols | tab | tscale
     const size_t cols_b = align_up((size_t)G * ncol * col_stride_bytes(f.gk), 256);
-    const size_t tab_b = align_up(tab_floats(c.fmt, kp, ncol, ncol8) * 4 + 4, 256);
+    const size_t tab_b = align_up(tab_floats(c.fmt, kp, ncol) * 4 + 4, 256);
     if (cols_b + tab_b + 256 > c.ws_bytes) {
       *plan_error = 1;
       return cudaSuccess;
@@ -1569,7 +1325,7 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
         case FMT_Q4K: e = launch_prep_diag<FMT_Q4K>(pa, c.stream); break;
         case FMT_Q6K: e = launch_prep_diag<FMT_Q6K>(pa, c.stream); break;
         case FMT_Q80: e = launch_prep_diag<FMT_Q80>(pa, c.stream); break;
-        default:      e = launch_prep<FMT_FP8>(pa, c.stream); break;
+        default:      e = launch_prep_diag<FMT_FP8>(pa, c.stream); break;
       }
       if (e != cudaSuccess) return e;
     }
@@ -1615,9 +1371,27 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_xloc = pl.off_xloc;
     a.xcs = pl.xcs;
     a.off_tabloc = pl.off_tabloc;
-    a.tstride = local_ok ? local_tstride(ncol) : ncol8;
-    a.tabw = diag ? ncol * (f.gk / f.sbe + 4) : (f.gk / f.sbe) * ncol8;
+    a.tabw = ncol * (f.gk / f.sbe + 4);
     a.off_zero = pl.off_zero;
+    a.tp_world = 1;
+    if (c.tp && c.tp->world > 1) {
+      const TpReduce& tp = *c.tp;
+      if (c.N > tp.max_n || T > tp.max_tiles || Mt > 4) {
+        *plan_error = 1;
+        return cudaSuccess;
+      }
+      const uint32_t epoch = ++*tp.epoch;
+      const int par = (int)(epoch & 1u);
+      a.tp_world = tp.world;
+      a.tp_rank = tp.rank;
+      a.tp_max_n = tp.max_n;
+      a.tp_max_tiles = tp.max_tiles;
+      a.tp_epoch = epoch;
+      for (int p = 0; p < tp.world; ++p) {
+        a.tp_recv[p] = tp.recv[p] + (size_t)par * tp.world * 4 * tp.max_n;
+        a.tp_flags[p] = tp.flags[p] + (size_t)par * tp.world * tp.max_tiles;
+      }
+    }
     a.status = c.status;
     switch (c.fmt) {
       case FMT_Q4K: e = launch_gemv_nt<FMT_Q4K>(a, NT, (unsigned)nctas, pl.smem, c.stream); break;

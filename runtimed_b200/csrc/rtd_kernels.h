@@ -18,6 +18,19 @@ cudaError_t launch_embed(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_
 cudaError_t launch_fp8_encode(const float* x, int64_t n, uint8_t* out, cudaStream_t st);
 
 // Decode GEMV / skinny GEMM: y[M, N] = x[M, K] . W^T (+ bias), W in the group layout.
+constexpr int kMaxTpWorld = 8;
+
+// Tensor-parallel row reduction attached to one GEMV: every rank computes the
+// partial y of its K shard; each tile's partial goes to every rank's receive slot
+// over NVLink, and each rank writes the tile once all partials have arrived.
+struct TpReduce {
+  int world, rank;
+  float* recv[kMaxTpWorld];      // rank p's receive region [2 parities][world][4 * max_n] f32
+  uint32_t* flags[kMaxTpWorld];  // rank p's arrival flags [2 parities][world][max_tiles]
+  int64_t max_n, max_tiles;
+  uint32_t* epoch;               // host counter, advanced once per launch (all ranks in step)
+};
+
 struct QGemvCall {
   int fmt;
   const uint8_t* w;
@@ -33,13 +46,14 @@ struct QGemvCall {
   void* y;
   int y_dtype;
   int64_t ldy;
-  float* ws;               // split-K partials (context workspace)
+  float* ws;               // activation staging workspace (prep-mode calls)
   size_t ws_bytes;
-  uint32_t* counters;      // per-tile arrival counters, all zero between calls
+  uint32_t* counters;      // unused by the current kernels
   int64_t n_counters;
   int* status;             // device status word
   int sm_count;
   cudaStream_t stream;
+  const TpReduce* tp;      // null, or the row-parallel reduction of this call
 };
 
 // Returns cudaSuccess or the launch error; *plan_error is set (non-zero) when the

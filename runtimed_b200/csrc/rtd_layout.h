@@ -34,8 +34,9 @@
 //                         [qs: pass(4) x lane(32) x 16 B]
 //         lane t owns block t of the group (32 int8); passes as for Q4_K.
 //         K is a multiple of 32; a trailing partial group is zero-filled.
-//   FP8   GK=32  GB=512:  [lane(32) x 16 B, row g bytes 8t..8t+7 ++ row g+8]
-//         (bytes 1 and 2 of every 4-byte word swapped).
+//   FP8   GK=128 GB=2048: [codes: pass(4) x lane(32) x 16 B]
+//         lane t owns the 32 E4M3 codes k = 32t..32t+31 of the group; passes as
+//         for Q4_K.  The per-row scales live in a separate f32 array.
 //
 // Q6_K code triples.  The 6-bit code of element e of a superblock row is
 // (ql nibble | 2 qh bits << 4), dequant_k.rs:87-111.  The 16 codes c0..c15 of one
@@ -72,7 +73,7 @@ RTD_HD inline FmtInfo fmt_info(int fmt) {
     case FMT_Q4K: return FmtInfo{256, 2304, 32, 256, 144};
     case FMT_Q6K: return FmtInfo{256, 3360, 16, 256, 210};
     case FMT_Q80: return FmtInfo{128, 2176, 32, 32, 34};
-    default:      return FmtInfo{32, 512, 32, 1, 1};
+    default:      return FmtInfo{128, 2048, 32, 1, 1};
   }
 }
 

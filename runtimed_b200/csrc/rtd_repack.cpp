@@ -1,7 +1,8 @@
 // rtd_repack.cpp -- host re-tiling of GGUF / E4M3 weight bytes into the device
 // group layout described in rtd_layout.h.  A pure permutation of bytes (Q4_K,
 // Q8_0, FP8) or of 6-bit codes (Q6_K): no value changes, so the device decoders
-// reproduce the reference dequantization bit for bit.
+// reproduce the reference dequantization bit for bit.  Padding (rows past N, k
+// past K) is zero bytes.
 #include <cstring>
 #include <vector>
 
@@ -26,17 +27,6 @@ inline uint32_t q6k_code(const uint8_t* blk, int e) {
 // the pair (c0, c1) and ((w >> 6) & 0x003F003F) the pair (c2, c3).
 inline uint32_t pack4(const uint32_t c[4]) {
   return c[0] | (c[1] << 16) | (c[2] << 6) | (c[3] << 22);
-}
-
-// Copy 8 bytes swapping bytes 1 and 2 of each 4-byte word, so that the halves
-// of a 16-bit pair extraction are two consecutive elements (FP8 groups).
-inline void copy8_swapped(uint8_t* dst, const uint8_t* src) {
-  for (int w = 0; w < 2; ++w) {
-    dst[4 * w + 0] = src[4 * w + 0];
-    dst[4 * w + 1] = src[4 * w + 2];
-    dst[4 * w + 2] = src[4 * w + 1];
-    dst[4 * w + 3] = src[4 * w + 3];
-  }
 }
 
 }  // namespace
@@ -85,16 +75,14 @@ void repack_host(int fmt, const uint8_t* raw, int64_t N, int64_t K, uint8_t* out
         }
       } else if (fmt == FMT_FP8) {
         for (int lane = 0; lane < 32; ++lane) {
-          int g = lane >> 2, tg = lane & 3;
-          uint8_t* v = grp + lane * 16;
-          for (int half = 0; half < 2; ++half) {
-            int64_t n = t * 16 + g + 8 * half;
-            uint8_t nat[8];
-            for (int i = 0; i < 8; ++i) {
-              int64_t k = s * 32 + 8 * tg + i;
-              nat[i] = (n < N && k < K) ? raw[(size_t)n * row_bytes + (size_t)k] : 0;
+          const int g = lane >> 2, tg = lane & 3;
+          for (int p = 0; p < 4; ++p) {
+            const int64_t n = t * 16 + g + 8 * (p >> 1);
+            uint8_t* v = grp + p * 512 + lane * 16;
+            for (int i = 0; i < 16; ++i) {
+              const int64_t k = s * 128 + 32 * tg + 16 * (p & 1) + i;
+              v[i] = (n < N && k < K) ? raw[(size_t)n * row_bytes + (size_t)k] : 0;
             }
-            copy8_swapped(v + 8 * half, nat);
           }
         }
       } else {  // FMT_Q6K

@@ -1,0 +1,190 @@
+"""Tensor-parallel quantized linears (one process per GPU).
+
+Mirrors the reference's Megatron-style layers:
+
+- `ColumnParallelLinear`: crates/runtimed-model/src/tp/column_linear.rs:20-61. It splits
+  the N output rows, so every rank holds whole GGUF rows and no data is re-quantized.
+  Its forward needs no exchange.
+- `RowParallelLinear`: crates/runtimed-model/src/tp/row_linear.rs:20-66. It splits K on
+  superblock boundaries. The reduction that the reference runs as a separate
+  `ring_all_reduce` (crates/runtimed-model/src/tp/ring_reduce.rs:7-65) is fused into
+  the GEMV epilogue here (`rtd_tp_qlinear_row`): tile partials cross NVLink as peer
+  stores, and every rank writes the full y.
+
+`forward_nccl` computes the same result with an NCCL all-reduce, as the measured
+comparison. The shard helpers work on raw GGUF bytes and are plain numpy, so the host
+side can be tested without a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from .errors import ConfigError, ShapeError
+
+BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210)}  # ggml type -> (elements, bytes)
+
+
+def _geometry(ggml_type: int):
+    if ggml_type not in BLOCK:
+        raise ConfigError(f"ggml type {ggml_type} has no tensor-parallel shard layout")
+    return BLOCK[ggml_type]
+
+
+def shard_rows(raw, ggml_type: int, n: int, k: int, rank: int, world: int) -> np.ndarray:
+    """Bytes of output rows [rank*n/world, (rank+1)*n/world) (column-parallel shard)."""
+    if world == 0:
+        raise ConfigError("TP size cannot be zero")
+    if n % world:
+        raise ConfigError(f"Output dimension {n} not divisible by TP size {world}")
+    elems, bb = _geometry(ggml_type)
+    row = (k // elems) * bb
+    raw = np.asarray(raw, dtype=np.uint8).reshape(-1)
+    if raw.size != n * row:
+        raise ShapeError("tp_weight", [n * row], [raw.size])
+    rows = n // world
+    return raw[rank * rows * row:(rank + 1) * rows * row].copy()
+
+
+def shard_cols(raw, ggml_type: int, n: int, k: int, rank: int, world: int) -> np.ndarray:
+    """Bytes of input columns [rank*k/world, (rank+1)*k/world) of every row (row-parallel
+    shard).  The split must fall on superblock boundaries."""
+    if world == 0:
+        raise ConfigError("TP size cannot be zero")
+    if k % world:
+        raise ConfigError(f"Input dimension {k} not divisible by TP size {world}")
+    elems, bb = _geometry(ggml_type)
+    ks = k // world
+    if ks % elems:
+        raise ConfigError(f"Input shard {ks} is not a multiple of the {elems}-element block")
+    raw = np.asarray(raw, dtype=np.uint8).reshape(-1)
+    nb = k // elems
+    if raw.size != n * nb * bb:
+        raise ShapeError("tp_weight", [n * nb * bb], [raw.size])
+    blocks = raw.reshape(n, nb, bb)
+    per = ks // elems
+    return np.ascontiguousarray(blocks[:, rank * per:(rank + 1) * per, :]).reshape(-1)
+
+
+class TpComm:
+    """Row-reduction communicator of one rank: `rtd_tp_comm_create` on every rank, the
+    IPC handles gathered over torch.distributed (rank order), then `rtd_tp_comm_open`."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, ctx, rank: int, world: int, max_n: int, group=None):
+        import torch.distributed as dist
+
+        self.ctx, self.rank, self.world, self.max_n = ctx, rank, world, int(max_n)
+        L = _lib.lib()
+        self.handle = ctypes.c_void_p()
+        h = (ctypes.c_ubyte * self.HANDLE_BYTES)()
+        _lib.check(L.rtd_tp_comm_create(ctx.handle, rank, world, self.max_n, ctypes.byref(self.handle), h),
+                   ctx.handle)
+        mine = bytes(h)
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        allh = (ctypes.c_ubyte * (self.HANDLE_BYTES * world)).from_buffer_copy(b"".join(everyone))
+        _lib.check(L.rtd_tp_comm_open(self.handle, allh), ctx.handle)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            _lib.lib().rtd_tp_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class ColumnParallelLinear:
+    """Output rows split across ranks; y_rank = x . W_rank^T + b_rank."""
+
+    def __init__(self, weight, bias, rank: int, tp_size: int):
+        self.weight, self.bias, self.rank, self.tp_size = weight, bias, rank, tp_size
+
+    @classmethod
+    def from_full_weight(cls, raw, ggml_type: int, n: int, k: int, full_bias, rank: int, tp_size: int,
+                         device="cuda:0") -> "ColumnParallelLinear":
+        from .weights import QMatMul
+
+        shard = shard_rows(raw, ggml_type, n, k, rank, tp_size)
+        rows = n // tp_size
+        qm = QMatMul(ggml_type, shard, rows, k, device=device)
+        bias = None
+        if full_bias is not None:
+            import torch
+
+            b = torch.as_tensor(np.asarray(full_bias, dtype=np.float32))
+            bias = b[rank * rows:(rank + 1) * rows].contiguous().to(qm.device)
+        return cls(qm, bias, rank, tp_size)
+
+    def forward(self, x):
+        return self.weight.forward(x, bias=self.bias)
+
+
+class RowParallelLinear:
+    """Input columns split across ranks.  With a communicator, forward returns the
+    full reduced y on every rank (bias added once); without one it returns the rank's
+    partial with the bias on rank 0 only, as the reference does."""
+
+    def __init__(self, weight, bias, rank: int, tp_size: int, comm: Optional[TpComm] = None):
+        self.weight, self.bias, self.rank, self.tp_size, self.comm = weight, bias, rank, tp_size, comm
+
+    @classmethod
+    def from_full_weight(cls, raw, ggml_type: int, n: int, k: int, full_bias, rank: int, tp_size: int,
+                         comm: Optional[TpComm] = None, device="cuda:0") -> "RowParallelLinear":
+        from .weights import QMatMul
+
+        shard = shard_cols(raw, ggml_type, n, k, rank, tp_size)
+        qm = QMatMul(ggml_type, shard, n, k // tp_size, device=device)
+        bias = None
+        if full_bias is not None:
+            import torch
+
+            bias = torch.as_tensor(np.asarray(full_bias, dtype=np.float32)).contiguous().to(qm.device)
+        return cls(qm, bias, rank, tp_size, comm)
+
+    def _flat(self, x):
+        import torch
+
+        if x.shape[-1] != self.weight.k:
+            raise ShapeError("row_parallel_linear", [self.weight.k], list(x.shape))
+        m = 1
+        for d in x.shape[:-1]:
+            m *= int(d)
+        return x.reshape(m, self.weight.k).contiguous().to(self.weight.device), m
+
+    def forward(self, x):
+        import torch
+        from .weights import _DT, _stream_ptr
+
+        if self.comm is None or self.tp_size == 1:
+            b = self.bias if (self.rank == 0 or self.tp_size == 1) else None
+            return self.weight.forward(x, bias=b)
+        x2, m = self._flat(x)
+        if x2.dtype not in _DT:
+            x2 = x2.to(torch.float32)
+        y = torch.empty((m, self.weight.n), dtype=x2.dtype, device=self.weight.device)
+        bp = None if self.bias is None else self.bias.data_ptr()
+        st = _lib.lib().rtd_tp_qlinear_row(self.comm.handle, self.weight.handle, x2.data_ptr(), _DT[x2.dtype],
+                                           self.weight.k, m, bp, y.data_ptr(), _DT[y.dtype], self.weight.n,
+                                           _stream_ptr(self.weight.device))
+        _lib.check(st, self.weight.ctx.handle)
+        return y.reshape(*x.shape[:-1], self.weight.n)
+
+    def forward_nccl(self, x, group=None):
+        """The comparison path: local partial GEMV, then an NCCL all-reduce."""
+        import torch
+        import torch.distributed as dist
+
+        y = self.weight.forward(x, out_dtype=torch.float32)
+        dist.all_reduce(y, group=group)
+        if self.bias is not None:
+            y = y + self.bias
+        return y.to(x.dtype) if x.dtype in (torch.float16, torch.bfloat16) else y

@@ -1,0 +1,111 @@
+"""Row-parallel quantized linear with the all-reduce fused into the GEMV epilogue,
+on two GPUs (one process each, NCCL for set-up only), against the unsharded CPU
+oracle and against the NCCL all-reduce comparison path.
+
+Skipped with fewer than two GPUs.  NVLS is switched off and the kernel's peer
+traffic is plain stores, so a rank that leaves early cannot fault the others; the
+timeout case makes one rank skip a call and checks that the other finishes with
+RTD_ERR_PEER_TIMEOUT instead of waiting.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL_EXACT = 2e-5
+
+
+def _rel(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-300))
+
+
+def _rank_main(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.errors import ConfigError
+    from runtimed_b200.tp import RowParallelLinear, TpComm
+    from runtimed_b200.weights import Context
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    out = {}
+    try:
+        ctx = Context.for_device(dev)
+        comm = TpComm(ctx, rank, world, max_n=4096)
+        for t, n, k in [(12, 4096, 2048), (14, 1000, 1024), (8, 2056, 512)]:
+            raw = synth.quant_matrix(t, n, k, seed=5, stream=t)
+            bias = np.random.default_rng(t).normal(0, 0.02, n).astype(np.float32)
+            rpl = RowParallelLinear.from_full_weight(raw, t, n, k, bias, rank, world, comm=comm, device=dev)
+            ks = k // world
+            for call, (m, dt) in enumerate([(1, torch.bfloat16), (3, torch.float32), (4, torch.float16), (1, torch.bfloat16)]):
+                x = synth.activations(m, k, seed=100 * t + call)
+                xt = torch.from_numpy(x).to(dt)
+                want = oracle.qgemv_f64(t, raw, n, k, xt.float().numpy()) + bias[None, :]
+                xs = xt[:, rank * ks:(rank + 1) * ks].contiguous().to(dev)
+                y = rpl.forward(xs).float()
+                yn = rpl.forward_nccl(xs).float()
+                torch.cuda.synchronize()
+                ctx.check_device_status()
+                gathered = [torch.empty_like(y) for _ in range(world)]
+                dist.all_gather(gathered, y)
+                tol = RTOL_EXACT if dt != torch.float16 else 1e-3  # f16 output rounding
+                out[(t, call)] = (_rel(y.cpu().numpy(), want) <= tol,
+                                  _rel(yn.cpu().numpy(), want) <= max(tol, 1e-3 if dt != torch.float32 else tol),
+                                  all(bool(torch.equal(g, gathered[0])) for g in gathered))
+        # a rank that skips a call: the other finishes with RTD_ERR_PEER_TIMEOUT
+        raw = synth.quant_matrix(12, 16, 512, seed=1)
+        rpl = RowParallelLinear.from_full_weight(raw, 12, 16, 512, None, rank, world, comm=comm, device=dev)
+        dist.barrier()
+        timed_out = None
+        if rank == 0:
+            xs = torch.zeros((1, 256), dtype=torch.bfloat16, device=dev)
+            rpl.forward(xs)
+            torch.cuda.synchronize()
+            try:
+                ctx.check_device_status()
+                timed_out = False
+            except ConfigError as e:
+                timed_out = f"status {_lib.RTD_ERR_PEER_TIMEOUT}" in str(e)
+        dist.barrier()
+        out["timeout"] = timed_out
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+    q.put((rank, out))
+
+
+def test_row_parallel_fused_allreduce_two_gpus():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank, out in res.items():
+        for key, (fused_ok, nccl_ok, same) in ((k, v) for k, v in out.items() if k != "timeout"):
+            assert fused_ok, (rank, key, "fused")
+            assert nccl_ok, (rank, key, "nccl")
+            assert same, (rank, key, "ranks differ")
+    assert res[0]["timeout"] is True

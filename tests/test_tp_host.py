@@ -1,0 +1,107 @@
+"""Host-side tensor-parallel logic on the CPU: the shard byte layouts, the
+reference's divisibility errors, and a two-rank gloo run of the row-parallel
+reduction (restated oracle partials summed by all_reduce) against the unsharded GEMV.
+
+Reference: crates/runtimed-model/src/tp/{column_linear,row_linear,mod}.rs
+(the mod.rs:18-34 test checks that column shards concatenate to the full output).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from runtimed_b200 import synth
+from runtimed_b200.errors import ConfigError
+from runtimed_b200.tp import shard_cols, shard_rows
+
+
+def _dequant(t, raw, n, k):
+    rc, y = oracle.dequant_tensor(t, raw, n * k)
+    assert rc == oracle.OK
+    return y.reshape(n, k)
+
+
+@pytest.mark.parametrize("t", [12, 14, 8])
+@pytest.mark.parametrize("world", [2, 4])
+def test_shards_are_exact_slices(t, world):
+    n, k = 32, 2048
+    raw = synth.quant_matrix(t, n, k, seed=3, stream=t)
+    full = _dequant(t, raw, n, k)
+    for r in range(world):
+        rows = _dequant(t, shard_rows(raw, t, n, k, r, world), n // world, k)
+        assert np.array_equal(rows.view(np.uint32), full[r * n // world:(r + 1) * n // world].view(np.uint32))
+        cols = _dequant(t, shard_cols(raw, t, n, k, r, world), n, k // world)
+        assert np.array_equal(cols.view(np.uint32), full[:, r * k // world:(r + 1) * k // world].view(np.uint32))
+
+
+def test_column_and_row_parallel_recombine():
+    """Column shards concatenate to the full output; row-shard partials sum to it."""
+    t, n, k, world = 12, 48, 1024, 4
+    raw = synth.quant_matrix(t, n, k, seed=9)
+    x = synth.activations(3, k, seed=9)
+    full = oracle.qgemv_f64(t, raw, n, k, x)
+    cat = np.concatenate([oracle.qgemv_f64(t, shard_rows(raw, t, n, k, r, world), n // world, k, x)
+                          for r in range(world)], axis=1)
+    assert np.allclose(cat, full, rtol=0, atol=1e-12)
+    ks = k // world
+    part = sum(oracle.qgemv_f64(t, shard_cols(raw, t, n, k, r, world), n, ks, x[:, r * ks:(r + 1) * ks])
+               for r in range(world))
+    assert np.allclose(part, full, rtol=1e-12, atol=1e-12)
+
+
+def test_reference_divisibility_errors():
+    raw = synth.quant_matrix(12, 6, 512, seed=1)
+    with pytest.raises(ConfigError, match="TP size cannot be zero"):
+        shard_rows(raw, 12, 6, 512, 0, 0)
+    with pytest.raises(ConfigError, match="Output dimension 6 not divisible by TP size 4"):
+        shard_rows(raw, 12, 6, 512, 0, 4)
+    with pytest.raises(ConfigError, match="Input dimension 512 not divisible by TP size 3"):
+        shard_cols(raw, 12, 6, 512, 0, 3)
+    with pytest.raises(ConfigError, match="not a multiple of the 256-element block"):
+        shard_cols(raw, 12, 6, 512, 0, 4)  # 128-element shards split a Q4_K superblock
+
+
+def _gloo_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        t, n, k = 14, 40, 1024
+        raw = synth.quant_matrix(t, n, k, seed=21)
+        x = synth.activations(2, k, seed=21)
+        ks = k // world
+        part = oracle.qgemv_f64(t, shard_cols(raw, t, n, k, rank, world), n, ks, x[:, rank * ks:(rank + 1) * ks])
+        y = torch.from_numpy(part)
+        dist.all_reduce(y)
+        # the communicator's handle exchange: every rank receives every rank's bytes in rank order
+        got = [None] * world
+        dist.all_gather_object(got, bytes([rank]) * 64)
+        ok_handles = got == [bytes([r]) * 64 for r in range(world)]
+        full = oracle.qgemv_f64(t, raw, n, k, x)
+        q.put((rank, bool(np.allclose(y.numpy(), full, rtol=1e-12, atol=1e-12)), ok_handles))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_reduction_over_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(r for r, _, _ in res) == [0, 1]
+    assert all(ok and hok for _, ok, hok in res)
