@@ -152,6 +152,24 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
                               int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
                               void* stream);
 
+/* ---- allocation-free linear -------------------------------------------------
+ * No counterpart in the reference: an addition for callers that must not allocate
+ * device memory while they run (e.g. code working under another allocator's fixed
+ * device-memory budget, where a cudaMalloc can fail or stall the device).
+ * Same contract and kernels as rtd_qlinear, but no context argument: the scratch is a
+ * fixed 1 MiB array per device inside the library (256 B status word + workspace);
+ * the call allocates nothing and calls no allocating routine.
+ *   - The first call on a device looks the array up (cudaGetSymbolAddress) with that
+ *     device current; make that first call before any stream capture.
+ *   - A call whose staging would exceed the scratch returns RTD_ERR_WORKSPACE and
+ *     launches nothing (bf16 / f16 rows up to K = 16384 stage on chip and need
+ *     no scratch beyond their small carve; f32 rows need about 4*K*M bytes).
+ *   - Every call shares the one array and clears its status word first: calls
+ *     that overlap on the GPU race, so issue them on one stream (or serialise them).
+ *   - Errors are recorded on the calling thread: read them with rtd_last_error(NULL). */
+rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx, int64_t M,
+                               const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

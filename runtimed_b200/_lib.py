@@ -44,6 +44,7 @@ SIGNATURES = {
     "rtd_qweight_info": (_c.c_int32, [_vp, _c.POINTER(_u32), _c.POINTER(_i64), _c.POINTER(_i64),
                                       _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
     "rtd_qlinear": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
+    "rtd_qlinear_noalloc": (_c.c_int32, [_vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
     "rtd_tp_comm_create": (_c.c_int32, [_vp, _c.c_int, _c.c_int, _i64, _vp, _vp]),
     "rtd_tp_comm_open": (_c.c_int32, [_vp, _vp]),
     "rtd_tp_comm_destroy": (_c.c_int32, [_vp]),

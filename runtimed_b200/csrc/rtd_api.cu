@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -534,5 +535,109 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
   if (plan_err) return fail(ctx, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the workspace", who,
                             (long long)shard->N, (long long)shard->K);
   if (e != cudaSuccess) return cuda_fail(ctx, e, who);
+  return RTD_OK;
+}
+
+// ---- allocation-free quantized linear ---------------------------------------
+//
+// For callers that must not allocate device memory while they run -- for example
+// code that executes inside a host framework whose caching allocator owns the
+// device's memory budget, where an extra cudaMalloc can fail or stall every stream
+// on the device.  rtd_qlinear_noalloc runs the same kernels as rtd_qlinear but
+// takes its scratch (the activation staging of prep-mode calls and the device
+// status word) from the fixed array below instead of a context workspace.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device, fixed at build time
+constexpr size_t kNoAllocStatusBytes = 256;        // the status word, then the GEMV workspace
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int sm_count = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// Once per device, with that device current: look up the array's device address.
+rtd_status noalloc_setup(int dev, NoAllocDevice** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "rtd_qlinear_noalloc: cudaGetSymbolAddress");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "rtd_qlinear_noalloc: cudaDeviceGetAttribute");
+    d.scratch = static_cast<unsigned char*>(p);
+    d.sm_count = sms;
+    d.ready = true;
+  }
+  *out = &d;
+  return RTD_OK;
+}
+
+}  // namespace
+
+rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx, int64_t M,
+                               const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
+  const char* who = "rtd_qlinear_noalloc";
+  if (!w || !w->ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: NULL weight", who);
+  if (M < 0) return fail(nullptr, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(nullptr, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (M == 0 || w->N == 0) return RTD_OK;
+  if ((w->K > 0 && !x) || !y) return fail(nullptr, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if (ldx < w->K || ldy < w->N)
+    return fail(nullptr, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who,
+                (long long)ldx, (long long)ldy, (long long)w->K, (long long)w->N);
+  const int dev = w->ctx->device;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(nullptr, RTD_ERR_INVALID, "%s: device %d out of range", who, dev);
+  DeviceGuard g(dev);
+  if (g.err != cudaSuccess) return cuda_fail(nullptr, g.err, who);
+  NoAllocDevice* d = nullptr;
+  rtd_status st = noalloc_setup(dev, &d);
+  if (st != RTD_OK) return st;
+  cudaError_t e;
+  if (w->K == 0) {
+    e = rtd::launch_fill_rows(bias, y, y_dtype, ldy, M, w->N, (cudaStream_t)stream);
+    return e == cudaSuccess ? RTD_OK : cuda_fail(nullptr, e, who);
+  }
+  rtd::QGemvCall c{};
+  c.fmt = w->fmt;
+  c.w = w->dev;
+  c.N = w->N;
+  c.K = w->K;
+  c.G = w->G;
+  c.x = x;
+  c.x_dtype = (int)x_dtype;
+  c.ldx = ldx;
+  c.M = M;
+  c.bias = bias;
+  c.y = y;
+  c.y_dtype = (int)y_dtype;
+  c.ldy = ldy;
+  c.ws = reinterpret_cast<float*>(d->scratch + kNoAllocStatusBytes);
+  c.ws_bytes = kNoAllocScratchBytes - kNoAllocStatusBytes;
+  c.status = reinterpret_cast<int*>(d->scratch);
+  c.sm_count = d->sm_count;
+  c.stream = (cudaStream_t)stream;
+  const size_t need = rtd::qgemv_workspace_bytes(c);
+  if (need > c.ws_bytes)
+    return fail(nullptr, RTD_ERR_WORKSPACE,
+                "%s: [%lld x %lld] at M=%lld needs %zu bytes of scratch; the static scratch holds %zu "
+                "(use rtd_qlinear, or fewer tokens per call)",
+                who, (long long)w->N, (long long)w->K, (long long)M, need, c.ws_bytes);
+  // the status word must start at zero; the workspace is fully rewritten before it is read
+  e = cudaMemsetAsync(d->scratch, 0, sizeof(int), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
+  int plan_err = 0;
+  e = rtd::launch_qgemv(c, &plan_err);
+  if (plan_err) return fail(nullptr, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the static scratch", who,
+                            (long long)w->N, (long long)w->K);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
   return RTD_OK;
 }

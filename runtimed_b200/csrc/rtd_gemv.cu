@@ -1405,4 +1405,33 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
   return cudaSuccess;
 }
 
+// Workspace bytes launch_qgemv carves for this call: the largest of its token chunks,
+// computed with the same chunking and plan (a call whose ws_bytes is at least this
+// never fails with a plan error for lack of workspace).
+size_t qgemv_workspace_bytes(const QGemvCall& c) {
+  if (c.M <= 0 || c.N <= 0 || c.K <= 0) return 0;
+  const FmtInfo f = fmt_info(c.fmt);
+  const int64_t G = c.G;
+  const int64_t kp = G * f.gk;
+  const int IG = items_group(c.fmt, G);
+  const int P = (c.x_dtype == 0 && !c.w8a8) ? 2 : 1;
+  const int max_tokens = 4 / P;
+  const int ns = [] {
+    const char* s = std::getenv("RTD_GEMV_STAGES");
+    const int v = s ? std::atoi(s) : 0;
+    return (v >= 2 && v <= kMaxStages) ? v : kMaxStages;
+  }();
+  size_t need = 0;
+  for (int64_t m0 = 0; m0 < c.M;) {
+    int Mt = (int)std::min<int64_t>(max_tokens, c.M - m0);
+    while (Mt > 1 && make_plan(c.fmt, IG, Mt * P, 8 * ((Mt * P + 7) / 8), ns).smem > 220 * 1024) Mt = (Mt + 1) / 2;
+    const int ncol = Mt * P;
+    const size_t cols_b = align_up((size_t)G * ncol * col_stride_bytes(f.gk), 256);
+    const size_t tab_b = align_up(tab_floats(c.fmt, kp, ncol) * 4 + 4, 256);
+    need = std::max(need, cols_b + tab_b + 256);
+    m0 += Mt;
+  }
+  return need;
+}
+
 }  // namespace rtd

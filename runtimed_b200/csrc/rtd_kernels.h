@@ -59,6 +59,8 @@ struct QGemvCall {
 // Returns cudaSuccess or the launch error; *plan_error is set (non-zero) when the
 // call cannot be planned within the workspace (no launch happens then).
 cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error);
+// Workspace bytes launch_qgemv needs for `c` (its largest token chunk).
+size_t qgemv_workspace_bytes(const QGemvCall& c);
 
 // y[m, n] = bias[n] (or 0) for every row m < M: the K = 0 case of a linear.
 cudaError_t launch_fill_rows(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N,
