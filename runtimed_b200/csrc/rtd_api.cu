@@ -49,7 +49,8 @@ struct rtd_fp8weight {
 
 namespace {
 
-constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging of prep-mode GEMV calls
+constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging (GEMV prep, GEMM tiles)
+constexpr int64_t kGemvMaxTokens = 4;            // tokens one decode-GEMV pass handles
 constexpr int64_t kCounters = 1 << 17;           // per-tile arrival counters
 
 thread_local std::string g_thread_err;
@@ -300,7 +301,12 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
   int plan_err = 0;
-  e = rtd::launch_qgemv(c, &plan_err);
+  // more tokens than the decode GEMV streams per pass go to the tensor-core GEMM
+  // when its staged activations fit the workspace
+  if (M > kGemvMaxTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
+    e = rtd::launch_qgemm(c, &plan_err);
+  else
+    e = rtd::launch_qgemv(c, &plan_err);
   if (plan_err) return fail(ctx, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the context workspace", who, (long long)N, (long long)K);
   if (e != cudaSuccess) return cuda_fail(ctx, e, who);
   return RTD_OK;

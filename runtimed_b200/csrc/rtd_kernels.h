@@ -62,6 +62,11 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error);
 // Workspace bytes launch_qgemv needs for `c` (its largest token chunk).
 size_t qgemv_workspace_bytes(const QGemvCall& c);
 
+// Tensor-core (tcgen05) GEMM for larger token counts; same call description.  The
+// workspace holds the staged activations (qgemm_workspace_bytes).
+cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error);
+size_t qgemm_workspace_bytes(const QGemvCall& c);
+
 // y[m, n] = bias[n] (or 0) for every row m < M: the K = 0 case of a linear.
 cudaError_t launch_fill_rows(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N,
                              cudaStream_t st);

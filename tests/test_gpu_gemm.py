@@ -1,0 +1,93 @@
+"""Tensor-core (tcgen05) GEMM path: calls with more than four tokens.
+
+Weights are decoded in shared memory to f16 (the reference dequantisation formulas
+in f32, rounded once) and multiplied on the 5th-generation tensor cores with f32
+accumulation in tensor memory, so outputs are gated at the north-star relative L2
+of 1e-3 against the f64 oracle.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from runtimed_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+FORMATS = [("Q4_K", 12), ("Q6_K", 14), ("Q8_0", 8)]
+
+
+def rel_l2(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-300))
+
+
+@pytest.mark.parametrize("name,t", FORMATS)
+@pytest.mark.parametrize("M", [5, 16, 64, 200, 512])
+def test_gemm_parity(name, t, M):
+    import torch
+    from runtimed_b200.weights import QMatMul
+
+    N, K = 200, 2048  # N: one full and one partial 128-row CTA tile
+    raw = synth.quant_matrix(t, N, K, seed=M, stream=t)
+    qm = QMatMul(t, raw, N, K)
+    x = synth.bf16_round(synth.activations(M, K, seed=M, stream=3))
+    y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32).cpu().numpy()
+    assert rel_l2(y, oracle.qgemv_f64(t, raw, N, K, x)) <= RTOL
+
+
+@pytest.mark.parametrize("M", [7, 130])
+def test_gemm_fp8_parity(M):
+    import torch
+    from runtimed_b200.weights import Fp8Weight
+
+    N, K = 136, 1000  # ragged K: a zero-padded trailing group
+    w, s = synth.fp8_matrix(N, K, seed=M)
+    fw = Fp8Weight(w, s, K, N)
+    x = synth.activations(M, K, seed=M)
+    for mode, ref in (("w8a16", oracle.fp8_gemm_cpu_f64), ("w8a8", oracle.fp8_gemm_w8a8_f64)):
+        y = fw.forward(torch.from_numpy(x).cuda(), mode=mode).cpu().numpy()
+        assert rel_l2(y, ref(x, w, s, N, K)) <= RTOL, mode
+
+
+def test_gemm_bias_strides_dtypes_and_determinism():
+    import torch
+    from runtimed_b200 import _lib
+    from runtimed_b200.weights import QMatMul
+
+    N, K, M = 300, 1024, 40
+    raw = synth.quant_matrix(12, N, K, seed=2)
+    qm = QMatMul(12, raw, N, K)
+    x = synth.activations(M, K, seed=2)
+    bias = (synth.rng(2, 5).standard_normal(N) * 0.02).astype(np.float32)
+    want = oracle.qgemv_f64(12, raw, N, K, x, bias)
+    xs = torch.zeros((M, K + 32), dtype=torch.float32, device="cuda")
+    xs[:, :K] = torch.from_numpy(x).cuda()
+    ys = torch.full((M, N + 8), 7.0, dtype=torch.float32, device="cuda")
+    bt = torch.from_numpy(bias).cuda()
+    L = _lib.lib()
+    outs = []
+    for _ in range(2):
+        st = L.rtd_qlinear(qm.ctx.handle, qm.handle, xs.data_ptr(), _lib.DT_F32, K + 32, M, bt.data_ptr(),
+                           ys.data_ptr(), _lib.DT_F32, N + 8, torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        outs.append(ys.cpu().numpy().copy())
+    assert np.array_equal(outs[0], outs[1])
+    assert rel_l2(outs[0][:, :N], want) <= RTOL
+    assert np.all(outs[0][:, N:] == 7.0)
+    for odt, tol in ((torch.float16, RTOL), (torch.bfloat16, 8e-3)):
+        y = qm.forward(torch.from_numpy(x).cuda(), bias=bt, out_dtype=odt).float().cpu().numpy()
+        assert rel_l2(y, want) <= tol
+
+
+def test_gemm_prefill_shape():
+    """Config-1-sized prefill chunk: M = 512 tokens, K = 4096."""
+    import torch
+    from runtimed_b200.weights import QMatMul
+
+    N, K, M = 1024, 4096, 512
+    raw = synth.quant_matrix(12, N, K, seed=9)
+    qm = QMatMul(12, raw, N, K)
+    x = synth.bf16_round(synth.activations(M, K, seed=9))
+    y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32).cpu().numpy()
+    assert rel_l2(y, oracle.qgemv_f64(12, raw, N, K, x)) <= RTOL

@@ -87,7 +87,8 @@ def test_gemv_parity_small(name, t, M, xdt):
     want = oracle.qgemv_f64(t, raw, N, K, xt.float().numpy())
     y = qm.forward(xt.cuda(), out_dtype=torch.float32).cpu().numpy()
     err = rel_l2(y, want)
-    assert err <= RTOL_EXACT, err
+    # M > 4 runs the tensor-core GEMM, whose weights are rounded once to f16
+    assert err <= (RTOL_EXACT if M <= 4 else RTOL), err
 
 
 @pytest.mark.parametrize("name,t", FORMATS)
