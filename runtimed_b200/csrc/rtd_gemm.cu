@@ -74,6 +74,8 @@ struct GemmArgs {
   int y_dtype;
   int64_t ldy;
   int* status;
+  int splits;              // K splits (grid z); > 1: write f32 partials instead of y
+  float* partial;          // [splits][Mp][N] when splits > 1
 };
 
 // ---------------------------------------------------------------- tcgen05
@@ -289,7 +291,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
 
   const int64_t tile0 = (int64_t)blockIdx.y * 8;           // first 16-row tile of this CTA
   const int64_t t0 = (int64_t)blockIdx.x * TN;             // first token
-  const int nkb = a.nkb;
+  // this CTA's k range: whole groups [g_lo, g_hi) of the split blockIdx.z
+  const int ngroups = a.nkb / SPG;
+  const int g_lo = (int)((int64_t)ngroups * blockIdx.z / a.splits);
+  const int g_hi = (int)((int64_t)ngroups * (blockIdx.z + 1) / a.splits);
+  const int kb0 = g_lo * SPG;
+  const int nkb = (g_hi - g_lo) * SPG;
 
   if (warp == 0) {
     tmem_alloc(smem_u32(&misc[0]), kCols);
@@ -334,14 +341,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
           if (s >= kRawSlots && !wait(&raw_empty[rs], (uint32_t)((s / kRawSlots - 1) & 1))) break;
           mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(ntile * GB));
           for (int64_t i = 0; i < ntile; ++i)
-            bulk_g2s(sm + L::offRaw + rs * L::kRaw + i * GB, a.w + ((tile0 + i) * a.G + s) * GB, GB, &raw_full[rs]);
+            bulk_g2s(sm + L::offRaw + rs * L::kRaw + i * GB, a.w + ((tile0 + i) * a.G + g_lo + s) * GB, GB,
+                     &raw_full[rs]);
           ++groups;
         }
         const int st = kb % kStages;
         if (kb >= kStages && !wait(&st_empty[st], (uint32_t)((kb / kStages - 1) & 1))) break;
         mbar_arrive_expect_tx(&b_full[st], (uint32_t)L::kB);
-        bulk_g2s(sm + L::offB + st * L::kB, xw + ((size_t)kb * (a.Mp / 8) + (size_t)(t0 / 8)) * 1024, L::kB,
-                 &b_full[st]);
+        bulk_g2s(sm + L::offB + st * L::kB, xw + ((size_t)(kb0 + kb) * (a.Mp / 8) + (size_t)(t0 / 8)) * 1024,
+                 L::kB, &b_full[st]);
         ++stages;
       }
       if (*abort_flag) {  // no copy may still be landing when the CTA exits
@@ -397,6 +405,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         float v[8];
         tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         if (!ok) continue;
+        if (a.splits > 1) {  // partial sums of this k split; the reduce kernel finishes them
+          if (n < a.N) {
+            float* pp = a.partial + ((size_t)blockIdx.z * a.Mp + (size_t)(t0 + c0)) * a.N + n;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pp[(size_t)j * a.N] = v[j];
+          }
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int64_t t = t0 + c0 + j;
@@ -468,6 +484,28 @@ __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x,
   }
 }
 
+// y[t, n] = sum over splits of the partials, scaled and biased as the GEMM epilogue does.
+__global__ void gemm_reduce_kernel(const float* partial, int splits, int64_t Mp, int64_t M, int64_t N,
+                                   const float* tscale, const float* row_scale, int scale_len, const float* bias,
+                                   void* y, int y_dtype, int64_t ldy) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / N, n = i - t * N;
+    float v = 0.0f;
+    for (int z = 0; z < splits; ++z) v += partial[((size_t)z * Mp + (size_t)t) * N + n];
+    v *= tscale[t];
+    if (row_scale) v *= row_scale[scale_len == 1 ? 0 : n];
+    if (bias) v += bias[n];
+    const int64_t off = t * ldy + n;
+    if (y_dtype == 0)
+      static_cast<float*>(y)[off] = v;
+    else if (y_dtype == 1)
+      static_cast<__half*>(y)[off] = __float2half_rn(v);
+    else
+      static_cast<__nv_bfloat16*>(y)[off] = __float2bfloat16_rn(v);
+  }
+}
+
 template <int FMT, int TN>
 cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
   using L = GemmSmem<FMT, TN>;
@@ -479,7 +517,7 @@ cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured[dev & 63] = 1;
   }
-  const dim3 grid((unsigned)(a.Mp / TN), (unsigned)((a.T + 7) / 8));
+  const dim3 grid((unsigned)(a.Mp / TN), (unsigned)((a.T + 7) / 8), (unsigned)a.splits);
   qgemm_kernel<FMT, TN><<<grid, kGemmThreads, L::bytes, st>>>(a);
   return cudaGetLastError();
 }
@@ -503,29 +541,54 @@ int gemm_tn_for(int64_t M) {
   return 256;
 }
 
+// K splits: enough CTAs for one wave over the SMs (one CTA per SM fits in shared
+// memory), whole groups per split, at least two groups each.
+int gemm_splits(const QGemvCall& c, int TN) {
+  const int64_t ctas = ((c.M + TN - 1) / TN) * ((tiles_for(c.N) + 7) / 8);
+  const int64_t want = (c.sm_count + ctas - 1) / ctas;
+  const int64_t most = std::max<int64_t>(1, c.G / 2);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(want, most));
+}
+
+struct GemmPlan {
+  int TN, splits;
+  int64_t Mp, kp;
+  size_t xw_bytes, partial_bytes;
+};
+
+GemmPlan gemm_plan(const QGemvCall& c) {
+  GemmPlan p{};
+  const FmtInfo f = fmt_info(c.fmt);
+  p.TN = gemm_tn_for(c.M);
+  p.Mp = (c.M + p.TN - 1) / p.TN * p.TN;
+  p.kp = c.G * f.gk;
+  p.splits = gemm_splits(c, p.TN);
+  p.xw_bytes = (size_t)p.Mp * (size_t)p.kp * 2;
+  p.partial_bytes = p.splits > 1 ? (size_t)p.splits * (size_t)p.Mp * (size_t)c.N * 4 : 0;
+  return p;
+}
+
 }  // namespace
 
 size_t qgemm_workspace_bytes(const QGemvCall& c) {
-  const FmtInfo f = fmt_info(c.fmt);
-  const int TN = gemm_tn_for(c.M);
-  const int64_t Mp = (c.M + TN - 1) / TN * TN;
-  const int64_t kp = c.G * f.gk;
-  return (size_t)Mp * (size_t)kp * 2 + (size_t)Mp * 4 + 512;
+  const GemmPlan p = gemm_plan(c);
+  return p.xw_bytes + (((size_t)p.Mp * 4 + 255) / 256) * 256 + p.partial_bytes + 512;
 }
 
 cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   *plan_error = 0;
   if (c.M <= 0 || c.N <= 0) return cudaSuccess;
-  const FmtInfo f = fmt_info(c.fmt);
-  const int TN = gemm_tn_for(c.M);
-  const int64_t Mp = (c.M + TN - 1) / TN * TN;
-  const int64_t kp = c.G * f.gk;
+  const GemmPlan p = gemm_plan(c);
+  const int TN = p.TN;
+  const int64_t Mp = p.Mp, kp = p.kp;
   if (qgemm_workspace_bytes(c) > c.ws_bytes || Mp / TN > 65535) {
     *plan_error = 1;
     return cudaSuccess;
   }
-  __half* xw = reinterpret_cast<__half*>(c.ws);
-  float* tscale = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c.ws) + (size_t)Mp * (size_t)kp * 2);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(c.ws);
+  __half* xw = reinterpret_cast<__half*>(ws);
+  float* tscale = reinterpret_cast<float*>(ws + p.xw_bytes);
+  float* partial = reinterpret_cast<float*>(ws + p.xw_bytes + (((size_t)Mp * 4 + 255) / 256) * 256);
   gemm_prep_kernel<<<(unsigned)Mp, kPrepThreadsG, 0, c.stream>>>(c.x, c.x_dtype, c.ldx, c.M, Mp, c.K, kp, c.w8a8,
                                                                   xw, tscale);
   cudaError_t e = cudaGetLastError();
@@ -547,12 +610,21 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   a.y_dtype = c.y_dtype;
   a.ldy = c.ldy;
   a.status = c.status;
+  a.splits = p.splits;
+  a.partial = partial;
   switch (c.fmt) {
-    case FMT_Q4K: return launch_gemm_fmt<FMT_Q4K>(a, TN, c.stream);
-    case FMT_Q6K: return launch_gemm_fmt<FMT_Q6K>(a, TN, c.stream);
-    case FMT_Q80: return launch_gemm_fmt<FMT_Q80>(a, TN, c.stream);
-    default: return launch_gemm_fmt<FMT_FP8>(a, TN, c.stream);
+    case FMT_Q4K: e = launch_gemm_fmt<FMT_Q4K>(a, TN, c.stream); break;
+    case FMT_Q6K: e = launch_gemm_fmt<FMT_Q6K>(a, TN, c.stream); break;
+    case FMT_Q80: e = launch_gemm_fmt<FMT_Q80>(a, TN, c.stream); break;
+    default: e = launch_gemm_fmt<FMT_FP8>(a, TN, c.stream); break;
   }
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int64_t total = c.M * c.N;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 4096);
+  gemm_reduce_kernel<<<blocks, 256, 0, c.stream>>>(partial, p.splits, Mp, c.M, c.N, tscale,
+                                                   c.fmt == FMT_FP8 ? c.row_scale : nullptr, c.scale_len, c.bias,
+                                                   c.y, c.y_dtype, c.ldy);
+  return cudaGetLastError();
 }
 
 }  // namespace rtd
