@@ -312,36 +312,44 @@ def _dominant_launch_ms(it, call, stream, dev, rank, reps: int = 24) -> float:
 
 
 def profile_one(spec: str, calls: int) -> int:
-    """Run `calls` M=1 bf16 calls of one sweep GEMV (FMT:N:K) and exit: the target of
-    the ncu captures summarised under profiles/."""
+    """Run `calls` M=1 bf16 calls of one sweep GEMV (FMT:N:K), or of every sweep GEMV in
+    step order ("sweep"), eagerly, and exit: the target of the ncu captures summarised
+    under profiles/ (the bench's own step is a CUDA graph, which ncu reports as one
+    result)."""
     import torch
     from runtimed_b200 import _lib, synth
     from runtimed_b200.weights import Fp8Weight, QMatMul
 
-    name, n, k = spec.split(":")
-    n, k = int(n), int(k)
-    t = dict(FORMATS)[name]
-    dev = torch.device("cuda", 0)
-    x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=0))).to(torch.bfloat16).to(dev)
-    y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
-    if t == 0:
-        w, s = synth.fp8_matrix(n, k, seed=0, stream=k)
-        o = Fp8Weight(w, s, k, n, device=dev)
+    if spec == "sweep":
+        todo = [(t, n, k) for _, t, n, k in sweep()]
     else:
-        o = QMatMul(t, synth.quant_matrix(t, n, k, seed=0, stream=k), n, k, device=dev)
+        name, n, k = spec.split(":")
+        todo = [(dict(FORMATS)[name], int(n), int(k))]
+    dev = torch.device("cuda", 0)
     L = _lib.lib()
     st = torch.cuda.current_stream(dev).cuda_stream
-    for _ in range(calls):
+    items = []
+    for t, n, k in todo:
+        x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=0))).to(torch.bfloat16).to(dev)
+        y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
         if t == 0:
-            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, y.data_ptr(),
-                                  _lib.DT_BF16, n, _lib.FP8_W8A16, st)
+            w, s = synth.fp8_matrix(n, k, seed=0, stream=k)
+            o = Fp8Weight(w, s, k, n, device=dev)
         else:
-            rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, None, y.data_ptr(),
-                               _lib.DT_BF16, n, st)
-        if rc != 0:
-            raise RuntimeError(f"status {rc}")
+            o = QMatMul(t, synth.quant_matrix(t, n, k, seed=0, stream=k), n, k, device=dev)
+        items.append((t, n, k, o, x, y))
+    for _ in range(calls):
+        for t, n, k, o, x, y in items:
+            if t == 0:
+                rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, y.data_ptr(),
+                                      _lib.DT_BF16, n, _lib.FP8_W8A16, st)
+            else:
+                rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, None, y.data_ptr(),
+                                   _lib.DT_BF16, n, st)
+            if rc != 0:
+                raise RuntimeError(f"status {rc}")
     torch.cuda.synchronize(dev)
-    print(f"profile-one {spec}: {calls} calls ok")
+    print(f"profile-one {spec}: {calls} calls of {len(items)} GEMVs ok")
     return 0
 
 
@@ -351,8 +359,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K",
-                    help="only run a few calls of one sweep GEMV (ncu target), no JSON line")
+    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K|sweep",
+                    help="only run a few eager calls of one sweep GEMV or of the whole sweep (ncu target), "
+                         "no JSON line")
     ap.add_argument("--calls", type=int, default=4)
     args = ap.parse_args()
     if args.profile_one:
