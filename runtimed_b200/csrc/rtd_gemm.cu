@@ -6,18 +6,19 @@
 // One CTA computes 128 weight rows (eight 16-row tiles: the UMMA M) x TN tokens (the
 // UMMA N, 16..256) with the fp32 accumulator in tensor memory.  Per 64-element k
 // stage:
-//   - warp 0 (one lane) streams the packed groups of the eight tiles and the stage's
-//     activation tile into shared memory with cp.async.bulk (mbarrier transaction
-//     counts);
-//   - warps 2..9 decode the stage's weights into f16 (the reference formulas in f32,
-//     rounded once) straight into the UMMA K-major core-matrix layout;
+//   - warp 18 (one lane) streams the packed groups of the eight tiles into shared
+//     memory with cp.async.bulk (mbarrier transaction counts), up to 3-4 groups
+//     ahead; warp 0 (one lane) streams the stage's activation tile the same way;
+//   - warps 2..17 decode the stage's weights into f16 pairs (codes exact in f16, the
+//     reference's per-sub-block factors computed in f32 and rounded once to f16, one
+//     f16 FMA per pair) straight into the 128-byte swizzled K-major layout;
 //   - warp 1 (one lane) issues the four K=16 tcgen05.mma of the stage and commits them
 //     to the stage's "empty" barrier, which releases both buffers;
 //   - after the last stage warps 4..7 read the accumulator (tcgen05.ld, one TMEM lane
 //     quarter each) and write y with the per-token activation scale, the FP8 row
 //     scale and the bias.
 // The activations are staged once per call by gemm_prep_kernel: power-of-two-scaled
-// f16 per token, already in the core-matrix layout, so one bulk copy moves a tile.
+// f16 per token, already in the swizzled layout, so one bulk copy moves a tile.
 // Every wait is bounded by %globaltimer; a timeout records kDevWaitTimeout and the
 // CTA stops issuing work, drains what it issued and returns.
 #include <cuda_fp16.h>
@@ -32,13 +33,14 @@
 namespace rtd {
 namespace {
 
-constexpr int kGemmWarps = 10;
+constexpr int kGemmWarps = 19;
 constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kDecodeThreads = 256;  // warps 2..9
+constexpr int kDecodeThreads = 512;  // warps 2..17
+constexpr int kDecodeWarps = kDecodeThreads / 32;
 constexpr int kBM = 128;             // weight rows per CTA (UMMA M)
 constexpr int kBK = 64;              // k per stage
-constexpr int kStages = 3;
-constexpr int kRawSlots = 2;
+constexpr int kMaxStages = 8;
+constexpr int kSmemLimit = 227 * 1024;
 constexpr int kPrepThreadsG = 256;
 
 template <int FMT>
@@ -66,7 +68,7 @@ struct GemmArgs {
   int scale_len;
   int64_t N, T, G;         // rows, 16-row tiles, groups per row
   int nkb;                 // 64-element k blocks
-  const __half* xw;        // staged activations [nkb][Mp / 8][8 k-cores][8 x 8 f16]
+  const __half* xw;        // staged activations [nkb][Mp / 8][1024-byte swizzled atom]
   const float* tscale;     // [Mp] per-token scale
   int64_t M, Mp;
   const float* bias;
@@ -109,31 +111,44 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
+// Sixteen accumulator columns of this warp's TMEM lane quarter: two loads, one wait;
+// the registers pass through the wait so no use is scheduled before it.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15])
+               : "r"(taddr + 8u));
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major, unswizzled f16 operand: 8x8 core
-// matrices of 128 contiguous bytes, the two core matrices of one K=16 step 128 bytes
-// apart (leading byte offset), successive 8-row groups 1024 bytes apart (stride byte
-// offset); descriptor version 1 (sm_100).
+// Shared-memory matrix descriptor of a K-major f16 operand in the 128-byte swizzled
+// layout: each row's 64 k (128 bytes) is one line, eight lines form a 1024-byte atom
+// (stride byte offset), and the 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+// The tile base is 1024-byte aligned; the k-th K=16 slice starts 32 * k bytes in.
+// Descriptor version 1 (sm_100), layout type 2 (128-byte swizzle).
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(128u >> 4) << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 16;             // leading byte offset: unused for swizzled K-major
+  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
   d |= (uint64_t)1 << 46;
-  return d;  // base offset 0, legacy LBO mode, layout type 0 (no swizzle)
+  d |= (uint64_t)2 << 61;
+  return d;
 }
 
 // Instruction descriptor: f16 x f16 -> f32, both operands K-major, UMMA M = 128.
@@ -144,9 +159,10 @@ __host__ __device__ constexpr uint32_t idesc_f16(int n) {
          | ((uint32_t)(kBM >> 4) << 24);    // M / 16
 }
 
-// Byte offset of element (row r, k) inside a K-major core-matrix tile of 64 k.
-__device__ __forceinline__ uint32_t core_off(int r, int k) {
-  return (uint32_t)((r >> 3) * 1024 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+// Byte offset of the 8-element chunk holding (row r, k .. k+7), k % 8 == 0, in a
+// swizzled K-major tile of 64 k.
+__device__ __forceinline__ uint32_t sw_off(int r, int k) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ r) & 7) << 4));
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
@@ -160,114 +176,160 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
 
 __device__ __forceinline__ float hbits(uint32_t b16) { return __half2float(__ushort_as_half((unsigned short)b16)); }
 
-// ---------------------------------------------------------------- stage decode
-// Thread dt (0..255) of the decode warps: weight row r = dt / 2 of the CTA tile
-// (tile i = r / 16, row rr = r % 16 = g + 8 * hrow), half `part` of its 64 k.
-// raw: the eight groups of this stage's k range (group layouts of rtd_layout.h);
-// sub: which 64-wide block of the group; a_s: the stage's A tile.
-template <int FMT>
-__device__ __forceinline__ void decode_stage(const uint8_t* raw, int sub, uint32_t a_s, int dt) {
-  constexpr int GB = GemmFmt<FMT>::GB;
-  const int r = dt >> 1, part = dt & 1;
-  const int i = r >> 4, rr = r & 15, g = rr & 7, hrow = rr >> 3;
-  const uint8_t* grp = raw + (size_t)i * GB;
-  if constexpr (FMT == FMT_Q4K) {
-    // chunk c = sub: low nibbles are sub-block 2c (local k 0..31), high nibbles 2c+1 (32..63)
-    const uint8_t* hdr = grp + 16 * rr;
-    const uint32_t h0 = *reinterpret_cast<const uint32_t*>(hdr);
-    const float d = hbits(h0 & 0xFFFFu), dmin = hbits(h0 >> 16);
-    uint32_t sc0, m0, sc1, m1;
-    scale_min_k4(2 * sub, hdr + 4, sc0, m0);
-    scale_min_k4(2 * sub + 1, hdr + 4, sc1, m1);
-    const float d0 = d * (float)sc0, n0 = -(dmin * (float)m0);
-    const float d1 = d * (float)sc1, n1 = -(dmin * (float)m1);
-    const uint4 q = *reinterpret_cast<const uint4*>(grp + 256 + (2 * hrow + part) * 512 + (4 * g + sub) * 16);
-    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-    uint32_t lo[8], hi[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t w = wd[j >> 1] >> (16 * (j & 1));  // bytes 2j, 2j+1
-      const float a0 = (float)(w & 0xF), a1 = (float)((w >> 8) & 0xF);
-      const float b0 = (float)((w >> 4) & 0xF), b1 = (float)((w >> 12) & 0xF);
-      lo[j] = pack_f16x2(fmaf(d0, a0, n0), fmaf(d0, a1, n0));
-      hi[j] = pack_f16x2(fmaf(d1, b0, n1), fmaf(d1, b1, n1));
-    }
-    const int k0 = 16 * part;
-    sts128(a_s + core_off(r, k0), lo[0], lo[1], lo[2], lo[3]);
-    sts128(a_s + core_off(r, k0 + 8), lo[4], lo[5], lo[6], lo[7]);
-    sts128(a_s + core_off(r, 32 + k0), hi[0], hi[1], hi[2], hi[3]);
-    sts128(a_s + core_off(r, 32 + k0 + 8), hi[4], hi[5], hi[6], hi[7]);
-  } else if constexpr (FMT == FMT_Q6K) {
-    const float d = hbits(*reinterpret_cast<const uint16_t*>(grp + 4 * g + 2 * hrow));
-#pragma unroll
-    for (int ii = 0; ii < 2; ++ii) {
-      const int sb = 4 * sub + 2 * part + ii;  // 16-element sub-block of the superblock
-      const int h = sb >> 3, sbi = sb & 7, tq = sbi >> 1, side = sbi & 1;
-      const int lane = 4 * g + tq;
-      const float ds = d * (float)(int8_t)grp[32 + lane * 8 + 4 * hrow + 2 * h + side];
-      const int w0 = 12 * h + 3 * (2 * side + hrow);
-      auto word = [&](int w) -> uint32_t {
-        return *reinterpret_cast<const uint32_t*>(grp + 288 + (w >> 2) * 512 + lane * 16 + (w & 3) * 4);
-      };
-      const uint32_t X = word(w0), Y = word(w0 + 1), Z = word(w0 + 2);
-      const int sh[4] = {0, 16, 6, 22};
-      float v[16];
-#pragma unroll
-      for (int e = 0; e < 12; ++e) {
-        const uint32_t src = e < 4 ? X : (e < 8 ? Y : Z);
-        v[e] = ds * (float)((int)((src >> sh[e & 3]) & 63u) - 32);
-      }
-      v[12] = ds * (float)((int)(((X >> 12) & 15u) | (((Z >> 12) & 3u) << 4)) - 32);
-      v[13] = ds * (float)((int)(((X >> 28) & 15u) | (((Z >> 28) & 3u) << 4)) - 32);
-      v[14] = ds * (float)((int)(((Y >> 12) & 15u) | (((Z >> 14) & 3u) << 4)) - 32);
-      v[15] = ds * (float)((int)(((Y >> 28) & 15u) | (((Z >> 30) & 3u) << 4)) - 32);
-      const int k0 = 16 * (2 * part + ii);
-      sts128(a_s + core_off(r, k0), pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-             pack_f16x2(v[6], v[7]));
-      sts128(a_s + core_off(r, k0 + 8), pack_f16x2(v[8], v[9]), pack_f16x2(v[10], v[11]),
-             pack_f16x2(v[12], v[13]), pack_f16x2(v[14], v[15]));
-    }
-  } else {  // Q8_0 / FP8: block b = 2 * sub + part of the group, local k 32 * part ..
-    const int lane = 4 * g + 2 * sub + part;
-    float dq = 1.0f;
-    if constexpr (FMT == FMT_Q80) dq = hbits(*reinterpret_cast<const uint16_t*>(grp + 4 * lane + 2 * hrow));
-    constexpr int base = (FMT == FMT_Q80) ? 128 : 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint4 q = *reinterpret_cast<const uint4*>(grp + base + (2 * hrow + half) * 512 + lane * 16);
-      const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-      uint32_t o[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if constexpr (FMT == FMT_Q80) {
-          const int8_t* b = reinterpret_cast<const int8_t*>(&wd[j]);
-          o[2 * j] = pack_f16x2(dq * (float)b[0], dq * (float)b[1]);
-          o[2 * j + 1] = pack_f16x2(dq * (float)b[2], dq * (float)b[3]);
-        } else {
-          o[2 * j] = e4m3x2_to_f16x2((uint16_t)(wd[j] & 0xFFFFu));
-          o[2 * j + 1] = e4m3x2_to_f16x2((uint16_t)(wd[j] >> 16));
-        }
-      }
-      const int k0 = 32 * part + 16 * half;
-      sts128(a_s + core_off(r, k0), o[0], o[1], o[2], o[3]);
-      sts128(a_s + core_off(r, k0 + 8), o[4], o[5], o[6], o[7]);
-    }
+// ---------------------------------------------------------------- shared loads
+// Explicit ld.shared on 32-bit shared addresses: the stage buffers are addressed
+// through an aligned offset of the dynamic shared array, which the compiler can no
+// longer prove to be shared memory, and generic loads cost an address-space check
+// and long-scoreboard latency on every access.
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+
+// Q4_K scale / min pair j (0..7) from the 12 packed scale bytes held as three words
+// (bytes 0-3, 4-7, 8-11): the same bit selection as scale_min_k4 (dequant_k.rs:8-16).
+__device__ __forceinline__ void scale_min_words(int j, uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sc,
+                                                uint32_t& m) {
+  const int sh = 8 * (j & 3);
+  const uint32_t b0 = (s0 >> sh) & 0xFFu, b1 = (s1 >> sh) & 0xFFu;
+  if (j < 4) {
+    sc = b0 & 63u;
+    m = b1 & 63u;
+  } else {
+    const uint32_t b2 = (s2 >> sh) & 0xFFu;
+    sc = (b2 & 0xFu) | ((b0 >> 6) << 4);
+    m = (b2 >> 4) | ((b1 >> 6) << 4);
   }
 }
 
+// ---------------------------------------------------------------- stage decode
+// Codes become f16 pairs without the conversion pipe: 0x6400 | v is the f16 1024 + v
+// (v < 1024), and subtracting 1024 (+ a bias) is exact.  The weight is then one f16
+// FMA / multiply per pair with the factor (and offset) rounded once from f32.
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ __half2 h2_const(float v) { return __float2half2_rn(v); }
+
+// Thread dt (0..511) of the decode warps decodes 16 weights of one row:
+//   row r = 8 * (dt / 32) + dt % 8 of the CTA tile (tile i = r / 16, row rr = r % 16 =
+//   g + 8 * hrow), part = (dt / 8) % 2 and h = (dt / 16) % 2 pick its 16 of the 64 k.
+// Eight consecutive threads share (part, h) and hold eight consecutive rows, so each
+// quarter-warp stores eight 16-byte chunks that fall on distinct banks.
+// raw_s: shared address of the eight groups of this stage's k range (group layouts of
+// rtd_layout.h); sub: which 64-wide block of the group; a_s: the stage's A tile.
+template <int FMT>
+__device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a_s, int dt) {
+  constexpr int GB = GemmFmt<FMT>::GB;
+  const int r = 8 * (dt >> 5) + (dt & 7), part = (dt >> 3) & 1, h = (dt >> 4) & 1;
+  const int i = r >> 4, rr = r & 15, g = rr & 7, hrow = rr >> 3;
+  const uint32_t grp = raw_s + (uint32_t)(i * GB);
+  uint32_t o[8];
+  int k0;
+  if constexpr (FMT == FMT_Q4K) {
+    // chunk c = sub: low nibbles (h = 0) are sub-block 2c (local k 0..31), high
+    // nibbles (h = 1) sub-block 2c + 1 (local k 32..63)
+    const uint4 hdr = lds128(grp + 16 * rr);
+    const float d = hbits(hdr.x & 0xFFFFu), dmin = hbits(hdr.x >> 16);
+    uint32_t sc, mn;
+    scale_min_words(2 * sub + h, hdr.y, hdr.z, hdr.w, sc, mn);
+    const __half2 d1 = h2_const(d * (float)sc), n1 = h2_const(-(dmin * (float)mn));
+    const __half2 k1024 = h2_const(1024.0f);
+    const uint4 q = lds128(grp + 256 + (2 * hrow + part) * 512 + (4 * g + sub) * 16);
+    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    const int sh = 4 * h;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // bytes 2j, 2j+1 -> halves 0, 1; their nibble (low or high) -> 1024 + q
+      const uint32_t p2 = prmt(wd[j >> 1], 0u, (j & 1) ? 0x4342u : 0x4140u) >> sh;
+      const __half2 v = __hsub2(bits_h2((p2 & 0x000F000Fu) | 0x64006400u), k1024);
+      o[j] = h2_bits(__hfma2(d1, v, n1));
+    }
+    k0 = 32 * h + 16 * part;
+  } else if constexpr (FMT == FMT_Q6K) {
+    const float d = hbits(lds16(grp + 4 * g + 2 * hrow));
+    const int sb = 4 * sub + 2 * part + h;  // 16-element sub-block of the superblock
+    const int hh = sb >> 3, sbi = sb & 7, tq = sbi >> 1, side = sbi & 1;
+    const int lane = 4 * g + tq;
+    const uint32_t scw = lds32(grp + 32 + lane * 8 + 4 * hrow);  // this row's 4 scale bytes of the lane
+    const __half2 ds = h2_const(d * (float)(int)(int8_t)(uint8_t)(scw >> (8 * (2 * hh + side))));
+    const __half2 k1056 = h2_const(1056.0f);  // 1024 + 32
+    const int w0 = 12 * hh + 3 * (2 * side + hrow);
+    auto word = [&](int w) -> uint32_t { return lds32(grp + 288 + (w >> 2) * 512 + lane * 16 + (w & 3) * 4); };
+    const uint32_t X = word(w0), Y = word(w0 + 1), Z = word(w0 + 2);
+    // element pairs: each word holds codes at bits {0, 16} and {6, 22}; the spare bits
+    // 12..15 / 28..31 of X and Y with two bits of Z each make the last four codes
+    const uint32_t c[8] = {X & 0x003F003Fu,
+                           (X >> 6) & 0x003F003Fu,
+                           Y & 0x003F003Fu,
+                           (Y >> 6) & 0x003F003Fu,
+                           Z & 0x003F003Fu,
+                           (Z >> 6) & 0x003F003Fu,
+                           ((X >> 12) & 0x000F000Fu) | ((Z >> 8) & 0x00300030u),
+                           ((Y >> 12) & 0x000F000Fu) | ((Z >> 10) & 0x00300030u)};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = h2_bits(__hmul2(ds, __hsub2(bits_h2(c[j] | 0x64006400u), k1056)));
+    k0 = 16 * (2 * part + h);
+  } else {  // Q8_0 / FP8: block b = 2 * sub + part of the group, local k 32 * part + 16 * h ..
+    const int lane = 4 * g + 2 * sub + part;
+    const uint4 q = lds128(grp + ((FMT == FMT_Q80) ? 128 : 0) + (2 * hrow + h) * 512 + lane * 16);
+    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    if constexpr (FMT == FMT_Q80) {
+      // signed byte b -> (b ^ 0x80) in the low byte of 0x64xx -> 1024 + 128 + b
+      const __half2 dq = bits_h2(lds16(grp + 4 * lane + 2 * hrow) * 0x10001u);
+      const __half2 k1152 = h2_const(1152.0f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t p2 = prmt(wd[j >> 1] ^ 0x80808080u, 0x64u, (j & 1) ? 0x4342u : 0x4140u);
+        o[j] = h2_bits(__hmul2(dq, __hsub2(bits_h2(p2), k1152)));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[2 * j] = e4m3x2_to_f16x2((uint16_t)(wd[j] & 0xFFFFu));
+        o[2 * j + 1] = e4m3x2_to_f16x2((uint16_t)(wd[j] >> 16));
+      }
+    }
+    k0 = 32 * part + 16 * h;
+  }
+  sts128(a_s + sw_off(r, k0), o[0], o[1], o[2], o[3]);
+  sts128(a_s + sw_off(r, k0 + 8), o[4], o[5], o[6], o[7]);
+}
+
 // ---------------------------------------------------------------- GEMM kernel
+// Shared-memory plan of one CTA: kRawSlots packed-group buffers (each the eight tiles'
+// groups of one k range: three for the 256-element formats, four for the 128-element
+// ones, so two groups stay in flight while one is decoded), then as many k stages
+// (decoded A tile + activation tile) as the rest of the 227 KB holds, at most 8.
 template <int FMT, int TN>
 struct GemmSmem {
   static constexpr int kA = kBM * kBK * 2;                  // 16 KB
   static constexpr int kB = TN * kBK * 2;                   // TN * 128
   static constexpr int kRaw = 8 * GemmFmt<FMT>::GB;
+  static constexpr int kRawSlots = GemmFmt<FMT>::GK == 256 ? 3 : 4;
+  static constexpr int kFixed = kRawSlots * kRaw + 1024 + 512;  // + alignment slack, barriers, misc
+  static constexpr int kFit = (kSmemLimit - kFixed) / (kA + kB);
+  static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
   static constexpr int offA = 0;
   static constexpr int offB = offA + kStages * kA;
   static constexpr int offRaw = offB + kStages * kB;
   static constexpr int offBar = (offRaw + kRawSlots * kRaw + 127) / 128 * 128;
   static constexpr int nBars = 2 * kRawSlots + 3 * kStages + 1;
   static constexpr int offMisc = offBar + nBars * 8;
-  static constexpr int bytes = offMisc + 16 + 1024;          // + alignment slack
+  static constexpr int offScale = offMisc + 16;              // the CTA's TN token scales
+  static constexpr int bytes = offScale + TN * 4 + 1024;     // + alignment slack
+  static_assert(kStages >= 3, "at least three k stages");
+  static_assert(bytes <= kSmemLimit, "shared-memory plan exceeds 227 KB");
 };
 
 template <int FMT, int TN>
@@ -276,6 +338,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
   constexpr int SPG = GemmFmt<FMT>::GK / kBK;  // stages per group
   constexpr int GB = GemmFmt<FMT>::GB;
   constexpr uint32_t kCols = TN < 32 ? 32 : TN;
+  constexpr int kStages = L::kStages, kRawSlots = L::kRawSlots;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the operand tiles
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -305,17 +368,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
   if (tid == 32) {
     for (int s = 0; s < kRawSlots; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kDecodeThreads);
+      mbar_init(&raw_empty[s], kDecodeWarps);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&a_full[s], kDecodeThreads);
+      mbar_init(&a_full[s], kDecodeWarps);
       mbar_init(&st_empty[s], 1);
     }
     mbar_init(acc_full, 1);
     misc[1] = 0;
     fence_mbar_init();
   }
+  float* sscale = reinterpret_cast<float*>(sm + L::offScale);
+  for (int i = tid; i < TN; i += kGemmThreads) sscale[i] = (t0 + i < a.M) ? a.tscale[t0 + i] : 0.0f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -330,21 +395,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
   };
 
   if (warp == 0) {
-    // ---- producer: packed groups (per group) and activation tiles (per stage)
+    // ---- activation tiles, one bulk copy per k stage
     if (lane == 0) {
       const uint8_t* xw = reinterpret_cast<const uint8_t*>(a.xw);
-      const int64_t ntile = (a.T - tile0 < 8) ? a.T - tile0 : 8;
-      int groups = 0, stages = 0;  // copies issued so far
+      int stages = 0;  // copies issued so far
       for (int kb = 0; kb < nkb; ++kb) {
-        if (kb % SPG == 0) {
-          const int s = kb / SPG, rs = s % kRawSlots;
-          if (s >= kRawSlots && !wait(&raw_empty[rs], (uint32_t)((s / kRawSlots - 1) & 1))) break;
-          mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(ntile * GB));
-          for (int64_t i = 0; i < ntile; ++i)
-            bulk_g2s(sm + L::offRaw + rs * L::kRaw + i * GB, a.w + ((tile0 + i) * a.G + g_lo + s) * GB, GB,
-                     &raw_full[rs]);
-          ++groups;
-        }
         const int st = kb % kStages;
         if (kb >= kStages && !wait(&st_empty[st], (uint32_t)((kb / kStages - 1) & 1))) break;
         mbar_arrive_expect_tx(&b_full[st], (uint32_t)L::kB);
@@ -352,12 +407,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
                  L::kB, &b_full[st]);
         ++stages;
       }
-      if (*abort_flag) {  // no copy may still be landing when the CTA exits
-        for (int s = (groups > kRawSlots ? groups - kRawSlots : 0); s < groups; ++s)
-          mbar_wait_ns(&raw_full[s % kRawSlots], (uint32_t)((s / kRawSlots) & 1), kWaitBudgetNs, a.status);
+      if (*abort_flag)  // no copy may still be landing when the CTA exits
         for (int kb = (stages > kStages ? stages - kStages : 0); kb < stages; ++kb)
           mbar_wait_ns(&b_full[kb % kStages], (uint32_t)((kb / kStages) & 1), kWaitBudgetNs, a.status);
+    }
+  } else if (warp == kGemmWarps - 1) {
+    // ---- packed groups of the eight tiles, one slot per k range of one group; runs
+    // ahead of the decode by up to kRawSlots groups, independently of the k stages
+    if (lane == 0) {
+      const int64_t ntile = (a.T - tile0 < 8) ? a.T - tile0 : 8;
+      const int ngr = g_hi - g_lo;
+      int groups = 0;  // copies issued so far
+      for (int s = 0; s < ngr; ++s) {
+        const int rs = s % kRawSlots;
+        if (s >= kRawSlots && !wait(&raw_empty[rs], (uint32_t)((s / kRawSlots - 1) & 1))) break;
+        mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(ntile * GB));
+        for (int64_t i = 0; i < ntile; ++i)
+          bulk_g2s(sm + L::offRaw + rs * L::kRaw + i * GB, a.w + ((tile0 + i) * a.G + g_lo + s) * GB, GB,
+                   &raw_full[rs]);
+        ++groups;
       }
+      if (*abort_flag)
+        for (int s = (groups > kRawSlots ? groups - kRawSlots : 0); s < groups; ++s)
+          mbar_wait_ns(&raw_full[s % kRawSlots], (uint32_t)((s / kRawSlots) & 1), kWaitBudgetNs, a.status);
     }
   } else if (warp == 1) {
     // ---- MMA issuer
@@ -371,23 +443,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         const uint32_t as = smem_u32(sm + L::offA + st * L::kA), bs = smem_u32(sm + L::offB + st * L::kB);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16(tmem, kmajor_desc(as + kk * 256), kmajor_desc(bs + kk * 256), idesc, (kb | kk) ? 1u : 0u);
+          umma_f16(tmem, kmajor_desc(as + kk * 32), kmajor_desc(bs + kk * 32), idesc, (kb | kk) ? 1u : 0u);
         umma_commit(&st_empty[st]);
       }
       umma_commit(acc_full);  // fires once every MMA issued above has completed
     }
   } else {
-    // ---- decode warps (and, afterwards, warps 4..7 run the epilogue)
+    // ---- decode warps 2..17 (and, afterwards, warps 4..7 run the epilogue)
     const int dt = tid - 64;
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb / SPG, sub = kb % SPG, rs = s % kRawSlots;
-      if (sub == 0 && !wait(&raw_full[rs], (uint32_t)((s / kRawSlots) & 1))) break;
       const int st = kb % kStages;
-      if (kb >= kStages && !wait(&st_empty[st], (uint32_t)((kb / kStages - 1) & 1))) break;
-      decode_stage<FMT>(sm + L::offRaw + rs * L::kRaw, sub, smem_u32(sm + L::offA + st * L::kA), dt);
-      fence_async_shared();  // the tensor cores read A through the async proxy
-      mbar_arrive(&a_full[st]);
-      if (sub == SPG - 1) mbar_arrive(&raw_empty[rs]);
+      bool ok = true;
+      if (sub == 0) ok = wait(&raw_full[rs], (uint32_t)((s / kRawSlots) & 1));
+      if (ok && kb >= kStages) ok = wait(&st_empty[st], (uint32_t)((kb / kStages - 1) & 1));
+      if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the arrivals below are per warp
+      decode_stage<FMT>(smem_u32(sm + L::offRaw + rs * L::kRaw), sub, smem_u32(sm + L::offA + st * L::kA), dt);
+      fence_async_shared();  // every writer: the tensor cores read A through the async proxy
+      __syncwarp();
+      if (lane == 0) {  // one arrival per warp: 512 single-thread arrivals would serialise
+        mbar_arrive(&a_full[st]);
+        if (sub == SPG - 1) mbar_arrive(&raw_empty[rs]);
+      }
     }
     if (warp >= 4 && warp < 8) {
       const int q = warp - 4;  // TMEM lanes 32q .. 32q+31 = weight rows of this warp
@@ -401,31 +478,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         if (a.bias) eb = a.bias[n];
       }
 #pragma unroll 1
-      for (int c0 = 0; c0 < TN; c0 += 8) {
-        float v[8];
-        tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        if (!ok) continue;
+      for (int c0 = 0; c0 < TN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        if (!ok || n >= a.N) continue;
         if (a.splits > 1) {  // partial sums of this k split; the reduce kernel finishes them
-          if (n < a.N) {
-            float* pp = a.partial + ((size_t)blockIdx.z * a.Mp + (size_t)(t0 + c0)) * a.N + n;
+          float* pp = a.partial + ((size_t)blockIdx.z * a.Mp + (size_t)(t0 + c0)) * a.N + n;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) pp[(size_t)j * a.N] = v[j];
-          }
+          for (int j = 0; j < 16; ++j) pp[(size_t)j * a.N] = v[j];
           continue;
         }
+        const int jn = (a.M - (t0 + c0)) < 16 ? (int)(a.M - (t0 + c0)) : 16;  // tokens < M
+        const int ysz = a.y_dtype == 0 ? 4 : 2;
+        uint8_t* yp = static_cast<uint8_t*>(a.y) + ((t0 + c0) * a.ldy + n) * ysz;
+        const int64_t ystep = a.ldy * ysz;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int64_t t = t0 + c0 + j;
-          if (n < a.N && t < a.M) {
-            const float val = v[j] * a.tscale[t] * es + eb;
-            const int64_t off = t * a.ldy + n;
-            if (a.y_dtype == 0)
-              static_cast<float*>(a.y)[off] = val;
-            else if (a.y_dtype == 1)
-              static_cast<__half*>(a.y)[off] = __float2half_rn(val);
-            else
-              static_cast<__nv_bfloat16*>(a.y)[off] = __float2bfloat16_rn(val);
-          }
+        for (int j = 0; j < 16; ++j, yp += ystep) {
+          if (j >= jn) break;
+          const float val = v[j] * sscale[c0 + j] * es + eb;
+          if (a.y_dtype == 0)
+            *reinterpret_cast<float*>(yp) = val;
+          else if (a.y_dtype == 1)
+            *reinterpret_cast<__half*>(yp) = __float2half_rn(val);
+          else
+            *reinterpret_cast<__nv_bfloat16*>(yp) = __float2bfloat16_rn(val);
         }
       }
     }
@@ -441,26 +517,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
 
 // ---------------------------------------------------------------- activation staging
 // One block per token row t < Mp: max |x| -> power-of-two scale; the scaled f16 row
-// goes to the core-matrix layout [kb][Mp/8][8 k-cores][8 rows x 8 k]; tokens past M
+// goes to the swizzled layout [kb][Mp/8][8 rows x 128 bytes]; tokens past M
 // and k past K are zero.  W8A8 rounds x with the reference E4M3 encoder first.
-__global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x, int x_dtype, int64_t ldx,
-                                                                  int64_t M, int64_t Mp, int64_t K, int64_t kp,
-                                                                  int w8a8, __half* xw, float* tscale) {
-  const int64_t t = blockIdx.x;
-  __shared__ float red[kPrepThreadsG / 32];
-  auto load = [&](int64_t k) -> float {
-    if (t >= M || k >= K) return 0.0f;
-    float v;
-    if (x_dtype == 0)
-      v = static_cast<const float*>(x)[t * ldx + k];
-    else {
-      const unsigned short b = static_cast<const unsigned short*>(x)[t * ldx + k];
-      v = (x_dtype == 1) ? __half2float(__ushort_as_half(b)) : __uint_as_float((uint32_t)b << 16);
+// The row is read once in 8-element units (one 16-byte load each for 16-bit input,
+// two for f32) that stay in registers between the max and the conversion (up to
+// kUnits per thread: K <= 32768 for 16-bit input, 16384 for f32); units past that
+// are read a second time.
+template <int XDT>
+struct PrepUnit {
+  static constexpr int NR = XDT == 0 ? 2 : 1;            // 16-byte words per 8 elements
+  static constexpr int kUnits = XDT == 0 ? 8 : 16;       // units a thread holds
+  uint4 r[NR];
+};
+
+template <int XDT>
+__device__ __forceinline__ void prep_load(const void* x, int64_t row, int64_t k, int64_t K, bool vec,
+                                          PrepUnit<XDT>& u) {
+  constexpr int ES = XDT == 0 ? 4 : 2;
+  if (vec && k + 8 <= K) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + (row + k) * ES);
+#pragma unroll
+    for (int i = 0; i < PrepUnit<XDT>::NR; ++i) u.r[i] = __ldg(p + i);
+    return;
+  }
+  uint32_t w[4 * PrepUnit<XDT>::NR];
+#pragma unroll
+  for (int i = 0; i < 4 * PrepUnit<XDT>::NR; ++i) w[i] = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if (k + e < K) {
+      if (XDT == 0) {
+        w[e] = __ldg(static_cast<const uint32_t*>(x) + row + k + e);
+      } else {
+        const uint32_t b = __ldg(static_cast<const unsigned short*>(x) + row + k + e);
+        w[e >> 1] |= b << (16 * (e & 1));
+      }
     }
-    return w8a8 ? e4m3_round_ref(v) : v;
-  };
+  }
+#pragma unroll
+  for (int i = 0; i < PrepUnit<XDT>::NR; ++i) u.r[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+template <int XDT, bool W8A8>
+__device__ __forceinline__ void prep_values(const PrepUnit<XDT>& u, float (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint4 q = u.r[XDT == 0 ? (e >> 2) : 0];
+    const uint32_t wd = XDT == 0 ? (&q.x)[e & 3] : (&q.x)[e >> 1];
+    float f;
+    if (XDT == 0)
+      f = __uint_as_float(wd);
+    else {
+      const uint32_t b = (wd >> (16 * (e & 1))) & 0xFFFFu;
+      f = XDT == 1 ? __half2float(__ushort_as_half((unsigned short)b)) : __uint_as_float(b << 16);
+    }
+    if constexpr (W8A8) f = e4m3_round_ref(f);
+    v[e] = f;
+  }
+}
+
+template <int XDT, bool W8A8>
+__global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x, int64_t ldx, int64_t M, int64_t Mp,
+                                                                  int64_t K, int64_t kp, bool vec, __half* xw,
+                                                                  float* tscale) {
+  using U = PrepUnit<XDT>;
+  const int64_t t = blockIdx.x;
+  const int64_t units = kp / 8, row = t * ldx;
+  const bool live = t < M;
+  // units held by this thread: threadIdx.x + j * kPrepThreadsG for j < nh
+  const int64_t mine = units > threadIdx.x ? (units - 1 - threadIdx.x) / kPrepThreadsG + 1 : 0;
+  const int nh = (int)(mine < U::kUnits ? mine : U::kUnits);
+  __shared__ float red[kPrepThreadsG / 32];
+  U held[U::kUnits];
+#pragma unroll
+  for (int j = 0; j < U::kUnits; ++j) {
+#pragma unroll
+    for (int i = 0; i < U::NR; ++i) held[j].r[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (live && j < nh) prep_load<XDT>(x, row, 8 * (threadIdx.x + (int64_t)j * kPrepThreadsG), K, vec, held[j]);
+  }
   float m = 0.0f;
-  for (int64_t k = threadIdx.x; k < K; k += kPrepThreadsG) m = fmaxf(m, fabsf(load(k)));
+#pragma unroll
+  for (int j = 0; j < U::kUnits; ++j) {
+    if (live && j < nh) {
+      float v[8];
+      prep_values<XDT, W8A8>(held[j], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+    }
+  }
+  for (int64_t u = threadIdx.x + (int64_t)U::kUnits * kPrepThreadsG; live && u < units; u += kPrepThreadsG) {
+    U p;
+    prep_load<XDT>(x, row, 8 * u, K, vec, p);
+    float v[8];
+    prep_values<XDT, W8A8>(p, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -473,36 +625,74 @@ __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x,
   const float inv = ldexpf(1.0f, -e);
   if (threadIdx.x == 0) tscale[t] = ldexpf(1.0f, e);
   const int64_t tg = t >> 3, r = t & 7;
-  for (int64_t c = threadIdx.x; c < kp / 8; c += kPrepThreadsG) {  // 8 consecutive k per thread
-    const int64_t k = 8 * c, kb = k / 64, kc = (k % 64) / 8;
-    uint32_t o[4];
+  auto store = [&](int64_t u, const U& p) {
+    float v[8];
+    prep_values<XDT, W8A8>(p, v);
+    const int64_t kb = u / 8, kc = u % 8;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(xw) + ((size_t)kb * (Mp / 8) + (size_t)tg) * 1024 + (size_t)r * 128 +
+                   (size_t)((kc ^ r) & 7) * 16;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_f16x2(v[0] * inv, v[1] * inv), pack_f16x2(v[2] * inv, v[3] * inv),
+                                                pack_f16x2(v[4] * inv, v[5] * inv), pack_f16x2(v[6] * inv, v[7] * inv));
+  };
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = pack_f16x2(load(k + 2 * j) * inv, load(k + 2 * j + 1) * inv);
-    uint8_t* dst = reinterpret_cast<uint8_t*>(xw) + (((size_t)kb * (Mp / 8) + (size_t)tg) * 8 + (size_t)kc) * 128 +
-                   (size_t)r * 16;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int j = 0; j < U::kUnits; ++j)
+    if (j < nh) store(threadIdx.x + (int64_t)j * kPrepThreadsG, held[j]);
+  for (int64_t u = threadIdx.x + (int64_t)U::kUnits * kPrepThreadsG; u < units; u += kPrepThreadsG) {
+    U p;
+#pragma unroll
+    for (int i = 0; i < U::NR; ++i) p.r[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (live) prep_load<XDT>(x, row, 8 * u, K, vec, p);
+    store(u, p);
   }
 }
 
-// y[t, n] = sum over splits of the partials, scaled and biased as the GEMM epilogue does.
+// y[t, n] = sum over splits of the partials, scaled and biased as the GEMM epilogue
+// does; four consecutive n per thread (one 16-byte load per split) when N % 4 == 0.
+__device__ __forceinline__ void reduce_store(void* y, int y_dtype, int64_t off, float v) {
+  if (y_dtype == 0)
+    static_cast<float*>(y)[off] = v;
+  else if (y_dtype == 1)
+    static_cast<__half*>(y)[off] = __float2half_rn(v);
+  else
+    static_cast<__nv_bfloat16*>(y)[off] = __float2bfloat16_rn(v);
+}
+
 __global__ void gemm_reduce_kernel(const float* partial, int splits, int64_t Mp, int64_t M, int64_t N,
                                    const float* tscale, const float* row_scale, int scale_len, const float* bias,
                                    void* y, int y_dtype, int64_t ldy) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((N & 3) == 0) {
+    const int64_t n4 = N / 4, total = M * n4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+      const int64_t t = i / n4, n = 4 * (i - t * n4);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int z = 0; z < splits; ++z) {
+        const float4 p = __ldg(reinterpret_cast<const float4*>(partial + ((size_t)z * Mp + (size_t)t) * N + n));
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+      }
+      const float ts = tscale[t];
+      float v[4] = {acc.x * ts, acc.y * ts, acc.z * ts, acc.w * ts};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (row_scale) v[j] *= row_scale[scale_len == 1 ? 0 : n + j];
+        if (bias) v[j] += bias[n + j];
+        reduce_store(y, y_dtype, t * ldy + n + j, v[j]);
+      }
+    }
+    return;
+  }
   const int64_t total = M * N;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t t = i / N, n = i - t * N;
     float v = 0.0f;
     for (int z = 0; z < splits; ++z) v += partial[((size_t)z * Mp + (size_t)t) * N + n];
     v *= tscale[t];
     if (row_scale) v *= row_scale[scale_len == 1 ? 0 : n];
     if (bias) v += bias[n];
-    const int64_t off = t * ldy + n;
-    if (y_dtype == 0)
-      static_cast<float*>(y)[off] = v;
-    else if (y_dtype == 1)
-      static_cast<__half*>(y)[off] = __float2half_rn(v);
-    else
-      static_cast<__nv_bfloat16*>(y)[off] = __float2bfloat16_rn(v);
+    reduce_store(y, y_dtype, t * ldy + n, v);
   }
 }
 
@@ -533,39 +723,54 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, int TN, cudaStream_t st) {
   }
 }
 
-int gemm_tn_for(int64_t M) {
-  if (M <= 16) return 16;
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
-}
-
-// K splits: enough CTAs for one wave over the SMs (one CTA per SM fits in shared
-// memory), whole groups per split, at least two groups each.
-int gemm_splits(const QGemvCall& c, int TN) {
-  const int64_t ctas = ((c.M + TN - 1) / TN) * ((tiles_for(c.N) + 7) / 8);
-  const int64_t want = (c.sm_count + ctas - 1) / ctas;
-  const int64_t most = std::max<int64_t>(1, c.G / 2);
-  return (int)std::max<int64_t>(1, std::min<int64_t>(want, most));
-}
-
+// Tile width and K splits from a cost model of one launch (one CTA per SM fits in
+// shared memory, so CTAs run in waves of sm_count): a k stage costs the longer of its
+// four MMAs (128 x TN x 16 each, about TN / 2 cycles) and the decode of its 8192
+// weights by 256 threads; every CTA pays a pipeline fill and epilogue; a split launch
+// adds the reduce kernel's traffic.  The candidate with the fewest estimated cycles
+// wins (ties: fewer splits, then the wider tile).
 struct GemmPlan {
   int TN, splits;
   int64_t Mp, kp;
   size_t xw_bytes, partial_bytes;
 };
 
+constexpr double kDecodeStageCycles = 450.0;
+constexpr double kCtaFixedCycles = 4000.0;
+constexpr double kReduceFixedCycles = 3000.0;
+constexpr double kCyclesPerReduceByte = 1.9e9 / 3.0e12;  // ~3 TB/s at ~1.9 GHz
+
 GemmPlan gemm_plan(const QGemvCall& c) {
-  GemmPlan p{};
   const FmtInfo f = fmt_info(c.fmt);
-  p.TN = gemm_tn_for(c.M);
-  p.Mp = (c.M + p.TN - 1) / p.TN * p.TN;
-  p.kp = c.G * f.gk;
-  p.splits = gemm_splits(c, p.TN);
-  p.xw_bytes = (size_t)p.Mp * (size_t)p.kp * 2;
-  p.partial_bytes = p.splits > 1 ? (size_t)p.splits * (size_t)p.Mp * (size_t)c.N * 4 : 0;
-  return p;
+  const int spg = f.gk / kBK;
+  const int64_t rowctas = (tiles_for(c.N) + 7) / 8;
+  const int64_t sms = c.sm_count > 0 ? c.sm_count : 148;
+  GemmPlan best{};
+  double best_cyc = -1.0;
+  for (int TN = 16; TN <= 256; TN *= 2) {
+    if (TN > 16 && TN / 2 >= c.M) break;  // a narrower tile already covers every token
+    const int64_t colctas = (c.M + TN - 1) / TN;
+    if (colctas > 65535) continue;
+    const int64_t Mp = colctas * TN;
+    const int64_t most = std::max<int64_t>(1, std::min<int64_t>(16, c.G / 2));
+    for (int64_t s = 1; s <= most; ++s) {
+      const int64_t ctas = colctas * rowctas * s;
+      const int64_t waves = (ctas + sms - 1) / sms;
+      const int64_t stages = ((c.G + s - 1) / s) * spg;
+      double cyc = (double)waves * ((double)stages * std::max(2.0 * TN, kDecodeStageCycles) + kCtaFixedCycles);
+      if (s > 1) cyc += kReduceFixedCycles + kCyclesPerReduceByte * (double)(s * Mp * c.N * 4 + c.M * c.N * 4);
+      if (best_cyc < 0.0 || cyc < best_cyc * 0.98) {
+        best_cyc = cyc;
+        best.TN = TN;
+        best.splits = (int)s;
+        best.Mp = Mp;
+      }
+    }
+  }
+  best.kp = c.G * f.gk;
+  best.xw_bytes = (size_t)best.Mp * (size_t)best.kp * 2;
+  best.partial_bytes = best.splits > 1 ? (size_t)best.splits * (size_t)best.Mp * (size_t)c.N * 4 : 0;
+  return best;
 }
 
 }  // namespace
@@ -581,7 +786,7 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   const GemmPlan p = gemm_plan(c);
   const int TN = p.TN;
   const int64_t Mp = p.Mp, kp = p.kp;
-  if (qgemm_workspace_bytes(c) > c.ws_bytes || Mp / TN > 65535) {
+  if (TN == 0 || qgemm_workspace_bytes(c) > c.ws_bytes) {
     *plan_error = 1;
     return cudaSuccess;
   }
@@ -589,8 +794,24 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   __half* xw = reinterpret_cast<__half*>(ws);
   float* tscale = reinterpret_cast<float*>(ws + p.xw_bytes);
   float* partial = reinterpret_cast<float*>(ws + p.xw_bytes + (((size_t)Mp * 4 + 255) / 256) * 256);
-  gemm_prep_kernel<<<(unsigned)Mp, kPrepThreadsG, 0, c.stream>>>(c.x, c.x_dtype, c.ldx, c.M, Mp, c.K, kp, c.w8a8,
-                                                                  xw, tscale);
+  const int es = c.x_dtype == 0 ? 4 : 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(c.x) % 16 == 0) && ((c.ldx * es) % 16 == 0);
+  const unsigned pblocks = (unsigned)Mp;
+  if (c.w8a8) {
+    if (c.x_dtype == 0)
+      gemm_prep_kernel<0, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+    else if (c.x_dtype == 1)
+      gemm_prep_kernel<1, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+    else
+      gemm_prep_kernel<2, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+  } else {
+    if (c.x_dtype == 0)
+      gemm_prep_kernel<0, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+    else if (c.x_dtype == 1)
+      gemm_prep_kernel<1, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+    else
+      gemm_prep_kernel<2, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmArgs a{};
@@ -619,8 +840,8 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
     default: e = launch_gemm_fmt<FMT_FP8>(a, TN, c.stream); break;
   }
   if (e != cudaSuccess || p.splits == 1) return e;
-  const int64_t total = c.M * c.N;
-  const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 4096);
+  const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * (int64_t)c.sm_count));
   gemm_reduce_kernel<<<blocks, 256, 0, c.stream>>>(partial, p.splits, Mp, c.M, c.N, tscale,
                                                    c.fmt == FMT_FP8 ? c.row_scale : nullptr, c.scale_len, c.bias,
                                                    c.y, c.y_dtype, c.ldy);

@@ -91,3 +91,45 @@ def test_gemm_prefill_shape():
     x = synth.bf16_round(synth.activations(M, K, seed=9))
     y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32).cpu().numpy()
     assert rel_l2(y, oracle.qgemv_f64(12, raw, N, K, x)) <= RTOL
+
+
+def test_gemm_staging_paths():
+    """Activation staging: rows whose stride is not a multiple of 16 bytes (element
+    loads), f16 input, and K past what a staging thread holds in registers (the row
+    is read a second time)."""
+    import torch
+    from runtimed_b200 import _lib
+    from runtimed_b200.weights import QMatMul
+
+    N, K, M = 64, 33024, 6
+    raw = synth.quant_matrix(12, N, K, seed=5)
+    qm = QMatMul(12, raw, N, K)
+    x16 = synth.activations(M, K, seed=5).astype(np.float16)
+    want = oracle.qgemv_f64(12, raw, N, K, x16.astype(np.float32))
+    ld = K + 3
+    xs = torch.zeros((M, ld), dtype=torch.float16, device="cuda")
+    xs[:, :K] = torch.from_numpy(x16).cuda()
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    L = _lib.lib()
+    st = L.rtd_qlinear(qm.ctx.handle, qm.handle, xs.data_ptr(), _lib.DT_F16, ld, M, None, y.data_ptr(),
+                       _lib.DT_F32, N, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    assert rel_l2(y.cpu().numpy(), want) <= RTOL
+    xa = torch.from_numpy(x16).cuda()  # aligned rows: 16-byte loads, same result bits
+    ya = qm.forward(xa, out_dtype=torch.float32)
+    assert torch.equal(ya, y)
+
+
+@pytest.mark.parametrize("M", [9, 300])
+def test_gemm_fp8_ragged_k(M):
+    import torch
+    from runtimed_b200.weights import Fp8Weight
+
+    N, K = 72, 1003  # K % 8 != 0: the row tail is staged element by element
+    w, s = synth.fp8_matrix(N, K, seed=M + 1)
+    fw = Fp8Weight(w, s, K, N)
+    x = synth.bf16_round(synth.activations(M, K, seed=M + 1))
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    for mode, ref in (("w8a16", oracle.fp8_gemm_cpu_f64), ("w8a8", oracle.fp8_gemm_w8a8_f64)):
+        y = fw.forward(xt, mode=mode).float().cpu().numpy()
+        assert rel_l2(y, ref(x, w, s, N, K)) <= RTOL, mode
