@@ -12,19 +12,24 @@
 //   - warps 2..17 decode the stage's weights into f16 pairs (codes exact in f16, the
 //     reference's per-sub-block factors computed in f32 and rounded once to f16, one
 //     f16 FMA per pair) straight into the 128-byte swizzled K-major layout;
-//   - warp 1 (one lane) issues the four K=16 tcgen05.mma of the stage and commits them
-//     to the stage's "empty" barrier, which releases both buffers;
-//   - after the last stage warps 4..7 read the accumulator (tcgen05.ld, one TMEM lane
-//     quarter each) and write y with the per-token activation scale, the FP8 row
-//     scale and the bias.
+//   - one lane of warp 1 (even stages) or of warp 19 (odd stages) issues the four
+//     K=16 tcgen05.mma of the stage into its own accumulator and commits them to the
+//     stage's "empty" barrier, which releases both buffers;
+//   - after the last stage warps 4..7 read both accumulators (tcgen05.ld, one TMEM
+//     lane quarter each), add them, and write y with the per-token activation scale,
+//     the FP8 row scale and the bias.
 // The activations are staged once per call by gemm_prep_kernel: power-of-two-scaled
-// f16 per token, already in the swizzled layout, so one bulk copy moves a tile.
+// f16 per token, already in the swizzled layout, so one bulk copy moves a tile.  The
+// prep, GEMM and (split-K) reduce kernels are chained with programmatic dependent
+// launch: the GEMM allocates tensor memory, loads and decodes weights while the prep
+// kernel runs, and only the activation producer and the epilogue wait for it.
 // Every wait is bounded by %globaltimer; a timeout records kDevWaitTimeout and the
 // CTA stops issuing work, drains what it issued and returns.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <utility>
 #include <cstdint>
 
 #include "rtd_common.cuh"
@@ -33,10 +38,16 @@
 namespace rtd {
 namespace {
 
-constexpr int kGemmWarps = 19;
+#ifndef RTD_GEMM_DECODE_WARPS
+#define RTD_GEMM_DECODE_WARPS 16
+#endif
+constexpr int kDecodeWarps = RTD_GEMM_DECODE_WARPS;  // warps 2 .. 2 + kDecodeWarps - 1
+constexpr int kGemmWarps = kDecodeWarps + 4;
+constexpr int kWarpRaw = kDecodeWarps + 2;      // packed-group producer
+constexpr int kWarpMmaOdd = kDecodeWarps + 3;   // MMA issuer of the odd k stages (warp 1: the even ones)
 constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kDecodeThreads = 512;  // warps 2..17
-constexpr int kDecodeWarps = kDecodeThreads / 32;
+constexpr int kDecodeThreads = kDecodeWarps * 32;
+constexpr int kHalvesPerThread = 512 / kDecodeThreads;  // 16-weight halves a decode thread takes per stage
 constexpr int kBM = 128;             // weight rows per CTA (UMMA M)
 constexpr int kBK = 64;              // k per stage
 constexpr int kMaxStages = 8;
@@ -132,6 +143,11 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Programmatic dependent launch: the three kernels of a call (prep, GEMM, reduce) are
+// chained so each can start its independent work while the previous one runs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -221,17 +237,15 @@ __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cas
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 __device__ __forceinline__ __half2 h2_const(float v) { return __float2half2_rn(v); }
 
-// Thread dt (0..511) of the decode warps decodes 16 weights of one row:
-//   row r = 8 * (dt / 32) + dt % 8 of the CTA tile (tile i = r / 16, row rr = r % 16 =
-//   g + 8 * hrow), part = (dt / 8) % 2 and h = (dt / 16) % 2 pick its 16 of the 64 k.
-// Eight consecutive threads share (part, h) and hold eight consecutive rows, so each
-// quarter-warp stores eight 16-byte chunks that fall on distinct banks.
+// 16 weights of row r of the CTA tile (tile i = r / 16, row rr = r % 16 = g + 8 * hrow):
+// part and h pick its 16 of the stage's 64 k.  Eight consecutive threads share
+// (part, h) and hold eight consecutive rows, so each quarter-warp stores eight 16-byte
+// chunks that fall on distinct banks.
 // raw_s: shared address of the eight groups of this stage's k range (group layouts of
 // rtd_layout.h); sub: which 64-wide block of the group; a_s: the stage's A tile.
 template <int FMT>
-__device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a_s, int dt) {
+__device__ __forceinline__ void decode_half(uint32_t raw_s, int sub, uint32_t a_s, int r, int part, int h) {
   constexpr int GB = GemmFmt<FMT>::GB;
-  const int r = 8 * (dt >> 5) + (dt & 7), part = (dt >> 3) & 1, h = (dt >> 4) & 1;
   const int i = r >> 4, rr = r & 15, g = rr & 7, hrow = rr >> 3;
   const uint32_t grp = raw_s + (uint32_t)(i * GB);
   uint32_t o[8];
@@ -306,6 +320,20 @@ __device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a
   sts128(a_s + sw_off(r, k0 + 8), o[4], o[5], o[6], o[7]);
 }
 
+// Thread dt of the decode warps: with 16 warps it decodes one 16-weight half of a row
+// (row r = 8 * (dt / 32) + dt % 8, part = (dt / 8) % 2, half h = (dt / 16) % 2); with 8
+// warps both halves of row r = 8 * (dt / 16) + dt % 8.  Eight consecutive threads
+// always hold eight consecutive rows with the same k chunk.
+template <int FMT>
+__device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a_s, int dt) {
+  if constexpr (kHalvesPerThread == 1) {
+    decode_half<FMT>(raw_s, sub, a_s, 8 * (dt >> 5) + (dt & 7), (dt >> 3) & 1, (dt >> 4) & 1);
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) decode_half<FMT>(raw_s, sub, a_s, 8 * (dt >> 4) + (dt & 7), (dt >> 3) & 1, h);
+  }
+}
+
 // ---------------------------------------------------------------- GEMM kernel
 // Shared-memory plan of one CTA: kRawSlots packed-group buffers (each the eight tiles'
 // groups of one k range: three for the 256-element formats, four for the 128-element
@@ -337,7 +365,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
   using L = GemmSmem<FMT, TN>;
   constexpr int SPG = GemmFmt<FMT>::GK / kBK;  // stages per group
   constexpr int GB = GemmFmt<FMT>::GB;
-  constexpr uint32_t kCols = TN < 32 ? 32 : TN;
+  // two accumulators (even / odd k stages, one MMA-issuing thread each), added in the
+  // epilogue in a fixed order
+  constexpr uint32_t kAccStride = TN < 32 ? 32 : TN;
+  constexpr uint32_t kCols = 2 * kAccStride;
   constexpr int kStages = L::kStages, kRawSlots = L::kRawSlots;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the operand tiles
@@ -375,19 +406,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
       mbar_init(&a_full[s], kDecodeWarps);
       mbar_init(&st_empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, 2);  // one commit per MMA-issuing thread
     misc[1] = 0;
     fence_mbar_init();
   }
   float* sscale = reinterpret_cast<float*>(sm + L::offScale);
-  for (int i = tid; i < TN; i += kGemmThreads) sscale[i] = (t0 + i < a.M) ? a.tscale[t0 + i] : 0.0f;
+  pdl_trigger();  // the reduce kernel (or the next call) may launch; it waits for this grid
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
   volatile uint32_t* abort_flag = &misc[1];
 
+  // The common case -- the phase has already completed -- costs one try_wait; the
+  // abort flag and the bounded wait are only consulted when it has not.
   auto wait = [&](uint64_t* b, uint32_t parity) -> bool {
+    if (mbar_try_wait(b, parity)) return true;
     if (*abort_flag) return false;
     if (mbar_wait_ns(b, parity, kWaitBudgetNs, a.status)) return true;
     *abort_flag = 1;
@@ -397,6 +431,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
   if (warp == 0) {
     // ---- activation tiles, one bulk copy per k stage
     if (lane == 0) {
+      pdl_wait();  // the staged activations are the prep kernel's output
       const uint8_t* xw = reinterpret_cast<const uint8_t*>(a.xw);
       int stages = 0;  // copies issued so far
       for (int kb = 0; kb < nkb; ++kb) {
@@ -411,7 +446,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         for (int kb = (stages > kStages ? stages - kStages : 0); kb < stages; ++kb)
           mbar_wait_ns(&b_full[kb % kStages], (uint32_t)((kb / kStages) & 1), kWaitBudgetNs, a.status);
     }
-  } else if (warp == kGemmWarps - 1) {
+  } else if (warp == kWarpRaw) {
     // ---- packed groups of the eight tiles, one slot per k range of one group; runs
     // ahead of the decode by up to kRawSlots groups, independently of the k stages
     if (lane == 0) {
@@ -431,25 +466,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         for (int s = (groups > kRawSlots ? groups - kRawSlots : 0); s < groups; ++s)
           mbar_wait_ns(&raw_full[s % kRawSlots], (uint32_t)((s / kRawSlots) & 1), kWaitBudgetNs, a.status);
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer
+  } else if (warp == 1 || warp == kWarpMmaOdd) {
+    // ---- MMA issuers: warp 1 the even k stages into accumulator 0, warp 19 the odd
+    // ones into accumulator 1 (the issue loop of one thread is longer than a stage's
+    // MMAs; two threads halve it)
     if (lane == 0) {
+      const int par = warp == 1 ? 0 : 1;
+      const uint32_t acc = tmem + (uint32_t)par * kAccStride;
       constexpr uint32_t idesc = idesc_f16(TN);
-      for (int kb = 0; kb < nkb; ++kb) {
+      // descriptors of stage 0; stage st and K slice kk add (st * tile + 32 * kk) / 16
+      // to the start-address field (shared addresses stay below 2^18: no carry out)
+      const uint64_t da0 = kmajor_desc(smem_u32(sm + L::offA)), db0 = kmajor_desc(smem_u32(sm + L::offB));
+      for (int kb = par; kb < nkb; kb += 2) {
         const int st = kb % kStages;
         const uint32_t ph = (uint32_t)((kb / kStages) & 1);
-        if (!wait(&a_full[st], ph) || !wait(&b_full[st], ph)) break;
+        if (!wait(&b_full[st], ph) || !wait(&a_full[st], ph)) break;
         tc_fence_after();
-        const uint32_t as = smem_u32(sm + L::offA + st * L::kA), bs = smem_u32(sm + L::offB + st * L::kB);
+        const uint64_t da = da0 + (uint64_t)((st * L::kA) >> 4), db = db0 + (uint64_t)((st * L::kB) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16(tmem, kmajor_desc(as + kk * 32), kmajor_desc(bs + kk * 32), idesc, (kb | kk) ? 1u : 0u);
+        for (int kk = 0; kk < kBK / 16; ++kk) umma_f16(acc, da + 2 * kk, db + 2 * kk, idesc, (kb > 1 || kk) ? 1u : 0u);
         umma_commit(&st_empty[st]);
       }
-      umma_commit(acc_full);  // fires once every MMA issued above has completed
+      umma_commit(acc_full);  // fires once every MMA this thread issued has completed
     }
   } else {
     // ---- decode warps 2..17 (and, afterwards, warps 4..7 run the epilogue)
+    // (the warp counts follow kDecodeWarps; 16 is the built configuration)
     const int dt = tid - 64;
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb / SPG, sub = kb % SPG, rs = s % kRawSlots;
@@ -468,6 +510,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
     }
     if (warp >= 4 && warp < 8) {
       const int q = warp - 4;  // TMEM lanes 32q .. 32q+31 = weight rows of this warp
+      pdl_wait();                // the token scales are the prep kernel's output
+      for (int i = tid - 128; i < TN; i += 128) sscale[i] = (t0 + i < a.M) ? a.tscale[t0 + i] : 0.0f;
+      named_sync(1, 128);        // warps 4..7
       const bool ok = wait(acc_full, 0u);
       tc_fence_after();
       const int r = q * 32 + lane;
@@ -479,8 +524,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
       }
 #pragma unroll 1
       for (int c0 = 0; c0 < TN; c0 += 16) {
-        float v[16];
+        float v[16], v1[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + kAccStride + (uint32_t)c0, v1);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += v1[j];
         if (!ok || n >= a.N) continue;
         if (a.splits > 1) {  // partial sums of this k split; the reduce kernel finishes them
           float* pp = a.partial + ((size_t)blockIdx.z * a.Mp + (size_t)(t0 + c0)) * a.N + n;
@@ -581,6 +629,8 @@ __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x,
                                                                   int64_t K, int64_t kp, bool vec, __half* xw,
                                                                   float* tscale) {
   using U = PrepUnit<XDT>;
+  pdl_trigger();
+  pdl_wait();  // x may be the previous kernel's output
   const int64_t t = blockIdx.x;
   const int64_t units = kp / 8, row = t * ldx;
   const bool live = t < M;
@@ -660,6 +710,8 @@ __device__ __forceinline__ void reduce_store(void* y, int y_dtype, int64_t off, 
 __global__ void gemm_reduce_kernel(const float* partial, int splits, int64_t Mp, int64_t M, int64_t N,
                                    const float* tscale, const float* row_scale, int scale_len, const float* bias,
                                    void* y, int y_dtype, int64_t ldy) {
+  pdl_trigger();
+  pdl_wait();  // the partials are the GEMM's output
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if ((N & 3) == 0) {
     const int64_t n4 = N / 4, total = M * n4;
@@ -696,6 +748,24 @@ __global__ void gemm_reduce_kernel(const float* partial, int splits, int64_t Mp,
   }
 }
 
+// Launch with programmatic stream serialization: the kernel may start before the
+// previous kernel in the stream completes; it calls griddepcontrol.wait before it reads
+// anything that kernel writes.
+template <typename... P, typename... A>
+cudaError_t launch_pdl(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+}
+
 template <int FMT, int TN>
 cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
   using L = GemmSmem<FMT, TN>;
@@ -708,8 +778,7 @@ cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
     configured[dev & 63] = 1;
   }
   const dim3 grid((unsigned)(a.Mp / TN), (unsigned)((a.T + 7) / 8), (unsigned)a.splits);
-  qgemm_kernel<FMT, TN><<<grid, kGemmThreads, L::bytes, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(qgemm_kernel<FMT, TN>, grid, dim3(kGemmThreads), (size_t)L::bytes, st, a);
 }
 
 template <int FMT>
@@ -796,23 +865,23 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   float* partial = reinterpret_cast<float*>(ws + p.xw_bytes + (((size_t)Mp * 4 + 255) / 256) * 256);
   const int es = c.x_dtype == 0 ? 4 : 2;
   const bool vec = (reinterpret_cast<uintptr_t>(c.x) % 16 == 0) && ((c.ldx * es) % 16 == 0);
-  const unsigned pblocks = (unsigned)Mp;
+  const dim3 pg((unsigned)Mp), pb(kPrepThreadsG);
+  cudaError_t e;
   if (c.w8a8) {
     if (c.x_dtype == 0)
-      gemm_prep_kernel<0, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<0, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
     else if (c.x_dtype == 1)
-      gemm_prep_kernel<1, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<1, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
     else
-      gemm_prep_kernel<2, true><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<2, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
   } else {
     if (c.x_dtype == 0)
-      gemm_prep_kernel<0, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<0, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
     else if (c.x_dtype == 1)
-      gemm_prep_kernel<1, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<1, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
     else
-      gemm_prep_kernel<2, false><<<pblocks, kPrepThreadsG, 0, c.stream>>>(c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+      e = launch_pdl(gemm_prep_kernel<2, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmArgs a{};
   a.w = c.w;
@@ -842,10 +911,9 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;
   const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * (int64_t)c.sm_count));
-  gemm_reduce_kernel<<<blocks, 256, 0, c.stream>>>(partial, p.splits, Mp, c.M, c.N, tscale,
-                                                   c.fmt == FMT_FP8 ? c.row_scale : nullptr, c.scale_len, c.bias,
-                                                   c.y, c.y_dtype, c.ldy);
-  return cudaGetLastError();
+  return launch_pdl(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, c.stream, (const float*)partial, p.splits, Mp,
+                    c.M, c.N, (const float*)tscale, (const float*)(c.fmt == FMT_FP8 ? c.row_scale : nullptr),
+                    c.scale_len, c.bias, c.y, c.y_dtype, c.ldy);
 }
 
 }  // namespace rtd
