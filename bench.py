@@ -277,6 +277,78 @@ def _tp_rowparallel(world, rank, dev, stream, reps: int = 50):
     return out
 
 
+def _m_sweep(dev, rank: int):
+    """The rest of the config-1 sweep's token counts at (N, K) = (14336, 4096) for every
+    format (the four M = 1 shapes are the headline step): skinny M = 4, 16, 64 in GB/s of
+    algorithmic bytes (HBM roofline) and prefill M = 512, 2048 in TFLOP/s (tensor
+    roofline against the measured bf16 burst peak).  Each point is a CUDA graph of 10
+    calls over 3 weight copies (L2 is not reused between calls), 5 replays, CUDA events."""
+    import torch
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.weights import Fp8Weight, QMatMul
+
+    L = _lib.lib()
+    n, k = 14336, 4096
+    tflops_peak = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            tflops_peak = json.load(f).get("bf16_tflops")
+    out = {"shape_nk": [n, k], "timing": "CUDA graph of 10 calls over 3 weight copies, 5 replays, CUDA events",
+           "tflops_peak": tflops_peak, "tflops_peak_source": "MEASURED_PEAKS.json bf16_tflops (measured)"}
+    for name, t in FORMATS:
+        objs = []
+        for c in range(3):
+            if t == 0:
+                w, sc = synth.fp8_matrix(n, k, seed=rank + 20 + c, stream=k)
+                objs.append(Fp8Weight(w, sc, k, n, device=dev))
+            else:
+                objs.append(QMatMul(t, synth.quant_matrix(t, n, k, seed=rank + 20 + c, stream=k), n, k, device=dev))
+        row = {}
+        for m in (4, 16, 64, 512, 2048):
+            x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+            def call(o, st):
+                if t == 0:
+                    rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, y.data_ptr(),
+                                          _lib.DT_BF16, n, _lib.FP8_W8A16, st)
+                else:
+                    rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, None, y.data_ptr(),
+                                       _lib.DT_BF16, n, st)
+                if rc != 0:
+                    raise RuntimeError(f"m-sweep {name} M={m}: status {rc}")
+
+            for o in objs:
+                call(o, torch.cuda.current_stream(dev).cuda_stream)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for r in range(10):
+                    call(objs[r % 3], torch.cuda.current_stream(dev).cuda_stream)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(5):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            del g
+            us = a.elapsed_time(b) * 1e3 / 50
+            if m <= 64:
+                gbs = (weight_bytes(t, n, k) + m * k * 2 + m * n * 2) / (us * 1e-6) / 1e9
+                row[f"m{m}"] = {"us": round(us, 2), "gbs": round(gbs, 1)}
+            else:
+                tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+                row[f"m{m}"] = {"us": round(us, 2), "tflops": round(tf, 1),
+                                "frac": round(tf / tflops_peak, 3) if tflops_peak else None}
+        out[name] = row
+        del objs
+    return out
+
+
 def _dominant_launch_ms(it, call, stream, dev, rank, reps: int = 24) -> float:
     import torch
     from runtimed_b200 import synth
@@ -312,26 +384,29 @@ def _dominant_launch_ms(it, call, stream, dev, rank, reps: int = 24) -> float:
 
 
 def profile_one(spec: str, calls: int) -> int:
-    """Run `calls` M=1 bf16 calls of one sweep GEMV (FMT:N:K), or of every sweep GEMV in
-    step order ("sweep"), eagerly, and exit: the target of the ncu captures summarised
-    under profiles/ (the bench's own step is a CUDA graph, which ncu reports as one
-    result)."""
+    """Run `calls` bf16 calls of one linear (FMT:N:K, or FMT:N:K:M for M tokens; M = 1 by
+    default), or of every sweep GEMV in step order ("sweep"), eagerly, and exit: the
+    target of the ncu captures summarised under profiles/ (the bench's own step is a
+    CUDA graph, which ncu reports as one result)."""
     import torch
     from runtimed_b200 import _lib, synth
     from runtimed_b200.weights import Fp8Weight, QMatMul
 
+    m = 1
     if spec == "sweep":
         todo = [(t, n, k) for _, t, n, k in sweep()]
     else:
-        name, n, k = spec.split(":")
+        parts = spec.split(":")
+        name, n, k = parts[:3]
+        m = int(parts[3]) if len(parts) > 3 else 1
         todo = [(dict(FORMATS)[name], int(n), int(k))]
     dev = torch.device("cuda", 0)
     L = _lib.lib()
     st = torch.cuda.current_stream(dev).cuda_stream
     items = []
     for t, n, k in todo:
-        x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=0))).to(torch.bfloat16).to(dev)
-        y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+        x = torch.from_numpy(synth.bf16_round(synth.activations(m, k, seed=0))).to(torch.bfloat16).to(dev)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
         if t == 0:
             w, s = synth.fp8_matrix(n, k, seed=0, stream=k)
             o = Fp8Weight(w, s, k, n, device=dev)
@@ -341,10 +416,10 @@ def profile_one(spec: str, calls: int) -> int:
     for _ in range(calls):
         for t, n, k, o, x, y in items:
             if t == 0:
-                rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, y.data_ptr(),
+                rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, y.data_ptr(),
                                       _lib.DT_BF16, n, _lib.FP8_W8A16, st)
             else:
-                rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, 1, None, y.data_ptr(),
+                rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, None, y.data_ptr(),
                                    _lib.DT_BF16, n, st)
             if rc != 0:
                 raise RuntimeError(f"status {rc}")
@@ -359,7 +434,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K|sweep",
+    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep",
                     help="only run a few eager calls of one sweep GEMV or of the whole sweep (ncu target), "
                          "no JSON line")
     ap.add_argument("--calls", type=int, default=4)
@@ -518,6 +593,7 @@ def main() -> int:
     e2e_val = world * step_bytes * e2e_steps / (float(e2e_ms.item()) * 1e-3) / 1e9
 
     tp = _tp_rowparallel(world, rank, dev, stream) if world > 1 else None
+    msweep = _m_sweep(dev, rank) if world == 1 else None
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
     del graph
     if world > 1:
@@ -534,6 +610,7 @@ def main() -> int:
                     "path": "rtd_qlinear / rtd_fp8_linear per GEMV, eager, pinned-host x in and y out"},
             "gpu_launches": sum(launches_per_gemv(it["t"], it["k"]) for it in items) * args.steps,
             "tp": tp,
+            "m_sweep": msweep,
             "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0

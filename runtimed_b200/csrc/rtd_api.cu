@@ -50,7 +50,10 @@ struct rtd_fp8weight {
 namespace {
 
 constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging (GEMV prep, GEMM tiles)
-constexpr int64_t kGemvMaxTokens = 4;            // tokens one decode-GEMV pass handles
+// calls with at least this many tokens go to the tensor-core GEMM: measured on B200,
+// the four-column GEMV pass is slower than one TN = 16 GEMM tile from M = 4 on, and
+// faster up to M = 3
+constexpr int64_t kGemmMinTokens = 4;
 constexpr int64_t kCounters = 1 << 17;           // per-tile arrival counters
 
 thread_local std::string g_thread_err;
@@ -301,9 +304,9 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
   int plan_err = 0;
-  // more tokens than the decode GEMV streams per pass go to the tensor-core GEMM
-  // when its staged activations fit the workspace
-  if (M > kGemvMaxTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
+  // four or more tokens go to the tensor-core GEMM when its staged activations fit
+  // the workspace
+  if (M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
     e = rtd::launch_qgemm(c, &plan_err);
   else
     e = rtd::launch_qgemv(c, &plan_err);

@@ -1,4 +1,4 @@
-"""Tensor-core (tcgen05) GEMM path: calls with more than four tokens.
+"""Tensor-core (tcgen05) GEMM path: calls with four or more tokens.
 
 Weights are decoded in shared memory to f16 (the reference dequantisation formulas
 in f32, rounded once) and multiplied on the 5th-generation tensor cores with f32

@@ -87,8 +87,8 @@ def test_gemv_parity_small(name, t, M, xdt):
     want = oracle.qgemv_f64(t, raw, N, K, xt.float().numpy())
     y = qm.forward(xt.cuda(), out_dtype=torch.float32).cpu().numpy()
     err = rel_l2(y, want)
-    # M > 4 runs the tensor-core GEMM, whose weights are rounded once to f16
-    assert err <= (RTOL_EXACT if M <= 4 else RTOL), err
+    # M >= 4 runs the tensor-core GEMM, whose weights are rounded once to f16
+    assert err <= (RTOL_EXACT if M <= 3 else RTOL), err
 
 
 @pytest.mark.parametrize("name,t", FORMATS)
@@ -96,11 +96,12 @@ def test_gemv_parity_small(name, t, M, xdt):
 def test_gemv_parity_config1_shapes(name, t, N, K):
     torch = _torch()
     qm, raw = make_qm(t, N, K, seed=1, stream=t)
-    for M in (1, 4):
+    for M in (1, 3, 4):
         x = synth.bf16_round(synth.activations(M, K, seed=2, stream=M))
         want = oracle.qgemv_f64(t, raw, N, K, x)
         y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32).cpu().numpy()
-        assert rel_l2(y, want) <= RTOL_EXACT
+        # M >= 4 runs the tensor-core GEMM (weights rounded once to f16)
+        assert rel_l2(y, want) <= (RTOL_EXACT if M <= 3 else RTOL)
 
 
 def test_gemv_parity_vocab_q8_0():
