@@ -493,19 +493,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
     // ---- decode warps 2..17 (and, afterwards, warps 4..7 run the epilogue)
     // (the warp counts follow kDecodeWarps; 16 is the built configuration)
     const int dt = tid - 64;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb / SPG, sub = kb % SPG, rs = s % kRawSlots;
-      const int st = kb % kStages;
+    // With four or more stages the warps decode two consecutive stages per iteration
+    // (always within one group: SPG is 2 or 4 and kb is even), so the waits, the proxy
+    // fence and the arrivals are paid once per pair and the two decodes overlap.
+    constexpr int KPI = kStages >= 4 ? 2 : 1;
+    for (int kb = 0; kb < nkb; kb += KPI) {
       bool ok = true;
-      if (sub == 0) ok = wait(&raw_full[rs], (uint32_t)((s / kRawSlots) & 1));
-      if (ok && kb >= kStages) ok = wait(&st_empty[st], (uint32_t)((kb / kStages - 1) & 1));
+#pragma unroll
+      for (int u = 0; u < KPI; ++u) {
+        const int k2 = kb + u, s = k2 / SPG, sub = k2 % SPG, st = k2 % kStages;
+        if (ok && sub == 0) ok = wait(&raw_full[s % kRawSlots], (uint32_t)((s / kRawSlots) & 1));
+        if (ok && k2 >= kStages) ok = wait(&st_empty[st], (uint32_t)((k2 / kStages - 1) & 1));
+      }
       if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the arrivals below are per warp
-      decode_stage<FMT>(smem_u32(sm + L::offRaw + rs * L::kRaw), sub, smem_u32(sm + L::offA + st * L::kA), dt);
+#pragma unroll
+      for (int u = 0; u < KPI; ++u) {
+        const int k2 = kb + u, s = k2 / SPG;
+        decode_stage<FMT>(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
+                          smem_u32(sm + L::offA + (k2 % kStages) * L::kA), dt);
+      }
       fence_async_shared();  // every writer: the tensor cores read A through the async proxy
       __syncwarp();
       if (lane == 0) {  // one arrival per warp: 512 single-thread arrivals would serialise
-        mbar_arrive(&a_full[st]);
-        if (sub == SPG - 1) mbar_arrive(&raw_empty[rs]);
+#pragma unroll
+        for (int u = 0; u < KPI; ++u) {
+          const int k2 = kb + u, s = k2 / SPG;
+          mbar_arrive(&a_full[k2 % kStages]);
+          if (k2 % SPG == SPG - 1) mbar_arrive(&raw_empty[s % kRawSlots]);
+        }
       }
     }
     if (warp >= 4 && warp < 8) {
