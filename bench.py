@@ -221,14 +221,16 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def launches_per_gemv(t: int, k: int) -> int:
-    """Kernels one M=1 bf16 call launches: the GEMV alone when every CTA can stage the
-    activation row itself (rtd_gemv.cu launch_qgemv: K % 8 == 0 and the staged row plus
-    its column-sum table within 40 KB), else a prep kernel as well."""
+def launches_per_gemv(t: int, n: int, k: int) -> int:
+    """Kernels one M=1 bf16 call launches (rtd_gemv.cu launch_qgemv): the GEMV alone when
+    the launch runs in whole mode (at least two 16-row tiles per warp of two 8-warp CTAs
+    on each of the 148 SMs) and every CTA can stage the activation row itself (K % 8 == 0,
+    the staged row plus its column-sum table within 40 KB); otherwise a prep kernel too."""
     gk, sbe = {0: (128, 32), 8: (128, 32), 12: (256, 32), 14: (256, 16)}[t]
     kp = -(-k // gk) * gk
     tab = (kp // gk) * (gk // sbe + 4)
-    return 1 if (k % 8 == 0 and kp * 2 + tab * 4 <= 40 * 1024) else 2
+    whole = -(-n // 16) >= 2 * 148 * 2 * 8
+    return 1 if (whole and k % 8 == 0 and kp * 2 + tab * 4 <= 40 * 1024) else 2
 
 
 def config_dict():
@@ -642,7 +644,7 @@ def main() -> int:
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "rtd_qlinear / rtd_fp8_linear per GEMV, eager; per step one pinned-host copy of the 14 "
                             "activation rows in and one of the 14 outputs out, then a host wait"},
-            "gpu_launches": sum(launches_per_gemv(it["t"], it["k"]) for it in items) * args.steps,
+            "gpu_launches": sum(launches_per_gemv(it["t"], it["n"], it["k"]) for it in items) * args.steps,
             "tp": tp,
             "m_sweep": msweep,
             "clocks": clk.summary()}
