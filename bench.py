@@ -253,11 +253,13 @@ def _time_steps(graph, stream, dev, n: int) -> float:
     return a.elapsed_time(b) * 1e-3
 
 
-def _tp_rowparallel(world, rank, dev, stream, reps: int = 50):
+def _tp_rowparallel(world, rank, dev, stream, reps: int = 20):
     """Row-parallel down_proj of the 70B-shaped config (Q6_K, N = 8192, K = 28672 split
     over the ranks): the reduction fused into the GEMV epilogue (peer stores over NVLink)
-    against the same GEMV followed by an NCCL all-reduce.  Device time per call, max
-    over ranks; every rank issues the same calls in the same order."""
+    against the same GEMV followed by an NCCL all-reduce.  Each path is captured in a
+    CUDA graph of `reps` calls (the fused call keeps its epoch on the device, so replays
+    are valid); device time per call, max over ranks; every rank issues the same calls
+    and collectives in the same order."""
     import torch
     import torch.distributed as dist
     from runtimed_b200 import synth
@@ -269,22 +271,31 @@ def _tp_rowparallel(world, rank, dev, stream, reps: int = 50):
     comm = TpComm(Context.for_device(dev), rank, world, max_n=n)
     rpl = RowParallelLinear.from_full_weight(raw, t, n, k, None, rank, world, comm=comm, device=dev)
     del raw
-    out = {"shape_nk": [n, k], "format": "Q6_K", "world": world, "k_shard": k // world}
+    out = {"shape_nk": [n, k], "format": "Q6_K", "world": world, "k_shard": k // world,
+           "timing": f"CUDA graph of {reps} calls per path, 5 replays, CUDA events, max over ranks"}
     for m in (1, 4):
         x = torch.from_numpy(synth.activations(m, k // world, seed=rank)).to(torch.bfloat16).to(dev)
         res = {}
         for name, fn in (("fused", rpl.forward), ("nccl", rpl.forward_nccl)):
-            for _ in range(5):
+            for _ in range(3):
                 fn(x)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(reps):
+                    fn(x)
+            g.replay()
             torch.cuda.synchronize(dev)
             dist.barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            for _ in range(reps):
-                fn(x)
+            for _ in range(5):
+                g.replay()
             b.record(stream)
             torch.cuda.synchronize(dev)
-            ms = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=dev)
+            del g  # graphs holding NCCL work go before the process group
+            ms = torch.tensor([a.elapsed_time(b) / (5 * reps)], dtype=torch.float64, device=dev)
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
             res[name] = float(ms.item()) * 1e3
         shard_bytes = n * (k // world // 256) * 210

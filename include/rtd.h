@@ -142,7 +142,9 @@ rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out,
  *   3. rtd_tp_comm_open with all handles.
  * Every rank must issue the same sequence of rtd_tp_qlinear_row calls; a rank that
  * does not arrive within 2 s makes the others finish with RTD_ERR_PEER_TIMEOUT in
- * the device status word (rtd_check_device_status). */
+ * the device status word (rtd_check_device_status).  The call keeps its exchange
+ * epoch on the device, so it may be captured in a CUDA graph and replayed (all ranks
+ * replaying their graphs in step). */
 #define RTD_IPC_HANDLE_BYTES 64
 typedef struct rtd_comm rtd_comm;
 rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, rtd_comm** out, void* handle_out);

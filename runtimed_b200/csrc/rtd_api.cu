@@ -412,7 +412,9 @@ rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out,
 // One communicator per rank (one process per GPU).  Its device buffer holds, for
 // both call parities, a receive slot per rank ([world][4 * max_n] f32, up to four
 // activation columns per launch) and a flag per (rank, tile); peers map it through
-// CUDA IPC and store into it over NVLink.
+// CUDA IPC and store into it over NVLink.  Two more device words (epoch, finished
+// CTAs) carry the launch epoch from one launch to the next on the device, so the
+// call can be captured in a CUDA graph.
 struct rtd_comm {
   rtd_ctx* ctx = nullptr;
   int world = 1, rank = 0;
@@ -421,7 +423,7 @@ struct rtd_comm {
   size_t recv_bytes = 0, bytes = 0;
   unsigned char* peer[rtd::kMaxTpWorld] = {};  // mapped peer buffers (peer[rank] = base)
   bool opened = false;
-  uint32_t epoch = 0;
+  size_t ctrl_off = 0;  // this rank's epoch / finished-CTA words (not used by peers)
   rtd::TpReduce tp{};
 };
 
@@ -441,7 +443,8 @@ rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, 
   c->max_n = max_n;
   c->max_tiles = (max_n + 15) / 16;
   c->recv_bytes = (size_t)2 * world * 4 * (size_t)max_n * sizeof(float);
-  c->bytes = c->recv_bytes + (size_t)2 * world * (size_t)c->max_tiles * sizeof(uint32_t);
+  c->ctrl_off = (c->recv_bytes + (size_t)2 * world * (size_t)c->max_tiles * sizeof(uint32_t) + 255) / 256 * 256;
+  c->bytes = c->ctrl_off + 256;
   cudaError_t e = cudaMalloc(&c->base, c->bytes);
   if (e != cudaSuccess) {
     delete c;
@@ -480,7 +483,7 @@ rtd_status rtd_tp_comm_open(rtd_comm* c, const void* handles) {
   c->tp.rank = c->rank;
   c->tp.max_n = c->max_n;
   c->tp.max_tiles = c->max_tiles;
-  c->tp.epoch = &c->epoch;
+  c->tp.ctrl = reinterpret_cast<uint32_t*>(c->base + c->ctrl_off);
   for (int p = 0; p < c->world; ++p) {
     c->tp.recv[p] = reinterpret_cast<float*>(c->peer[p]);
     c->tp.flags[p] = reinterpret_cast<uint32_t*>(c->peer[p] + c->recv_bytes);

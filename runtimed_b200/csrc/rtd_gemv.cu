@@ -644,7 +644,7 @@ struct Args {
   float* tp_recv[kMaxTpWorld];
   uint32_t* tp_flags[kMaxTpWorld];
   int64_t tp_max_n, tp_max_tiles;
-  uint32_t tp_epoch;
+  uint32_t* tp_ctrl;  // [0] epoch, [1] finished-CTA count (device)
   int* status;
 };
 
@@ -674,9 +674,12 @@ __device__ __forceinline__ void named_bar_arrive(int id, int n) {
 // every rank writes the same bits.  A peer that never arrives ends the wait after
 // kWaitBudgetNs with RTD_ERR_PEER_TIMEOUT in the status word.
 __device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const float* rb, const float* ep,
-                                                 int lane) {
+                                                 int lane, uint32_t epoch) {
   const int W = a.tp_world, R = a.tp_rank;
   const int64_t slot_elems = 4 * a.tp_max_n;
+  // this launch's parity half of every rank's receive slots and flags
+  const int64_t par = (int64_t)(epoch & 1u);
+  const int64_t recv_par = par * W * slot_elems, flag_par = par * W * a.tp_max_tiles;
   for (int o = lane; o < 16 * a.M; o += 32) {
     const int r = o / a.M, t = o - r * a.M;
     const int64_t n = (int64_t)tile * 16 + r;
@@ -686,24 +689,24 @@ __device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const 
       for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
     if (n < a.N) {
       const int64_t off = (int64_t)R * slot_elems + (int64_t)t * a.N + n;
-      for (int p = 0; p < W; ++p) a.tp_recv[p][off] = sum * ep[16 + r];
+      for (int p = 0; p < W; ++p) a.tp_recv[p][recv_par + off] = sum * ep[16 + r];
     }
   }
   __syncwarp();
   if (lane == 0) {
     __threadfence_system();
-    for (int p = 0; p < W; ++p) st_release_sys(a.tp_flags[p] + (int64_t)R * a.tp_max_tiles + tile, a.tp_epoch);
+    for (int p = 0; p < W; ++p) st_release_sys(a.tp_flags[p] + flag_par + (int64_t)R * a.tp_max_tiles + tile, epoch);
   }
   if (lane < W && lane != R)
-    wait_flag_sys(a.tp_flags[R] + (int64_t)lane * a.tp_max_tiles + tile, a.tp_epoch, kWaitBudgetNs, a.status);
+    wait_flag_sys(a.tp_flags[R] + flag_par + (int64_t)lane * a.tp_max_tiles + tile, epoch, kWaitBudgetNs, a.status);
   __syncwarp();
   for (int q = 0; q < W; ++q)  // every reading lane acquires the arrivals itself
-    if (q != R) (void)ld_acquire_sys(a.tp_flags[R] + (int64_t)q * a.tp_max_tiles + tile);
+    if (q != R) (void)ld_acquire_sys(a.tp_flags[R] + flag_par + (int64_t)q * a.tp_max_tiles + tile);
   for (int o = lane; o < 16 * a.M; o += 32) {
     const int r = o / a.M, t = o - r * a.M;
     const int64_t n = (int64_t)tile * 16 + r;
     if (n < a.N) {
-      const volatile float* src = a.tp_recv[R] + (int64_t)t * a.N + n;
+      const volatile float* src = a.tp_recv[R] + recv_par + (int64_t)t * a.N + n;
       float v = 0.0f;
       for (int q = 0; q < W; ++q) v += src[(int64_t)q * slot_elems];
       store_y(a, t, n, v + ep[r]);
@@ -886,6 +889,9 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   }
   griddep_wait();  // earlier work in the stream (x, the prep kernel's output) is visible from here on
   griddep_launch_dependents();  // the next call may launch; it waits for this grid before touching x
+  // row-parallel launches: this launch's epoch (the previous TP launch, complete by now,
+  // left its own in ctrl[0])
+  const uint32_t tp_epoch = a.tp_world > 1 ? *reinterpret_cast<volatile uint32_t*>(a.tp_ctrl) + 1u : 0u;
   for (int s = 0; s < npro; ++s) {
     if (lane == 0 && !local_x) issue_x(s, it_g0, min(a.IG, a.G - it_g0));
     advance();
@@ -1027,7 +1033,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       }
       __syncwarp();
       if (a.tp_world > 1) {
-        tp_exchange_tile(a, tile, rb, ep, lane);
+        tp_exchange_tile(a, tile, rb, ep, lane, tp_epoch);
       } else {
         for (int o = lane; o < 16 * a.M; o += 32) {
           const int r = o / a.M, t = o - r * a.M;
@@ -1048,6 +1054,17 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     for (int s = 0; s < NS && s < next_issue; ++s) {
       const int last = s + ((next_issue - 1 - s) / NS) * NS;  // the last item issued into slot s
       mbar_wait_ns(&bar[s], (uint32_t)(last / NS) & 1u, kWaitBudgetNs, a.status);
+    }
+  }
+  if (a.tp_world > 1) {  // the last CTA of the launch publishes its epoch for the next one
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      if (atomicAdd(a.tp_ctrl + 1, 1u) == gridDim.x - 1) {
+        a.tp_ctrl[1] = 0u;
+        a.tp_ctrl[0] = tp_epoch;
+        __threadfence();
+      }
     }
   }
 }
@@ -1405,16 +1422,14 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
         *plan_error = 1;
         return cudaSuccess;
       }
-      const uint32_t epoch = ++*tp.epoch;
-      const int par = (int)(epoch & 1u);
       a.tp_world = tp.world;
       a.tp_rank = tp.rank;
       a.tp_max_n = tp.max_n;
       a.tp_max_tiles = tp.max_tiles;
-      a.tp_epoch = epoch;
-      for (int p = 0; p < tp.world; ++p) {
-        a.tp_recv[p] = tp.recv[p] + (size_t)par * tp.world * 4 * tp.max_n;
-        a.tp_flags[p] = tp.flags[p] + (size_t)par * tp.world * tp.max_tiles;
+      a.tp_ctrl = tp.ctrl;
+      for (int p = 0; p < tp.world; ++p) {  // parity-0 bases; the kernel picks its half by epoch
+        a.tp_recv[p] = tp.recv[p];
+        a.tp_flags[p] = tp.flags[p];
       }
     }
     a.status = c.status;

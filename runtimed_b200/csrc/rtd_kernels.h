@@ -28,7 +28,11 @@ struct TpReduce {
   float* recv[kMaxTpWorld];      // rank p's receive region [2 parities][world][4 * max_n] f32
   uint32_t* flags[kMaxTpWorld];  // rank p's arrival flags [2 parities][world][max_tiles]
   int64_t max_n, max_tiles;
-  uint32_t* epoch;               // host counter, advanced once per launch (all ranks in step)
+  uint32_t* ctrl;                // this rank's device words: [0] epoch of the last launch,
+                                 // [1] CTAs finished in the current launch; the launch reads
+                                 // the epoch after griddepcontrol.wait and its last CTA
+                                 // advances it, so a CUDA graph replays with fresh epochs
+                                 // (all ranks make the same calls, so epochs stay in step)
 };
 
 struct QGemvCall {

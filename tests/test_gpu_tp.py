@@ -50,7 +50,9 @@ def _rank_main(rank, world, port, q):
             bias = np.random.default_rng(t).normal(0, 0.02, n).astype(np.float32)
             rpl = RowParallelLinear.from_full_weight(raw, t, n, k, bias, rank, world, comm=comm, device=dev)
             ks = k // world
-            for call, (m, dt) in enumerate([(1, torch.bfloat16), (3, torch.float32), (4, torch.float16), (1, torch.bfloat16)]):
+            # M = 6 runs as two launches (four tokens each at most): two epochs in one call
+            for call, (m, dt) in enumerate([(1, torch.bfloat16), (3, torch.float32), (4, torch.float16),
+                                            (6, torch.float32), (1, torch.bfloat16)]):
                 x = synth.activations(m, k, seed=100 * t + call)
                 xt = torch.from_numpy(x).to(dt)
                 want = oracle.qgemv_f64(t, raw, n, k, xt.float().numpy()) + bias[None, :]
@@ -64,8 +66,33 @@ def _rank_main(rank, world, port, q):
                 # y comes back in x's dtype: its rounding bounds the error (bf16 ~2^-9 RMS)
                 tol = OUT_TOL[dt]
                 rf, rn = _rel(y.cpu().numpy(), want), _rel(yn.cpu().numpy(), want)
-                out[(t, call)] = (rf <= tol, rn <= tol, all(bool(torch.equal(g, gathered[0])) for g in gathered),
+                # the NCCL path's local partial runs the single-GPU linear: the tensor-core
+                # GEMM (f16-rounded weights, 1e-3 gate) from four tokens on
+                tol_n = tol if m <= 3 else max(tol, 1e-3)
+                out[(t, call)] = (rf <= tol, rn <= tol_n, all(bool(torch.equal(g, gathered[0])) for g in gathered),
                                   rf, rn)
+        # the fused call captured in a CUDA graph: the epoch lives on the device, so
+        # every replay exchanges fresh partials (new x each replay, checked each time)
+        t, n, k = 14, 1000, 1024
+        raw = synth.quant_matrix(t, n, k, seed=6, stream=t)
+        rpl = RowParallelLinear.from_full_weight(raw, t, n, k, None, rank, world, comm=comm, device=dev)
+        ks = k // world
+        xs = torch.zeros((2, ks), dtype=torch.float32, device=dev)
+        rpl.forward(xs)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            yg = rpl.forward(xs)
+        graph_ok = []
+        for rep in range(3):
+            x = synth.activations(2, k, seed=900 + rep)
+            xs.copy_(torch.from_numpy(x[:, rank * ks:(rank + 1) * ks]).to(dev))
+            g.replay()
+            torch.cuda.synchronize()
+            ctx.check_device_status()
+            graph_ok.append(_rel(yg.cpu().numpy(), oracle.qgemv_f64(t, raw, n, k, x)) <= RTOL_EXACT)
+        del g
+        out["graph"] = all(graph_ok)
         # a rank that skips a call: the other finishes with RTD_ERR_PEER_TIMEOUT
         raw = synth.quant_matrix(12, 16, 512, seed=1)
         rpl = RowParallelLinear.from_full_weight(raw, 12, 16, 512, None, rank, world, comm=comm, device=dev)
@@ -83,9 +110,13 @@ def _rank_main(rank, world, port, q):
         dist.barrier()
         out["timeout"] = timed_out
         comm.close()
+    except BaseException as e:  # reported to the parent, which fails the test with it
+        out["error"] = f"{type(e).__name__}: {e}"
     finally:
-        dist.destroy_process_group()
-    q.put((rank, out))
+        try:
+            dist.destroy_process_group()
+        finally:
+            q.put((rank, out))  # always: a rank that raised must not leave the parent waiting
 
 
 def test_row_parallel_fused_allreduce_two_gpus():
@@ -102,11 +133,13 @@ def test_row_parallel_fused_allreduce_two_gpus():
     procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in procs)
+    res = dict(q.get(timeout=300) for _ in procs)
     for p in procs:
         p.join(timeout=120)
     for rank, out in res.items():
-        for key, (fused_ok, nccl_ok, same, rf, rn) in ((k, v) for k, v in out.items() if k != "timeout"):
+        assert "error" not in out, (rank, out.get("error"))
+        assert out["graph"] is True, (rank, "graph replay")
+        for key, (fused_ok, nccl_ok, same, rf, rn) in ((k, v) for k, v in out.items() if k not in ("timeout", "graph", "error")):
             assert fused_ok, (rank, key, "fused", rf)
             assert nccl_ok, (rank, key, "nccl", rn)
             assert same, (rank, key, "ranks differ")
