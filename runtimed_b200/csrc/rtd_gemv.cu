@@ -666,15 +666,16 @@ __device__ __forceinline__ void named_bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// Row-parallel tile exchange, run by the tile's writer warp in place of the plain
-// store.  rb holds the 8 warps' partial sums of the tile, ep the bias (full, added
-// once after the reduction) and the row scale.  The rank's partials go to its slot on
-// every rank (peer stores over NVLink), are published with a system-scope release,
-// and the tile is written once every rank's partial has arrived -- in rank order, so
-// every rank writes the same bits.  A peer that never arrives ends the wait after
-// kWaitBudgetNs with RTD_ERR_PEER_TIMEOUT in the status word.
-__device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const float* rb, const float* ep,
-                                                 int lane, uint32_t epoch) {
+// Row-parallel tile exchange in two halves.  tp_publish_tile runs in the tile's writer
+// warp as soon as the tile's 8 warp partials are in shared memory: the rank's partial
+// (row scale applied) goes to its slot on every rank (peer stores over NVLink) and is
+// published with a system-scope release.  tp_finish_tile runs after the CTA's last tile,
+// so no warp waits for a peer while it still has groups to stream: it waits (bounded)
+// for every rank's flag of the tile, sums the partials in rank order -- every rank writes
+// the same bits -- and adds the bias once.  A peer that never arrives ends the wait
+// after kWaitBudgetNs with RTD_ERR_PEER_TIMEOUT in the status word.
+__device__ __forceinline__ void tp_publish_tile(const Args& a, int tile, const float* rb, const float* ep,
+                                                int lane, uint32_t epoch) {
   const int W = a.tp_world, R = a.tp_rank;
   const int64_t slot_elems = 4 * a.tp_max_n;
   // this launch's parity half of every rank's receive slots and flags
@@ -697,6 +698,14 @@ __device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const 
     __threadfence_system();
     for (int p = 0; p < W; ++p) st_release_sys(a.tp_flags[p] + flag_par + (int64_t)R * a.tp_max_tiles + tile, epoch);
   }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void tp_finish_tile(const Args& a, int tile, int lane, uint32_t epoch) {
+  const int W = a.tp_world, R = a.tp_rank;
+  const int64_t slot_elems = 4 * a.tp_max_n;
+  const int64_t par = (int64_t)(epoch & 1u);
+  const int64_t recv_par = par * W * slot_elems, flag_par = par * W * a.tp_max_tiles;
   if (lane < W && lane != R)
     wait_flag_sys(a.tp_flags[R] + flag_par + (int64_t)lane * a.tp_max_tiles + tile, epoch, kWaitBudgetNs, a.status);
   __syncwarp();
@@ -709,9 +718,10 @@ __device__ __forceinline__ void tp_exchange_tile(const Args& a, int tile, const 
       const volatile float* src = a.tp_recv[R] + recv_par + (int64_t)t * a.N + n;
       float v = 0.0f;
       for (int q = 0; q < W; ++q) v += src[(int64_t)q * slot_elems];
-      store_y(a, t, n, v + ep[r]);
+      store_y(a, t, n, v + (a.bias ? __ldg(a.bias + n) : 0.0f));
     }
   }
+  __syncwarp();
 }
 
 // Local-x staging for DIAG formats.  The CTA copies the raw bf16 / f16 rows into
@@ -1033,7 +1043,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       }
       __syncwarp();
       if (a.tp_world > 1) {
-        tp_exchange_tile(a, tile, rb, ep, lane, tp_epoch);
+        tp_publish_tile(a, tile, rb, ep, lane, tp_epoch);  // finished after the last tile
       } else {
         for (int o = lane; o < 16 * a.M; o += 32) {
           const int r = o / a.M, t = o - r * a.M;
@@ -1055,6 +1065,10 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       const int last = s + ((next_issue - 1 - s) / NS) * NS;  // the last item issued into slot s
       mbar_wait_ns(&bar[s], (uint32_t)(last / NS) & 1u, kWaitBudgetNs, a.status);
     }
+  }
+  if (a.tp_world > 1) {  // each writer warp finishes the tiles it published (split mode)
+    for (int tile = t0; tile < t1; ++tile)
+      if (warp == (tile & (kWarps - 1))) tp_finish_tile(a, tile, lane, tp_epoch);
   }
   if (a.tp_world > 1) {  // the last CTA of the launch publishes its epoch for the next one
     __syncthreads();
