@@ -638,7 +638,16 @@ def main() -> int:
     if not torch.equal(hy[:items[0]["n"]].to(dev), dy[:items[0]["n"]]):
         raise RuntimeError("e2e: host copy of the outputs differs from the device")
 
-    tp = _tp_rowparallel(world, rank, dev, stream) if world > 1 else None
+    tp = None
+    if world > 1:
+        # the TP comparison runs after the headline is measured; a failure there is
+        # reported in its own object instead of losing the line (a rank that fails
+        # alone leaves the others to the process group's 120 s timeout)
+        try:
+            tp = _tp_rowparallel(world, rank, dev, stream)
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            tp = {"error": f"{type(e).__name__}: {e}"}
+            torch.cuda.synchronize(dev)
     msweep = _m_sweep(dev, rank) if world == 1 else None
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
     del graph
