@@ -11,10 +11,18 @@ weights, well above the 126 MB L2, so each weight byte comes from HBM.
 Metric: quant-GEMV HBM GB/s from algorithmic bytes (packed weights + x + y (+ FP8
 channel scales)); dequantized weights never count.  value = device-timed
 (weights and x resident in HBM, CUDA graph of the step, CUDA events); e2e = the
-same through the C ABI with the activation copied from pinned host memory and
-the output read back every call.
+same through the C ABI, every step copying its 14 activation rows in from pinned
+host memory and reading its 14 outputs back before the next step.
+
+The line also carries the roofline of the longest GEMV (against the measured HBM
+copy bandwidth), the CPU baseline (the restated reference path on the host cores),
+the SM clocks sampled during the timed steps, and:
+  m_sweep  the rest of the config-1 token counts (M = 4..2048) at 14336 x 4096,
+           1 GPU only (M >= 4 runs the tensor-core GEMM);
+  tp       N > 1: the fused row-parallel linear against GEMV + NCCL all-reduce.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --profile-one FMT:N:K[:M] | sweep   (ncu target, no JSON line)
 
 N > 1 runs under torchrun, one rank per GPU, each rank its own copy of the sweep
 (weak scaling: independent weight shards), max time over ranks.
