@@ -72,6 +72,9 @@ rtd_status rtd_init(int device, rtd_ctx** out);
 rtd_status rtd_destroy(rtd_ctx* ctx);
 /* Last error message recorded on `ctx` (or on the calling thread when ctx is NULL). */
 const char* rtd_last_error(const rtd_ctx* ctx);
+/* No counterpart in the reference (diagnostics): kernels the library has launched,
+ * or recorded into a capturing stream, since it was loaded. */
+uint64_t rtd_kernel_launches(void);
 /* Synchronises `stream` and reads then clears the device status word. */
 rtd_status rtd_check_device_status(rtd_ctx* ctx, void* stream);
 /* Block geometry (crates/runtimed-gguf/src/quant/dtype.rs:49-64). */
@@ -85,6 +88,11 @@ rtd_status rtd_block_geometry(uint32_t ggml_type, int64_t* elems, int64_t* bytes
 rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host_blocks,
                               size_t nbytes, int64_t N, int64_t K, rtd_qweight** out);
 rtd_status rtd_qweight_free(rtd_qweight* w);
+/* A copy of `src` owned by `ctx` (same or another device), made on the devices without
+ * a host round trip.  Replaces Weights::to_device (crates/runtimed-model/src/weights/store.rs:170-205)
+ * for quantized entries, which stay quantized (the reference leaves q_map entries in place). */
+rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweight** out);
+
 /* raw_bytes = the GGUF byte count (QTensor::storage_size_in_bytes, store.rs:57-76);
  * device_bytes = what the device copy occupies (rows padded to a tile of 16). */
 rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* N, int64_t* K,
@@ -130,20 +138,63 @@ rtd_status rtd_fp8_linear(rtd_ctx* ctx, const rtd_fp8weight* w, const void* x, u
  * (crates/runtimed-model/src/weights/load_safetensors.rs:53-69) used at fp8_gemm.rs:98-99. */
 rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out, void* stream);
 
+/* ---- decoder-layer operations ------------------------------------------------
+ * The SubstratePort operations between the linears of a decoder layer
+ * (crates/runtimed-model/src/substrate/port.rs:14-90), on device buffers.  The KV cache
+ * is PAGED: k_cache / v_cache are f16 [blocks][n_kv][16][head_dim]; block_table is
+ * int32 [sequences][max_blocks] (block ids per 16-token span of a sequence); every
+ * token of a call carries its own sequence (tok_seq) and position (tok_pos), int32 on
+ * the device, so one call serves a prefill chunk, a batched decode step or a verify of
+ * several positions. */
+
+/* h[T, H] (f32, in place) += delta (optional, delta_dtype), then
+ * y = (h / sqrt(mean(h^2) + eps)) * w: rmsnorm (crates/runtimed-model/src/ops/norm.rs:7-11)
+ * fused with the residual add before it (crates/runtimed-model/src/arch/qwen2.rs:112,126). */
+rtd_status rtd_rmsnorm(rtd_ctx* ctx, float* h, int64_t ldh, const void* delta, uint32_t delta_dtype, int64_t ldd,
+                       const float* w, float eps, int64_t T, int64_t H, void* y, uint32_t y_dtype, int64_t ldy,
+                       void* stream);
+/* NeoX rope (crates/runtimed-model/src/ops/rope.rs:24-60) on the query and key heads of
+ * the q / k / v linear outputs (f32), queries into q_out [T][n_head][head_dim] (f32), keys
+ * and values appended to the paged cache at each token's (sequence, position):
+ * SubstratePort::rope + Cache::append (crates/runtimed-model/src/arch/qwen2.rs:100-103). */
+rtd_status rtd_rope_kv_append(rtd_ctx* ctx, const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                              int64_t ldv, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t rot_dim,
+                              float theta, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
+                              int32_t max_blocks, void* k_cache, void* v_cache, float* q_out, void* stream);
+/* o[T, n_head * head_dim] = softmax(q k^T * scale + causal mask) v with GQA, over keys
+ * [0, tok_pos[t]] of each token's sequence: SubstratePort::attention + causal_mask
+ * (crates/runtimed-model/src/ops/attention.rs:38-58,107-128).  max_ctx bounds
+ * tok_pos + 1 (it sizes the split of long contexts across CTAs). */
+rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim,
+                               float scale, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
+                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache, void* o,
+                               uint32_t o_dtype, int64_t ldo, void* stream);
+/* y[i] = silu(gate[i]) * up[i]: SubstratePort::silu + broadcast_mul
+ * (crates/runtimed-model/src/ops/activation.rs:6-10, arch/qwen2.rs:120-123). */
+rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, const void* up, uint32_t up_dtype,
+                        int64_t n, void* y, uint32_t y_dtype, void* stream);
+/* out[t] = argmax of row t of x[T, V] (f32; lowest index among equal maxima):
+ * SubstratePort::argmax behind greedy sampling (crates/runtimed-model/src/decode/sample.rs:11-18). */
+rtd_status rtd_argmax(rtd_ctx* ctx, const float* x, int64_t ldx, int64_t T, int64_t V, int32_t* out, void* stream);
+
 /* ---- tensor-parallel row reduction -----------------------------------------
  * Replaces RowParallelLinear::forward + ring_all_reduce
  * (crates/runtimed-model/src/tp/row_linear.rs:20-66, crates/runtimed-model/src/tp/ring_reduce.rs:7-65)
  * for one process per GPU: each rank holds the [N, K/world] column shard of a
- * quantized matrix (rtd_qweight_upload of the shard's blocks) and its slice of x; the
- * GEMV's epilogue exchanges the tile partials over NVLink and every rank writes the
- * full, reduced y[M, N] (+ bias once).  Set-up:
+ * quantized matrix (rtd_qweight_upload of the shard's blocks) and its slice of x, and
+ * every rank receives the full, reduced y[M, N] (+ bias once), bit-identical on every
+ * rank.  Up to three tokens run the decode GEMV with the exchange fused into its
+ * epilogue (tile partials stored into the peers' buffers over NVLink as they are
+ * produced); four or more run the tensor-core GEMM into an f32 partial followed by the
+ * two-shot all-reduce of rtd_tp_allreduce.  Set-up:
  *   1. rtd_tp_comm_create on every rank -> RTD_IPC_HANDLE_BYTES of handle bytes;
  *   2. the caller exchanges the handles (rank order) by its own means;
  *   3. rtd_tp_comm_open with all handles.
- * Every rank must issue the same sequence of rtd_tp_qlinear_row calls; a rank that
- * does not arrive within 2 s makes the others finish with RTD_ERR_PEER_TIMEOUT in
- * the device status word (rtd_check_device_status).  The call keeps its exchange
- * epoch on the device, so it may be captured in a CUDA graph and replayed (all ranks
+ * Every rank must issue the same sequence of rtd_tp_qlinear_row / rtd_tp_allreduce
+ * calls with the same M and N; a rank that does not arrive within 2 s makes the others
+ * finish with RTD_ERR_PEER_TIMEOUT in the device status word (rtd_check_device_status),
+ * after which the communicator must be re-created.  The calls keep their exchange epoch
+ * on the device, so they may be captured in a CUDA graph and replayed (all ranks
  * replaying their graphs in step). */
 #define RTD_IPC_HANDLE_BYTES 64
 typedef struct rtd_comm rtd_comm;
@@ -153,24 +204,40 @@ rtd_status rtd_tp_comm_destroy(rtd_comm* comm);
 rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const void* x, uint32_t x_dtype,
                               int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
                               void* stream);
+/* y[M, N] = sum over ranks of partial[M, N] (+ bias once) on every rank: the all-reduce
+ * of ring_all_reduce / RingReducer (crates/runtimed-model/src/tp/ring_reduce.rs:7-65).
+ * partial is f32 on the device (rows ldp apart); y is y_dtype (rows ldy apart); N must
+ * not exceed the communicator's max_n.  Two-shot over NVLink: each rank reduces one
+ * sub-chunk of every block and stores the sums into every rank's buffer. */
+rtd_status rtd_tp_allreduce(rtd_comm* comm, const float* partial, int64_t ldp, int64_t M, int64_t N,
+                            const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream);
 
 /* ---- allocation-free linear -------------------------------------------------
  * No counterpart in the reference: an addition for callers that must not allocate
  * device memory while they run (e.g. code working under another allocator's fixed
  * device-memory budget, where a cudaMalloc can fail or stall the device).
- * Same contract and kernels as rtd_qlinear, but no context argument: the scratch is a
- * fixed 1 MiB array per device inside the library (256 B status word + workspace);
- * the call allocates nothing and calls no allocating routine.
+ * Same contract and dispatch as rtd_qlinear (the tensor-core GEMM from four tokens on
+ * when its staging fits, the decode GEMV otherwise), but no context argument: the
+ * scratch is a fixed 1 MiB array per device inside the library (256 B status word +
+ * workspace); the call allocates nothing and calls no allocating routine.
  *   - The first call on a device looks the array up (cudaGetSymbolAddress) with that
  *     device current; make that first call before any stream capture.
  *   - A call whose staging would exceed the scratch returns RTD_ERR_WORKSPACE and
  *     launches nothing (bf16 / f16 rows up to K = 16384 stage on chip and need
- *     no scratch beyond their small carve; f32 rows need about 4*K*M bytes).
- *   - Every call shares the one array and clears its status word first: calls
- *     that overlap on the GPU race, so issue them on one stream (or serialise them).
- *   - Errors are recorded on the calling thread: read them with rtd_last_error(NULL). */
+ *     no scratch beyond their small carve; f32 rows need about 4*K*M bytes).  Calls
+ *     of four or more tokens whose GEMM staging (about 2*K*M bytes plus split-K
+ *     partials) does not fit run the decode GEMV in passes of up to four tokens.
+ *   - Every call shares the one array: calls that overlap on the GPU race, so issue
+ *     them on one stream (or serialise them).
+ *   - Host-side errors are recorded on the calling thread: read them with
+ *     rtd_last_error(NULL).  Device-side errors (a bounded wait that gave up) raise
+ *     the array's status word, which stays raised until rtd_noalloc_check_status
+ *     reads and clears it. */
 rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx, int64_t M,
                                const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream);
+/* No counterpart in the reference: synchronises `stream`, then reads and clears the
+ * status word of `device`'s allocation-free scratch (RTD_OK, or the raised code). */
+rtd_status rtd_noalloc_check_status(int device, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -37,18 +37,31 @@ SIGNATURES = {
     "rtd_init": (_c.c_int32, [_c.c_int, _c.POINTER(_vp)]),
     "rtd_destroy": (_c.c_int32, [_vp]),
     "rtd_last_error": (_c.c_char_p, [_vp]),
+    "rtd_kernel_launches": (_c.c_uint64, []),
     "rtd_check_device_status": (_c.c_int32, [_vp, _vp]),
     "rtd_block_geometry": (_c.c_int32, [_u32, _c.POINTER(_i64), _c.POINTER(_i64)]),
     "rtd_qweight_upload": (_c.c_int32, [_vp, _u32, _vp, _c.c_size_t, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_free": (_c.c_int32, [_vp]),
+    "rtd_qweight_to_device": (_c.c_int32, [_vp, _vp, _c.POINTER(_vp)]),
     "rtd_qweight_info": (_c.c_int32, [_vp, _c.POINTER(_u32), _c.POINTER(_i64), _c.POINTER(_i64),
                                       _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
     "rtd_qlinear": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
     "rtd_qlinear_noalloc": (_c.c_int32, [_vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
+    "rtd_noalloc_check_status": (_c.c_int32, [_c.c_int, _vp]),
     "rtd_tp_comm_create": (_c.c_int32, [_vp, _c.c_int, _c.c_int, _i64, _vp, _vp]),
     "rtd_tp_comm_open": (_c.c_int32, [_vp, _vp]),
     "rtd_tp_comm_destroy": (_c.c_int32, [_vp]),
     "rtd_tp_qlinear_row": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
+    "rtd_tp_allreduce": (_c.c_int32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
+    "rtd_rmsnorm": (_c.c_int32, [_vp, _vp, _i64, _vp, _u32, _i64, _vp, _c.c_float, _i64, _i64, _vp, _u32, _i64,
+                                 _vp]),
+    "rtd_rope_kv_append": (_c.c_int32, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _c.c_int32, _c.c_int32,
+                                        _c.c_int32, _c.c_int32, _c.c_float, _vp, _vp, _vp, _c.c_int32, _vp, _vp,
+                                        _vp, _vp]),
+    "rtd_attention_paged": (_c.c_int32, [_vp, _vp, _i64, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_float, _vp, _vp,
+                                         _vp, _c.c_int32, _c.c_int32, _vp, _vp, _vp, _u32, _i64, _vp]),
+    "rtd_silu_mul": (_c.c_int32, [_vp, _vp, _u32, _vp, _u32, _i64, _vp, _u32, _vp]),
+    "rtd_argmax": (_c.c_int32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "rtd_qembed": (_c.c_int32, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "rtd_qdequant": (_c.c_int32, [_vp, _vp, _vp, _vp]),
     "rtd_fp8weight_upload": (_c.c_int32, [_vp, _vp, _vp, _i64, _i64, _i64, _c.POINTER(_vp)]),

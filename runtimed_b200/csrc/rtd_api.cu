@@ -8,6 +8,8 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
+#include <climits>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -23,8 +25,6 @@ struct rtd_ctx {
   int sm_count = 148;
   float* ws = nullptr;
   size_t ws_bytes = 0;
-  uint32_t* counters = nullptr;
-  int64_t n_counters = 0;
   int* status = nullptr;
   std::string err;
 };
@@ -54,7 +54,6 @@ constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging (GEMV pre
 // the four-column GEMV pass is slower than one TN = 16 GEMM tile from M = 4 on, and
 // faster up to M = 3
 constexpr int64_t kGemmMinTokens = 4;
-constexpr int64_t kCounters = 1 << 17;           // per-tile arrival counters
 
 thread_local std::string g_thread_err;
 
@@ -107,6 +106,8 @@ extern "C" {
 
 const char* rtd_last_error(const rtd_ctx* ctx) { return ctx ? ctx->err.c_str() : g_thread_err.c_str(); }
 
+uint64_t rtd_kernel_launches(void) { return rtd::launch_counter().load(std::memory_order_relaxed); }
+
 rtd_status rtd_block_geometry(uint32_t ggml_type, int64_t* elems, int64_t* bytes) {
   int64_t e, b;
   switch (ggml_type) {
@@ -145,18 +146,14 @@ rtd_status rtd_init(int device, rtd_ctx** out) {
   }
   cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
   if ((e = cudaMalloc(&c->ws, kWorkspaceBytes)) != cudaSuccess ||
-      (e = cudaMalloc(&c->counters, kCounters * sizeof(uint32_t))) != cudaSuccess ||
       (e = cudaMalloc(&c->status, sizeof(int))) != cudaSuccess ||
-      (e = cudaMemset(c->counters, 0, kCounters * sizeof(uint32_t))) != cudaSuccess ||
       (e = cudaMemset(c->status, 0, sizeof(int))) != cudaSuccess) {
     cudaFree(c->ws);
-    cudaFree(c->counters);
     cudaFree(c->status);
     delete c;
     return fail(nullptr, RTD_ERR_OOM, "rtd_init: workspace allocation failed: %s", cudaGetErrorString(e));
   }
   c->ws_bytes = kWorkspaceBytes;
-  c->n_counters = kCounters;
   *out = c;
   return RTD_OK;
 }
@@ -165,7 +162,6 @@ rtd_status rtd_destroy(rtd_ctx* ctx) {
   if (!ctx) return RTD_OK;
   DeviceGuard g(ctx->device);
   cudaFree(ctx->ws);
-  cudaFree(ctx->counters);
   cudaFree(ctx->status);
   delete ctx;
   return RTD_OK;
@@ -240,6 +236,34 @@ rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host
   return RTD_OK;
 }
 
+rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweight** out) {
+  const char* who = "rtd_qweight_to_device";
+  if (!src || !ctx || !out) return fail(ctx, RTD_ERR_INVALID, "%s: NULL argument", who);
+  *out = nullptr;
+  rtd_qweight* w = new (std::nothrow) rtd_qweight(*src);
+  if (!w) return fail(ctx, RTD_ERR_OOM, "%s: host allocation failed", who);
+  w->ctx = ctx;
+  w->dev = nullptr;
+  if (w->dev_bytes > 0) {
+    DeviceGuard g(ctx->device);
+    cudaError_t e = cudaMalloc(&w->dev, w->dev_bytes);
+    if (e != cudaSuccess) {
+      delete w;
+      return fail(ctx, RTD_ERR_OOM, "%s: cudaMalloc(%zu): %s", who, src->dev_bytes, cudaGetErrorString(e));
+    }
+    e = (src->ctx->device == ctx->device)
+            ? cudaMemcpy(w->dev, src->dev, w->dev_bytes, cudaMemcpyDeviceToDevice)
+            : cudaMemcpyPeer(w->dev, ctx->device, src->dev, src->ctx->device, w->dev_bytes);
+    if (e != cudaSuccess) {
+      cudaFree(w->dev);
+      delete w;
+      return cuda_fail(ctx, e, who);
+    }
+  }
+  *out = w;
+  return RTD_OK;
+}
+
 rtd_status rtd_qweight_free(rtd_qweight* w) {
   if (!w) return RTD_OK;
   if (w->dev) {
@@ -298,8 +322,6 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.ldy = ldy;
   c.ws = ctx->ws;
   c.ws_bytes = ctx->ws_bytes;
-  c.counters = ctx->counters;
-  c.n_counters = ctx->n_counters;
   c.status = ctx->status;
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
@@ -408,22 +430,135 @@ rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out,
 }  // extern "C"
 
 
+// ---- decoder-layer operations ------------------------------------------------
+// The SubstratePort operations between the linears of a decoder layer
+// (crates/runtimed-model/src/substrate/port.rs:14-90), over a paged f16 KV cache.
+rtd_status rtd_rmsnorm(rtd_ctx* ctx, float* h, int64_t ldh, const void* delta, uint32_t delta_dtype, int64_t ldd,
+                       const float* w, float eps, int64_t T, int64_t H, void* y, uint32_t y_dtype, int64_t ldy,
+                       void* stream) {
+  const char* who = "rtd_rmsnorm";
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
+  if (T < 0 || H < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: negative shape", who);
+  if (T == 0 || H == 0) return RTD_OK;
+  if (!h || !w || !y) return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer", who);
+  if (!valid_dtype(y_dtype) || (delta && !valid_dtype(delta_dtype))) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (ldh < H || ldy < H || (delta && ldd < H)) return fail(ctx, RTD_ERR_SHAPE, "%s: row strides below H", who);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_add_rmsnorm(h, ldh, delta, (int)delta_dtype, ldd, w, eps, T, H, y, (int)y_dtype, ldy,
+                                          (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
+namespace {
+rtd_status check_heads(rtd_ctx* ctx, int32_t n_head, int32_t n_kv, int32_t head_dim, const char* who) {
+  if (n_head <= 0 || n_kv <= 0 || n_head % n_kv != 0)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: %d query heads are not a multiple of %d kv heads", who, n_head, n_kv);
+  if (n_head / n_kv > 8) return fail(ctx, RTD_ERR_SHAPE, "%s: more than 8 query heads per kv head", who);
+  if (head_dim <= 0 || head_dim % 8 != 0 || head_dim > 128)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: head_dim %d (a multiple of 8, at most 128)", who, head_dim);
+  return RTD_OK;
+}
+}  // namespace
+
+rtd_status rtd_rope_kv_append(rtd_ctx* ctx, const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                              int64_t ldv, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t rot_dim,
+                              float theta, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
+                              int32_t max_blocks, void* k_cache, void* v_cache, float* q_out, void* stream) {
+  const char* who = "rtd_rope_kv_append";
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
+  rtd_status st = check_heads(ctx, n_head, n_kv, head_dim, who);
+  if (st != RTD_OK) return st;
+  if (rot_dim < 0 || rot_dim > head_dim || rot_dim % 2 != 0)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: rot_dim %d for head_dim %d", who, rot_dim, head_dim);
+  if (T < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: T is negative", who);
+  if (T == 0) return RTD_OK;
+  if (!q || !k || !v || !tok_seq || !tok_pos || !block_table || !k_cache || !v_cache || !q_out || max_blocks <= 0)
+    return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer or no block table", who);
+  if (ldq < (int64_t)n_head * head_dim || ldk < (int64_t)n_kv * head_dim || ldv < (int64_t)n_kv * head_dim)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: row strides below the head widths", who);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_rope_kv(q, ldq, k, ldk, v, ldv, T, n_head, n_kv, head_dim, rot_dim, theta, tok_seq,
+                                      tok_pos, block_table, max_blocks, k_cache, v_cache, q_out, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
+rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim,
+                               float scale, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
+                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache, void* o,
+                               uint32_t o_dtype, int64_t ldo, void* stream) {
+  const char* who = "rtd_attention_paged";
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
+  rtd_status st = check_heads(ctx, n_head, n_kv, head_dim, who);
+  if (st != RTD_OK) return st;
+  if (T < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: T is negative", who);
+  if (T == 0) return RTD_OK;
+  if (!q || !tok_seq || !tok_pos || !block_table || !k_cache || !v_cache || !o || max_blocks <= 0)
+    return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer or no block table", who);
+  if (!valid_dtype(o_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (ldo < (int64_t)n_head * head_dim) return fail(ctx, RTD_ERR_SHAPE, "%s: ldo below n_head * head_dim", who);
+  if (max_ctx <= 0 || max_ctx > max_blocks * 16)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: max_ctx %d outside the block table (%d blocks)", who, max_ctx, max_blocks);
+  // split long contexts across CTAs when the (token, kv head) blocks leave SMs idle
+  int splits = 1;
+  const int64_t blocks = T * n_kv;
+  if (blocks < ctx->sm_count && max_ctx > 256) {
+    splits = (int)std::min<int64_t>({(int64_t)(max_ctx + 255) / 256, (ctx->sm_count + blocks - 1) / blocks, 32});
+    while (splits > 1 && rtd::attn_workspace_bytes(T, n_head, n_kv, head_dim, splits) > ctx->ws_bytes) --splits;
+  }
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_attention(q, T, n_head, n_kv, head_dim, scale, tok_seq, tok_pos, block_table, max_blocks,
+                                        k_cache, v_cache, o, (int)o_dtype, ldo, splits, ctx->ws, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
+rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, const void* up, uint32_t up_dtype,
+                        int64_t n, void* y, uint32_t y_dtype, void* stream) {
+  const char* who = "rtd_silu_mul";
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
+  if (n < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: n is negative", who);
+  if (n == 0) return RTD_OK;
+  if (!gate || !up || !y) return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer", who);
+  if (!valid_dtype(gate_dtype) || !valid_dtype(up_dtype) || !valid_dtype(y_dtype))
+    return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_silu_mul(gate, (int)gate_dtype, up, (int)up_dtype, n, y, (int)y_dtype, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
+rtd_status rtd_argmax(rtd_ctx* ctx, const float* x, int64_t ldx, int64_t T, int64_t V, int32_t* out, void* stream) {
+  const char* who = "rtd_argmax";
+  if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
+  if (T < 0 || V <= 0 || V > INT32_MAX) return fail(ctx, RTD_ERR_SHAPE, "%s: T=%lld V=%lld", who, (long long)T, (long long)V);
+  if (T == 0) return RTD_OK;
+  if (!x || !out) return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer", who);
+  if (ldx < V) return fail(ctx, RTD_ERR_SHAPE, "%s: ldx below V", who);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_argmax(x, ldx, T, V, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
 // ---- tensor-parallel row reduction ------------------------------------------
-// One communicator per rank (one process per GPU).  Its device buffer holds, for
-// both call parities, a receive slot per rank ([world][4 * max_n] f32, up to four
-// activation columns per launch) and a flag per (rank, tile); peers map it through
-// CUDA IPC and store into it over NVLink.  Two more device words (epoch, finished
-// CTAs) carry the launch epoch from one launch to the next on the device, so the
-// call can be captured in a CUDA graph.
+// One communicator per rank (one process per GPU).  Its device buffer holds the three
+// LL exchange regions of rtd_kernels.h (TpReduce) -- each in two parity halves -- and
+// two control words; peers map it through CUDA IPC and store into it over NVLink.
+//   ll : [2][world][4 * max_n]              the GEMV's one-shot tile exchange
+//   rs : [2][world][rs_per_src]             the all-reduce's reduce-scatter slots
+//   ag : [2][ag_elems]                      the all-reduce's all-gather slots
+// The control words (epoch, finished CTAs) carry the exchange epoch from one launch to
+// the next on the device, so calls can be captured in a CUDA graph.
+namespace {
+constexpr int64_t kArTokens = 128;       // tokens one all-reduce launch exchanges
+constexpr int64_t kArBlockSlack = 4096;  // room for the per-CTA block rounding
+}  // namespace
+
 struct rtd_comm {
   rtd_ctx* ctx = nullptr;
   int world = 1, rank = 0;
-  int64_t max_n = 0, max_tiles = 0;
+  int64_t max_n = 0;
   unsigned char* base = nullptr;  // this rank's buffer (cudaMalloc, exported by IPC)
-  size_t recv_bytes = 0, bytes = 0;
+  size_t ll_off = 0, rs_off = 0, ag_off = 0, ctrl_off = 0, bytes = 0;
   unsigned char* peer[rtd::kMaxTpWorld] = {};  // mapped peer buffers (peer[rank] = base)
   bool opened = false;
-  size_t ctrl_off = 0;  // this rank's epoch / finished-CTA words (not used by peers)
   rtd::TpReduce tp{};
 };
 
@@ -441,9 +576,16 @@ rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, 
   c->world = world;
   c->rank = rank;
   c->max_n = max_n;
-  c->max_tiles = (max_n + 15) / 16;
-  c->recv_bytes = (size_t)2 * world * 4 * (size_t)max_n * sizeof(float);
-  c->ctrl_off = (c->recv_bytes + (size_t)2 * world * (size_t)c->max_tiles * sizeof(uint32_t) + 255) / 256 * 256;
+  const int64_t ar_max = kArTokens * max_n;
+  int64_t ag_elems = ar_max + kArBlockSlack * 2 * world;
+  ag_elems = (ag_elems + 1) / 2 * 2;
+  int64_t rs_per_src = (ag_elems + world - 1) / world;
+  rs_per_src = (rs_per_src + 1) / 2 * 2;
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  c->ll_off = 0;
+  c->rs_off = up((size_t)2 * world * 4 * (size_t)max_n * sizeof(uint64_t));
+  c->ag_off = c->rs_off + up((size_t)2 * world * (size_t)rs_per_src * sizeof(uint64_t));
+  c->ctrl_off = c->ag_off + up((size_t)2 * (size_t)ag_elems * sizeof(uint64_t));
   c->bytes = c->ctrl_off + 256;
   cudaError_t e = cudaMalloc(&c->base, c->bytes);
   if (e != cudaSuccess) {
@@ -451,12 +593,23 @@ rtd_status rtd_tp_comm_create(rtd_ctx* ctx, int rank, int world, int64_t max_n, 
     return fail(ctx, RTD_ERR_OOM, "%s: cudaMalloc(%zu): %s", who, c->bytes, cudaGetErrorString(e));
   }
   if ((e = cudaMemset(c->base, 0, c->bytes)) != cudaSuccess ||
+      (e = cudaDeviceSynchronize()) != cudaSuccess ||
       (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), c->base)) != cudaSuccess) {
     cudaFree(c->base);
     delete c;
     return cuda_fail(ctx, e, who);
   }
   c->peer[rank] = c->base;
+  c->tp.world = world;
+  c->tp.rank = rank;
+  c->tp.max_n = max_n;
+  c->tp.rs_per_src = rs_per_src;
+  c->tp.ag_elems = ag_elems;
+  c->tp.ar_max_elems = ar_max;
+  c->tp.ctrl = reinterpret_cast<uint32_t*>(c->base + c->ctrl_off);
+  c->tp.ll[rank] = reinterpret_cast<uint64_t*>(c->base + c->ll_off);
+  c->tp.rs[rank] = reinterpret_cast<uint64_t*>(c->base + c->rs_off);
+  c->tp.ag[rank] = reinterpret_cast<uint64_t*>(c->base + c->ag_off);
   *out = c;
   return RTD_OK;
 }
@@ -479,14 +632,10 @@ rtd_status rtd_tp_comm_open(rtd_comm* c, const void* handles) {
     }
     c->peer[p] = static_cast<unsigned char*>(ptr);
   }
-  c->tp.world = c->world;
-  c->tp.rank = c->rank;
-  c->tp.max_n = c->max_n;
-  c->tp.max_tiles = c->max_tiles;
-  c->tp.ctrl = reinterpret_cast<uint32_t*>(c->base + c->ctrl_off);
   for (int p = 0; p < c->world; ++p) {
-    c->tp.recv[p] = reinterpret_cast<float*>(c->peer[p]);
-    c->tp.flags[p] = reinterpret_cast<uint32_t*>(c->peer[p] + c->recv_bytes);
+    c->tp.ll[p] = reinterpret_cast<uint64_t*>(c->peer[p] + c->ll_off);
+    c->tp.rs[p] = reinterpret_cast<uint64_t*>(c->peer[p] + c->rs_off);
+    c->tp.ag[p] = reinterpret_cast<uint64_t*>(c->peer[p] + c->ag_off);
   }
   c->opened = true;
   return RTD_OK;
@@ -502,20 +651,31 @@ rtd_status rtd_tp_comm_destroy(rtd_comm* c) {
   return RTD_OK;
 }
 
+namespace {
+rtd_status tp_check_common(rtd_comm* comm, int64_t M, uint32_t y_dtype, const void* y, const char* who) {
+  rtd_ctx* ctx = comm->ctx;
+  if (comm->world > 1 && !comm->opened) return fail(ctx, RTD_ERR_INVALID, "%s: communicator not opened", who);
+  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (!valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (M > 0 && !y) return fail(ctx, RTD_ERR_INVALID, "%s: y is NULL", who);
+  return RTD_OK;
+}
+}  // namespace
+
 rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const void* x, uint32_t x_dtype, int64_t ldx,
                               int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
   const char* who = "rtd_tp_qlinear_row";
   if (!comm || !shard) return fail(nullptr, RTD_ERR_INVALID, "%s: NULL comm or weight", who);
   rtd_ctx* ctx = comm->ctx;
-  if (comm->world > 1 && !comm->opened) return fail(ctx, RTD_ERR_INVALID, "%s: communicator not opened", who);
+  rtd_status st = tp_check_common(comm, M, y_dtype, y, who);
+  if (st != RTD_OK) return st;
   if (shard->ctx != ctx) return fail(ctx, RTD_ERR_INVALID, "%s: weight and communicator on different contexts", who);
   if (shard->N > comm->max_n)
     return fail(ctx, RTD_ERR_SHAPE, "%s: N=%lld above the communicator's max_n=%lld", who, (long long)shard->N,
                 (long long)comm->max_n);
-  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
-  if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (!valid_dtype(x_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
   if (M == 0 || shard->N == 0) return RTD_OK;
-  if ((shard->K > 0 && !x) || !y) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if (shard->K > 0 && !x) return fail(ctx, RTD_ERR_INVALID, "%s: x is NULL", who);
   if (shard->K == 0) return fail(ctx, RTD_ERR_SHAPE, "%s: empty K shard", who);
   if (ldx < shard->K || ldy < shard->N)
     return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who, (long long)ldx,
@@ -541,13 +701,82 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
   c.status = ctx->status;
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
-  c.tp = comm->world > 1 ? &comm->tp : nullptr;
+  const bool tp = comm->world > 1;
+  c.tp = tp ? &comm->tp : nullptr;
   int plan_err = 0;
-  cudaError_t e = rtd::launch_qgemv(c, &plan_err);
+  cudaError_t e = cudaSuccess;
+  if (M < kGemmMinTokens || !tp) {
+    // decode: the GEMV with the exchange fused into its epilogue (world 1: a plain GEMV;
+    // four or more tokens on one rank go through the single-GPU dispatch)
+    if (!tp && M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
+      e = rtd::launch_qgemm(c, &plan_err);
+    else
+      e = rtd::launch_qgemv(c, &plan_err);
+  } else {
+    // four or more tokens: the tensor-core GEMM writes this rank's f32 partial into the
+    // top of the workspace, then the two-shot all-reduce, in chunks of kArTokens tokens
+    const size_t esz = x_dtype == RTD_DT_F32 ? 4 : 2, ysz = y_dtype == RTD_DT_F32 ? 4 : 2;
+    for (int64_t m0 = 0; m0 < M && e == cudaSuccess && !plan_err; m0 += kArTokens) {
+      const int64_t mc = std::min<int64_t>(kArTokens, M - m0);
+      const size_t part_b = ((size_t)mc * (size_t)shard->N * 4 + 255) / 256 * 256;
+      if (part_b >= ctx->ws_bytes) {
+        plan_err = 1;
+        break;
+      }
+      float* part = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ctx->ws) + (ctx->ws_bytes - part_b));
+      rtd::QGemvCall gc = c;
+      gc.x = static_cast<const unsigned char*>(x) + (size_t)m0 * (size_t)ldx * esz;
+      gc.M = mc;
+      gc.bias = nullptr;
+      gc.y = part;
+      gc.y_dtype = RTD_DT_F32;
+      gc.ldy = shard->N;
+      gc.ws_bytes = ctx->ws_bytes - part_b;
+      gc.tp = nullptr;
+      if (rtd::qgemm_workspace_bytes(gc) <= gc.ws_bytes)
+        e = rtd::launch_qgemm(gc, &plan_err);
+      else
+        e = rtd::launch_qgemv(gc, &plan_err);
+      if (e != cudaSuccess || plan_err) break;
+      e = rtd::launch_tp_allreduce(comm->tp, part, shard->N, mc, shard->N, bias,
+                                   static_cast<unsigned char*>(y) + (size_t)m0 * (size_t)ldy * ysz, (int)y_dtype, ldy,
+                                   ctx->status, ctx->sm_count, (cudaStream_t)stream);
+    }
+  }
   if (plan_err) return fail(ctx, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the workspace", who,
                             (long long)shard->N, (long long)shard->K);
   if (e != cudaSuccess) return cuda_fail(ctx, e, who);
   return RTD_OK;
+}
+
+rtd_status rtd_tp_allreduce(rtd_comm* comm, const float* partial, int64_t ldp, int64_t M, int64_t N,
+                            const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
+  const char* who = "rtd_tp_allreduce";
+  if (!comm) return fail(nullptr, RTD_ERR_INVALID, "%s: NULL comm", who);
+  rtd_ctx* ctx = comm->ctx;
+  rtd_status st = tp_check_common(comm, M, y_dtype, y, who);
+  if (st != RTD_OK) return st;
+  if (N < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: N=%lld is negative", who, (long long)N);
+  if (N > comm->max_n)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: N=%lld above the communicator's max_n=%lld", who, (long long)N,
+                (long long)comm->max_n);
+  if (M == 0 || N == 0) return RTD_OK;
+  if (!partial) return fail(ctx, RTD_ERR_INVALID, "%s: partial is NULL", who);
+  if (ldp < N || ldy < N)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldp=%lld ldy=%lld below N=%lld", who, (long long)ldp,
+                (long long)ldy, (long long)N);
+  DeviceGuard g(ctx->device);
+  if (g.err != cudaSuccess) return cuda_fail(ctx, g.err, who);
+  const size_t ysz = y_dtype == RTD_DT_F32 ? 4 : 2;
+  cudaError_t e = cudaSuccess;
+  // one rank runs the same kernel over its own buffers: y = partial + bias
+  for (int64_t m0 = 0; m0 < M && e == cudaSuccess; m0 += kArTokens) {
+    const int64_t mc = std::min<int64_t>(kArTokens, M - m0);
+    e = rtd::launch_tp_allreduce(comm->tp, partial + m0 * ldp, ldp, mc, N, bias,
+                                 static_cast<unsigned char*>(y) + (size_t)m0 * (size_t)ldy * ysz, (int)y_dtype, ldy,
+                                 ctx->status, ctx->sm_count, (cudaStream_t)stream);
+  }
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 
 // ---- allocation-free quantized linear ---------------------------------------
@@ -555,13 +784,14 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
 // For callers that must not allocate device memory while they run -- for example
 // code that executes inside a host framework whose caching allocator owns the
 // device's memory budget, where an extra cudaMalloc can fail or stall every stream
-// on the device.  rtd_qlinear_noalloc runs the same kernels as rtd_qlinear but
-// takes its scratch (the activation staging of prep-mode calls and the device
-// status word) from the fixed array below instead of a context workspace.
+// on the device.  rtd_qlinear_noalloc dispatches like rtd_qlinear (the tensor-core
+// GEMM from four tokens on when its staging fits, the decode GEMV otherwise) but
+// takes its scratch -- the staged activations and the device status word -- from
+// the fixed array below instead of a context workspace.
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device, fixed at build time
-constexpr size_t kNoAllocStatusBytes = 256;        // the status word, then the GEMV workspace
+constexpr size_t kNoAllocStatusBytes = 256;        // the status word, then the workspace
 constexpr int kNoAllocMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -575,16 +805,16 @@ std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
 
 // Once per device, with that device current: look up the array's device address.
-rtd_status noalloc_setup(int dev, NoAllocDevice** out) {
+rtd_status noalloc_setup(int dev, NoAllocDevice** out, const char* who) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   NoAllocDevice& d = g_noalloc_dev[dev];
   if (!d.ready) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(nullptr, e, "rtd_qlinear_noalloc: cudaGetSymbolAddress");
+    if (e != cudaSuccess) return fail(nullptr, RTD_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return cuda_fail(nullptr, e, "rtd_qlinear_noalloc: cudaDeviceGetAttribute");
+    if (e != cudaSuccess) return fail(nullptr, RTD_ERR_CUDA, "%s: cudaDeviceGetAttribute: %s", who, cudaGetErrorString(e));
     d.scratch = static_cast<unsigned char*>(p);
     d.sm_count = sms;
     d.ready = true;
@@ -611,7 +841,7 @@ rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_d
   DeviceGuard g(dev);
   if (g.err != cudaSuccess) return cuda_fail(nullptr, g.err, who);
   NoAllocDevice* d = nullptr;
-  rtd_status st = noalloc_setup(dev, &d);
+  rtd_status st = noalloc_setup(dev, &d, who);
   if (st != RTD_OK) return st;
   cudaError_t e;
   if (w->K == 0) {
@@ -634,22 +864,46 @@ rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_d
   c.ldy = ldy;
   c.ws = reinterpret_cast<float*>(d->scratch + kNoAllocStatusBytes);
   c.ws_bytes = kNoAllocScratchBytes - kNoAllocStatusBytes;
+  // the status word is zero when the library loads and is cleared by
+  // rtd_noalloc_check_status after it reports a raised code
   c.status = reinterpret_cast<int*>(d->scratch);
   c.sm_count = d->sm_count;
   c.stream = (cudaStream_t)stream;
-  const size_t need = rtd::qgemv_workspace_bytes(c);
-  if (need > c.ws_bytes)
-    return fail(nullptr, RTD_ERR_WORKSPACE,
-                "%s: [%lld x %lld] at M=%lld needs %zu bytes of scratch; the static scratch holds %zu "
-                "(use rtd_qlinear, or fewer tokens per call)",
-                who, (long long)w->N, (long long)w->K, (long long)M, need, c.ws_bytes);
-  // the status word must start at zero; the workspace is fully rewritten before it is read
-  e = cudaMemsetAsync(d->scratch, 0, sizeof(int), (cudaStream_t)stream);
-  if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
+  const bool gemm = M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes;
+  if (!gemm) {
+    const size_t need = rtd::qgemv_workspace_bytes(c);
+    if (need > c.ws_bytes)
+      return fail(nullptr, RTD_ERR_WORKSPACE,
+                  "%s: [%lld x %lld] at M=%lld needs %zu bytes of scratch; the static scratch holds %zu "
+                  "(use rtd_qlinear, or fewer tokens per call)",
+                  who, (long long)w->N, (long long)w->K, (long long)M, need, c.ws_bytes);
+  }
   int plan_err = 0;
-  e = rtd::launch_qgemv(c, &plan_err);
+  e = gemm ? rtd::launch_qgemm(c, &plan_err) : rtd::launch_qgemv(c, &plan_err);
   if (plan_err) return fail(nullptr, RTD_ERR_WORKSPACE, "%s: [%lld x %lld] does not fit the static scratch", who,
                             (long long)w->N, (long long)w->K);
   if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
   return RTD_OK;
+}
+
+rtd_status rtd_noalloc_check_status(int device, void* stream) {
+  const char* who = "rtd_noalloc_check_status";
+  if (device < 0 || device >= kNoAllocMaxDevices) return fail(nullptr, RTD_ERR_INVALID, "%s: device %d out of range", who, device);
+  DeviceGuard g(device);
+  if (g.err != cudaSuccess) return cuda_fail(nullptr, g.err, who);
+  NoAllocDevice* d = nullptr;
+  rtd_status st = noalloc_setup(device, &d, who);
+  if (st != RTD_OK) return st;
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
+  int v = 0;
+  if ((e = cudaMemcpy(&v, d->scratch, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(nullptr, e, who);
+  if (v == 0) return RTD_OK;
+  const int zero = 0;
+  if ((e = cudaMemcpy(d->scratch, &zero, sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess)
+    return cuda_fail(nullptr, e, who);
+  if (v == RTD_ERR_PEER_TIMEOUT)
+    return fail(nullptr, RTD_ERR_PEER_TIMEOUT, "a tensor-parallel peer did not arrive within the wait budget");
+  return fail(nullptr, RTD_ERR_DEVICE, "%s: an allocation-free call raised device status code %d", who, v);
 }

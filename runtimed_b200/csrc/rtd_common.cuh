@@ -1,8 +1,9 @@
 // rtd_common.cuh -- device helpers shared by the sm_100a kernels of libruntimed_b200.
 //
 // Inline PTX for the Blackwell data-movement primitives the kernels use
-// (mbarrier + cp.async.bulk global->shared), the legacy m16n8k16 tensor-core
-// MMA used by the decode GEMV, and bit-exact scalar conversions.
+// (mbarrier + cp.async.bulk global->shared), the LL words of the cross-GPU
+// exchanges, the m16n8k16 tensor-core MMA used by the decode GEMV, and bit-exact
+// scalar conversions.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -103,33 +104,82 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// ---------------------------------------------------------------- cross-GPU flags
-// System-scope release store / acquire load: pair a peer's data stores (made
-// visible by __threadfence_system before the release) with the reader's loads.
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// ---------------------------------------------------------------- cross-GPU LL words
+// A value travels between GPUs as one 8-byte word: the f32 bits in the low half and
+// the exchange epoch in the high half.  An aligned 8-byte relaxed store is single-copy
+// atomic, so a reader that sees the epoch it waits for also sees the value stored with
+// it: no fence and no separate flag are needed.  Buffers start zeroed and epochs start
+// at 1, and every exchange alternates between two buffer halves by epoch parity, so a
+// word left from an earlier exchange never carries the epoch a reader waits for.
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(v);
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void st_ll(uint64_t* p, float v, uint32_t epoch) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, epoch)) : "memory");
 }
 
-// Waits until *p has reached `epoch` (wrap-safe) for at most `budget_ns`; on
-// timeout records kDevPeerTimeout and returns false, so no wait outlives a peer
-// that never arrives.
-__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t epoch, uint64_t budget_ns, int* status) {
-  if ((int32_t)(ld_acquire_sys(p) - epoch) >= 0) return true;
+// Two consecutive words (16-byte aligned); each 8-byte half is single-copy atomic.
+__device__ __forceinline__ void st_ll2(uint64_t* p, float v0, float v1, uint32_t epoch) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(ll_word(v0, epoch)),
+               "l"(ll_word(v1, epoch))
+               : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+__device__ __forceinline__ void ld_ll2(const uint64_t* p, uint64_t& w0, uint64_t& w1) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
+
+// Waits (bounded) for the word at p to carry `epoch` and returns its value.  After one
+// timeout in this thread (`dead`), later waits return 0 at once, so a peer that never
+// arrives costs one wait budget per thread, not one per word.
+__device__ __forceinline__ float wait_ll(const uint64_t* p, uint32_t epoch, bool& dead, int* status) {
+  uint64_t w = ld_ll(p);
+  if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+  if (dead) return 0.0f;
   const uint64_t t0 = global_ns();
   for (;;) {
-    __nanosleep(64);
-    if ((int32_t)(ld_acquire_sys(p) - epoch) >= 0) return true;
-    if (global_ns() - t0 > budget_ns) {
+    __nanosleep(20);
+    w = ld_ll(p);
+    if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+    if (global_ns() - t0 > 2000000000ull) {
       raise_status(status, kDevPeerTimeout);
-      return false;
+      dead = true;
+      return 0.0f;
     }
   }
+}
+
+__device__ __forceinline__ void wait_ll2(const uint64_t* p, uint32_t epoch, bool& dead, int* status, float& v0,
+                                         float& v1) {
+  uint64_t w0, w1;
+  ld_ll2(p, w0, w1);
+  if ((uint32_t)(w0 >> 32) != epoch || (uint32_t)(w1 >> 32) != epoch) {
+    if (dead) {
+      v0 = v1 = 0.0f;
+      return;
+    }
+    const uint64_t t0 = global_ns();
+    for (;;) {
+      __nanosleep(20);
+      ld_ll2(p, w0, w1);
+      if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch) break;
+      if (global_ns() - t0 > 2000000000ull) {
+        raise_status(status, kDevPeerTimeout);
+        dead = true;
+        v0 = v1 = 0.0f;
+        return;
+      }
+    }
+  }
+  v0 = __uint_as_float((uint32_t)w0);
+  v1 = __uint_as_float((uint32_t)w1);
 }
 
 // ---------------------------------------------------------------- MMA

@@ -113,6 +113,7 @@ cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int6
   for (int64_t r0 = 0; r0 < N && K > 0; r0 += 65535) {
     const int64_t rows = (N - r0 < 65535) ? N - r0 : 65535;
     const dim3 grid = row_grid(K, rows);
+    count_launch();
     switch (fmt) {
       case FMT_Q4K: dequant_kernel<FMT_Q4K><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
       case FMT_Q6K: dequant_kernel<FMT_Q6K><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
@@ -128,6 +129,7 @@ cudaError_t launch_embed(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_
   for (int64_t r0 = 0; r0 < n && K > 0; r0 += 65535) {
     const int64_t rows = (n - r0 < 65535) ? n - r0 : 65535;
     const dim3 grid = row_grid(K, rows);
+    count_launch();
     switch (fmt) {
       case FMT_Q4K: embed_kernel<FMT_Q4K><<<grid, 256, 0, st>>>(w, N, K, G, ids, r0, y, status); break;
       case FMT_Q6K: embed_kernel<FMT_Q6K><<<grid, 256, 0, st>>>(w, N, K, G, ids, r0, y, status); break;
@@ -142,6 +144,7 @@ cudaError_t launch_fp8_encode(const float* x, int64_t n, uint8_t* out, cudaStrea
   if (n <= 0) return cudaSuccess;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
+  count_launch();
   fp8_encode_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, n, out);
   return cudaGetLastError();
 }

@@ -778,6 +778,7 @@ cudaError_t launch_pdl(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
 }
 

@@ -8,37 +8,41 @@
 //
 // Every weight byte is read from HBM exactly once per call; the kernels are built
 // to keep HBM busy with as little synchronisation as possible:
-//  * prep kernel, one 8-CTA thread-block cluster per token: each CTA takes 1/8 of
-//    the row, the row's max |x| is combined through distributed shared memory,
-//    and x is scaled by a power of two so that max sits in [2^14, 2^15), split
-//    into f16 hi (+ lo for f32 input: 22 significant bits; bf16 / f16 inputs are
-//    exact in one column) and written group-major to the context workspace with
-//    the per-sub-block column sums the scale algebra needs.  It triggers
-//    programmatic completion at once, so the GEMV grid launches behind it (PDL)
-//    and prefetches weights while x is prepared.
+//  * Activation staging.  Each group of GK activations gets a power-of-two scale from
+//    its own max |x| (warp shuffles, no cross-CTA reduction), is rounded to f16 (f32
+//    rows: an f16 hi and an f16 lo column), and is stored transposed into 16-byte
+//    units so that the lanes feeding different MMA columns in one load hit distinct
+//    banks; a small table per (group, column) holds the per-sub-block column sums the
+//    scale algebra needs and the group's scale.  Whole-mode launches with bf16 / f16
+//    rows stage x inside every CTA (stage_local_diag, no second launch); the others
+//    run prep_diag_kernel first, chained by programmatic dependent launch, and the
+//    GEMV bulk-copies the staged units together with the weights.
 //  * GEMV kernel: every warp is an independent streaming pipeline.  The flattened
-//    (16-row tile, item of IG groups) space is split evenly over all warps of the
-//    persistent grid; each warp keeps NS items in flight in its own shared-memory
-//    ring with cp.async.bulk (TMA engine) on its own mbarriers -- weights plus the
-//    matching x and column-sum slices, three copies per item -- so no CTA-wide
-//    barrier ever stalls the stream.  In the device layout (rtd_layout.h) an item
-//    is one contiguous 16-byte aligned byte range.
-//  * No dequantized weight is materialised.  Each lane turns its 16-byte vector
-//    of packed codes into exact integer-valued f16 pairs with one LOP3 or PRMT per
-//    pair ((code | 0x6400) is the half 1024 + code) and m16n8k16 tensor-core MMAs
-//    form sum_k x_k * (1024 + code_k) in f32 (A = 16 weight rows, B = up to 8
-//    activation columns per n-tile).  Per sub-block the reference's scale algebra
-//    is applied in f32:
-//      Q4_K  y += (d*sc) * S - (1024*d*sc + dmin*m) * sum(x)    (high nibbles: extra 1/16)
-//      Q6_K  y += (d*sc) * (S - 1056 * sum(x))                  (code - 32, offset 1024)
-//      Q8_0  y += d * (S - 1152 * sum(x))                       (q + 128, offset 1024)
-//      FP8   y += S (E4M3 -> f16 is exact), times the channel scale at the end
-//    so products are exact and only f32 rounding remains.
-//  * A tile finished inside one warp is written straight from the MMA
-//    accumulators; a tile split between warps leaves per-warp partials in the
-//    workspace and the last warp to arrive (per-tile counter) sums them in warp
-//    order, writes y and re-arms the counter, so every call leaves the counters
-//    at zero.
+//    (16-row tile, item of IG groups) space is split over all warps of the persistent
+//    grid; each warp keeps NS items in flight in its own shared-memory ring with
+//    cp.async.bulk on its own mbarriers, so no CTA-wide barrier stalls the stream.  In
+//    the device layout (rtd_layout.h) an item is one contiguous 16-byte aligned range.
+//    Weight copies are issued before griddepcontrol.wait, so they overlap the previous
+//    kernel's tail.
+//  * No dequantized weight is materialised.  The 8 columns of each m16n8k16 MMA are
+//    the group's SUB-BLOCKS (not tokens): every lane owns whole sub-blocks of two rows
+//    (rtd_layout.h), feeds its packed codes to the MMA as exact f16 SUBNORMALS (code
+//    bits in the mantissa, value code * 2^-24; one LOP3 or PRMT per pair), and only the
+//    lane whose column a sub-block is supplies that sub-block's activations as B.  After
+//    a group, C[row][n] is sub-block n's code-weighted dot product alone, so each lane
+//    applies the reference's scale algebra for exactly its own (row, sub-block) pairs
+//    in f32 (Q4_K: d*sc on the codes and -dmin*m on the column sums; Q6_K / Q8_0: the
+//    code bias 32 / 128 enters as a C-init from the column sums; FP8: E4M3 -> f16 is
+//    exact and the channel scale is applied on write).  Products are exact; only f32
+//    rounding remains.
+//  * Whole mode (enough 16-row tiles for every warp of the grid): a warp owns whole
+//    tiles and writes them from its accumulators.  Split mode: the 8 warps of a CTA
+//    split each tile's items, leave their partials in shared memory (double buffered,
+//    named barriers) and the tile's writer warp sums them in warp order.
+//  * Row-parallel tensor parallelism (split mode): the writer warp stores the tile's
+//    partial into every rank's exchange buffer over NVLink as LL words (value and
+//    epoch in one 8-byte store); after the CTA's last tile it waits (bounded) for
+//    every rank's words of its tiles and writes their rank-ordered sum.
 
 #include <algorithm>
 #include <cstdlib>
@@ -638,12 +642,11 @@ struct Args {
   int off_xloc, xcs, off_tabloc;
   int tabw;      // table floats per group: ncol * (GK / SBE + 4)
   int off_zero;  // kZeroPage bytes of zeros
-  // row-parallel reduction (tp_world > 1): this launch's parity half of every rank's
-  // receive slots [world][4 * max_n] and arrival flags [world][max_tiles]
+  // row-parallel reduction (tp_world > 1): every rank's exchange region
+  // [2 parities][world][4 * max_n] LL words
   int tp_world, tp_rank;
-  float* tp_recv[kMaxTpWorld];
-  uint32_t* tp_flags[kMaxTpWorld];
-  int64_t tp_max_n, tp_max_tiles;
+  uint64_t* tp_ll[kMaxTpWorld];
+  int64_t tp_max_n;
   uint32_t* tp_ctrl;  // [0] epoch, [1] finished-CTA count (device)
   int* status;
 };
@@ -667,20 +670,19 @@ __device__ __forceinline__ void named_bar_arrive(int id, int n) {
 }
 
 // Row-parallel tile exchange in two halves.  tp_publish_tile runs in the tile's writer
-// warp as soon as the tile's 8 warp partials are in shared memory: the rank's partial
-// (row scale applied) goes to its slot on every rank (peer stores over NVLink) and is
-// published with a system-scope release.  tp_finish_tile runs after the CTA's last tile,
-// so no warp waits for a peer while it still has groups to stream: it waits (bounded)
-// for every rank's flag of the tile, sums the partials in rank order -- every rank writes
-// the same bits -- and adds the bias once.  A peer that never arrives ends the wait
-// after kWaitBudgetNs with RTD_ERR_PEER_TIMEOUT in the status word.
+// warp as soon as the tile's 8 warp partials are in shared memory: the rank's partial of
+// every (row, token) of the tile (row scale applied) goes to its slot on every rank as an
+// LL word (value + epoch in one 8-byte store over NVLink), with no fence and no flag.
+// tp_finish_tile runs after the CTA's last tile, so no warp waits for a peer while it
+// still has groups to stream: it waits (bounded) until every rank's word of each element
+// carries this launch's epoch, sums the partials in rank order -- every rank writes the
+// same bits -- and adds the bias once.  A peer that never arrives ends the wait after
+// 2 s with RTD_ERR_PEER_TIMEOUT in the status word.
 __device__ __forceinline__ void tp_publish_tile(const Args& a, int tile, const float* rb, const float* ep,
                                                 int lane, uint32_t epoch) {
   const int W = a.tp_world, R = a.tp_rank;
-  const int64_t slot_elems = 4 * a.tp_max_n;
-  // this launch's parity half of every rank's receive slots and flags
-  const int64_t par = (int64_t)(epoch & 1u);
-  const int64_t recv_par = par * W * slot_elems, flag_par = par * W * a.tp_max_tiles;
+  const int64_t slot = 4 * a.tp_max_n;
+  const int64_t base = (int64_t)(epoch & 1u) * W * slot + (int64_t)R * slot;
   for (int o = lane; o < 16 * a.M; o += 32) {
     const int r = o / a.M, t = o - r * a.M;
     const int64_t n = (int64_t)tile * 16 + r;
@@ -689,35 +691,28 @@ __device__ __forceinline__ void tp_publish_tile(const Args& a, int tile, const f
     for (int w = 0; w < kWarps; ++w)
       for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
     if (n < a.N) {
-      const int64_t off = (int64_t)R * slot_elems + (int64_t)t * a.N + n;
-      for (int p = 0; p < W; ++p) a.tp_recv[p][recv_par + off] = sum * ep[16 + r];
+      const int64_t off = base + (int64_t)t * a.N + n;
+      const float v = sum * ep[16 + r];
+      for (int q = 1; q <= W; ++q) {  // peers first, own slot last
+        const int p = (R + q) % W;
+        st_ll(a.tp_ll[p] + off, v, epoch);
+      }
     }
-  }
-  __syncwarp();
-  if (lane == 0) {
-    __threadfence_system();
-    for (int p = 0; p < W; ++p) st_release_sys(a.tp_flags[p] + flag_par + (int64_t)R * a.tp_max_tiles + tile, epoch);
   }
   __syncwarp();
 }
 
-__device__ __forceinline__ void tp_finish_tile(const Args& a, int tile, int lane, uint32_t epoch) {
+__device__ __forceinline__ void tp_finish_tile(const Args& a, int tile, int lane, uint32_t epoch, bool& dead) {
   const int W = a.tp_world, R = a.tp_rank;
-  const int64_t slot_elems = 4 * a.tp_max_n;
-  const int64_t par = (int64_t)(epoch & 1u);
-  const int64_t recv_par = par * W * slot_elems, flag_par = par * W * a.tp_max_tiles;
-  if (lane < W && lane != R)
-    wait_flag_sys(a.tp_flags[R] + flag_par + (int64_t)lane * a.tp_max_tiles + tile, epoch, kWaitBudgetNs, a.status);
-  __syncwarp();
-  for (int q = 0; q < W; ++q)  // every reading lane acquires the arrivals itself
-    if (q != R) (void)ld_acquire_sys(a.tp_flags[R] + flag_par + (int64_t)q * a.tp_max_tiles + tile);
+  const int64_t slot = 4 * a.tp_max_n;
+  const uint64_t* mine = a.tp_ll[R] + (int64_t)(epoch & 1u) * W * slot;
   for (int o = lane; o < 16 * a.M; o += 32) {
     const int r = o / a.M, t = o - r * a.M;
     const int64_t n = (int64_t)tile * 16 + r;
     if (n < a.N) {
-      const volatile float* src = a.tp_recv[R] + recv_par + (int64_t)t * a.N + n;
+      const uint64_t* src = mine + (int64_t)t * a.N + n;
       float v = 0.0f;
-      for (int q = 0; q < W; ++q) v += src[(int64_t)q * slot_elems];
+      for (int q = 0; q < W; ++q) v += wait_ll(src + (int64_t)q * slot, epoch, dead, a.status);
       store_y(a, t, n, v + (a.bias ? __ldg(a.bias + n) : 0.0f));
     }
   }
@@ -1067,8 +1062,9 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
     }
   }
   if (a.tp_world > 1) {  // each writer warp finishes the tiles it published (split mode)
+    bool dead = false;
     for (int tile = t0; tile < t1; ++tile)
-      if (warp == (tile & (kWarps - 1))) tp_finish_tile(a, tile, lane, tp_epoch);
+      if (warp == (tile & (kWarps - 1))) tp_finish_tile(a, tile, lane, tp_epoch, dead);
   }
   if (a.tp_world > 1) {  // the last CTA of the launch publishes its epoch for the next one
     __syncthreads();
@@ -1235,6 +1231,7 @@ cudaError_t launch_gemv(const Args& a, unsigned nctas, size_t smem, cudaStream_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<FMT, NT>, a);
 }
 
@@ -1260,6 +1257,7 @@ cudaError_t launch_prep_diag(const PrepArgs& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   return cudaLaunchKernelEx(&cfg, prep_diag_kernel<FMT>, p);
 }
 
@@ -1285,6 +1283,7 @@ cudaError_t launch_fill_rows(const float* bias, void* y, int y_dtype, int64_t ld
   if (M <= 0 || N <= 0) return cudaSuccess;
   int64_t blocks = (M * N + 255) / 256;
   if (blocks > 4096) blocks = 4096;
+  count_launch();
   fill_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(bias, y, y_dtype, ldy, M, N);
   return cudaGetLastError();
 }
@@ -1432,19 +1431,15 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.tp_world = 1;
     if (c.tp && c.tp->world > 1) {
       const TpReduce& tp = *c.tp;
-      if (c.N > tp.max_n || T > tp.max_tiles || Mt > 4) {
+      if (c.N > tp.max_n || Mt > 4) {
         *plan_error = 1;
         return cudaSuccess;
       }
       a.tp_world = tp.world;
       a.tp_rank = tp.rank;
       a.tp_max_n = tp.max_n;
-      a.tp_max_tiles = tp.max_tiles;
       a.tp_ctrl = tp.ctrl;
-      for (int p = 0; p < tp.world; ++p) {  // parity-0 bases; the kernel picks its half by epoch
-        a.tp_recv[p] = tp.recv[p];
-        a.tp_flags[p] = tp.flags[p];
-      }
+      for (int p = 0; p < tp.world; ++p) a.tp_ll[p] = tp.ll[p];  // the kernel picks its half by epoch
     }
     a.status = c.status;
     switch (c.fmt) {

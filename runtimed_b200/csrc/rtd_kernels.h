@@ -4,9 +4,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "rtd_layout.h"
 
 namespace rtd {
+
+// Kernels this library has launched (or recorded into a capturing stream) since it
+// was loaded; every launch site adds one.  Read through rtd_kernel_launches.
+inline std::atomic<uint64_t>& launch_counter() {
+  static std::atomic<uint64_t> n{0};
+  return n;
+}
+inline void count_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
 
 // Decode all N rows of an uploaded weight to f32 [N, K] (bit-exact).
 cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, float* y,
@@ -20,19 +30,31 @@ cudaError_t launch_fp8_encode(const float* x, int64_t n, uint8_t* out, cudaStrea
 // Decode GEMV / skinny GEMM: y[M, N] = x[M, K] . W^T (+ bias), W in the group layout.
 constexpr int kMaxTpWorld = 8;
 
-// Tensor-parallel row reduction attached to one GEMV: every rank computes the
-// partial y of its K shard; each tile's partial goes to every rank's receive slot
-// over NVLink, and each rank writes the tile once all partials have arrived.
+// Tensor-parallel row reduction (one process per GPU).  Every exchanged value is an
+// LL word (f32 value + epoch, rtd_common.cuh) stored straight into the receiving
+// rank's buffer over NVLink; each exchange uses the buffer half of its epoch's parity.
+//   ll : the GEMV's one-shot exchange: rank q's tile partials for rank p land in
+//        ll[p][parity][q][t * N + n] (up to 4 tokens a launch), and every rank sums
+//        the world's partials in rank order.
+//   rs / ag : the two-shot all-reduce after the tensor-core GEMM (and rtd_tp_allreduce):
+//        element i of a block goes to its owner rank's rs[owner][parity][source][...],
+//        the owner sums them in rank order and stores the result into every rank's
+//        ag[p][parity][i].
+// Every rank therefore writes identical bits.
 struct TpReduce {
   int world, rank;
-  float* recv[kMaxTpWorld];      // rank p's receive region [2 parities][world][4 * max_n] f32
-  uint32_t* flags[kMaxTpWorld];  // rank p's arrival flags [2 parities][world][max_tiles]
-  int64_t max_n, max_tiles;
-  uint32_t* ctrl;                // this rank's device words: [0] epoch of the last launch,
-                                 // [1] CTAs finished in the current launch; the launch reads
-                                 // the epoch after griddepcontrol.wait and its last CTA
-                                 // advances it, so a CUDA graph replays with fresh epochs
-                                 // (all ranks make the same calls, so epochs stay in step)
+  uint64_t* ll[kMaxTpWorld];
+  uint64_t* rs[kMaxTpWorld];
+  uint64_t* ag[kMaxTpWorld];
+  int64_t max_n;        // GEMV exchange: at most 4 * max_n words per source
+  int64_t rs_per_src;   // words per source in one parity half of rs
+  int64_t ag_elems;     // words in one parity half of ag
+  int64_t ar_max_elems; // elements one all-reduce launch may exchange
+  uint32_t* ctrl;       // this rank's device words: [0] epoch of the last exchange launch,
+                        // [1] CTAs finished in the current launch; a launch reads the
+                        // epoch after griddepcontrol.wait and its last CTA advances it, so
+                        // a CUDA graph replays with fresh epochs (all ranks make the same
+                        // calls, so their epochs stay in step)
 };
 
 struct QGemvCall {
@@ -52,8 +74,6 @@ struct QGemvCall {
   int64_t ldy;
   float* ws;               // activation staging workspace (prep-mode calls)
   size_t ws_bytes;
-  uint32_t* counters;      // unused by the current kernels
-  int64_t n_counters;
   int* status;             // device status word
   int sm_count;
   cudaStream_t stream;
@@ -70,6 +90,29 @@ size_t qgemv_workspace_bytes(const QGemvCall& c);
 // workspace holds the staged activations (qgemm_workspace_bytes).
 cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error);
 size_t qgemm_workspace_bytes(const QGemvCall& c);
+
+// y[M, N] (y_dtype, rows ldy apart) = sum over ranks of partial[M, N] (f32, rows ldp
+// apart) + bias (added once), on every rank: the two-shot all-reduce over NVLink.
+// M * N must not exceed tp.ar_max_elems.
+cudaError_t launch_tp_allreduce(const TpReduce& tp, const float* partial, int64_t ldp, int64_t M, int64_t N,
+                                const float* bias, void* y, int y_dtype, int64_t ldy, int* status, int sm_count,
+                                cudaStream_t st);
+
+// Decoder-layer operations (rtd_model.cu).
+cudaError_t launch_add_rmsnorm(float* h, int64_t ldh, const void* delta, int ddt, int64_t ldd, const float* w,
+                               float eps, int64_t T, int64_t H, void* y, int ydt, int64_t ldy, cudaStream_t st);
+cudaError_t launch_rope_kv(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                           int64_t T, int n_head, int n_kv, int head_dim, int rot_dim, float theta, const int* tok_seq,
+                           const int* tok_pos, const int* block_table, int max_blocks, void* k_cache, void* v_cache,
+                           float* q_out, cudaStream_t st);
+size_t attn_workspace_bytes(int64_t T, int n_head, int n_kv, int head_dim, int splits);
+cudaError_t launch_attention(const float* q, int64_t T, int n_head, int n_kv, int head_dim, float scale,
+                             const int* tok_seq, const int* tok_pos, const int* block_table, int max_blocks,
+                             const void* k_cache, const void* v_cache, void* o, int o_dtype, int64_t ldo, int splits,
+                             float* part, cudaStream_t st);
+cudaError_t launch_silu_mul(const void* gate, int gdt, const void* up, int udt, int64_t n, void* y, int ydt,
+                            cudaStream_t st);
+cudaError_t launch_argmax(const float* x, int64_t ldx, int64_t T, int64_t V, int* out, cudaStream_t st);
 
 // y[m, n] = bias[n] (or 0) for every row m < M: the K = 0 case of a linear.
 cudaError_t launch_fill_rows(const float* bias, void* y, int y_dtype, int64_t ldy, int64_t M, int64_t N,

@@ -7,13 +7,15 @@ Mirrors the reference's Megatron-style layers:
   Its forward needs no exchange.
 - `RowParallelLinear`: crates/runtimed-model/src/tp/row_linear.rs:20-66. It splits K on
   superblock boundaries. The reduction that the reference runs as a separate
-  `ring_all_reduce` (crates/runtimed-model/src/tp/ring_reduce.rs:7-65) is fused into
-  the GEMV epilogue here (`rtd_tp_qlinear_row`): tile partials cross NVLink as peer
-  stores, and every rank writes the full y.
+  `ring_all_reduce` (crates/runtimed-model/src/tp/ring_reduce.rs:7-65) runs inside
+  `rtd_tp_qlinear_row`: fused into the GEMV epilogue for decode-sized M (tile partials
+  cross NVLink as peer stores), a two-shot all-reduce kernel after the tensor-core GEMM
+  from four tokens on; every rank writes the full y.
 
 `forward_nccl` computes the same result with an NCCL all-reduce, as the measured
-comparison. The shard helpers work on raw GGUF bytes and are plain numpy, so the host
-side can be tested without a GPU.
+comparison; `forward_ar` runs the unfused GEMV followed by this library's all-reduce.
+The shard helpers work on raw GGUF bytes and are plain numpy, so the host side can be
+tested without a GPU.
 """
 from __future__ import annotations
 
@@ -89,6 +91,27 @@ class TpComm:
         dist.all_gather_object(everyone, mine, group=group)
         allh = (ctypes.c_ubyte * (self.HANDLE_BYTES * world)).from_buffer_copy(b"".join(everyone))
         _lib.check(L.rtd_tp_comm_open(self.handle, allh), ctx.handle)
+
+    def allreduce(self, partial, bias=None, out_dtype=None):
+        """Sum of every rank's f32 partial [M, N] (+ bias once), on every rank
+        (rtd_tp_allreduce: two-shot over NVLink; replaces ring_all_reduce,
+        crates/runtimed-model/src/tp/ring_reduce.rs:7-34)."""
+        import torch
+        from .weights import _DT, _stream_ptr
+
+        p = partial.to(torch.float32)
+        n = int(p.shape[-1])
+        p2 = p.reshape(-1, n).contiguous()
+        m = int(p2.shape[0])
+        out_dtype = out_dtype or torch.float32
+        y = torch.empty((m, n), dtype=out_dtype, device=p2.device)
+        b = None
+        if bias is not None:
+            b = bias.to(device=p2.device, dtype=torch.float32).contiguous()
+        st = _lib.lib().rtd_tp_allreduce(self.handle, p2.data_ptr(), n, m, n, None if b is None else b.data_ptr(),
+                                         y.data_ptr(), _DT[out_dtype], n, _stream_ptr(p2.device))
+        _lib.check(st, self.ctx.handle)
+        return y.reshape(*partial.shape[:-1], n)
 
     def close(self) -> None:
         if getattr(self, "handle", None):
@@ -177,6 +200,14 @@ class RowParallelLinear:
                                            _stream_ptr(self.weight.device))
         _lib.check(st, self.weight.ctx.handle)
         return y.reshape(*x.shape[:-1], self.weight.n)
+
+    def forward_ar(self, x):
+        """Local partial GEMV (f32), then this library's two-shot all-reduce kernel."""
+        import torch
+
+        y = self.weight.forward(x, out_dtype=torch.float32)
+        out = x.dtype if x.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float32
+        return self.comm.allreduce(y, bias=self.bias, out_dtype=out)
 
     def forward_nccl(self, x, group=None):
         """The comparison path: local partial GEMV, then an NCCL all-reduce."""

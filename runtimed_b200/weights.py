@@ -162,6 +162,18 @@ class QMatMul:
         _raise(st, self.ctx.handle)
         return y
 
+    def to_device(self, device) -> "QMatMul":
+        """A copy on `device` (the same device gives a second, distinct device copy),
+        made without a host round trip (rtd_qweight_to_device)."""
+        ctx = Context.for_device(device)
+        h = ctypes.c_void_p()
+        _raise(_lib.lib().rtd_qweight_to_device(self.handle, ctx.handle, ctypes.byref(h)), ctx.handle)
+        out = QMatMul.__new__(QMatMul)
+        out.ctx, out.ggml_type, out.n, out.k = ctx, self.ggml_type, self.n, self.k
+        out.handle = h
+        out._raw_bytes, out._dev_bytes = self._raw_bytes, self._dev_bytes
+        return out
+
     def free(self) -> None:
         if getattr(self, "handle", None):
             _lib.lib().rtd_qweight_free(self.handle)
@@ -284,7 +296,45 @@ class Weights:
         fw = self.fp8_map.get(name)
         if fw is not None:
             return fw.forward(x).to(x.dtype)
+        if name in self.map:
+            return self.linear_dense(x, name)
         raise MissingWeight(name)
+
+    FP8_SCALE_SUFFIXES = (".scale", "_scale", ".weight_scale_inv")
+
+    def fp8_scale(self, name: str, out_dim: int) -> torch.Tensor:
+        """The scale of an E4M3 weight in ``map``: the first of ``{name}.scale``,
+        ``{name}_scale`` and ``{name}.weight_scale_inv`` that exists, else ones
+        (crates/runtimed-model/src/weights/linear_layer.rs:78-86)."""
+        for suffix in self.FP8_SCALE_SUFFIXES:
+            s = self.map.get(name + suffix)
+            if s is not None:
+                return s.to(torch.float32)
+        return torch.ones(out_dim, dtype=torch.float32)
+
+    def linear_dense(self, x: torch.Tensor, name: str, mode: str = "w8a8") -> torch.Tensor:
+        """Weights::linear_dense (linear_layer.rs:68-101) for E4M3 entries of ``map``
+        (torch.float8_e4m3fn, [out, in]): the scale by key lookup, then the FP8 linear
+        with the reference CUDA semantics (W8A8: x encoded to E4M3 first,
+        fp8_gemm.rs:96-101); the device weight is built once per entry."""
+        w = self.map.get(name)
+        if w is None:
+            raise MissingWeight(name)
+        if w.dtype != torch.float8_e4m3fn:
+            raise ConfigError(f"{name}: dense {w.dtype} weights are not on this path")
+        if w.dim() != 2:
+            raise ShapeError(name, [2], list(w.shape))
+        out_dim, in_dim = int(w.shape[0]), int(w.shape[1])
+        if x.shape[-1] != in_dim:
+            raise ShapeError(name, [in_dim], list(x.shape))
+        cache = self.__dict__.setdefault("_fp8_dense", {})
+        fw = cache.get(name)
+        if fw is None:
+            scale = self.fp8_scale(name, out_dim).reshape(-1).cpu().numpy()
+            codes = w.detach().cpu().view(torch.uint8).numpy()
+            fw = Fp8Weight(codes, scale, in_dim, out_dim, device=self.dev)
+            cache[name] = fw
+        return fw.forward(x, mode=mode).to(x.dtype)
 
     def linear_bias(self, x: torch.Tensor, name: str, bias: Optional[str] = None) -> torch.Tensor:
         if bias is None:

@@ -65,3 +65,19 @@ def test_init_fails_cleanly_without_gpu():
     h = ctypes.c_void_p()
     assert _lib.lib().rtd_init(0, ctypes.byref(h)) == _lib.RTD_ERR_CUDA
     assert not h.value
+
+
+def test_noalloc_status_reader_reports_without_a_device():
+    # the reader binds the device first: on a host without one it returns a CUDA error
+    # (with a message on the calling thread) instead of touching memory
+    L = _lib.lib()
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            pytest.skip("covered by the GPU tests")
+    except ImportError:
+        pass
+    assert L.rtd_noalloc_check_status(0, None) == _lib.RTD_ERR_CUDA
+    assert L.rtd_last_error(None)
+    assert L.rtd_noalloc_check_status(-1, None) == _lib.RTD_ERR_INVALID

@@ -177,3 +177,26 @@ def test_weights_mirror_routes_and_errors():
             bad()
     with pytest.raises(ModelError):
         ws.embed("q", [N])
+
+
+def test_weights_linear_dense_scale_key_lookup():
+    # Weights::linear_dense on an E4M3 map entry: the scale comes from the first of
+    # "{name}.scale", "{name}_scale", "{name}.weight_scale_inv", else ones
+    # (crates/runtimed-model/src/weights/linear_layer.rs:78-86); the GEMM runs the
+    # reference CUDA semantics (W8A8)
+    import torch
+    from runtimed_b200.weights import Weights
+
+    N, K, M = 48, 256, 3
+    w, s = synth.fp8_matrix(N, K, seed=8)
+    x = synth.bf16_round(synth.activations(M, K, seed=9))
+    wt = torch.from_numpy(w).view(torch.float8_e4m3fn)
+    for key in (".scale", "_scale", ".weight_scale_inv", None):
+        m = {"blk.w": wt}
+        if key is not None:
+            m["blk.w" + key] = torch.from_numpy(s)
+        W = Weights(device="cuda:0", map=m)
+        y = W.linear(torch.from_numpy(x).cuda(), "blk.w").cpu().numpy()
+        sc = s if key is not None else np.ones(N, np.float32)
+        want = oracle.fp8_gemm_w8a8_f64(x, w, sc, N, K)
+        assert rel_l2(y, want) <= 1e-3, key

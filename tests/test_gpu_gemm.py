@@ -133,3 +133,77 @@ def test_gemm_fp8_ragged_k(M):
     for mode, ref in (("w8a16", oracle.fp8_gemm_cpu_f64), ("w8a8", oracle.fp8_gemm_w8a8_f64)):
         y = fw.forward(xt, mode=mode).float().cpu().numpy()
         assert rel_l2(y, ref(x, w, s, N, K)) <= RTOL, mode
+
+
+_SWEEP_CACHE = {}
+
+
+def _sweep_weight(t, N, K):
+    """One device weight per (format, shape), shared by the sweep tests below."""
+    key = (t, N, K)
+    if key not in _SWEEP_CACHE:
+        from runtimed_b200.weights import Fp8Weight, QMatMul
+
+        _SWEEP_CACHE.clear()  # one shape resident at a time
+        if t == 0:
+            w, s = synth.fp8_matrix(N, K, seed=31, stream=K)
+            _SWEEP_CACHE[key] = (Fp8Weight(w, s, K, N), (w, s))
+        else:
+            raw = synth.quant_matrix(t, N, K, seed=31, stream=K)
+            _SWEEP_CACHE[key] = (QMatMul(t, raw, N, K), raw)
+    return _SWEEP_CACHE[key]
+
+
+def _sampled_rows(N, n=96):
+    rows = np.unique(np.linspace(0, N - 1, n).astype(np.int64))
+    return np.concatenate([rows, [N - 1]]) if rows[-1] != N - 1 else rows
+
+
+@pytest.mark.parametrize("name,t", FORMATS + [("FP8", 0)])
+@pytest.mark.parametrize("N,K", [(14336, 4096), (4096, 14336)])
+@pytest.mark.parametrize("M", [16, 64, 512, 2048])
+def test_gemm_parity_config1_sweep_points(name, t, N, K, M):
+    # the bench's m_sweep points at full size: the whole [M, N] output is computed on the
+    # GPU and a spread of 96 rows (first and last included) is checked against the oracle
+    import torch
+
+    obj, host = _sweep_weight(t, N, K)
+    x = synth.bf16_round(synth.activations(M, K, seed=M, stream=K))
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    rows = _sampled_rows(N)
+    if t == 0:
+        y = obj.forward(xt.float())
+        w, s = host
+        want = oracle.fp8_gemm_cpu_f64(x, np.ascontiguousarray(w[rows]), np.ascontiguousarray(s[rows]),
+                                       len(rows), K)
+    else:
+        y = obj.forward(xt, out_dtype=torch.float32)
+        elems, bb = synth.BLOCK[t]
+        row_bytes = (K // elems) * bb
+        sub = np.ascontiguousarray(host.reshape(N, row_bytes)[rows]).reshape(-1)
+        want = oracle.qgemv_f64(t, sub, len(rows), K, x)
+    got = y[:, torch.from_numpy(rows).cuda()].cpu().numpy()
+    assert np.isfinite(y.cpu().numpy()).all()
+    assert rel_l2(got, want) <= RTOL
+
+
+@pytest.mark.parametrize("name,t", [("Q6_K", 14), ("Q8_0", 8)])
+def test_lm_head_vocab_152064(name, t):
+    # the 152064-row LM head of the 7B- and 70B-shaped configs (K = 3584), sampled rows,
+    # at decode (GEMV, M = 1) and speculative-verify (GEMM, M = 5) token counts
+    import torch
+    from runtimed_b200.weights import QMatMul
+
+    N, K = 152064, 3584
+    raw = synth.quant_matrix(t, N, K, seed=11, stream=t)
+    qm = QMatMul(t, raw, N, K)
+    rows = _sampled_rows(N, 128)
+    elems, bb = synth.BLOCK[t]
+    sub = np.ascontiguousarray(raw.reshape(N, (K // elems) * bb)[rows]).reshape(-1)
+    del raw
+    for M in (1, 5):
+        x = synth.bf16_round(synth.activations(M, K, seed=12))
+        y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32)
+        want = oracle.qgemv_f64(t, sub, len(rows), K, x)
+        got = y[:, torch.from_numpy(rows).cuda()].cpu().numpy()
+        assert rel_l2(got, want) <= (RTOL if M >= 4 else 2e-5), M

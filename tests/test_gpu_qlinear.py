@@ -211,3 +211,20 @@ def test_embed_out_of_range_raises_status():
         qm.ctx.check_device_status()
     assert np.all(y[1].cpu().numpy() == 0)
     qm.ctx.check_device_status()  # the status word was cleared
+
+
+@pytest.mark.parametrize("name,t", FORMATS)
+def test_to_device_copy_is_identical(name, t):
+    # rtd_qweight_to_device: a second device copy that dequantizes and multiplies to the
+    # same bits as the original, and stays valid after the original is freed
+    torch = _torch()
+    qm, raw = make_qm(t, 100, 512, seed=3, stream=t)
+    cp = qm.to_device("cuda:0")
+    x = torch.from_numpy(synth.activations(2, 512, seed=4)).cuda()
+    y0 = qm.forward(x)
+    d0 = qm.dequantize()
+    qm.free()
+    y1 = cp.forward(x)
+    assert torch.equal(y0, y1)
+    assert torch.equal(d0, cp.dequantize())
+    assert cp.storage_size_in_bytes() == len(raw)

@@ -1,8 +1,10 @@
-"""Row-parallel quantized linear with the all-reduce fused into the GEMV epilogue,
-on two GPUs (one process each, NCCL for set-up only), against the unsharded CPU
-oracle and against the NCCL all-reduce comparison path.
+"""Row-parallel quantized linear on 2, 4 and 8 GPUs (one process each, NCCL for set-up
+and the comparison path only), against the unsharded CPU oracle and against the NCCL
+all-reduce comparison path: up to three tokens run the GEMV with the all-reduce fused
+into its epilogue, four or more the tensor-core GEMM followed by the library's two-shot
+all-reduce kernel, which is also checked on its own (rtd_tp_allreduce).
 
-Skipped with fewer than two GPUs.  NVLS is switched off and the kernel's peer
+Each world size is skipped when the box has fewer GPUs.  NVLS is switched off and the kernel's peer
 traffic is plain stores, so a rank that leaves early cannot fault the others; the
 timeout case makes one rank skip a call and checks that the other finishes with
 RTD_ERR_PEER_TIMEOUT instead of waiting.
@@ -45,14 +47,17 @@ def _rank_main(rank, world, port, q):
     try:
         ctx = Context.for_device(dev)
         comm = TpComm(ctx, rank, world, max_n=4096)
-        for t, n, k in [(12, 4096, 2048), (14, 1000, 1024), (8, 2056, 512)]:
+        shapes = [(12, 4096, 256 * world), (14, 1000, 256 * world), (8, 2056, 64 * world)]
+        for t, n, k in shapes:
             raw = synth.quant_matrix(t, n, k, seed=5, stream=t)
             bias = np.random.default_rng(t).normal(0, 0.02, n).astype(np.float32)
             rpl = RowParallelLinear.from_full_weight(raw, t, n, k, bias, rank, world, comm=comm, device=dev)
             ks = k // world
-            # M = 6 runs as two launches (four tokens each at most): two epochs in one call
+            # M <= 3: the fused GEMV (f32 rows at M = 3: two launches, two epochs in one
+            # call); M >= 4: the GEMM and the two-shot all-reduce (M = 130: two chunks)
             for call, (m, dt) in enumerate([(1, torch.bfloat16), (3, torch.float32), (4, torch.float16),
-                                            (6, torch.float32), (1, torch.bfloat16)]):
+                                            (6, torch.float32), (64, torch.bfloat16), (130, torch.float32),
+                                            (1, torch.bfloat16)]):
                 x = synth.activations(m, k, seed=100 * t + call)
                 xt = torch.from_numpy(x).to(dt)
                 want = oracle.qgemv_f64(t, raw, n, k, xt.float().numpy()) + bias[None, :]
@@ -66,36 +71,57 @@ def _rank_main(rank, world, port, q):
                 # y comes back in x's dtype: its rounding bounds the error (bf16 ~2^-9 RMS)
                 tol = OUT_TOL[dt]
                 rf, rn = _rel(y.cpu().numpy(), want), _rel(yn.cpu().numpy(), want)
-                # the NCCL path's local partial runs the single-GPU linear: the tensor-core
-                # GEMM (f16-rounded weights, 1e-3 gate) from four tokens on
-                tol_n = tol if m <= 3 else max(tol, 1e-3)
-                out[(t, call)] = (rf <= tol, rn <= tol_n, all(bool(torch.equal(g, gathered[0])) for g in gathered),
+                # four or more tokens run the tensor-core GEMM (f16-rounded weights, 1e-3
+                # gate) on both paths
+                tol = tol if m <= 3 else max(tol, 1e-3)
+                out[(t, call)] = (rf <= tol, rn <= tol, all(bool(torch.equal(g, gathered[0])) for g in gathered),
                                   rf, rn)
+        # the stand-alone two-shot all-reduce: sum of every rank's f32 partial + bias once
+        for call, (m, n, dt) in enumerate([(1, 4096, torch.float32), (7, 1000, torch.bfloat16),
+                                           (128, 4096, torch.float32), (300, 33, torch.float16)]):
+            parts = [torch.from_numpy(synth.activations(m, n, seed=700 + call, stream=q)) for q in range(world)]
+            bias = torch.from_numpy(np.random.default_rng(call).normal(0, 0.5, n).astype(np.float32))
+            want = sum(p.double() for p in parts) + bias.double()
+            y = comm.allreduce(parts[rank].to(dev), bias=bias.to(dev), out_dtype=dt).float()
+            torch.cuda.synchronize()
+            ctx.check_device_status()
+            gathered = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(gathered, y)
+            r = _rel(y.cpu().numpy(), want.numpy())
+            out[("ar", call)] = (r <= OUT_TOL[dt], True, all(bool(torch.equal(g, gathered[0])) for g in gathered),
+                                 r, 0.0)
         # the fused call captured in a CUDA graph: the epoch lives on the device, so
         # every replay exchanges fresh partials (new x each replay, checked each time)
-        t, n, k = 14, 1000, 1024
+        # (one fused GEMV launch at M = 2, the GEMM + all-reduce at M = 8 in the same graph)
+        t, n, k = 14, 1000, 256 * world
         raw = synth.quant_matrix(t, n, k, seed=6, stream=t)
         rpl = RowParallelLinear.from_full_weight(raw, t, n, k, None, rank, world, comm=comm, device=dev)
         ks = k // world
         xs = torch.zeros((2, ks), dtype=torch.float32, device=dev)
+        xb = torch.zeros((8, ks), dtype=torch.float32, device=dev)
         rpl.forward(xs)
+        rpl.forward(xb)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             yg = rpl.forward(xs)
+            yb = rpl.forward(xb)
         graph_ok = []
         for rep in range(3):
             x = synth.activations(2, k, seed=900 + rep)
+            x8 = synth.activations(8, k, seed=950 + rep)
             xs.copy_(torch.from_numpy(x[:, rank * ks:(rank + 1) * ks]).to(dev))
+            xb.copy_(torch.from_numpy(x8[:, rank * ks:(rank + 1) * ks]).to(dev))
             g.replay()
             torch.cuda.synchronize()
             ctx.check_device_status()
             graph_ok.append(_rel(yg.cpu().numpy(), oracle.qgemv_f64(t, raw, n, k, x)) <= RTOL_EXACT)
+            graph_ok.append(_rel(yb.cpu().numpy(), oracle.qgemv_f64(t, raw, n, k, x8)) <= 1e-3)
         del g
         out["graph"] = all(graph_ok)
-        # a rank that skips a call: the other finishes with RTD_ERR_PEER_TIMEOUT
-        raw = synth.quant_matrix(12, 16, 512, seed=1)
-        rpl = RowParallelLinear.from_full_weight(raw, 12, 16, 512, None, rank, world, comm=comm, device=dev)
+        # only rank 0 makes a call: it finishes with RTD_ERR_PEER_TIMEOUT instead of waiting
+        raw = synth.quant_matrix(12, 16, 256 * world, seed=1)
+        rpl = RowParallelLinear.from_full_weight(raw, 12, 16, 256 * world, None, rank, world, comm=comm, device=dev)
         dist.barrier()
         timed_out = None
         if rank == 0:
@@ -119,10 +145,11 @@ def _rank_main(rank, world, port, q):
             q.put((rank, out))  # always: a rank that raised must not leave the parent waiting
 
 
-def test_row_parallel_fused_allreduce_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_parallel_fused_allreduce(world):
     torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     with socket.socket() as s:
@@ -130,7 +157,7 @@ def test_row_parallel_fused_allreduce_two_gpus():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

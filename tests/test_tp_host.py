@@ -105,3 +105,16 @@ def test_row_parallel_reduction_over_gloo():
         p.join(timeout=60)
     assert sorted(r for r, _, _ in res) == [0, 1]
     assert all(ok and hok for _, ok, hok in res)
+
+
+def test_fp8_scale_key_order_and_default():
+    # the lookup order of linear_layer.rs:78-86, on the host side of the mirror
+    torch = pytest.importorskip("torch")
+    from runtimed_b200.weights import Weights
+
+    W = Weights.__new__(Weights)
+    W.map = {"a.weight_scale_inv": torch.full((3,), 3.0), "a_scale": torch.full((3,), 2.0)}
+    assert float(W.fp8_scale("a", 3)[0]) == 2.0  # "_scale" before ".weight_scale_inv"
+    W.map["a.scale"] = torch.full((3,), 1.5)
+    assert float(W.fp8_scale("a", 3)[0]) == 1.5  # ".scale" first
+    assert torch.equal(W.fp8_scale("b", 4), torch.ones(4))  # none: ones of out_dim

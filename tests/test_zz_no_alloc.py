@@ -1,22 +1,27 @@
-"""The allocation-free linear, rtd_qlinear_noalloc, against rtd_qlinear.
+"""The allocation-free linear, rtd_qlinear_noalloc, against the CPU oracle and rtd_qlinear.
 
-Both run the same kernels. The allocation-free entry takes its scratch from a fixed
-array inside the library instead of a context workspace. Two calls in a row, with
-different activations, must each match the context-based entry point on the same
-input. A call whose staging would not fit the fixed scratch is refused before any
-launch. This file is collected last, and it must also pass alone in a fresh process
-(the first call on a device sets the scratch up).
+Some callers cannot allocate device memory while they run: code that works inside
+another allocator's fixed device-memory budget, where an extra cudaMalloc can fail or
+stall every stream on the device.  rtd_qlinear_noalloc serves them: it dispatches like
+rtd_qlinear but takes its scratch from a fixed array inside the library instead of a
+context workspace.  Two calls in a row, with different activations, must each match
+the oracle within the path's bar and match rtd_qlinear on the same input.  The cases
+cover one-launch GEMV calls, a multi-pass GEMV call (f32 rows at M = 3 run as 2 + 1
+tokens, both passes on the one scratch array) and the tensor-core GEMM (M = 5).  A call
+whose staging would not fit is refused before any launch, and the status word of the
+scratch is read through rtd_noalloc_check_status.  This file is collected last, and it
+must also pass alone in a fresh process (the first call on a device sets the scratch up).
 """
-import ctypes
-
 import numpy as np
 import pytest
 
+import oracle
 from runtimed_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
 
-RTOL_EXACT = 2e-5  # the GEMV tests' bound for exact-product kernels (f32 rounding only)
+RTOL_EXACT = 2e-5  # exact-product GEMV passes (f32 rounding only)
+RTOL_GEMM = 1e-3   # the tensor-core GEMM rounds decoded weights once to f16
 DT = {"f32": _lib.DT_F32, "f16": _lib.DT_F16, "bf16": _lib.DT_BF16}
 
 
@@ -43,24 +48,30 @@ def _call(L, fn, qm, x, y, xdt, bias=None):
 
 
 @pytest.mark.parametrize("t", [12, 14, 8])
-@pytest.mark.parametrize("xdt,M", [("bf16", 1), ("f16", 3), ("f32", 2)])
-def test_noalloc_matches_qlinear_twice(t, xdt, M):
+@pytest.mark.parametrize("xdt,M", [("bf16", 1), ("f16", 3), ("f32", 2), ("f32", 3), ("bf16", 5)])
+def test_noalloc_matches_oracle_and_qlinear_twice(t, xdt, M):
     torch = pytest.importorskip("torch")
     from runtimed_b200.weights import QMatMul
 
     N, K = 200, 2048
-    qm = QMatMul(t, synth.quant_matrix(t, N, K, seed=7, stream=t), N, K)
-    bias = torch.from_numpy(np.random.default_rng(3).normal(0, 0.02, N).astype(np.float32)).cuda()
+    raw = synth.quant_matrix(t, N, K, seed=7, stream=t)
+    qm = QMatMul(t, raw, N, K)
+    bias_np = np.random.default_rng(3).normal(0, 0.02, N).astype(np.float32)
+    bias = torch.from_numpy(bias_np).cuda()
+    tol = RTOL_GEMM if M >= 4 else RTOL_EXACT
     L = _lib.lib()
     for call in range(2):  # two calls in a row share the one scratch array
-        x = torch.from_numpy(synth.activations(M, K, seed=100 + call, stream=t)).to(_torch_dtype(torch, xdt)).cuda()
-        want = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        xt = torch.from_numpy(synth.activations(M, K, seed=100 + call, stream=t)).to(_torch_dtype(torch, xdt))
+        want = oracle.qgemv_f64(t, raw, N, K, xt.float().numpy()) + bias_np[None, :]
+        x = xt.cuda()
+        ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
         got = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-        assert _call(L, "ctx", qm, x, want, xdt, bias) == 0
+        assert _call(L, "ctx", qm, x, ref, xdt, bias) == 0
         rc = _call(L, "noalloc", qm, x, got, xdt, bias)
         assert rc == 0, L.rtd_last_error(None)
-        torch.cuda.synchronize()
-        assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) <= RTOL_EXACT
+        assert L.rtd_noalloc_check_status(0, torch.cuda.current_stream().cuda_stream) == 0
+        assert rel_l2(got.cpu().numpy(), want) <= tol
+        assert rel_l2(got.cpu().numpy(), ref.cpu().numpy()) <= tol
 
 
 def test_noalloc_rejects_oversized_staging():
@@ -81,3 +92,4 @@ def test_noalloc_rejects_oversized_staging():
     assert "static scratch" in msg
     torch.cuda.synchronize()
     assert bool((y == 7.0).all())  # nothing was launched
+    assert L.rtd_noalloc_check_status(0, None) == 0
