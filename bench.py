@@ -1,35 +1,40 @@
-"""Benchmark of the quantized decode-GEMV hot path on B200 (driver contract: one JSON line).
+"""Benchmark of the quantized forward-pass hot path on B200 (driver contract: one JSON line).
 
-Workload (the reference's op-sweep config): y = x . W^T at M = 1 (one decode
-token, bf16 activations) for every feasible (format, shape) of
-  formats Q4_K, Q6_K, Q8_0 (GGUF blocks) and FP8 E4M3 (per-channel scale)
-  shapes (N, K) = (4096, 4096), (14336, 4096), (4096, 14336), (151936, 896)
-(Q4_K / Q6_K need K % 256 == 0, so their K = 896 points are infeasible).
-A "step" is one pass over the 14 GEMVs; every step reads 0.74 GB of distinct
-weights, well above the 126 MB L2, so each weight byte comes from HBM.
-
-Metric: quant-GEMV HBM GB/s from algorithmic bytes (packed weights + x + y (+ FP8
-channel scales)); dequantized weights never count.  value = device-timed
-(weights and x resident in HBM, CUDA graph of the step, CUDA events); e2e = the
-same through the C ABI, every step copying its 14 activation rows in from pinned
-host memory and reading its 14 outputs back before the next step.
-
-The line also carries the roofline of the longest GEMV (against the measured HBM
-copy bandwidth), the CPU baseline (the restated reference path on the host cores),
-the SM clocks sampled during the timed steps, and:
-  m_sweep  the rest of the config-1 token counts (M = 4..2048) at 14336 x 4096,
-           1 GPU only (M >= 4 runs the tensor-core GEMM);
-  tp       N > 1: the fused row-parallel linear against GEMV + NCCL all-reduce.
+Headline: decode tokens/s of config 3, the 70B-shaped Qwen2 decoder (hidden 8192, FFN
+28672, 64 query / 8 KV heads of 128, 80 layers, Q4_K_M-style: Q4_K q/k/o/gate/up, Q6_K
+v/down, q/k/v bias), batch 64, tensor parallel over the N GPUs of the run:
+  * a step is one decode token for each of the 64 sequences through the seven linears of
+    all 80 layers -- 43.5 GB of packed weights at N = 1, 1/N of them on each rank;
+  * column parallel (output rows split, no exchange): attn_q / attn_k / attn_v, ffn_gate,
+    ffn_up; row parallel (input columns split, all-reduce of the outputs): attn_output and
+    ffn_down, through rtd_tp_qlinear_row -- the exchange fused into the GEMV epilogue up to
+    three tokens, the tensor-core GEMM plus the library's two-shot NVLink all-reduce from
+    four on;
+  * the step carries the layer's real data flow between linears (q's head shard feeds
+    attn_output, ffn_gate's shard feeds ffn_down); attention, RMSNorm and SwiGLU are not
+    part of this path.  Each layer reads its own device copy of the weights (80 distinct
+    copies of one seeded random layer: the kernels' work and HBM traffic do not depend on
+    the weight values), so every step streams all 80 layers from HBM.
+value = B * steps / device time of the step's CUDA graph (max over ranks, strong
+scaling: the same model and batch at every N).  e2e = the same through the public API
+with the step's hidden states copied in from pinned host memory and its outputs read
+back every step.  The line also carries the batch-1 step, the roofline of the step's
+dominant kernel and of the whole step, the CPU baseline (the restated reference CPU path
+on the host cores, scaled to the step), the SM clocks of the timed window, and:
+  tp          N > 1: the config-3 row-parallel linears (attn_output, ffn_down) fused vs the
+              library's all-reduce vs NCCL, at M = 1 and 64, each checked against the
+              unsharded single-GPU result (rel_l2);
+  gemv_sweep  N = 1: the config-1 quantized-linear sweep at decode M = 1 (14 GEMVs, HBM
+              GB/s of algorithmic bytes) with the roofline of its longest GEMV;
+  m_sweep     N = 1: the config-1 token counts M = 4..2048 at (14336, 4096).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     python bench.py --profile-one FMT:N:K[:M] | sweep   (ncu target, no JSON line)
-
-N > 1 runs under torchrun, one rank per GPU, each rank its own copy of the sweep
-(weak scaling: independent weight shards), max time over ranks.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -42,10 +47,26 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+# config 3: the 70B-shaped decoder
+HIDDEN, FFN, N_HEAD, N_KV, HEAD_DIM, N_LAYERS = 8192, 28672, 64, 8, 128, 80
+BATCH = 64
+# (name, ggml type, N out, K in, split, bias): the seven linears of one layer in call order
+LAYER_LINEARS = [
+    ("attn_q", Q4_K, N_HEAD * HEAD_DIM, HIDDEN, "col", True),
+    ("attn_k", Q4_K, N_KV * HEAD_DIM, HIDDEN, "col", True),
+    ("attn_v", Q6_K, N_KV * HEAD_DIM, HIDDEN, "col", True),
+    ("attn_output", Q4_K, HIDDEN, N_HEAD * HEAD_DIM, "row", False),
+    ("ffn_gate", Q4_K, FFN, HIDDEN, "col", False),
+    ("ffn_up", Q4_K, FFN, HIDDEN, "col", False),
+    ("ffn_down", Q6_K, HIDDEN, FFN, "row", False),
+]
+TYPE_NAMES = {Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+METRIC = "decode tokens/s (config-3 70B-shaped Qwen2, linears of all 80 layers, batch 64, TP over N GPUs)"
+UNIT = "tokens/s"
+
 SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (151936, 896)]
 FORMATS = [("Q4_K", 12), ("Q6_K", 14), ("Q8_0", 8), ("FP8", 0)]
-METRIC = "quant-GEMV HBM GB/s (decode M=1, config-1 sweep)"
-UNIT = "GB/s"
 
 
 def sweep():
@@ -69,13 +90,22 @@ def alg_bytes(t, n, k, m=1):
     return weight_bytes(t, n, k) + m * k * 2 + m * n * 2  # bf16 x in, bf16 y out
 
 
+def shard_shape(n, k, split, world):
+    return (n // world, k) if split == "col" else (n, k // world)
+
+
+def step_weight_bytes(world: int) -> int:
+    """Packed weight bytes one rank streams per step (all layers, its shards)."""
+    return N_LAYERS * sum(weight_bytes(t, *shard_shape(n, k, sp, world)) for _, t, n, k, sp, _ in LAYER_LINEARS)
+
+
 def read_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), "measured", d.get("bf16_tflops")
+    return 6650.0, "fallback", 1590.0
 
 
 def profile_traffic(kernel_tag: str):
@@ -151,16 +181,17 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-_CPU_ROWS = 1024  # rows of each sweep point's CPU sample
-_CPU_SAMPLES = {}  # (type, K) -> the sample rows of one sweep point, generated once per process
+# ---------------------------------------------------------------- CPU baseline
+_CPU_ROWS = 256      # rows of each linear's CPU sample (full K)
+_CPU_SAMPLES = {}    # (type, n, k) -> (x, raw rows), generated once per process
 
 
-def _cpu_sample(t, k):
+def _cpu_sample(t, k, m):
     from runtimed_b200 import synth
 
-    key = (t, k)
+    key = (t, k, m)
     if key not in _CPU_SAMPLES:
-        x = synth.bf16_round(synth.activations(1, k, seed=0))
+        x = synth.bf16_round(synth.activations(m, k, seed=0))
         if t == 0:
             _CPU_SAMPLES[key] = (x, synth.fp8_matrix(_CPU_ROWS, k, seed=0))
         else:
@@ -168,42 +199,35 @@ def _cpu_sample(t, k):
     return _CPU_SAMPLES[key]
 
 
-def cpu_baseline(budget_s: float = 20.0):
-    """The restated reference CPU path (oracle/: bit-exact block decode + f32 dot,
-    OpenMP over all host threads) on a bounded row sample of every sweep point.  Only
-    the oracle calls are timed; the samples are generated once per process."""
+def cpu_baseline(budget_s: float = 20.0, batch: int = BATCH):
+    """The restated reference CPU path (oracle/: bit-exact block decode + f32 dots, OpenMP
+    over all host threads) on a row sample of each of the seven layer linears at full K
+    and M = batch; the measured seconds per row, times the rows of all 80 layers, give the
+    step's CPU time and tokens/s.  Only the oracle calls are timed."""
     import oracle
 
     threads = os.cpu_count() or 1
-    tot_bytes, tot_s = 0.0, 0.0
-    per = budget_s / len(sweep())
+    per = budget_s / len(LAYER_LINEARS)
+    step_s = 0.0
     rows_used = {}
-    for name, t, n, k in sweep():
-        rows = 64
-        x, sample = _cpu_sample(t, k)
-        if t == 0:
-            w, s = sample
-        else:
-            raw = sample
-        spent, done_b = 0.0, 0.0
-        while spent < per:  # row blocks double up to the whole sample, then repeat
+    for name, t, n, k, _, _ in LAYER_LINEARS:
+        x, raw = _cpu_sample(t, k, batch)
+        row_b = weight_bytes(t, 1, k)
+        rows, spent, done = 8, 0.0, 0
+        while spent < per:
             t0 = time.perf_counter()
-            if t == 0:
-                oracle.ref_cpu_fp8_linear(x, w[:rows], s[:rows], rows, k, threads=threads)
-            else:
-                row_b = weight_bytes(t, 1, k)
-                oracle.ref_cpu_linear(t, raw[: rows * row_b], rows, k, x, threads=threads)
+            oracle.ref_cpu_linear(t, raw[: rows * row_b], rows, k, x, threads=threads)
             dt = time.perf_counter() - t0
             spent += dt
-            done_b += alg_bytes(t, rows, k)
+            done += rows
             if dt < 0.25 and rows < _CPU_ROWS:
                 rows *= 2
-        tot_bytes += done_b
-        tot_s += spent
-        rows_used[f"{name}:{n}x{k}"] = rows
-    return {"value": tot_bytes / tot_s / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"row samples of every sweep point (~{budget_s:.0f} s of CPU work), oracle/rtd_oracle.c "
-                      f"restating the reference block decoders + f32 dot, OpenMP {threads} threads"}
+        step_s += N_LAYERS * n * spent / done
+        rows_used[name] = done
+    return {"value": batch / step_s, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"row samples of the 7 config-3 layer linears at full K and M={batch} "
+                      f"(~{budget_s:.0f} s of CPU work), scaled to the 80-layer step; oracle/rtd_oracle.c "
+                      f"restating the reference block decoders + f32 dots, OpenMP {threads} threads"}
 
 
 def run_reference(args) -> None:
@@ -212,136 +236,323 @@ def run_reference(args) -> None:
         return
     base = None
     for _ in range(max(args.warmup, 0)):
-        cpu_baseline(budget_s=2.0)
+        cpu_baseline(budget_s=1.0)
     vals = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        base = cpu_baseline(budget_s=max(5.0, 60.0 / max(args.steps, 1)))
+        base = cpu_baseline(budget_s=max(3.5, 60.0 / max(args.steps, 1)))
         vals.append(base["value"])
     wall = time.perf_counter() - t0
     value = statistics.mean(vals)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": config_dict(),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": config_dict(args.gpus),
             "cpu_baseline": dict(base, value=value),
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def launches_per_gemv(t: int, n: int, k: int) -> int:
-    """Kernels one M=1 bf16 call launches (rtd_gemv.cu launch_qgemv): the GEMV alone when
-    the launch runs in whole mode (at least two 16-row tiles per warp of two 8-warp CTAs
-    on each of the 148 SMs) and every CTA can stage the activation row itself (K % 8 == 0,
-    the staged row plus its column-sum table within 40 KB); otherwise a prep kernel too."""
-    gk, sbe = {0: (128, 32), 8: (128, 32), 12: (256, 32), 14: (256, 16)}[t]
-    kp = -(-k // gk) * gk
-    tab = (kp // gk) * (gk // sbe + 4)
-    whole = -(-n // 16) >= 2 * 148 * 2 * 8
-    return 1 if (whole and k % 8 == 0 and kp * 2 + tab * 4 <= 40 * 1024) else 2
+def config_dict(world: int):
+    return {"workload": "config-3 decode step: 70B-shaped Qwen2 linears of all 80 layers, batch 64 "
+                        "(one token per sequence), tensor parallel over the run's GPUs",
+            "model": "config3-qwen2-70b-shaped (random init, Q4_K_M-style)", "layers": N_LAYERS,
+            "hidden": HIDDEN, "ffn": FFN, "heads": [N_HEAD, N_KV, HEAD_DIM], "global_batch": BATCH,
+            "linears": [f"{n}:{TYPE_NAMES[t]}:{N}x{K}:{sp}" for n, t, N, K, sp, _ in LAYER_LINEARS],
+            "parallelism": f"tp{world}: column-parallel q/k/v/gate/up, row-parallel o/down (fused NVLink exchange)",
+            "activations": "bf16", "weights": "80 device copies of one seeded random-init layer (config-3 "
+                                                "block distributions)",
+            "l2": f"inputs larger than L2: {step_weight_bytes(world) / 1e9:.1f} GB of weights per rank per step "
+                  "vs 126 MB L2",
+            "not_in_step": "attention over the KV cache, RMSNorm, RoPE, SwiGLU, embedding and LM head"}
 
 
-def config_dict():
-    return {"workload": "config1 quantized-linear op sweep at decode M=1 (y = x.W^T), one step = 14 GEMVs",
-            "formats": [f for f, _ in FORMATS], "shapes_nk": SHAPES, "m": 1, "activations": "bf16",
-            "weights": "random-init GGUF blocks with the config-1 distributions (seed 0)",
-            "l2": "inputs larger than L2: 0.74 GB of distinct weights per step vs 126 MB L2",
-            "parallelism": "replicas: each rank streams its own weight copy"}
+# ---------------------------------------------------------------- the TP decode step
+class TpStack:
+    """The seven linears of every layer, sharded for this rank, and the step's buffers."""
+
+    def __init__(self, rank, world, dev, comm, batches):
+        import torch
+        from runtimed_b200 import _lib, synth
+        from runtimed_b200.weights import QMatMul
+
+        self.L = _lib.lib()
+        self.rank, self.world, self.dev, self.comm = rank, world, dev, comm
+        self.layers = []
+        first = {}
+        for i, (name, t, n, k, sp, has_b) in enumerate(LAYER_LINEARS):
+            ns, ks = shard_shape(n, k, sp, world)
+            raw = synth.quant_matrix(t, ns, ks, seed=1000 + rank, stream=i)
+            qm = QMatMul(t, raw, ns, ks, device=dev)
+            del raw
+            bias = None
+            if has_b:
+                b = np.random.default_rng(50 + i).normal(0, 0.02, n).astype(np.float32)
+                bias = torch.from_numpy(b[rank * ns:(rank + 1) * ns].copy()).to(dev)
+            first[name] = (qm, bias)
+        for layer in range(N_LAYERS):
+            ent = {}
+            for name, *_ in LAYER_LINEARS:
+                qm, bias = first[name]
+                ent[name] = (qm if layer == 0 else qm.to_device(dev), bias)
+            self.layers.append(ent)
+        torch.cuda.synchronize(dev)
+        self.bufs = {}
+        for b in batches:
+            bf = torch.bfloat16
+            kv = N_KV * HEAD_DIM // world
+            self.bufs[b] = dict(
+                x=torch.from_numpy(synth.activations(b, HIDDEN, seed=rank, stream=3)).to(bf).to(dev),
+                q=torch.empty((b, N_HEAD * HEAD_DIM // world), dtype=bf, device=dev),
+                k=torch.empty((b, kv), dtype=bf, device=dev), v=torch.empty((b, kv), dtype=bf, device=dev),
+                o=torch.empty((b, HIDDEN), dtype=bf, device=dev),
+                g=torch.empty((b, FFN // world), dtype=bf, device=dev),
+                u=torch.empty((b, FFN // world), dtype=bf, device=dev),
+                d=torch.empty((b, HIDDEN), dtype=bf, device=dev))
+
+    def _lin(self, qm, bias, x, y, m, st):
+        from runtimed_b200 import _lib
+
+        rc = self.L.rtd_qlinear(qm.ctx.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, qm.k, m,
+                                None if bias is None else bias.data_ptr(), y.data_ptr(), _lib.DT_BF16, qm.n, st)
+        if rc != 0:
+            raise RuntimeError(f"rtd_qlinear status {rc}: {self.L.rtd_last_error(qm.ctx.handle)}")
+
+    def _row(self, qm, x, y, m, st):
+        from runtimed_b200 import _lib
+
+        if self.world == 1:
+            return self._lin(qm, None, x, y, m, st)
+        rc = self.L.rtd_tp_qlinear_row(self.comm.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, qm.k, m, None,
+                                       y.data_ptr(), _lib.DT_BF16, qm.n, st)
+        if rc != 0:
+            raise RuntimeError(f"rtd_tp_qlinear_row status {rc}: {self.L.rtd_last_error(qm.ctx.handle)}")
+
+    def step(self, b, st, layers=None):
+        """One decode token for b sequences through every layer's linears."""
+        B = self.bufs[b]
+        for ent in (self.layers if layers is None else layers):
+            self._lin(*ent["attn_q"], B["x"], B["q"], b, st)
+            self._lin(*ent["attn_k"], B["x"], B["k"], b, st)
+            self._lin(*ent["attn_v"], B["x"], B["v"], b, st)
+            self._row(ent["attn_output"][0], B["q"], B["o"], b, st)
+            self._lin(*ent["ffn_gate"], B["o"], B["g"], b, st)
+            self._lin(*ent["ffn_up"], B["o"], B["u"], b, st)
+            self._row(ent["ffn_down"][0], B["g"], B["d"], b, st)
+
+    def one(self, name, layer, b, st):
+        """One linear of one layer (for the per-linear timing)."""
+        B = self.bufs[b]
+        io = {"attn_q": ("x", "q"), "attn_k": ("x", "k"), "attn_v": ("x", "v"), "attn_output": ("q", "o"),
+              "ffn_gate": ("o", "g"), "ffn_up": ("o", "u"), "ffn_down": ("g", "d")}[name]
+        qm, bias = self.layers[layer][name]
+        if name in ("attn_output", "ffn_down"):
+            self._row(qm, B[io[0]], B[io[1]], b, st)
+        else:
+            self._lin(qm, bias, B[io[0]], B[io[1]], b, st)
 
 
-def _time_steps(graph, stream, dev, n: int) -> float:
+def _capture(fn, dev):
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn(torch.cuda.current_stream(dev).cuda_stream)
+    return g
+
+
+def _time_graph(g, stream, dev, n: int) -> float:
+    """Seconds per replay of n back-to-back replays (CUDA events on the launching stream)."""
     import torch
 
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     for _ in range(n):
-        graph.replay()
+        g.replay()
     b.record(stream)
     torch.cuda.synchronize(dev)
-    return a.elapsed_time(b) * 1e-3
+    return a.elapsed_time(b) * 1e-3 / n
+
+
+def _max_over_ranks(v: float, dev, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _per_linear(stack, b, stream, dev, world, reps: int = 24):
+    """Device time of each of the seven linears at batch b: a graph of `reps` calls rotating
+    over three layers' weight copies (no call re-reads another's weights from L2)."""
+    import torch
+    import torch.distributed as dist
+
+    out = {}
+    for name, t, n, k, sp, _ in LAYER_LINEARS:
+        if world > 1:
+            dist.barrier()
+        g = _capture(lambda st: [stack.one(name, r % 3, b, st) for r in range(reps)], dev)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        s = _max_over_ranks(_time_graph(g, stream, dev, 5) / reps, dev, world)
+        del g
+        ns, ks = shard_shape(n, k, sp, world)
+        byts = weight_bytes(t, ns, ks) + b * ks * 2 + b * (n if sp == "row" else ns) * 2
+        out[name] = {"us": s * 1e6, "shard_nk": [ns, ks], "bytes": byts, "gbs": byts / s / 1e9}
+    return out
 
 
 def _tp_rowparallel(world, rank, dev, stream, reps: int = 20):
-    """Row-parallel down_proj of the 70B-shaped config (Q6_K, N = 8192, K = 28672 split
-    over the ranks): the reduction fused into the GEMV epilogue (peer stores over NVLink)
-    against the same GEMV followed by an NCCL all-reduce.  Each path is captured in a
-    CUDA graph of `reps` calls (the fused call keeps its epoch on the device, so replays
-    are valid); device time per call, max over ranks; every rank issues the same calls
-    and collectives in the same order."""
+    """The config-3 row-parallel linears (attn_output Q4_K 8192 x 8192, ffn_down Q6_K
+    8192 x 28672, K split over the ranks) at M = 1 and 64: the fused call, the unfused GEMV
+    plus the library's all-reduce, and the GEMV plus an NCCL all-reduce.  Each path is a
+    CUDA graph of `reps` calls (device time per call, max over ranks); each output is
+    checked against the unsharded single-GPU linear of the same full weight (rel_l2)."""
     import torch
     import torch.distributed as dist
     from runtimed_b200 import synth
     from runtimed_b200.tp import RowParallelLinear, TpComm
-    from runtimed_b200.weights import Context
+    from runtimed_b200.weights import Context, QMatMul
 
-    t, n, k = 14, 8192, 28672
-    raw = synth.quant_matrix(t, n, k, seed=7)
-    comm = TpComm(Context.for_device(dev), rank, world, max_n=n)
-    rpl = RowParallelLinear.from_full_weight(raw, t, n, k, None, rank, world, comm=comm, device=dev)
-    del raw
-    out = {"shape_nk": [n, k], "format": "Q6_K", "world": world, "k_shard": k // world,
-           "timing": f"CUDA graph of {reps} calls per path, 5 replays, CUDA events, max over ranks"}
-    for m in (1, 4):
-        x = torch.from_numpy(synth.activations(m, k // world, seed=rank)).to(torch.bfloat16).to(dev)
-        res = {}
-        for name, fn in (("fused", rpl.forward), ("nccl", rpl.forward_nccl)):
-            for _ in range(3):
-                fn(x)
-            torch.cuda.synchronize(dev)
-            dist.barrier()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for _ in range(reps):
-                    fn(x)
-            g.replay()
-            torch.cuda.synchronize(dev)
-            dist.barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            for _ in range(5):
+    comm = TpComm(Context.for_device(dev), rank, world, max_n=HIDDEN)
+    out = {"timing": f"CUDA graph of {reps} calls per path, 5 replays, CUDA events, max over ranks",
+           "parity": "rel_l2 of each rank's output against the unsharded single-GPU rtd_qlinear (f32 out)"}
+    for name, t, n, k in (("attn_output", Q4_K, HIDDEN, HIDDEN), ("ffn_down", Q6_K, HIDDEN, FFN)):
+        raw = synth.quant_matrix(t, n, k, seed=77, stream=t)
+        full = QMatMul(t, raw, n, k, device=dev)
+        rpl = RowParallelLinear.from_full_weight(raw, t, n, k, None, rank, world, comm=comm, device=dev)
+        del raw
+        ks = k // world
+        res = {"shape_nk": [n, k], "format": "Q4_K" if t == Q4_K else "Q6_K", "k_shard": ks}
+        for m in (1, 64):
+            xf = torch.from_numpy(synth.activations(m, k, seed=9)).to(torch.bfloat16).to(dev)
+            xs = xf[:, rank * ks:(rank + 1) * ks].contiguous()
+            want = full.forward(xf, out_dtype=torch.float32).double()
+            row = {}
+            for path, fn in (("fused", rpl.forward), ("ar", rpl.forward_ar), ("nccl", rpl.forward_nccl)):
+                got = fn(xs.float()).double()
+                torch.cuda.synchronize(dev)
+                rel = float(torch.linalg.norm(got - want) / torch.linalg.norm(want))
+                rel = _max_over_ranks(rel, dev, world)
+                for _ in range(3):
+                    fn(xs)
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(reps):
+                        fn(xs)
                 g.replay()
-            b.record(stream)
-            torch.cuda.synchronize(dev)
-            del g  # graphs holding NCCL work go before the process group
-            ms = torch.tensor([a.elapsed_time(b) / (5 * reps)], dtype=torch.float64, device=dev)
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-            res[name] = float(ms.item()) * 1e3
-        shard_bytes = n * (k // world // 256) * 210
-        out[f"m{m}"] = {"fused_us": res["fused"], "nccl_us": res["nccl"],
-                        "fused_shard_gbs": shard_bytes / (res["fused"] * 1e-6) / 1e9}
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                s = _max_over_ranks(_time_graph(g, stream, dev, 5) / reps, dev, world)
+                del g  # graphs holding NCCL work go before the process group
+                row[path] = {"us": round(s * 1e6, 2), "rel_l2": rel}
+            row["shard_gbs_fused"] = round(weight_bytes(t, n, ks) / (row["fused"]["us"] * 1e-6) / 1e9, 1)
+            res[f"m{m}"] = row
+        out[name] = res
+        del full, rpl
     torch.cuda.synchronize(dev)
     dist.barrier()
     comm.close()
     return out
 
 
-def _m_sweep(dev, rank: int):
-    """The rest of the config-1 sweep's token counts at (N, K) = (14336, 4096) for every
-    format (the four M = 1 shapes are the headline step): skinny M = 4, 16, 64 in GB/s of
-    algorithmic bytes (HBM roofline) and prefill M = 512, 2048 in TFLOP/s (tensor
-    roofline against the measured bf16 burst peak).  Each point is a CUDA graph of 10
-    calls over 3 weight copies (L2 is not reused between calls), 5 replays, CUDA events."""
+# ---------------------------------------------------------------- config-1 sweeps (N = 1)
+def _gemv_sweep(dev, stream, rank, peak):
+    """The config-1 quantized-linear sweep at decode M = 1: 14 GEMVs (0.74 GB of distinct
+    weights per pass), a CUDA graph of the pass, HBM GB/s of algorithmic bytes; the roofline
+    of its longest GEMV (a graph of 24 launches over 3 weight copies)."""
+    import torch
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.weights import Fp8Weight, QMatMul
+
+    L = _lib.lib()
+    items = []
+    for name, t, n, k in sweep():
+        if t == 0:
+            w, s = synth.fp8_matrix(n, k, seed=rank, stream=k)
+            objs = [Fp8Weight(w, s, k, n, device=dev)]
+        else:
+            objs = [QMatMul(t, synth.quant_matrix(t, n, k, seed=rank, stream=k), n, k, device=dev)]
+            objs += [objs[0].to_device(dev) for _ in range(2)]
+        x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=rank, stream=n))).to(torch.bfloat16).to(dev)
+        y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+        items.append(dict(name=name, t=t, n=n, k=k, objs=objs, x=x, y=y, bytes=alg_bytes(t, n, k)))
+
+    def call(it, st, c=0):
+        o = it["objs"][c % len(it["objs"])]
+        if it["t"] == 0:
+            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, it["x"].data_ptr(), _lib.DT_BF16, it["k"], 1,
+                                  it["y"].data_ptr(), _lib.DT_BF16, it["n"], _lib.FP8_W8A16, st)
+        else:
+            rc = L.rtd_qlinear(o.ctx.handle, o.handle, it["x"].data_ptr(), _lib.DT_BF16, it["k"], 1, None,
+                               it["y"].data_ptr(), _lib.DT_BF16, it["n"], st)
+        if rc != 0:
+            raise RuntimeError(f"sweep {it['name']} {it['n']}x{it['k']}: status {rc}")
+
+    for it in items:
+        call(it, stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    g = _capture(lambda st: [call(it, st) for it in items], dev)
+    for _ in range(3):
+        g.replay()
+    s = _time_graph(g, stream, dev, 20)
+    del g
+    step_bytes = sum(it["bytes"] for it in items)
+    per = {}
+    for it in items:
+        if it["t"] == 0:
+            continue  # FP8 holds one copy: its per-call figure would re-read L2
+        gi = _capture(lambda st: [call(it, st, c) for c in range(24)], dev)
+        gi.replay()
+        per[f"{it['name']}:{it['n']}x{it['k']}"] = it["bytes"] / (_time_graph(gi, stream, dev, 5) / 24) / 1e9
+        del gi
+    key = {f"{it['name']}:{it['n']}x{it['k']}": it for it in items}
+    dom = max(per, key=lambda kk: key[kk]["bytes"] / per[kk])  # the longest GEMV
+    dit = key[dom]
+    achieved = per[dom]
+    return {"workload": "config-1 sweep at decode M=1: 14 GEMVs (Q4_K/Q6_K/Q8_0/FP8 x (4096,4096), (14336,4096), "
+                        "(4096,14336), (151936,896); K=896 Q4_K/Q6_K infeasible), bf16 activations",
+            "value_gbs": step_bytes / s / 1e9, "ms_per_pass": s * 1e3, "bytes_per_pass": step_bytes,
+            "frac_of_peak": step_bytes / s / 1e9 / peak,
+            "roofline": {"bound": "hbm", "kernel": f"qgemv_kernel, {dit['name']} {dit['n']}x{dit['k']} M=1",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": profile_traffic(f"qgemv_{dit['name'].lower()}_{dit['n']}x{dit['k']}_m1")},
+            "per_gemv_gbs": {k2: round(v, 1) for k2, v in per.items()},
+            "timing": "CUDA graph of the 14-GEMV pass (20 replays); per GEMV a graph of 24 launches over 3 "
+                      "device copies, CUDA events"}
+
+
+def _m_sweep(dev, rank, tflops_peak):
+    """The rest of the config-1 token counts at (N, K) = (14336, 4096) for every format:
+    skinny M = 4, 16, 64 in GB/s of algorithmic bytes (HBM roofline) and prefill M = 512,
+    2048 in TFLOP/s (against the measured bf16 burst peak).  Each point is a CUDA graph of
+    10 calls over 3 weight copies, 5 replays, CUDA events."""
     import torch
     from runtimed_b200 import _lib, synth
     from runtimed_b200.weights import Fp8Weight, QMatMul
 
     L = _lib.lib()
     n, k = 14336, 4096
-    tflops_peak = None
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        with open(p) as f:
-            tflops_peak = json.load(f).get("bf16_tflops")
     out = {"shape_nk": [n, k], "timing": "CUDA graph of 10 calls over 3 weight copies, 5 replays, CUDA events",
            "tflops_peak": tflops_peak, "tflops_peak_source": "MEASURED_PEAKS.json bf16_tflops (measured)"}
+    stream = torch.cuda.current_stream(dev)
     for name, t in FORMATS:
         objs = []
         for c in range(3):
             if t == 0:
                 w, sc = synth.fp8_matrix(n, k, seed=rank + 20 + c, stream=k)
                 objs.append(Fp8Weight(w, sc, k, n, device=dev))
+            elif c == 0:
+                objs.append(QMatMul(t, synth.quant_matrix(t, n, k, seed=rank + 20, stream=k), n, k, device=dev))
             else:
-                objs.append(QMatMul(t, synth.quant_matrix(t, n, k, seed=rank + 20 + c, stream=k), n, k, device=dev))
+                objs.append(objs[0].to_device(dev))
         row = {}
         for m in (4, 16, 64, 512, 2048):
             x = torch.randn(m, k, device=dev).to(torch.bfloat16)
@@ -358,23 +569,13 @@ def _m_sweep(dev, rank: int):
                     raise RuntimeError(f"m-sweep {name} M={m}: status {rc}")
 
             for o in objs:
-                call(o, torch.cuda.current_stream(dev).cuda_stream)
+                call(o, stream.cuda_stream)
             torch.cuda.synchronize(dev)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for r in range(10):
-                    call(objs[r % 3], torch.cuda.current_stream(dev).cuda_stream)
+            g = _capture(lambda st: [call(objs[r % 3], st) for r in range(10)], dev)
             for _ in range(2):
                 g.replay()
-            torch.cuda.synchronize(dev)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(5):
-                g.replay()
-            b.record()
-            torch.cuda.synchronize(dev)
+            us = _time_graph(g, stream, dev, 5) * 1e6 / 10
             del g
-            us = a.elapsed_time(b) * 1e3 / 50
             if m <= 64:
                 gbs = (weight_bytes(t, n, k) + m * k * 2 + m * n * 2) / (us * 1e-6) / 1e9
                 row[f"m{m}"] = {"us": round(us, 2), "gbs": round(gbs, 1)}
@@ -387,45 +588,10 @@ def _m_sweep(dev, rank: int):
     return out
 
 
-def _dominant_launch_ms(it, call, stream, dev, rank, reps: int = 24) -> float:
-    import torch
-    from runtimed_b200 import synth
-    from runtimed_b200.weights import Fp8Weight, QMatMul
-
-    t, n, k = it["t"], it["n"], it["k"]
-    copies = [it]
-    for c in range(2):
-        if t == 0:
-            w, s = synth.fp8_matrix(n, k, seed=rank + 10 + c, stream=k)
-            obj = Fp8Weight(w, s, k, n, device=dev)
-        else:
-            obj = QMatMul(t, synth.quant_matrix(t, n, k, seed=rank + 10 + c, stream=k), n, k, device=dev)
-        copies.append(dict(it, obj=obj))
-    for cp in copies:
-        call(cp)
-    torch.cuda.synchronize(dev)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for r in range(reps):
-            call(copies[r % 3], st=torch.cuda.current_stream(dev))
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize(dev)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(5):
-        g.replay()
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    del g
-    return a.elapsed_time(b) / (5 * reps)
-
-
 def profile_one(spec: str, calls: int) -> int:
     """Run `calls` bf16 calls of one linear (FMT:N:K, or FMT:N:K:M for M tokens; M = 1 by
-    default), or of every sweep GEMV in step order ("sweep"), eagerly, and exit: the
-    target of the ncu captures summarised under profiles/ (the bench's own step is a
-    CUDA graph, which ncu reports as one result)."""
+    default), or of every config-1 sweep GEMV in order ("sweep"), eagerly, and exit: the
+    target of the ncu captures summarised under profiles/."""
     import torch
     from runtimed_b200 import _lib, synth
     from runtimed_b200.weights import Fp8Weight, QMatMul
@@ -462,7 +628,7 @@ def profile_one(spec: str, calls: int) -> int:
             if rc != 0:
                 raise RuntimeError(f"status {rc}")
     torch.cuda.synchronize(dev)
-    print(f"profile-one {spec}: {calls} calls of {len(items)} GEMVs ok")
+    print(f"profile-one {spec}: {calls} calls of {len(items)} linears ok")
     return 0
 
 
@@ -473,7 +639,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep",
-                    help="only run a few eager calls of one sweep GEMV or of the whole sweep (ncu target), "
+                    help="only run a few eager calls of one linear or of the config-1 sweep (ncu target), "
                          "no JSON line")
     ap.add_argument("--calls", type=int, default=4)
     args = ap.parse_args()
@@ -494,142 +660,97 @@ def main() -> int:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
-    from runtimed_b200 import _lib, synth
-    from runtimed_b200.weights import Fp8Weight, QMatMul
+    from runtimed_b200 import _lib
+    from runtimed_b200.tp import TpComm
+    from runtimed_b200.weights import Context
 
     L = _lib.lib()
     stream = torch.cuda.current_stream(dev)
-    items = []
-    for name, t, n, k in sweep():
-        if t == 0:
-            w, s = synth.fp8_matrix(n, k, seed=rank, stream=k)
-            obj = Fp8Weight(w, s, k, n, device=dev)
-        else:
-            obj = QMatMul(t, synth.quant_matrix(t, n, k, seed=rank, stream=k), n, k, device=dev)
-        x = synth.bf16_round(synth.activations(1, k, seed=rank, stream=n))
-        xd = torch.from_numpy(x).to(torch.bfloat16).to(dev)
-        yd = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
-        items.append(dict(name=name, t=t, n=n, k=k, obj=obj, x=xd, y=yd, bytes=alg_bytes(t, n, k)))
-    step_bytes = sum(it["bytes"] for it in items)
+    peak, peak_kind, tflops_peak = read_peaks()
+    comm = TpComm(Context.for_device(dev), rank, world, max_n=HIDDEN) if world > 1 else None
+    stack = TpStack(rank, world, dev, comm, batches=(BATCH, 1))
+    w_bytes = step_weight_bytes(world)
 
-    def call(it, x=None, y=None, st=None):
-        x = it["x"] if x is None else x
-        y = it["y"] if y is None else y
-        s = (stream if st is None else st).cuda_stream
-        o = it["obj"]
-        if it["t"] == 0:
-            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, it["k"], 1, y.data_ptr(),
-                                  _lib.DT_BF16, it["n"], _lib.FP8_W8A16, s)
-        else:
-            rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, it["k"], 1, None, y.data_ptr(),
-                               _lib.DT_BF16, it["n"], s)
-        if rc != 0:
-            raise RuntimeError(f"{it['name']} {it['n']}x{it['k']}: status {rc}: {L.rtd_last_error(o.ctx.handle)}")
-
-    for it in items:  # first calls configure kernel attributes outside capture
-        call(it)
+    for b in (BATCH, 1):  # first calls configure kernel attributes outside capture
+        stack.step(b, stream.cuda_stream, layers=stack.layers[:1])
     torch.cuda.synchronize(dev)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for it in items:
-            call(it, st=torch.cuda.current_stream(dev))
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-
-    # ---- timed region (device time, CUDA events, max over ranks)
     if world > 1:
         dist.barrier()
+    n0 = L.rtd_kernel_launches()
+    g64 = _capture(lambda st: stack.step(BATCH, st), dev)
+    launches_per_step = L.rtd_kernel_launches() - n0
+    g1 = _capture(lambda st: stack.step(1, st), dev)
+    for _ in range(max(args.warmup, 3)):
+        g64.replay()
+        g1.replay()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # nvidia-smi samples every 200 ms: the timed K steps sit inside a window of the same
-    # load (an untimed pre-roll of about a second and a short post-roll), so the clock
-    # samples are taken while the GPU runs exactly this work.
-    step_s = max(1e-5, _time_steps(graph, stream, dev, 5) / 5)
+
+    # ---- timed region (device time, CUDA events, max over ranks).  nvidia-smi samples
+    # every 200 ms: the timed steps sit inside a window of the same load (an untimed
+    # pre-roll of about a second and a short post-roll).
+    if world > 1:
+        dist.barrier()
+    step_s = max(1e-5, _time_graph(g64, stream, dev, 2))
     roll = max(1, int(1.0 / step_s))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         clk.wait_first_sample()
         for _ in range(roll):
-            graph.replay()
+            g64.replay()
         e0.record(stream)
         for _ in range(args.steps):
-            graph.replay()
+            g64.replay()
         e1.record(stream)
-        for _ in range(roll // 2):
-            graph.replay()
+        for _ in range(max(1, roll // 2)):
+            g64.replay()
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    ms = e0.elapsed_time(e1)
-    t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
+    ms_max = _max_over_ranks(e0.elapsed_time(e1), dev, world)
+    value = BATCH * args.steps / (ms_max * 1e-3)
     if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    ms_max = float(t_max.item())
-    value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+        dist.barrier()
+    s1 = _max_over_ranks(_time_graph(g1, stream, dev, max(5, args.steps // 2)), dev, world)
 
-    # ---- per-GEMV device time (each call preceded by a sleep so only GPU time is measured)
-    reps = 5
-    per = {i: [] for i in range(len(items))}
-    for _ in range(reps):
-        for i, it in enumerate(items):
-            torch.cuda._sleep(200_000)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            call(it)
-            b.record(stream)
-            per[i].append((a, b))
-    torch.cuda.synchronize(dev)
-    per_ms = {i: statistics.mean(a.elapsed_time(b) for a, b in v) for i, v in per.items()}
-    dom = max(per_ms, key=lambda i: per_ms[i])
-    dit = items[dom]
-    peak, peak_kind = read_peaks()
-    # roofline kernel: its average launch duration back to back, as inside the step --
-    # a graph of R launches rotating over 3 weight copies (no launch re-reads L2)
-    launch_ms = _dominant_launch_ms(dit, call, stream, dev, rank)
-    achieved = dit["bytes"] / (launch_ms * 1e-3) / 1e9
-    tag = f"qgemv_{dit['name'].lower()}_{dit['n']}x{dit['k']}_m1"
-    traffic = profile_traffic(tag)
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": f"qgemv_kernel, {dit['name']} {dit['n']}x{dit['k']} M=1",
-                "launch_us": launch_ms * 1e3,
-                "duration_source": "CUDA events around a graph of 24 back-to-back launches over 3 weight copies",
+    # ---- roofline: the step's dominant kernel and the whole step
+    per64 = _per_linear(stack, BATCH, stream, dev, world)
+    per1 = _per_linear(stack, 1, stream, dev, world)
+    dom = max(per64, key=lambda n: per64[n]["us"])
+    d = per64[dom]
+    dt = dict((n, t) for n, t, *_ in LAYER_LINEARS)[dom]
+    fmt = {Q4_K: "q4k", Q6_K: "q6k"}[dt]
+    step_gbs = w_bytes / (ms_max * 1e-3 / args.steps) / 1e9
+    roofline = {"bound": "hbm", "achieved": d["gbs"], "peak": peak, "unit": "GB/s", "frac": d["gbs"] / peak,
+                "traffic": profile_traffic(f"qgemm_{fmt}_{d['shard_nk'][0]}x{d['shard_nk'][1]}_m{BATCH}"),
+                "kernel": f"{dom} (rank shard {d['shard_nk'][0]}x{d['shard_nk'][1]}, M={BATCH}): "
+                          f"tensor-core GEMM (qgemm_kernel) and its prep",
+                "launch_us": d["us"], "duration_source": "CUDA events around a graph of 24 back-to-back calls over "
+                                                         "3 layers' weight copies",
                 "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                "per_gemv_gbs": {f"{it['name']}:{it['n']}x{it['k']}": round(it["bytes"] / (per_ms[i] * 1e-3) / 1e9, 1)
-                                 for i, it in enumerate(items)}}
+                "step": {"weight_bytes_per_rank": w_bytes, "gbs": step_gbs, "frac": step_gbs / peak},
+                "per_linear_b64": {n: {"us": round(v["us"], 2), "gbs": round(v["gbs"], 1)} for n, v in per64.items()},
+                "per_linear_b1": {n: {"us": round(v["us"], 2), "gbs": round(v["gbs"], 1)} for n, v in per1.items()}}
 
-    # ---- end to end through the C ABI: every step copies its 14 activation rows from
-    # pinned host memory (one copy into one device buffer), runs the 14 calls on them,
-    # and reads the 14 outputs back into pinned host memory (one copy), then waits for it
-    xoff, yoff, xo, yo = [], [], 0, 0
-    for it in items:
-        xoff.append(xo)
-        yoff.append(yo)
-        xo += it["k"]
-        yo += it["n"]
-    hx = torch.empty(xo, dtype=torch.bfloat16).pin_memory()
-    hy = torch.empty(yo, dtype=torch.bfloat16).pin_memory()
-    dx = torch.empty(xo, dtype=torch.bfloat16, device=dev)
-    dy = torch.empty(yo, dtype=torch.bfloat16, device=dev)
-    for i, it in enumerate(items):
-        hx[xoff[i]:xoff[i] + it["k"]].copy_(it["x"].reshape(-1).cpu())
-    xs = [dx[xoff[i]:xoff[i] + it["k"]] for i, it in enumerate(items)]
-    ys = [dy[yoff[i]:yoff[i] + it["n"]] for i, it in enumerate(items)]
+    # ---- end to end through the public API: every step copies the 64 hidden states in
+    # from pinned host memory, replays the step, and reads the last layer's outputs back
+    B = stack.bufs[BATCH]
+    hx = torch.empty(B["x"].shape, dtype=torch.bfloat16).pin_memory()
+    hx.copy_(B["x"].cpu())
+    hy = torch.empty(B["d"].shape, dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, args.steps // 2)
-    h2d = xo * 2
-    d2h = yo * 2
 
     def e2e_step():
-        dx.copy_(hx, non_blocking=True)
-        for i, it in enumerate(items):
-            call(it, x=xs[i], y=ys[i])
-        hy.copy_(dy, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        B["x"].copy_(hx, non_blocking=True)
+        g64.replay()
+        hy.copy_(B["d"], non_blocking=True)
+        stream.synchronize()
 
     for _ in range(2):
         e2e_step()
-    torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -638,27 +759,29 @@ def main() -> int:
         e2e_step()
     b.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_val = world * step_bytes * e2e_steps / (float(e2e_ms.item()) * 1e-3) / 1e9
-    # the outputs read back are the step's results: check one against the device copy
-    if not torch.equal(hy[:items[0]["n"]].to(dev), dy[:items[0]["n"]]):
+    e2e_ms = _max_over_ranks(a.elapsed_time(b), dev, world)
+    e2e_val = BATCH * e2e_steps / (e2e_ms * 1e-3)
+    if not torch.equal(hy.to(dev), B["d"]):
         raise RuntimeError("e2e: host copy of the outputs differs from the device")
+    del g64, g1
 
     tp = None
     if world > 1:
-        # the TP comparison runs after the headline is measured; a failure there is
-        # reported in its own object instead of losing the line (a rank that fails
-        # alone leaves the others to the process group's 120 s timeout)
+        # measured after the headline; a failure is reported in its own object (every
+        # rank runs the same steps, so a failure is seen by all of them)
         try:
             tp = _tp_rowparallel(world, rank, dev, stream)
         except Exception as e:  # noqa: BLE001 - reported in the JSON line
             tp = {"error": f"{type(e).__name__}: {e}"}
             torch.cuda.synchronize(dev)
-    msweep = _m_sweep(dev, rank) if world == 1 else None
+    del stack
+    gemv = _gemv_sweep(dev, stream, rank, peak) if world == 1 else None
+    msweep = _m_sweep(dev, rank, tflops_peak) if world == 1 else None
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
-    del graph
+    if comm is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -666,16 +789,19 @@ def main() -> int:
         return 0
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 tensor-core products of exact weight codes, f32 accumulate",
-            "data": "synthetic", "config": config_dict(), "roofline": roofline,
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "rtd_qlinear / rtd_fp8_linear per GEMV, eager; per step one pinned-host copy of the 14 "
-                            "activation rows in and one of the 14 outputs out, then a host wait"},
-            "gpu_launches": sum(launches_per_gemv(it["t"], it["n"], it["k"]) for it in items) * args.steps,
-            "tp": tp,
-            "m_sweep": msweep,
-            "clocks": clk.summary()}
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 activations; f16 tensor-core products of the decoded weights, f32 accumulate",
+            "data": "synthetic (seeded random-init weights and hidden states)", "config": config_dict(world),
+            "decode_b1": {"tokens_per_s": 1.0 / s1, "ms_per_step": s1 * 1e3,
+                          "gbs": w_bytes / s1 / 1e9, "frac": w_bytes / s1 / 1e9 / peak},
+            "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(hx.numel() * 2),
+                    "d2h_bytes_per_step": int(hy.numel() * 2),
+                    "path": "per step: pinned-host copy of the 64 hidden states in, replay of the step's CUDA graph "
+                            "of C-ABI calls, pinned-host copy of the last layer's outputs out, host wait"},
+            "gpu_launches": int(launches_per_step) * args.steps,
+            "launches_per_step": int(launches_per_step),
+            "tp": tp, "gemv_sweep": gemv, "m_sweep": msweep, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -1,6 +1,6 @@
 """Host-side pieces of bench.py that shape its JSON line, checked on the CPU: the
-config-1 sweep, the algorithmic bytes, the launch count it claims, and the ncu traffic
-figure it reads from profiles/ for the roofline kernel."""
+config-3 step's shards and bytes, the config-1 sweep, the algorithmic bytes, and the ncu
+traffic figure it reads from profiles/ for a roofline kernel."""
 import bench
 
 
@@ -18,13 +18,18 @@ def test_algorithmic_bytes():
     assert bench.weight_bytes(0, 4096, 4096) == 4096 * 4096 + 4 * 4096
 
 
-def test_launch_count_rule():
-    # split-mode launches stage activations in a prep kernel; the two LM-head GEMVs run
-    # in whole mode and stage in-kernel
-    per = {(n, k): bench.launches_per_gemv(t, n, k) for _, t, n, k in bench.sweep()}
-    assert per[(151936, 896)] == 1
-    assert all(v == 2 for (n, _), v in per.items() if n != 151936)
-    assert sum(bench.launches_per_gemv(t, n, k) for _, t, n, k in bench.sweep()) == 26
+def test_config3_step_bytes_and_shards():
+    # one layer at Q4_K_M-style formats: q, k, o, gate, up Q4_K; v, down Q6_K
+    layer = (8192 * 8192 + 1024 * 8192 + 8192 * 8192 + 2 * 28672 * 8192) * 144 // 256 \
+        + (1024 * 8192 + 8192 * 28672) * 210 // 256
+    assert bench.step_weight_bytes(1) == 80 * layer
+    assert abs(bench.step_weight_bytes(1) / 1e9 - 43.52) < 0.01
+    for world in (2, 4, 8):
+        # column shards split N, row shards split K on superblock boundaries
+        for _, t, n, k, sp, _ in bench.LAYER_LINEARS:
+            ns, ks = bench.shard_shape(n, k, sp, world)
+            assert ns * ks * world == n * k and ks % 256 == 0
+        assert bench.step_weight_bytes(world) * world == bench.step_weight_bytes(1)
 
 
 def test_roofline_traffic_from_profiles():
