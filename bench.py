@@ -26,7 +26,9 @@ on the host cores, scaled to the step), the SM clocks of the timed window, and:
               unsharded single-GPU result (rel_l2);
   gemv_sweep  N = 1: the config-1 quantized-linear sweep at decode M = 1 (14 GEMVs, HBM
               GB/s of algorithmic bytes) with the roofline of its longest GEMV;
-  m_sweep     N = 1: the config-1 token counts M = 4..2048 at (14336, 4096).
+  m_sweep     N = 1: the config-1 token counts M = 4..2048 at (14336, 4096);
+  model_decode  N = 1: config 0 end to end (GGUF load, 128-token prompt, greedy decode
+              steps as a CUDA graph) in tokens/s, beside the restated reference forward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     python bench.py --profile-one FMT:N:K[:M] | sweep   (ncu target, no JSON line)
@@ -588,6 +590,61 @@ def _m_sweep(dev, rank, tflops_peak):
     return out
 
 
+def _model_decode(dev, steps: int = 128, warm: int = 8):
+    """Config 0 end to end (Qwen2-0.5B-shaped, written as a GGUF and
+    loaded through the library): batch 1, 128 prompt ids, then `steps` greedy tokens
+    with the decode step captured as one CUDA graph (token and position on the device,
+    the argmax feeding the next replay), f16 paged KV cache.  Device time of the timed
+    replays (CUDA events), after `warm` untimed ones; the restated reference forward
+    (oracle/qwen2_ref.py, numpy f32 on the host cores) times a few decode steps beside it."""
+    import tempfile
+
+    import torch
+    from runtimed_b200 import fixtures
+    from runtimed_b200.qwen2 import Qwen2Model
+
+    shape = fixtures.CONFIGS["config0"]
+    with tempfile.TemporaryDirectory(prefix="rtd_bench_") as d:
+        path = os.path.join(d, "config0.gguf")
+        fixtures.write_qwen2_gguf(path, shape, seed=0)
+        prompt = list(np.random.default_rng(0).integers(0, shape.vocab, 128))
+        model = Qwen2Model(path, device=dev, max_ctx=len(prompt) + steps + warm + 16)
+        out, g, replay = model.greedy_graph(prompt, steps + warm)
+        for _ in range(warm):
+            replay()
+        torch.cuda.synchronize(dev)
+        stream = torch.cuda.current_stream(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        s = a.elapsed_time(b) * 1e-3 / steps
+        ids = [int(v) for v in out[:8].cpu()]
+        del g, model
+        torch.cuda.empty_cache()
+        # the restated reference forward on the host cores: a few decode steps
+        from oracle.qwen2_ref import RefQwen2
+
+        ref = RefQwen2(path)
+        logits = ref.forward(prompt, 0)[-1]
+        tok, pos, n_cpu = int(np.argmax(logits)), len(prompt), 4
+        t0 = time.perf_counter()
+        for _ in range(n_cpu):
+            logits = ref.forward([tok], pos)[-1]
+            tok, pos = int(np.argmax(logits)), pos + 1
+        cpu_s = (time.perf_counter() - t0) / n_cpu
+    weights = sum(weight_bytes(fixtures.tensor_format(shape, kind, k), n, k)
+                  for kind, n, k in fixtures.layer_tensors(shape)) * shape.n_layer + weight_bytes(8, shape.vocab, shape.hidden)
+    return {"workload": "config0: Qwen2-0.5B-shaped GGUF (Q8_0 / Q6_K), batch 1, 128-token prompt, greedy decode, "
+                        "f16 paged KV cache, decode step captured as a CUDA graph",
+            "tokens_per_s": 1.0 / s, "ms_per_token": s * 1e3, "timed_steps": steps, "warm_steps": warm,
+            "weight_bytes_per_token": weights, "gbs": weights / s / 1e9, "first_ids": ids,
+            "cpu_reference_tokens_per_s": 1.0 / cpu_s, "cpu_reference": f"oracle/qwen2_ref.py (numpy f32, "
+                                                                         f"{os.cpu_count()} host threads), {n_cpu} steps"}
+
+
 def profile_one(spec: str, calls: int) -> int:
     """Run `calls` bf16 calls of one linear (FMT:N:K, or FMT:N:K:M for M tokens; M = 1 by
     default), or of every config-1 sweep GEMV in order ("sweep"), eagerly, and exit: the
@@ -776,6 +833,10 @@ def main() -> int:
             torch.cuda.synchronize(dev)
     del stack
     gemv = _gemv_sweep(dev, stream, rank, peak) if world == 1 else None
+    try:
+        model = _model_decode(dev) if world == 1 else None
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        model = {"error": f"{type(e).__name__}: {e}"}
     msweep = _m_sweep(dev, rank, tflops_peak) if world == 1 else None
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
     if comm is not None:
@@ -801,7 +862,7 @@ def main() -> int:
                             "of C-ABI calls, pinned-host copy of the last layer's outputs out, host wait"},
             "gpu_launches": int(launches_per_step) * args.steps,
             "launches_per_step": int(launches_per_step),
-            "tp": tp, "gemv_sweep": gemv, "m_sweep": msweep, "clocks": clk.summary()}
+            "tp": tp, "gemv_sweep": gemv, "m_sweep": msweep, "model_decode": model, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
 

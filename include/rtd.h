@@ -141,7 +141,8 @@ rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out,
 /* ---- decoder-layer operations ------------------------------------------------
  * The SubstratePort operations between the linears of a decoder layer
  * (crates/runtimed-model/src/substrate/port.rs:14-90), on device buffers.  The KV cache
- * is PAGED: k_cache / v_cache are f16 [blocks][n_kv][16][head_dim]; block_table is
+ * is PAGED: k_cache / v_cache are [blocks][n_kv][16][head_dim] of kv_dtype
+ * (RTD_DT_F16, or RTD_DT_F32 for the reference's f32 cache precision); block_table is
  * int32 [sequences][max_blocks] (block ids per 16-token span of a sequence); every
  * token of a call carries its own sequence (tok_seq) and position (tok_pos), int32 on
  * the device, so one call serves a prefill chunk, a batched decode step or a verify of
@@ -160,15 +161,16 @@ rtd_status rtd_rmsnorm(rtd_ctx* ctx, float* h, int64_t ldh, const void* delta, u
 rtd_status rtd_rope_kv_append(rtd_ctx* ctx, const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
                               int64_t ldv, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t rot_dim,
                               float theta, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
-                              int32_t max_blocks, void* k_cache, void* v_cache, float* q_out, void* stream);
+                              int32_t max_blocks, void* k_cache, void* v_cache, uint32_t kv_dtype, float* q_out,
+                              void* stream);
 /* o[T, n_head * head_dim] = softmax(q k^T * scale + causal mask) v with GQA, over keys
  * [0, tok_pos[t]] of each token's sequence: SubstratePort::attention + causal_mask
  * (crates/runtimed-model/src/ops/attention.rs:38-58,107-128).  max_ctx bounds
  * tok_pos + 1 (it sizes the split of long contexts across CTAs). */
 rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim,
                                float scale, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
-                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache, void* o,
-                               uint32_t o_dtype, int64_t ldo, void* stream);
+                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache,
+                               uint32_t kv_dtype, void* o, uint32_t o_dtype, int64_t ldo, void* stream);
 /* y[i] = silu(gate[i]) * up[i]: SubstratePort::silu + broadcast_mul
  * (crates/runtimed-model/src/ops/activation.rs:6-10, arch/qwen2.rs:120-123). */
 rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, const void* up, uint32_t up_dtype,

@@ -58,8 +58,12 @@ def _silu(x: np.ndarray) -> np.ndarray:
 class RefQwen2:
     """The restated forward over one GGUF file; ``forward(ids, q0)`` -> logits [t, vocab]."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, kv_f16: bool = False):
+        """kv_f16 rounds the cached keys and values to f16, as the GPU's cache stores them
+        (a diagnostic knob: the reference's CPU cache is f32)."""
         import gguf
+
+        self.kv_f16 = kv_f16
 
         r = gguf.GGUFReader(path)
         meta = {f.name: f for f in r.fields.values()}
@@ -115,6 +119,8 @@ class RefQwen2:
         pos = np.arange(q0, q0 + t)
         q = _rope(q, pos, self.theta, hd)
         k = _rope(k, pos, self.theta, hd)
+        if self.kv_f16:
+            k, v = k.astype(np.float16).astype(F32), v.astype(np.float16).astype(F32)
         self.k_cache[i] = np.concatenate([self.k_cache[i], k], axis=1)
         self.v_cache[i] = np.concatenate([self.v_cache[i], v], axis=1)
         K = np.repeat(self.k_cache[i], G, axis=0)  # head h -> kv head h // G
@@ -134,11 +140,14 @@ class RefQwen2:
         u = self._lin(n, f"{p}.ffn_up.weight")
         return (h + self._lin(_silu(g) * u, f"{p}.ffn_down.weight")).astype(F32)
 
-    def forward(self, ids, q0: int) -> np.ndarray:
-        """Logits [t, vocab] of ids at positions q0 .. q0 + t - 1 (qwen2.rs:217-229)."""
+    def forward(self, ids, q0: int, trace=None) -> np.ndarray:
+        """Logits [t, vocab] of ids at positions q0 .. q0 + t - 1 (qwen2.rs:217-229);
+        `trace` (a list) receives the residual stream after every layer."""
         h = self.w["token_embd.weight"][np.asarray(ids, dtype=np.int64)].astype(F32)
         for i in range(self.n_layer):
             h = self._layer(i, h, q0)
+            if trace is not None:
+                trace.append(h.copy())
         h = _rmsnorm(h, self.w["output_norm.weight"], self.eps)
         return self._lin(h, "output.weight")
 

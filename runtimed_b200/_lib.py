@@ -57,9 +57,9 @@ SIGNATURES = {
                                  _vp]),
     "rtd_rope_kv_append": (_c.c_int32, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _c.c_int32, _c.c_int32,
                                         _c.c_int32, _c.c_int32, _c.c_float, _vp, _vp, _vp, _c.c_int32, _vp, _vp,
-                                        _vp, _vp]),
+                                        _u32, _vp, _vp]),
     "rtd_attention_paged": (_c.c_int32, [_vp, _vp, _i64, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_float, _vp, _vp,
-                                         _vp, _c.c_int32, _c.c_int32, _vp, _vp, _vp, _u32, _i64, _vp]),
+                                         _vp, _c.c_int32, _c.c_int32, _vp, _vp, _u32, _vp, _u32, _i64, _vp]),
     "rtd_silu_mul": (_c.c_int32, [_vp, _vp, _u32, _vp, _u32, _i64, _vp, _u32, _vp]),
     "rtd_argmax": (_c.c_int32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "rtd_qembed": (_c.c_int32, [_vp, _vp, _vp, _i64, _vp, _vp]),

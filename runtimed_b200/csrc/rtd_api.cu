@@ -463,7 +463,8 @@ rtd_status check_heads(rtd_ctx* ctx, int32_t n_head, int32_t n_kv, int32_t head_
 rtd_status rtd_rope_kv_append(rtd_ctx* ctx, const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
                               int64_t ldv, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t rot_dim,
                               float theta, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
-                              int32_t max_blocks, void* k_cache, void* v_cache, float* q_out, void* stream) {
+                              int32_t max_blocks, void* k_cache, void* v_cache, uint32_t kv_dtype, float* q_out,
+                              void* stream) {
   const char* who = "rtd_rope_kv_append";
   if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
   rtd_status st = check_heads(ctx, n_head, n_kv, head_dim, who);
@@ -476,16 +477,18 @@ rtd_status rtd_rope_kv_append(rtd_ctx* ctx, const float* q, int64_t ldq, const f
     return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer or no block table", who);
   if (ldq < (int64_t)n_head * head_dim || ldk < (int64_t)n_kv * head_dim || ldv < (int64_t)n_kv * head_dim)
     return fail(ctx, RTD_ERR_SHAPE, "%s: row strides below the head widths", who);
+  if (kv_dtype != RTD_DT_F16 && kv_dtype != RTD_DT_F32) return fail(ctx, RTD_ERR_INVALID, "%s: cache dtype", who);
   DeviceGuard g(ctx->device);
   cudaError_t e = rtd::launch_rope_kv(q, ldq, k, ldk, v, ldv, T, n_head, n_kv, head_dim, rot_dim, theta, tok_seq,
-                                      tok_pos, block_table, max_blocks, k_cache, v_cache, q_out, (cudaStream_t)stream);
+                                      tok_pos, block_table, max_blocks, k_cache, v_cache, kv_dtype == RTD_DT_F32 ? 1 : 0,
+                                      q_out, (cudaStream_t)stream);
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 
 rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t n_head, int32_t n_kv, int32_t head_dim,
                                float scale, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
-                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache, void* o,
-                               uint32_t o_dtype, int64_t ldo, void* stream) {
+                               int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache,
+                               uint32_t kv_dtype, void* o, uint32_t o_dtype, int64_t ldo, void* stream) {
   const char* who = "rtd_attention_paged";
   if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
   rtd_status st = check_heads(ctx, n_head, n_kv, head_dim, who);
@@ -495,6 +498,7 @@ rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t 
   if (!q || !tok_seq || !tok_pos || !block_table || !k_cache || !v_cache || !o || max_blocks <= 0)
     return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer or no block table", who);
   if (!valid_dtype(o_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (kv_dtype != RTD_DT_F16 && kv_dtype != RTD_DT_F32) return fail(ctx, RTD_ERR_INVALID, "%s: cache dtype", who);
   if (ldo < (int64_t)n_head * head_dim) return fail(ctx, RTD_ERR_SHAPE, "%s: ldo below n_head * head_dim", who);
   if (max_ctx <= 0 || max_ctx > max_blocks * 16)
     return fail(ctx, RTD_ERR_SHAPE, "%s: max_ctx %d outside the block table (%d blocks)", who, max_ctx, max_blocks);
@@ -507,7 +511,8 @@ rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t 
   }
   DeviceGuard g(ctx->device);
   cudaError_t e = rtd::launch_attention(q, T, n_head, n_kv, head_dim, scale, tok_seq, tok_pos, block_table, max_blocks,
-                                        k_cache, v_cache, o, (int)o_dtype, ldo, splits, ctx->ws, (cudaStream_t)stream);
+                                        k_cache, v_cache, kv_dtype == RTD_DT_F32 ? 1 : 0, o, (int)o_dtype, ldo, splits,
+                                        ctx->ws, (cudaStream_t)stream);
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 

@@ -29,8 +29,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <utility>
 #include <cstdint>
+#include <type_traits>
+#include <utility>
 
 #include "rtd_common.cuh"
 #include "rtd_kernels.h"
@@ -264,8 +265,9 @@ __device__ __forceinline__ void decode_half(uint32_t raw_s, int sub, uint32_t a_
     const int sh = 4 * h;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      // bytes 2j, 2j+1 -> halves 0, 1; their nibble (low or high) -> 1024 + q
-      const uint32_t p2 = prmt(wd[j >> 1], 0u, (j & 1) ? 0x4342u : 0x4140u) >> sh;
+      // bytes (0, 2) / (1, 3) of word j / 2 -> halves 0, 1 (the unit order of the staged
+      // Q4_K activations); their nibble (low or high) -> 1024 + q
+      const uint32_t p2 = prmt(wd[j >> 1], 0u, (j & 1) ? 0x4341u : 0x4240u) >> sh;
       const __half2 v = __hsub2(bits_h2((p2 & 0x000F000Fu) | 0x64006400u), k1024);
       o[j] = h2_bits(__hfma2(d1, v, n1));
     }
@@ -318,6 +320,65 @@ __device__ __forceinline__ void decode_half(uint32_t raw_s, int sub, uint32_t a_
   }
   sts128(a_s + sw_off(r, k0), o[0], o[1], o[2], o[3]);
   sts128(a_s + sw_off(r, k0 + 8), o[4], o[5], o[6], o[7]);
+}
+
+// Q4_K, two consecutive stages of one group per iteration (four or more pipeline
+// stages): thread dt decodes stage dt / 256 of the pair, row r, part p -- the 16 packed
+// bytes whose low nibbles are elements 16p .. 16p + 15 of sub-block 2c and whose high
+// nibbles are the same elements of sub-block 2c + 1 (dequant_k.rs:19-44), c = the stage
+// within the group: 32 weights from one header read.  Pairs are bytes (0, 2) and (1, 3)
+// of each word, so one LOP3 (plus a shift) makes a pair 1024 + q; the staged activations
+// of Q4_K follow the matching unit order (0, 2, 1, 3, 4, 6, 5, 7).
+struct Q4Thread {
+  uint32_t hdr;     // the row's 16 header bytes, relative to the stage's raw slot
+  uint32_t q;       // part p's 16 code bytes of chunk 0, relative to the raw slot
+  uint32_t st[4];   // swizzled store offsets of the lo / hi chunks, relative to the A tile
+};
+
+__device__ __forceinline__ Q4Thread q4_thread(int dt) {
+  const int w = dt & 255, r = 8 * (w >> 4) + (w & 7), p = (w >> 3) & 1;
+  const int i = r >> 4, rr = r & 15, g = rr & 7, hrow = rr >> 3;
+  Q4Thread t;
+  t.hdr = (uint32_t)(i * GemmFmt<FMT_Q4K>::GB + 16 * rr);
+  t.q = (uint32_t)(i * GemmFmt<FMT_Q4K>::GB + 256 + (2 * hrow + p) * 512 + (4 * g) * 16);
+  t.st[0] = sw_off(r, 16 * p);
+  t.st[1] = sw_off(r, 16 * p + 8);
+  t.st[2] = sw_off(r, 32 + 16 * p);
+  t.st[3] = sw_off(r, 32 + 16 * p + 8);
+  return t;
+}
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t c, int) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ void decode_q4k_pair(uint32_t raw_s, int sub, uint32_t a_s, const Q4Thread& t) {
+  const uint4 hdr = lds128(raw_s + t.hdr);
+  const float d = hbits(hdr.x & 0xFFFFu), dmin = hbits(hdr.x >> 16);
+  uint32_t sc0, m0, sc1, m1;
+  scale_min_words(2 * sub, hdr.y, hdr.z, hdr.w, sc0, m0);
+  scale_min_words(2 * sub + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
+  const __half2 dl = h2_const(d * (float)sc0), nl = h2_const(-(dmin * (float)m0));
+  const __half2 dh = h2_const(d * (float)sc1), nh = h2_const(-(dmin * (float)m1));
+  const __half2 k1024 = h2_const(1024.0f);
+  const uint4 q = lds128(raw_s + t.q + 16u * (uint32_t)sub);
+  const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+  constexpr uint32_t M = 0x000F000Fu, C = 0x64006400u;
+  uint32_t lo[8], hi[8];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t x = wd[w], x4 = x >> 4, x8 = x >> 8, x12 = x >> 12;
+    lo[2 * w] = h2_bits(__hfma2(dl, __hsub2(bits_h2(lop_and_or(x, M, C, 0)), k1024), nl));
+    lo[2 * w + 1] = h2_bits(__hfma2(dl, __hsub2(bits_h2(lop_and_or(x8, M, C, 0)), k1024), nl));
+    hi[2 * w] = h2_bits(__hfma2(dh, __hsub2(bits_h2(lop_and_or(x4, M, C, 0)), k1024), nh));
+    hi[2 * w + 1] = h2_bits(__hfma2(dh, __hsub2(bits_h2(lop_and_or(x12, M, C, 0)), k1024), nh));
+  }
+  sts128(a_s + t.st[0], lo[0], lo[1], lo[2], lo[3]);
+  sts128(a_s + t.st[1], lo[4], lo[5], lo[6], lo[7]);
+  sts128(a_s + t.st[2], hi[0], hi[1], hi[2], hi[3]);
+  sts128(a_s + t.st[3], hi[4], hi[5], hi[6], hi[7]);
 }
 
 // Thread dt of the decode warps: with 16 warps it decodes one 16-weight half of a row
@@ -493,6 +554,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
     // ---- decode warps 2..17 (and, afterwards, warps 4..7 run the epilogue)
     // (the warp counts follow kDecodeWarps; 16 is the built configuration)
     const int dt = tid - 64;
+    const Q4Thread q4t = q4_thread(dt);  // used by the two-stage Q4_K decoder only
     // With four or more stages the warps decode two consecutive stages per iteration
     // (always within one group: SPG is 2 or 4 and kb is even), so the waits, the proxy
     // fence and the arrivals are paid once per pair and the two decodes overlap.
@@ -506,11 +568,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         if (ok && k2 >= kStages) ok = wait(&st_empty[st], (uint32_t)((k2 / kStages - 1) & 1));
       }
       if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the arrivals below are per warp
+      if constexpr (FMT == FMT_Q4K && KPI == 2 && kDecodeThreads == 512) {
+        const int k2 = kb + (dt >> 8), s = k2 / SPG;
+        decode_q4k_pair(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
+                        smem_u32(sm + L::offA + (k2 % kStages) * L::kA), q4t);
+      } else {
 #pragma unroll
-      for (int u = 0; u < KPI; ++u) {
-        const int k2 = kb + u, s = k2 / SPG;
-        decode_stage<FMT>(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
-                          smem_u32(sm + L::offA + (k2 % kStages) * L::kA), dt);
+        for (int u = 0; u < KPI; ++u) {
+          const int k2 = kb + u, s = k2 / SPG;
+          decode_stage<FMT>(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
+                            smem_u32(sm + L::offA + (k2 % kStages) * L::kA), dt);
+        }
       }
       fence_async_shared();  // every writer: the tensor cores read A through the async proxy
       __syncwarp();
@@ -639,7 +707,7 @@ __device__ __forceinline__ void prep_values(const PrepUnit<XDT>& u, float (&v)[8
   }
 }
 
-template <int XDT, bool W8A8>
+template <int XDT, bool W8A8, bool Q4PERM>
 __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x, int64_t ldx, int64_t M, int64_t Mp,
                                                                   int64_t K, int64_t kp, bool vec, __half* xw,
                                                                   float* tscale) {
@@ -696,8 +764,12 @@ __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x,
     const int64_t kb = u / 8, kc = u % 8;
     uint8_t* dst = reinterpret_cast<uint8_t*>(xw) + ((size_t)kb * (Mp / 8) + (size_t)tg) * 1024 + (size_t)r * 128 +
                    (size_t)((kc ^ r) & 7) * 16;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_f16x2(v[0] * inv, v[1] * inv), pack_f16x2(v[2] * inv, v[3] * inv),
-                                                pack_f16x2(v[4] * inv, v[5] * inv), pack_f16x2(v[6] * inv, v[7] * inv));
+    if constexpr (Q4PERM)  // Q4_K's decoder pairs elements (0, 2), (1, 3), (4, 6), (5, 7)
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_f16x2(v[0] * inv, v[2] * inv), pack_f16x2(v[1] * inv, v[3] * inv),
+                                                  pack_f16x2(v[4] * inv, v[6] * inv), pack_f16x2(v[5] * inv, v[7] * inv));
+    else
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_f16x2(v[0] * inv, v[1] * inv), pack_f16x2(v[2] * inv, v[3] * inv),
+                                                  pack_f16x2(v[4] * inv, v[5] * inv), pack_f16x2(v[6] * inv, v[7] * inv));
   };
 #pragma unroll
   for (int j = 0; j < U::kUnits; ++j)
@@ -883,20 +955,21 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   const bool vec = (reinterpret_cast<uintptr_t>(c.x) % 16 == 0) && ((c.ldx * es) % 16 == 0);
   const dim3 pg((unsigned)Mp), pb(kPrepThreadsG);
   cudaError_t e;
-  if (c.w8a8) {
-    if (c.x_dtype == 0)
-      e = launch_pdl(gemm_prep_kernel<0, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
-    else if (c.x_dtype == 1)
-      e = launch_pdl(gemm_prep_kernel<1, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
-    else
-      e = launch_pdl(gemm_prep_kernel<2, true>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+  auto prep = [&](auto xdt, auto w8a8, auto perm) {
+    return launch_pdl(gemm_prep_kernel<decltype(xdt)::value, decltype(w8a8)::value, decltype(perm)::value>, pg, pb, 0,
+                      c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+  };
+  using T0 = std::integral_constant<int, 0>;
+  using T1 = std::integral_constant<int, 1>;
+  using T2 = std::integral_constant<int, 2>;
+  using Yes = std::true_type;
+  using No = std::false_type;
+  if (c.fmt == FMT_Q4K) {  // Q4_K takes no W8A8 (an FP8-only mode)
+    e = c.x_dtype == 0 ? prep(T0{}, No{}, Yes{}) : c.x_dtype == 1 ? prep(T1{}, No{}, Yes{}) : prep(T2{}, No{}, Yes{});
+  } else if (c.w8a8) {
+    e = c.x_dtype == 0 ? prep(T0{}, Yes{}, No{}) : c.x_dtype == 1 ? prep(T1{}, Yes{}, No{}) : prep(T2{}, Yes{}, No{});
   } else {
-    if (c.x_dtype == 0)
-      e = launch_pdl(gemm_prep_kernel<0, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
-    else if (c.x_dtype == 1)
-      e = launch_pdl(gemm_prep_kernel<1, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
-    else
-      e = launch_pdl(gemm_prep_kernel<2, false>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, vec, xw, tscale);
+    e = c.x_dtype == 0 ? prep(T0{}, No{}, No{}) : c.x_dtype == 1 ? prep(T1{}, No{}, No{}) : prep(T2{}, No{}, No{});
   }
   if (e != cudaSuccess) return e;
   GemmArgs a{};

@@ -104,12 +104,12 @@ cudaError_t launch_add_rmsnorm(float* h, int64_t ldh, const void* delta, int ddt
 cudaError_t launch_rope_kv(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                            int64_t T, int n_head, int n_kv, int head_dim, int rot_dim, float theta, const int* tok_seq,
                            const int* tok_pos, const int* block_table, int max_blocks, void* k_cache, void* v_cache,
-                           float* q_out, cudaStream_t st);
+                           int kv_f32, float* q_out, cudaStream_t st);
 size_t attn_workspace_bytes(int64_t T, int n_head, int n_kv, int head_dim, int splits);
 cudaError_t launch_attention(const float* q, int64_t T, int n_head, int n_kv, int head_dim, float scale,
                              const int* tok_seq, const int* tok_pos, const int* block_table, int max_blocks,
-                             const void* k_cache, const void* v_cache, void* o, int o_dtype, int64_t ldo, int splits,
-                             float* part, cudaStream_t st);
+                             const void* k_cache, const void* v_cache, int kv_f32, void* o, int o_dtype, int64_t ldo,
+                             int splits, float* part, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* gate, int gdt, const void* up, int udt, int64_t n, void* y, int ydt,
                             cudaStream_t st);
 cudaError_t launch_argmax(const float* x, int64_t ldx, int64_t T, int64_t V, int* out, cudaStream_t st);

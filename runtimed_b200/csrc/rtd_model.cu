@@ -103,10 +103,17 @@ struct RopeArgs {
   const int* tok_pos;
   const int* block_table;
   int max_blocks;
-  __half* k_cache;  // [blocks][n_kv][16][head_dim]
-  __half* v_cache;
+  void* k_cache;    // [blocks][n_kv][16][head_dim], f16 or f32
+  void* v_cache;
   float* q_out;     // [T][n_head][head_dim]
 };
+
+template <typename KV>
+__device__ __forceinline__ KV to_kv(float v);
+template <>
+__device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float to_kv<float>(float v) { return v; }
 
 constexpr int kKvBlock = 16;
 
@@ -115,15 +122,18 @@ __device__ __forceinline__ int64_t cache_row(const RopeArgs& a, int seq, int pos
   return (((int64_t)blk * a.n_kv + kvh) * kKvBlock + pos % kKvBlock) * a.head_dim;
 }
 
+template <typename KV>
 __global__ void rope_kv_kernel(const RopeArgs a) {
   const int t = blockIdx.x, j = blockIdx.y;
   const int seq = __ldg(a.tok_seq + t), pos = __ldg(a.tok_pos + t);
   const int half = a.rot_dim / 2;
+  KV* kc = static_cast<KV*>(a.k_cache);
+  KV* vc = static_cast<KV*>(a.v_cache);
   if (j >= a.n_head + a.n_kv) {  // value head: plain copy to the cache
     const int kvh = j - a.n_head - a.n_kv;
     const float* src = a.v + (int64_t)t * a.ldv + (int64_t)kvh * a.head_dim;
-    __half* dst = a.v_cache + cache_row(a, seq, pos, kvh);
-    for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) dst[d] = __float2half_rn(src[d]);
+    KV* dst = vc + cache_row(a, seq, pos, kvh);
+    for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) dst[d] = to_kv<KV>(src[d]);
     return;
   }
   const bool is_q = j < a.n_head;
@@ -131,7 +141,7 @@ __global__ void rope_kv_kernel(const RopeArgs a) {
   const float* src = is_q ? a.q + (int64_t)t * a.ldq + (int64_t)hh * a.head_dim
                           : a.k + (int64_t)t * a.ldk + (int64_t)hh * a.head_dim;
   float* qo = is_q ? a.q_out + ((int64_t)t * a.n_head + hh) * a.head_dim : nullptr;
-  __half* ko = is_q ? nullptr : a.k_cache + cache_row(a, seq, pos, hh);
+  KV* ko = is_q ? nullptr : kc + cache_row(a, seq, pos, hh);
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const float e = (-2.0f * (float)i) / (float)a.rot_dim;
     const float inv = powf(a.theta, e);
@@ -144,15 +154,15 @@ __global__ void rope_kv_kernel(const RopeArgs a) {
       qo[i] = o1;
       qo[i + half] = o2;
     } else {
-      ko[i] = __float2half_rn(o1);
-      ko[i + half] = __float2half_rn(o2);
+      ko[i] = to_kv<KV>(o1);
+      ko[i + half] = to_kv<KV>(o2);
     }
   }
   for (int d = a.rot_dim + threadIdx.x; d < a.head_dim; d += blockDim.x) {
     if (is_q)
       qo[d] = src[d];
     else
-      ko[d] = __float2half_rn(src[d]);
+      ko[d] = to_kv<KV>(src[d]);
   }
 }
 
@@ -176,8 +186,8 @@ struct AttnArgs {
   const int* tok_pos;
   const int* block_table;
   int max_blocks;
-  const __half* k_cache;
-  const __half* v_cache;
+  const void* k_cache;  // f16 or f32
+  const void* v_cache;
   void* o;         // [T][n_head * head_dim]
   int o_dtype;
   int64_t ldo;
@@ -185,15 +195,19 @@ struct AttnArgs {
   float* part;     // [T][n_kv][splits][G * (head_dim + 2)] when splits > 1
 };
 
+template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int t = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
-  const int G = a.n_head / a.n_kv, D = a.head_dim, KP = D + 2;  // K rows padded by 4 bytes (odd word stride)
+  const int G = a.n_head / a.n_kv, D = a.head_dim;
+  const int KP = D + 4 / (int)sizeof(KV);  // K rows padded by 4 bytes: an odd word stride, no bank conflicts
   float* sq = reinterpret_cast<float*>(smem);                    // [G][D]
   float* sp_ = sq + G * D;                                       // [G][kChunk] scores / probabilities
   float* salpha = sp_ + G * kChunk;                              // [G] rescale of this chunk
-  __half* sk = reinterpret_cast<__half*>(salpha + kMaxGroup);    // [kChunk][KP]
-  __half* sv = reinterpret_cast<__half*>(reinterpret_cast<uintptr_t>(sk + kChunk * KP + 7) & ~uintptr_t(15));  // [kChunk][D]
+  KV* sk = reinterpret_cast<KV*>(salpha + kMaxGroup);            // [kChunk][KP]
+  KV* sv = reinterpret_cast<KV*>(reinterpret_cast<uintptr_t>(sk + kChunk * KP + 15) & ~uintptr_t(15));  // [kChunk][D]
+  const KV* kcache = static_cast<const KV*>(a.k_cache);
+  const KV* vcache = static_cast<const KV*>(a.v_cache);
   const int seq = __ldg(a.tok_seq + t), pos = __ldg(a.tok_pos + t);
   const int L = pos + 1;
   const int per = (L + a.splits - 1) / a.splits;
@@ -215,19 +229,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     __syncthreads();  // the previous chunk's K / V / p are no longer read
     // stage K and V rows of the chunk (16-byte units; rows of one 16-token block are
     // contiguous in the cache)
-    const int upr = D / 8;  // 16-byte units per row
+    constexpr int EPU = 16 / sizeof(KV);  // elements per 16-byte unit
+    const int upr = D / EPU;              // 16-byte units per row
     for (int u = tid; u < nk * upr; u += kAttnThreads) {
       const int j = u / upr, c = u - j * upr;
       const int p = c0 + j;
       const int blk = __ldg(a.block_table + (int64_t)seq * a.max_blocks + p / kKvBlock);
       const int64_t row = (((int64_t)blk * a.n_kv + g) * kKvBlock + p % kKvBlock) * D;
-      const uint4 kq = __ldg(reinterpret_cast<const uint4*>(a.k_cache + row) + c);
-      uint32_t* kd = reinterpret_cast<uint32_t*>(sk + j * KP + 8 * c);
+      const uint4 kq = __ldg(reinterpret_cast<const uint4*>(kcache + row) + c);
+      uint32_t* kd = reinterpret_cast<uint32_t*>(sk + j * KP + EPU * c);
       kd[0] = kq.x;
       kd[1] = kq.y;
       kd[2] = kq.z;
       kd[3] = kq.w;
-      *reinterpret_cast<uint4*>(sv + j * D + 8 * c) = __ldg(reinterpret_cast<const uint4*>(a.v_cache + row) + c);
+      *reinterpret_cast<uint4*>(sv + j * D + EPU * c) = __ldg(reinterpret_cast<const uint4*>(vcache + row) + c);
     }
     __syncthreads();
     // scores: thread -> key j = tid % kChunk, heads h = tid / kChunk, + 2, ...
@@ -237,10 +252,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         float s = -INFINITY;
         if (j < nk) {
           const float* qh = sq + h * D;
-          const __half2* kr = reinterpret_cast<const __half2*>(sk + j * KP);
+          const KV* kr = sk + j * KP;
           float d0 = 0.0f, d1 = 0.0f;
           for (int d = 0; d < D / 2; ++d) {
-            const float2 kv = __half22float2(kr[d]);
+            float2 kv;
+            if constexpr (sizeof(KV) == 2)
+              kv = __half22float2(reinterpret_cast<const __half2*>(kr)[d]);
+            else
+              kv = make_float2((float)kr[2 * d], (float)kr[2 * d + 1]);
             d0 = fmaf(qh[2 * d], kv.x, d0);
             d1 = fmaf(qh[2 * d + 1], kv.y, d1);
           }
@@ -274,7 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         const int h = oi / D, d = oi - h * D;
         float s = acc[i] * salpha[h];
         const float* ph = sp_ + h * kChunk;
-        for (int j = 0; j < nk; ++j) s = fmaf(ph[j], __half2float(sv[j * D + d]), s);
+        for (int j = 0; j < nk; ++j) s = fmaf(ph[j], (float)sv[j * D + d], s);
         acc[i] = s;
       }
     }
@@ -407,13 +426,17 @@ cudaError_t launch_add_rmsnorm(float* h, int64_t ldh, const void* delta, int ddt
 cudaError_t launch_rope_kv(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                            int64_t T, int n_head, int n_kv, int head_dim, int rot_dim, float theta, const int* tok_seq,
                            const int* tok_pos, const int* block_table, int max_blocks, void* k_cache, void* v_cache,
-                           float* q_out, cudaStream_t st) {
+                           int kv_f32, float* q_out, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   RopeArgs a{q, k, v, ldq, ldk, ldv, n_head, n_kv, head_dim, rot_dim, theta, tok_seq, tok_pos, block_table,
-             max_blocks, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), q_out};
+             max_blocks, k_cache, v_cache, q_out};
   const int threads = std::max(32, std::min(256, (head_dim / 2 + 31) / 32 * 32));
+  const dim3 grid((unsigned)T, (unsigned)(n_head + 2 * n_kv));
   count_launch();
-  rope_kv_kernel<<<dim3((unsigned)T, (unsigned)(n_head + 2 * n_kv)), threads, 0, st>>>(a);
+  if (kv_f32)
+    rope_kv_kernel<float><<<grid, threads, 0, st>>>(a);
+  else
+    rope_kv_kernel<__half><<<grid, threads, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -424,22 +447,27 @@ size_t attn_workspace_bytes(int64_t T, int n_head, int n_kv, int head_dim, int s
 
 cudaError_t launch_attention(const float* q, int64_t T, int n_head, int n_kv, int head_dim, float scale,
                              const int* tok_seq, const int* tok_pos, const int* block_table, int max_blocks,
-                             const void* k_cache, const void* v_cache, void* o, int o_dtype, int64_t ldo, int splits,
-                             float* part, cudaStream_t st) {
+                             const void* k_cache, const void* v_cache, int kv_f32, void* o, int o_dtype, int64_t ldo,
+                             int splits, float* part, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  AttnArgs a{q, n_head, n_kv, head_dim, scale, tok_seq, tok_pos, block_table, max_blocks,
-             static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache), o, o_dtype, ldo,
-             std::max(1, splits), part};
+  AttnArgs a{q, n_head, n_kv, head_dim, scale, tok_seq, tok_pos, block_table, max_blocks, k_cache, v_cache, o,
+             o_dtype, ldo, std::max(1, splits), part};
   const int G = n_head / n_kv;
+  const size_t es = kv_f32 ? 4 : 2;
   const size_t smem = (size_t)G * head_dim * 4 + (size_t)G * kChunk * 4 + kMaxGroup * 4 +
-                      (size_t)kChunk * (head_dim + 2) * 2 + 16 + (size_t)kChunk * head_dim * 2;
+                      (size_t)kChunk * head_dim * es + 4 * kChunk + 16 + (size_t)kChunk * head_dim * es;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(attn_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(attn_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     configured = true;
   }
+  const dim3 grid((unsigned)T, (unsigned)n_kv, (unsigned)a.splits);
   count_launch();
-  attn_kernel<<<dim3((unsigned)T, (unsigned)n_kv, (unsigned)a.splits), kAttnThreads, smem, st>>>(a);
+  if (kv_f32)
+    attn_kernel<float><<<grid, kAttnThreads, smem, st>>>(a);
+  else
+    attn_kernel<__half><<<grid, kAttnThreads, smem, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || a.splits == 1) return e;
   count_launch();

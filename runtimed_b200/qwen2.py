@@ -86,13 +86,17 @@ class PagedKvCache:
     ``truncate`` shrinks it (blocks past the new length return to the pool), ``release``
     frees it."""
 
-    def __init__(self, cfg: Qwen2Config, num_blocks: int, max_seqs: int, max_ctx: int, device):
-        self.cfg, self.device = cfg, torch.device(device)
+    def __init__(self, cfg: Qwen2Config, num_blocks: int, max_seqs: int, max_ctx: int, device,
+                 dtype: torch.dtype = torch.float16):
+        if dtype not in (torch.float16, torch.float32):
+            raise ConfigError(f"KV cache dtype {dtype} (f16 or f32)")
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        self.abi_dtype = _lib.DT_F16 if dtype == torch.float16 else _lib.DT_F32
         self.num_blocks, self.max_seqs = int(num_blocks), int(max_seqs)
         self.max_blocks = -(-int(max_ctx) // KV_BLOCK)
         shape = (self.num_blocks, cfg.n_kv, KV_BLOCK, cfg.head_dim)
-        self.k = [torch.zeros(shape, dtype=torch.float16, device=self.device) for _ in range(cfg.n_layer)]
-        self.v = [torch.zeros(shape, dtype=torch.float16, device=self.device) for _ in range(cfg.n_layer)]
+        self.k = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(cfg.n_layer)]
+        self.v = [torch.zeros(shape, dtype=dtype, device=self.device) for _ in range(cfg.n_layer)]
         self.table = torch.zeros((self.max_seqs, self.max_blocks), dtype=torch.int32, device=self.device)
         self._host_table = np.zeros((self.max_seqs, self.max_blocks), dtype=np.int32)
         self._free: List[int] = list(range(self.num_blocks - 1, -1, -1))
@@ -136,10 +140,18 @@ class PagedKvCache:
 
 
 class Qwen2Model:
-    """Weights on one device and the forward over a paged KV cache."""
+    """Weights on one device and the forward over a paged KV cache.
+
+    ``kv_dtype`` is the cache precision (f16 by default, as the configs run; f32 is the
+    reference CPU cache's precision).  ``exact_linears`` runs every linear through the
+    decode GEMV in passes of at most three tokens, whose products are exact (f32 rounding
+    only), instead of the tensor-core GEMM, whose f16-rounded weights cost about 3e-4
+    relative per linear; the parity checks use it to separate the layer math from the
+    GEMM's rounding, which peaked attention over a long prompt amplifies."""
 
     def __init__(self, path_or_file, device="cuda:0", max_seqs: int = 1, max_ctx: int = 4096,
-                 kv_blocks: Optional[int] = None):
+                 kv_blocks: Optional[int] = None, kv_dtype: torch.dtype = torch.float16,
+                 exact_linears: bool = False):
         self.file = path_or_file if isinstance(path_or_file, GgufFile) else GgufFile.open(path_or_file)
         self.cfg = Qwen2Config.from_gguf(self.file)
         self.device = torch.device(device)
@@ -147,8 +159,9 @@ class Qwen2Model:
         self.L = _lib.lib()
         self.weights = self._load()
         blocks = kv_blocks if kv_blocks is not None else max_seqs * (-(-max_ctx // KV_BLOCK))
-        self.cache = PagedKvCache(self.cfg, blocks, max_seqs, max_ctx, self.device)
+        self.cache = PagedKvCache(self.cfg, blocks, max_seqs, max_ctx, self.device, kv_dtype)
         self.max_ctx = int(max_ctx)
+        self.exact_linears = bool(exact_linears)
 
     # ---- load (crates/runtimed-model/src/weights/load_gguf.rs:47-120)
     def _load(self) -> Weights:
@@ -175,13 +188,16 @@ class Qwen2Model:
         m = x.shape[0]
         y = torch.empty((m, qm.n), dtype=torch.float32, device=self.device)
         b = self.weights.map[bias].data_ptr() if bias else None
-        self._check(self.L.rtd_qlinear(self.ctx.handle, qm.handle, x.data_ptr(), _lib.DT_F32, qm.k, m, b,
-                                       y.data_ptr(), _lib.DT_F32, qm.n, _stream_ptr(self.device)))
+        step = 3 if self.exact_linears else m
+        for m0 in range(0, m, step):
+            mc = min(step, m - m0)
+            self._check(self.L.rtd_qlinear(self.ctx.handle, qm.handle, x[m0].data_ptr(), _lib.DT_F32, qm.k, mc, b,
+                                           y[m0].data_ptr(), _lib.DT_F32, qm.n, _stream_ptr(self.device)))
         return y
 
     # ---- one call over T tokens, each with its own (sequence, position)
     def _run(self, ids: torch.Tensor, tok_seq: torch.Tensor, tok_pos: torch.Tensor, max_ctx: int,
-             logits_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+             logits_rows: Optional[torch.Tensor] = None, trace: Optional[list] = None) -> torch.Tensor:
         cfg, L, st = self.cfg, self.L, _stream_ptr(self.device)
         T = int(ids.shape[0])
         c = self.ctx.handle
@@ -206,12 +222,13 @@ class Qwen2Model:
                                              v.shape[1], T, cfg.n_head, cfg.n_kv, cfg.head_dim, cfg.head_dim,
                                              cfg.rope_theta, tok_seq.data_ptr(), tok_pos.data_ptr(),
                                              self.cache.table.data_ptr(), self.cache.max_blocks,
-                                             self.cache.k[i].data_ptr(), self.cache.v[i].data_ptr(), qr.data_ptr(), st))
+                                             self.cache.k[i].data_ptr(), self.cache.v[i].data_ptr(),
+                                             self.cache.abi_dtype, qr.data_ptr(), st))
             self._check(L.rtd_attention_paged(c, qr.data_ptr(), T, cfg.n_head, cfg.n_kv, cfg.head_dim, scale,
                                               tok_seq.data_ptr(), tok_pos.data_ptr(), self.cache.table.data_ptr(),
                                               self.cache.max_blocks, max_ctx, self.cache.k[i].data_ptr(),
-                                              self.cache.v[i].data_ptr(), att.data_ptr(), _lib.DT_F32, att.shape[1],
-                                              st))
+                                              self.cache.v[i].data_ptr(), self.cache.abi_dtype, att.data_ptr(),
+                                              _lib.DT_F32, att.shape[1], st))
             o = self._linear(att, f"{p}.attn_output.weight")
             self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, o.data_ptr(), _lib.DT_F32, cfg.hidden,
                                       self.weights.map[f"{p}.ffn_norm.weight"].data_ptr(), cfg.eps, T, cfg.hidden,
@@ -221,6 +238,8 @@ class Qwen2Model:
             self._check(L.rtd_silu_mul(c, g.data_ptr(), _lib.DT_F32, u.data_ptr(), _lib.DT_F32, g.numel(),
                                        g.data_ptr(), _lib.DT_F32, st))
             delta = self._linear(g, f"{p}.ffn_down.weight")
+            if trace is not None:  # the residual stream after layer i (a diagnostic copy)
+                trace.append((h + delta).clone())
         self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, delta.data_ptr(), _lib.DT_F32, cfg.hidden,
                                   self.weights.map["output_norm.weight"].data_ptr(), cfg.eps, T, cfg.hidden,
                                   n.data_ptr(), _lib.DT_F32, cfg.hidden, st))
@@ -230,7 +249,8 @@ class Qwen2Model:
     def _tokens(self, values: Sequence[int]) -> torch.Tensor:
         return torch.tensor(np.asarray(values, dtype=np.int32), device=self.device)
 
-    def forward(self, ids: Sequence[int], q0: int, seq: int = 0, last_only: bool = False) -> torch.Tensor:
+    def forward(self, ids: Sequence[int], q0: int, seq: int = 0, last_only: bool = False,
+                trace: Optional[list] = None) -> torch.Tensor:
         """Logits [t, vocab] (f32) of `ids` at positions q0 .. q0 + t - 1 of sequence `seq`
         (qwen2.rs:217-229); `last_only` computes the LM head for the last position only."""
         t = len(ids)
@@ -242,7 +262,7 @@ class Qwen2Model:
         seq_d = self._tokens([seq] * t)
         pos_d = self._tokens(range(q0, q0 + t))
         rows = self._tokens([t - 1]) if last_only else None
-        return self._run(ids_d, seq_d, pos_d, q0 + t, rows)
+        return self._run(ids_d, seq_d, pos_d, q0 + t, rows, trace)
 
     def decode_batch(self, ids: Sequence[int], seqs: Sequence[int], positions: Sequence[int]) -> torch.Tensor:
         """One token for each of several sequences (batched decode); logits [b, vocab]."""
