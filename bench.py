@@ -31,7 +31,7 @@ on the host cores, scaled to the step), the SM clocks of the timed window, and:
               steps as a CUDA graph) in tokens/s, beside the restated reference forward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-    python bench.py --profile-one FMT:N:K[:M] | sweep   (ncu target, no JSON line)
+    python bench.py --profile-one FMT:N:K[:M] | sweep | tpstep[:B]   (ncu target, no JSON line)
 """
 from __future__ import annotations
 
@@ -262,6 +262,7 @@ def config_dict(world: int):
             "hidden": HIDDEN, "ffn": FFN, "heads": [N_HEAD, N_KV, HEAD_DIM], "global_batch": BATCH,
             "linears": [f"{n}:{TYPE_NAMES[t]}:{N}x{K}:{sp}" for n, t, N, K, sp, _ in LAYER_LINEARS],
             "parallelism": f"tp{world}: column-parallel q/k/v/gate/up, row-parallel o/down (fused NVLink exchange)",
+            "fused_calls": "attn_q + attn_k and ffn_gate + ffn_up each run as one call on row-concatenated weights",
             "activations": "bf16", "weights": "80 device copies of one seeded random-init layer (config-3 "
                                                 "block distributions)",
             "l2": f"inputs larger than L2: {step_weight_bytes(world) / 1e9:.1f} GB of weights per rank per step "
@@ -270,8 +271,16 @@ def config_dict(world: int):
 
 
 # ---------------------------------------------------------------- the TP decode step
+# Linears of one layer that read the same input and share a format run as ONE call on
+# row-concatenated weights (GGUF rows are independent, so the concatenation only places
+# byte ranges side by side): attn_q + attn_k and ffn_gate + ffn_up.
+FUSED = [("attn_qk", ("attn_q", "attn_k")), ("attn_v", ("attn_v",)), ("attn_output", ("attn_output",)),
+         ("ffn_gate_up", ("ffn_gate", "ffn_up")), ("ffn_down", ("ffn_down",))]
+
+
 class TpStack:
-    """The seven linears of every layer, sharded for this rank, and the step's buffers."""
+    """The linears of every layer, sharded for this rank (same-format siblings fused), and
+    the step's buffers."""
 
     def __init__(self, rank, world, dev, comm, batches):
         import torch
@@ -280,78 +289,80 @@ class TpStack:
 
         self.L = _lib.lib()
         self.rank, self.world, self.dev, self.comm = rank, world, dev, comm
-        self.layers = []
+        spec = {n: (i, t, nn, kk, sp, hb) for i, (n, t, nn, kk, sp, hb) in enumerate(LAYER_LINEARS)}
         first = {}
-        for i, (name, t, n, k, sp, has_b) in enumerate(LAYER_LINEARS):
-            ns, ks = shard_shape(n, k, sp, world)
-            raw = synth.quant_matrix(t, ns, ks, seed=1000 + rank, stream=i)
-            qm = QMatMul(t, raw, ns, ks, device=dev)
-            del raw
-            bias = None
-            if has_b:
-                b = np.random.default_rng(50 + i).normal(0, 0.02, n).astype(np.float32)
-                bias = torch.from_numpy(b[rank * ns:(rank + 1) * ns].copy()).to(dev)
-            first[name] = (qm, bias)
+        self.widths = {}
+        for fname, parts in FUSED:
+            raws, biases, ns_tot, t0, ks0 = [], [], 0, None, None
+            for name in parts:
+                i, t, n, k, sp, has_b = spec[name]
+                ns, ks = shard_shape(n, k, sp, world)
+                raws.append(synth.quant_matrix(t, ns, ks, seed=1000 + rank, stream=i))
+                if has_b:
+                    b = np.random.default_rng(50 + i).normal(0, 0.02, n).astype(np.float32)
+                    biases.append(b[rank * ns:(rank + 1) * ns])
+                ns_tot += ns
+                t0, ks0 = t, ks
+            qm = QMatMul(t0, np.concatenate(raws), ns_tot, ks0, device=dev)
+            bias = torch.from_numpy(np.concatenate(biases)).to(dev) if biases else None
+            first[fname] = (qm, bias)
+            self.widths[fname] = ns_tot
+        self.layers = []
         for layer in range(N_LAYERS):
-            ent = {}
-            for name, *_ in LAYER_LINEARS:
-                qm, bias = first[name]
-                ent[name] = (qm if layer == 0 else qm.to_device(dev), bias)
-            self.layers.append(ent)
+            self.layers.append({f: (q if layer == 0 else q.to_device(dev), b) for f, (q, b) in first.items()})
         torch.cuda.synchronize(dev)
+        self.nq = N_HEAD * HEAD_DIM // world   # q's columns at the front of attn_qk's output
+        self.nf = FFN // world                 # gate's columns at the front of ffn_gate_up's output
         self.bufs = {}
         for b in batches:
             bf = torch.bfloat16
-            kv = N_KV * HEAD_DIM // world
             self.bufs[b] = dict(
                 x=torch.from_numpy(synth.activations(b, HIDDEN, seed=rank, stream=3)).to(bf).to(dev),
-                q=torch.empty((b, N_HEAD * HEAD_DIM // world), dtype=bf, device=dev),
-                k=torch.empty((b, kv), dtype=bf, device=dev), v=torch.empty((b, kv), dtype=bf, device=dev),
+                qk=torch.empty((b, self.widths["attn_qk"]), dtype=bf, device=dev),
+                v=torch.empty((b, self.widths["attn_v"]), dtype=bf, device=dev),
                 o=torch.empty((b, HIDDEN), dtype=bf, device=dev),
-                g=torch.empty((b, FFN // world), dtype=bf, device=dev),
-                u=torch.empty((b, FFN // world), dtype=bf, device=dev),
+                gu=torch.empty((b, self.widths["ffn_gate_up"]), dtype=bf, device=dev),
                 d=torch.empty((b, HIDDEN), dtype=bf, device=dev))
 
-    def _lin(self, qm, bias, x, y, m, st):
+    def _lin(self, qm, bias, x, ldx, y, m, st):
         from runtimed_b200 import _lib
 
-        rc = self.L.rtd_qlinear(qm.ctx.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, qm.k, m,
+        rc = self.L.rtd_qlinear(qm.ctx.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, ldx, m,
                                 None if bias is None else bias.data_ptr(), y.data_ptr(), _lib.DT_BF16, qm.n, st)
         if rc != 0:
             raise RuntimeError(f"rtd_qlinear status {rc}: {self.L.rtd_last_error(qm.ctx.handle)}")
 
-    def _row(self, qm, x, y, m, st):
+    def _row(self, qm, x, ldx, y, m, st):
         from runtimed_b200 import _lib
 
         if self.world == 1:
-            return self._lin(qm, None, x, y, m, st)
-        rc = self.L.rtd_tp_qlinear_row(self.comm.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, qm.k, m, None,
+            return self._lin(qm, None, x, ldx, y, m, st)
+        rc = self.L.rtd_tp_qlinear_row(self.comm.handle, qm.handle, x.data_ptr(), _lib.DT_BF16, ldx, m, None,
                                        y.data_ptr(), _lib.DT_BF16, qm.n, st)
         if rc != 0:
             raise RuntimeError(f"rtd_tp_qlinear_row status {rc}: {self.L.rtd_last_error(qm.ctx.handle)}")
 
+    def one(self, name, layer, b, st):
+        """One (fused) linear of one layer."""
+        B = self.bufs[b]
+        qm, bias = self.layers[layer][name]
+        if name == "attn_qk":
+            self._lin(qm, bias, B["x"], HIDDEN, B["qk"], b, st)
+        elif name == "attn_v":
+            self._lin(qm, bias, B["x"], HIDDEN, B["v"], b, st)
+        elif name == "attn_output":  # reads q's head shard: the front of attn_qk's rows
+            self._row(qm, B["qk"], self.widths["attn_qk"], B["o"], b, st)
+        elif name == "ffn_gate_up":
+            self._lin(qm, bias, B["o"], HIDDEN, B["gu"], b, st)
+        else:  # ffn_down reads gate's shard: the front of ffn_gate_up's rows
+            self._row(qm, B["gu"], self.widths["ffn_gate_up"], B["d"], b, st)
+
     def step(self, b, st, layers=None):
         """One decode token for b sequences through every layer's linears."""
-        B = self.bufs[b]
-        for ent in (self.layers if layers is None else layers):
-            self._lin(*ent["attn_q"], B["x"], B["q"], b, st)
-            self._lin(*ent["attn_k"], B["x"], B["k"], b, st)
-            self._lin(*ent["attn_v"], B["x"], B["v"], b, st)
-            self._row(ent["attn_output"][0], B["q"], B["o"], b, st)
-            self._lin(*ent["ffn_gate"], B["o"], B["g"], b, st)
-            self._lin(*ent["ffn_up"], B["o"], B["u"], b, st)
-            self._row(ent["ffn_down"][0], B["g"], B["d"], b, st)
-
-    def one(self, name, layer, b, st):
-        """One linear of one layer (for the per-linear timing)."""
-        B = self.bufs[b]
-        io = {"attn_q": ("x", "q"), "attn_k": ("x", "k"), "attn_v": ("x", "v"), "attn_output": ("q", "o"),
-              "ffn_gate": ("o", "g"), "ffn_up": ("o", "u"), "ffn_down": ("g", "d")}[name]
-        qm, bias = self.layers[layer][name]
-        if name in ("attn_output", "ffn_down"):
-            self._row(qm, B[io[0]], B[io[1]], b, st)
-        else:
-            self._lin(qm, bias, B[io[0]], B[io[1]], b, st)
+        n = N_LAYERS if layers is None else layers
+        for layer in range(n):
+            for fname, _ in FUSED:
+                self.one(fname, layer, b, st)
 
 
 def _capture(fn, dev):
@@ -387,25 +398,33 @@ def _max_over_ranks(v: float, dev, world: int) -> float:
 
 
 def _per_linear(stack, b, stream, dev, world, reps: int = 24):
-    """Device time of each of the seven linears at batch b: a graph of `reps` calls rotating
+    """Device time of each (fused) linear call at batch b: a graph of `reps` calls rotating
     over three layers' weight copies (no call re-reads another's weights from L2)."""
     import torch
     import torch.distributed as dist
 
+    spec = {n: (t, nn, kk, sp) for n, t, nn, kk, sp, _ in LAYER_LINEARS}
     out = {}
-    for name, t, n, k, sp, _ in LAYER_LINEARS:
+    for fname, parts in FUSED:
         if world > 1:
             dist.barrier()
-        g = _capture(lambda st: [stack.one(name, r % 3, b, st) for r in range(reps)], dev)
+        g = _capture(lambda st: [stack.one(fname, r % 3, b, st) for r in range(reps)], dev)
         g.replay()
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         s = _max_over_ranks(_time_graph(g, stream, dev, 5) / reps, dev, world)
         del g
-        ns, ks = shard_shape(n, k, sp, world)
-        byts = weight_bytes(t, ns, ks) + b * ks * 2 + b * (n if sp == "row" else ns) * 2
-        out[name] = {"us": s * 1e6, "shard_nk": [ns, ks], "bytes": byts, "gbs": byts / s / 1e9}
+        byts, nk = 0, None
+        for name in parts:
+            t, n, k, sp = spec[name]
+            ns, ks = shard_shape(n, k, sp, world)
+            byts += weight_bytes(t, ns, ks) + b * (n if sp == "row" else ns) * 2
+            nk = ks
+        byts += b * nk * 2
+        qm = stack.layers[0][fname][0]
+        out[fname] = {"us": s * 1e6, "shard_nk": [qm.n, qm.k], "format": TYPE_NAMES[qm.ggml_type], "bytes": byts,
+                      "gbs": byts / s / 1e9}
     return out
 
 
@@ -645,6 +664,23 @@ def _model_decode(dev, steps: int = 128, warm: int = 8):
                                                                          f"{os.cpu_count()} host threads), {n_cpu} steps"}
 
 
+def profile_tpstep(b: int, calls: int, layers: int = 4) -> int:
+    """`calls` eager config-3 decode steps of `layers` layers at batch b on one GPU (the
+    launch-list target: every kernel of a step in order)."""
+    import torch
+
+    global N_LAYERS
+    N_LAYERS = layers  # the profile covers a few layers; every layer runs the same calls
+    dev = torch.device("cuda", 0)
+    stack = TpStack(0, 1, dev, None, batches=(b,))
+    st = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(calls):
+        stack.step(b, st)
+    torch.cuda.synchronize(dev)
+    print(f"profile-one tpstep:{b}: {calls} steps of {layers} layers ok")
+    return 0
+
+
 def profile_one(spec: str, calls: int) -> int:
     """Run `calls` bf16 calls of one linear (FMT:N:K, or FMT:N:K:M for M tokens; M = 1 by
     default), or of every config-1 sweep GEMV in order ("sweep"), eagerly, and exit: the
@@ -654,6 +690,8 @@ def profile_one(spec: str, calls: int) -> int:
     from runtimed_b200.weights import Fp8Weight, QMatMul
 
     m = 1
+    if spec.startswith("tpstep"):
+        return profile_tpstep(int(spec.split(":")[1]) if ":" in spec else BATCH, calls)
     if spec == "sweep":
         todo = [(t, n, k) for _, t, n, k in sweep()]
     else:
@@ -695,7 +733,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep",
+    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep|tpstep[:B]",
                     help="only run a few eager calls of one linear or of the config-1 sweep (ncu target), "
                          "no JSON line")
     ap.add_argument("--calls", type=int, default=4)
@@ -731,7 +769,7 @@ def main() -> int:
     w_bytes = step_weight_bytes(world)
 
     for b in (BATCH, 1):  # first calls configure kernel attributes outside capture
-        stack.step(b, stream.cuda_stream, layers=stack.layers[:1])
+        stack.step(b, stream.cuda_stream, layers=1)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -778,12 +816,11 @@ def main() -> int:
     per1 = _per_linear(stack, 1, stream, dev, world)
     dom = max(per64, key=lambda n: per64[n]["us"])
     d = per64[dom]
-    dt = dict((n, t) for n, t, *_ in LAYER_LINEARS)[dom]
-    fmt = {Q4_K: "q4k", Q6_K: "q6k"}[dt]
+    fmt = d["format"].lower().replace("_", "")
     step_gbs = w_bytes / (ms_max * 1e-3 / args.steps) / 1e9
     roofline = {"bound": "hbm", "achieved": d["gbs"], "peak": peak, "unit": "GB/s", "frac": d["gbs"] / peak,
                 "traffic": profile_traffic(f"qgemm_{fmt}_{d['shard_nk'][0]}x{d['shard_nk'][1]}_m{BATCH}"),
-                "kernel": f"{dom} (rank shard {d['shard_nk'][0]}x{d['shard_nk'][1]}, M={BATCH}): "
+                "kernel": f"{dom} ({d['format']}, rank shard {d['shard_nk'][0]}x{d['shard_nk'][1]}, M={BATCH}): "
                           f"tensor-core GEMM (qgemm_kernel) and its prep",
                 "launch_us": d["us"], "duration_source": "CUDA events around a graph of 24 back-to-back calls over "
                                                          "3 layers' weight copies",

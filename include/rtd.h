@@ -92,6 +92,13 @@ rtd_status rtd_qweight_free(rtd_qweight* w);
  * a host round trip.  Replaces Weights::to_device (crates/runtimed-model/src/weights/store.rs:170-205)
  * for quantized entries, which stay quantized (the reference leaves q_map entries in place). */
 rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweight** out);
+/* Rows [row0, row0 + rows) of an uploaded weight as a handle that shares its device memory
+ * (row0 a multiple of 16; the parent must outlive the view; freeing the view frees no
+ * memory): the quantized counterpart of narrowing a weight's rows
+ * (crates/runtimed-model/src/arch/qwen2.rs:182-184).  A caller can upload sibling weights
+ * that read the same input as one row-concatenated matrix -- one launch serves them all --
+ * and still address each by name. */
+rtd_status rtd_qweight_rows(const rtd_qweight* w, int64_t row0, int64_t rows, rtd_qweight** out);
 
 /* raw_bytes = the GGUF byte count (QTensor::storage_size_in_bytes, store.rs:57-76);
  * device_bytes = what the device copy occupies (rows padded to a tile of 16). */
@@ -171,10 +178,12 @@ rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t 
                                float scale, const int32_t* tok_seq, const int32_t* tok_pos, const int32_t* block_table,
                                int32_t max_blocks, int32_t max_ctx, const void* k_cache, const void* v_cache,
                                uint32_t kv_dtype, void* o, uint32_t o_dtype, int64_t ldo, void* stream);
-/* y[i] = silu(gate[i]) * up[i]: SubstratePort::silu + broadcast_mul
+/* y[t, f] = silu(gate[t, f]) * up[t, f] for t < T, f < F (rows ldg / ldu / ldy elements
+ * apart; y may alias gate): SubstratePort::silu + broadcast_mul
  * (crates/runtimed-model/src/ops/activation.rs:6-10, arch/qwen2.rs:120-123). */
-rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, const void* up, uint32_t up_dtype,
-                        int64_t n, void* y, uint32_t y_dtype, void* stream);
+rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, int64_t ldg, const void* up,
+                        uint32_t up_dtype, int64_t ldu, int64_t T, int64_t F, void* y, uint32_t y_dtype, int64_t ldy,
+                        void* stream);
 /* out[t] = argmax of row t of x[T, V] (f32; lowest index among equal maxima):
  * SubstratePort::argmax behind greedy sampling (crates/runtimed-model/src/decode/sample.rs:11-18). */
 rtd_status rtd_argmax(rtd_ctx* ctx, const float* x, int64_t ldx, int64_t T, int64_t V, int32_t* out, void* stream);

@@ -43,6 +43,7 @@ SIGNATURES = {
     "rtd_qweight_upload": (_c.c_int32, [_vp, _u32, _vp, _c.c_size_t, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_free": (_c.c_int32, [_vp]),
     "rtd_qweight_to_device": (_c.c_int32, [_vp, _vp, _c.POINTER(_vp)]),
+    "rtd_qweight_rows": (_c.c_int32, [_vp, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_info": (_c.c_int32, [_vp, _c.POINTER(_u32), _c.POINTER(_i64), _c.POINTER(_i64),
                                       _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
     "rtd_qlinear": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp]),
@@ -60,7 +61,7 @@ SIGNATURES = {
                                         _u32, _vp, _vp]),
     "rtd_attention_paged": (_c.c_int32, [_vp, _vp, _i64, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_float, _vp, _vp,
                                          _vp, _c.c_int32, _c.c_int32, _vp, _vp, _u32, _vp, _u32, _i64, _vp]),
-    "rtd_silu_mul": (_c.c_int32, [_vp, _vp, _u32, _vp, _u32, _i64, _vp, _u32, _vp]),
+    "rtd_silu_mul": (_c.c_int32, [_vp, _vp, _u32, _i64, _vp, _u32, _i64, _i64, _i64, _vp, _u32, _i64, _vp]),
     "rtd_argmax": (_c.c_int32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "rtd_qembed": (_c.c_int32, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "rtd_qdequant": (_c.c_int32, [_vp, _vp, _vp, _vp]),

@@ -36,6 +36,7 @@ struct rtd_qweight {
   int64_t N = 0, K = 0, G = 0, T = 0;
   uint8_t* dev = nullptr;
   size_t dev_bytes = 0, raw_bytes = 0;
+  bool owns = true;  // false for a row view (rtd_qweight_rows): the parent owns the memory
 };
 
 struct rtd_fp8weight {
@@ -264,9 +265,29 @@ rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweig
   return RTD_OK;
 }
 
+rtd_status rtd_qweight_rows(const rtd_qweight* w, int64_t row0, int64_t rows, rtd_qweight** out) {
+  const char* who = "rtd_qweight_rows";
+  if (!w || !out) return fail(w ? w->ctx : nullptr, RTD_ERR_INVALID, "%s: NULL argument", who);
+  *out = nullptr;
+  if (row0 < 0 || rows <= 0 || row0 + rows > w->N || row0 % 16 != 0)
+    return fail(w->ctx, RTD_ERR_SHAPE, "%s: rows [%lld, %lld) of %lld (the first row a multiple of 16)", who,
+                (long long)row0, (long long)(row0 + rows), (long long)w->N);
+  rtd_qweight* v = new (std::nothrow) rtd_qweight(*w);
+  if (!v) return fail(w->ctx, RTD_ERR_OOM, "%s: host allocation failed", who);
+  const rtd::FmtInfo f = rtd::fmt_info(w->fmt);
+  v->N = rows;
+  v->T = rtd::tiles_for(rows);
+  v->dev = w->dev + (size_t)(row0 / 16) * (size_t)w->G * (size_t)f.gb;
+  v->dev_bytes = (size_t)v->T * (size_t)w->G * (size_t)f.gb;
+  v->raw_bytes = w->raw_bytes / (size_t)(w->N > 0 ? w->N : 1) * (size_t)rows;
+  v->owns = false;
+  *out = v;
+  return RTD_OK;
+}
+
 rtd_status rtd_qweight_free(rtd_qweight* w) {
   if (!w) return RTD_OK;
-  if (w->dev) {
+  if (w->dev && w->owns) {
     DeviceGuard g(w->ctx->device);
     cudaFree(w->dev);
   }
@@ -516,17 +537,20 @@ rtd_status rtd_attention_paged(rtd_ctx* ctx, const float* q, int64_t T, int32_t 
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 
-rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, const void* up, uint32_t up_dtype,
-                        int64_t n, void* y, uint32_t y_dtype, void* stream) {
+rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, int64_t ldg, const void* up,
+                        uint32_t up_dtype, int64_t ldu, int64_t T, int64_t F, void* y, uint32_t y_dtype, int64_t ldy,
+                        void* stream) {
   const char* who = "rtd_silu_mul";
   if (!ctx) return fail(nullptr, RTD_ERR_INVALID, "%s: ctx is NULL", who);
-  if (n < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: n is negative", who);
-  if (n == 0) return RTD_OK;
+  if (T < 0 || F < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: negative shape", who);
+  if (T == 0 || F == 0) return RTD_OK;
   if (!gate || !up || !y) return fail(ctx, RTD_ERR_INVALID, "%s: NULL pointer", who);
   if (!valid_dtype(gate_dtype) || !valid_dtype(up_dtype) || !valid_dtype(y_dtype))
     return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
+  if (ldg < F || ldu < F || ldy < F) return fail(ctx, RTD_ERR_SHAPE, "%s: row strides below F", who);
   DeviceGuard g(ctx->device);
-  cudaError_t e = rtd::launch_silu_mul(gate, (int)gate_dtype, up, (int)up_dtype, n, y, (int)y_dtype, (cudaStream_t)stream);
+  cudaError_t e = rtd::launch_silu_mul(gate, (int)gate_dtype, ldg, up, (int)up_dtype, ldu, T, F, y, (int)y_dtype, ldy,
+                                       (cudaStream_t)stream);
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 

@@ -110,8 +110,8 @@ cudaError_t launch_attention(const float* q, int64_t T, int n_head, int n_kv, in
                              const int* tok_seq, const int* tok_pos, const int* block_table, int max_blocks,
                              const void* k_cache, const void* v_cache, int kv_f32, void* o, int o_dtype, int64_t ldo,
                              int splits, float* part, cudaStream_t st);
-cudaError_t launch_silu_mul(const void* gate, int gdt, const void* up, int udt, int64_t n, void* y, int ydt,
-                            cudaStream_t st);
+cudaError_t launch_silu_mul(const void* gate, int gdt, int64_t ldg, const void* up, int udt, int64_t ldu, int64_t T,
+                            int64_t F, void* y, int ydt, int64_t ldy, cudaStream_t st);
 cudaError_t launch_argmax(const float* x, int64_t ldx, int64_t T, int64_t V, int* out, cudaStream_t st);
 
 // y[m, n] = bias[n] (or 0) for every row m < M: the K = 0 case of a linear.

@@ -360,11 +360,14 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 }
 
 // ------------------------------------------------------------------ SiLU * up
-__global__ void silu_mul_kernel(const void* gate, int gdt, const void* up, int udt, int64_t n, void* y, int ydt) {
+__global__ void silu_mul_kernel(const void* gate, int gdt, int64_t ldg, const void* up, int udt, int64_t ldu,
+                                int64_t T, int64_t F, void* y, int ydt, int64_t ldy) {
+  const int64_t n = T * F;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float x = load_as_f32(gate, gdt, i);
+    const int64_t t = i / F, f = i - t * F;
+    const float x = load_as_f32(gate, gdt, t * ldg + f);
     const float sig = 1.0f / (expf(-x) + 1.0f);  // activation.rs:6-10
-    store_from_f32(y, ydt, i, (x * sig) * load_as_f32(up, udt, i));
+    store_from_f32(y, ydt, t * ldy + f, (x * sig) * load_as_f32(up, udt, t * ldu + f));
   }
 }
 
@@ -475,12 +478,13 @@ cudaError_t launch_attention(const float* q, int64_t T, int n_head, int n_kv, in
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu_mul(const void* gate, int gdt, const void* up, int udt, int64_t n, void* y, int ydt,
-                            cudaStream_t st) {
+cudaError_t launch_silu_mul(const void* gate, int gdt, int64_t ldg, const void* up, int udt, int64_t ldu, int64_t T,
+                            int64_t F, void* y, int ydt, int64_t ldy, cudaStream_t st) {
+  const int64_t n = T * F;
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 4096);
   count_launch();
-  silu_mul_kernel<<<(unsigned)blocks, 256, 0, st>>>(gate, gdt, up, udt, n, y, ydt);
+  silu_mul_kernel<<<(unsigned)blocks, 256, 0, st>>>(gate, gdt, ldg, up, udt, ldu, T, F, y, ydt, ldy);
   return cudaGetLastError();
 }
 

@@ -164,10 +164,41 @@ class Qwen2Model:
         self.exact_linears = bool(exact_linears)
 
     # ---- load (crates/runtimed-model/src/weights/load_gguf.rs:47-120)
+    FUSE = (("qkv", ("attn_q", "attn_k", "attn_v")), ("gate_up", ("ffn_gate", "ffn_up")))
+
     def _load(self) -> Weights:
+        """Every tensor to the device.  The linears of a layer that read the same input and
+        share a format (q / k / v; gate / up) are uploaded as one row-concatenated matrix --
+        one launch serves them -- and ``q_map`` holds a row view of it under each name."""
         q_map: Dict[str, QMatMul] = {}
         dense: Dict[str, torch.Tensor] = {}
+        infos = {t.name: t for t in self.file.tensors}
+        self.fused: Dict[tuple, tuple] = {}
+        for i in range(self.cfg.n_layer):
+            for key, parts in self.FUSE:
+                ts = [infos.get(f"blk.{i}.{p}.weight") for p in parts]
+                if any(t is None or len(t.dims) != 2 for t in ts):
+                    continue
+                if len({t.dtype for t in ts}) != 1 or len({int(t.dims[0]) for t in ts}) != 1:
+                    continue
+                if any(int(t.dims[1]) % 16 for t in ts[:-1]):  # views start on 16-row tiles
+                    continue
+                n_tot, k = sum(int(t.dims[1]) for t in ts), int(ts[0].dims[0])
+                raw = np.concatenate([self.file.tensor_bytes(t) for t in ts])
+                fused = QMatMul(ts[0].dtype, raw, n_tot, k, device=self.device)
+                row, biases = 0, []
+                for p, t in zip(parts, ts):
+                    q_map[t.name] = fused.rows(row, int(t.dims[1]))
+                    b = infos.get(f"blk.{i}.{p}.bias")
+                    biases.append(None if b is None else self.file.tensor_bytes(b).view(np.float32))
+                    row += int(t.dims[1])
+                bias = None
+                if all(b is not None for b in biases):
+                    bias = torch.from_numpy(np.concatenate(biases)).to(self.device)
+                self.fused[(i, key)] = (fused, bias, [int(t.dims[1]) for t in ts])
         for t in self.file.tensors:
+            if t.name in q_map:
+                continue
             raw = self.file.tensor_bytes(t)
             if t.dtype == 0:
                 dense[t.name] = torch.from_numpy(raw.view(np.float32).copy()).to(self.device)
@@ -181,19 +212,22 @@ class Qwen2Model:
     def _check(self, st: int) -> None:
         _raise(st, self.ctx.handle)
 
+    def _lin(self, x: torch.Tensor, ldx: int, m: int, qm: QMatMul, bias: Optional[torch.Tensor]) -> torch.Tensor:
+        """y[m, N] (f32) = x . W^T (+ bias), x f32 rows ldx elements apart."""
+        y = torch.empty((m, qm.n), dtype=torch.float32, device=self.device)
+        b = None if bias is None else bias.data_ptr()
+        step = 3 if self.exact_linears else m
+        for m0 in range(0, m, step):
+            mc = min(step, m - m0)
+            self._check(self.L.rtd_qlinear(self.ctx.handle, qm.handle, x.data_ptr() + 4 * m0 * ldx, _lib.DT_F32, ldx,
+                                           mc, b, y[m0].data_ptr(), _lib.DT_F32, qm.n, _stream_ptr(self.device)))
+        return y
+
     def _linear(self, x: torch.Tensor, name: str, bias: Optional[str] = None) -> torch.Tensor:
         qm = self.weights.q_map.get(name)
         if qm is None:
             raise MissingWeight(name)
-        m = x.shape[0]
-        y = torch.empty((m, qm.n), dtype=torch.float32, device=self.device)
-        b = self.weights.map[bias].data_ptr() if bias else None
-        step = 3 if self.exact_linears else m
-        for m0 in range(0, m, step):
-            mc = min(step, m - m0)
-            self._check(self.L.rtd_qlinear(self.ctx.handle, qm.handle, x[m0].data_ptr(), _lib.DT_F32, qm.k, mc, b,
-                                           y[m0].data_ptr(), _lib.DT_F32, qm.n, _stream_ptr(self.device)))
-        return y
+        return self._lin(x, qm.k, x.shape[0], qm, self.weights.map[bias] if bias else None)
 
     # ---- one call over T tokens, each with its own (sequence, position)
     def _run(self, ids: torch.Tensor, tok_seq: torch.Tensor, tok_pos: torch.Tensor, max_ctx: int,
@@ -214,13 +248,21 @@ class Qwen2Model:
             self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, None if delta is None else delta.data_ptr(),
                                       _lib.DT_F32, cfg.hidden, self.weights.map[f"{p}.attn_norm.weight"].data_ptr(),
                                       cfg.eps, T, cfg.hidden, n.data_ptr(), _lib.DT_F32, cfg.hidden, st))
-            bias = cfg.has_qkv_bias
-            q = self._linear(n, f"{p}.attn_q.weight", f"{p}.attn_q.bias" if bias else None)
-            k = self._linear(n, f"{p}.attn_k.weight", f"{p}.attn_k.bias" if bias else None)
-            v = self._linear(n, f"{p}.attn_v.weight", f"{p}.attn_v.bias" if bias else None)
-            self._check(L.rtd_rope_kv_append(c, q.data_ptr(), q.shape[1], k.data_ptr(), k.shape[1], v.data_ptr(),
-                                             v.shape[1], T, cfg.n_head, cfg.n_kv, cfg.head_dim, cfg.head_dim,
-                                             cfg.rope_theta, tok_seq.data_ptr(), tok_pos.data_ptr(),
+            fq = self.fused.get((i, "qkv"))
+            if fq is not None:  # q | k | v from one launch: column slices of one output
+                qkv = self._lin(n, cfg.hidden, T, fq[0], fq[1])
+                w = qkv.shape[1]
+                qp, kp = qkv.data_ptr(), qkv.data_ptr() + 4 * fq[2][0]
+                vp = kp + 4 * fq[2][1]
+                ldq = ldk = ldv = w
+            else:
+                bias = cfg.has_qkv_bias
+                q = self._linear(n, f"{p}.attn_q.weight", f"{p}.attn_q.bias" if bias else None)
+                k = self._linear(n, f"{p}.attn_k.weight", f"{p}.attn_k.bias" if bias else None)
+                v = self._linear(n, f"{p}.attn_v.weight", f"{p}.attn_v.bias" if bias else None)
+                qp, kp, vp, ldq, ldk, ldv = q.data_ptr(), k.data_ptr(), v.data_ptr(), q.shape[1], k.shape[1], v.shape[1]
+            self._check(L.rtd_rope_kv_append(c, qp, ldq, kp, ldk, vp, ldv, T, cfg.n_head, cfg.n_kv, cfg.head_dim,
+                                             cfg.head_dim, cfg.rope_theta, tok_seq.data_ptr(), tok_pos.data_ptr(),
                                              self.cache.table.data_ptr(), self.cache.max_blocks,
                                              self.cache.k[i].data_ptr(), self.cache.v[i].data_ptr(),
                                              self.cache.abi_dtype, qr.data_ptr(), st))
@@ -233,11 +275,20 @@ class Qwen2Model:
             self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, o.data_ptr(), _lib.DT_F32, cfg.hidden,
                                       self.weights.map[f"{p}.ffn_norm.weight"].data_ptr(), cfg.eps, T, cfg.hidden,
                                       n.data_ptr(), _lib.DT_F32, cfg.hidden, st))
-            g = self._linear(n, f"{p}.ffn_gate.weight")
-            u = self._linear(n, f"{p}.ffn_up.weight")
-            self._check(L.rtd_silu_mul(c, g.data_ptr(), _lib.DT_F32, u.data_ptr(), _lib.DT_F32, g.numel(),
-                                       g.data_ptr(), _lib.DT_F32, st))
-            delta = self._linear(g, f"{p}.ffn_down.weight")
+            fg = self.fused.get((i, "gate_up"))
+            if fg is not None:  # gate | up from one launch; silu(gate) * up written over gate
+                gu = self._lin(n, cfg.hidden, T, fg[0], None)
+                F, ld = fg[2][0], gu.shape[1]
+                self._check(L.rtd_silu_mul(c, gu.data_ptr(), _lib.DT_F32, ld, gu.data_ptr() + 4 * F, _lib.DT_F32, ld,
+                                           T, F, gu.data_ptr(), _lib.DT_F32, ld, st))
+                down = self.weights.q_map[f"{p}.ffn_down.weight"]
+                delta = self._lin(gu, ld, T, down, None)
+            else:
+                g = self._linear(n, f"{p}.ffn_gate.weight")
+                u = self._linear(n, f"{p}.ffn_up.weight")
+                self._check(L.rtd_silu_mul(c, g.data_ptr(), _lib.DT_F32, g.shape[1], u.data_ptr(), _lib.DT_F32,
+                                           u.shape[1], T, g.shape[1], g.data_ptr(), _lib.DT_F32, g.shape[1], st))
+                delta = self._linear(g, f"{p}.ffn_down.weight")
             if trace is not None:  # the residual stream after layer i (a diagnostic copy)
                 trace.append((h + delta).clone())
         self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, delta.data_ptr(), _lib.DT_F32, cfg.hidden,

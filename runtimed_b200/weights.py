@@ -174,6 +174,19 @@ class QMatMul:
         out._raw_bytes, out._dev_bytes = self._raw_bytes, self._dev_bytes
         return out
 
+    def rows(self, row0: int, n: int) -> "QMatMul":
+        """Rows [row0, row0 + n) as a QMatMul sharing this one's device memory (row0 a
+        multiple of 16; rtd_qweight_rows).  The view keeps a reference to its parent."""
+        h = ctypes.c_void_p()
+        _raise(_lib.lib().rtd_qweight_rows(self.handle, int(row0), int(n), ctypes.byref(h)), self.ctx.handle)
+        out = QMatMul.__new__(QMatMul)
+        out.ctx, out.ggml_type, out.n, out.k = self.ctx, self.ggml_type, int(n), self.k
+        out.handle = h
+        out._raw_bytes = self._raw_bytes // max(self.n, 1) * int(n)
+        out._dev_bytes = 0  # shares the parent's memory
+        out._parent = self
+        return out
+
     def free(self) -> None:
         if getattr(self, "handle", None):
             _lib.lib().rtd_qweight_free(self.handle)

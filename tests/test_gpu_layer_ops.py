@@ -192,9 +192,17 @@ def test_silu_mul_and_argmax():
     gd, ud = torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()
     y = torch.empty_like(gd)
     L, c = _lib.lib(), _ctx().handle
-    assert L.rtd_silu_mul(c, gd.data_ptr(), 0, ud.data_ptr(), 0, g.size, y.data_ptr(), 0, _st()) == 0
+    assert L.rtd_silu_mul(c, gd.data_ptr(), 0, g.size, ud.data_ptr(), 0, g.size, 1, g.size, y.data_ptr(), 0, g.size,
+                          _st()) == 0
     gg = g.astype(np.float64)
     assert rel_l2(y.cpu().numpy(), gg / (1 + np.exp(-gg)) * u) <= 1e-6
+    # rows of a fused [gate | up] output, written in place over gate
+    gu = np.concatenate([g.reshape(4, 2500), u.reshape(4, 2500)], axis=1)
+    gud = torch.from_numpy(gu).cuda()
+    assert L.rtd_silu_mul(c, gud.data_ptr(), 0, 5000, gud.data_ptr() + 4 * 2500, 0, 5000, 4, 2500, gud.data_ptr(), 0,
+                          5000, _st()) == 0
+    got = gud.cpu().numpy()[:, :2500].reshape(-1)
+    assert rel_l2(got, gg / (1 + np.exp(-gg)) * u) <= 1e-6
     # argmax: the lowest index among equal maxima, per row
     x = rng.normal(0, 1, (3, 151936)).astype(np.float32)
     x[1, [5, 70000, 151935]] = 9.0

@@ -228,3 +228,26 @@ def test_to_device_copy_is_identical(name, t):
     assert torch.equal(y0, y1)
     assert torch.equal(d0, cp.dequantize())
     assert cp.storage_size_in_bytes() == len(raw)
+
+
+def test_row_views_of_a_fused_upload():
+    # rtd_qweight_rows: q | k | v uploaded as one matrix, each addressed by its rows, give
+    # the same bits as separate uploads; the view shares the parent's memory
+    torch = _torch()
+    from runtimed_b200.weights import QMatMul
+
+    K = 512
+    parts = [synth.quant_matrix(8, n, K, seed=n, stream=8) for n in (96, 32, 48)]
+    fused = QMatMul(8, np.concatenate(parts), 176, K)
+    x = torch.from_numpy(synth.activations(2, K, seed=5)).cuda()
+    row = 0
+    yf = fused.forward(x)
+    for raw, n in zip(parts, (96, 32, 48)):
+        view = fused.rows(row, n)
+        alone = QMatMul(8, raw, n, K)
+        assert torch.equal(view.forward(x), alone.forward(x))
+        assert torch.equal(yf[:, row:row + n], alone.forward(x))
+        assert view.device_bytes() == 0 and view.storage_size_in_bytes() == len(raw)
+        row += n
+    with pytest.raises(Exception):
+        fused.rows(8, 16)  # a view must start on a 16-row tile
