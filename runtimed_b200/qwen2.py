@@ -14,6 +14,14 @@ sequence, ``decode_batch`` one token of many sequences, and a speculative verify
 k + 1 positions followed by ``PagedKvCache.truncate`` (the rollback of rejected
 positions, crates/runtimed-model/src/decode/speculate.rs:31-199).
 
+With a communicator (one process per GPU) the decoder runs tensor parallel over N ranks,
+the reference's dual-GPU blocks (crates/runtimed-model/src/tp/dual_gpu.rs:52-186,
+arch/qwen2.rs:142-197) generalised: every rank holds its query / kv heads and FFN rows of
+the column-parallel linears and the matching input columns of attn_output and ffn_down,
+whose outputs are summed over the ranks inside rtd_tp_qlinear_row; the embedding, norms
+and LM head are replicated, so every rank carries the same residual stream bit for bit
+and takes the same greedy token.
+
 The configuration comes from the GGUF metadata as ``parse_gguf_config`` reads it
 (crates/runtimed-model/src/config/parse_gguf.rs:52-90 for arch "qwen2": head_dim =
 hidden / n_head, rope over the whole head, q/k/v bias when ``blk.0.attn_q.bias``
@@ -151,25 +159,63 @@ class Qwen2Model:
 
     def __init__(self, path_or_file, device="cuda:0", max_seqs: int = 1, max_ctx: int = 4096,
                  kv_blocks: Optional[int] = None, kv_dtype: torch.dtype = torch.float16,
-                 exact_linears: bool = False):
+                 exact_linears: bool = False, comm=None):
         self.file = path_or_file if isinstance(path_or_file, GgufFile) else GgufFile.open(path_or_file)
         self.cfg = Qwen2Config.from_gguf(self.file)
         self.device = torch.device(device)
         self.ctx = Context.for_device(self.device)
         self.L = _lib.lib()
+        # tensor parallelism (one process per GPU, runtimed_b200.tp.TpComm): this rank's
+        # query / kv heads and FFN rows; o_proj and ffn_down reduce over the ranks
+        self.comm = comm
+        self.rank, self.world = (comm.rank, comm.world) if comm is not None else (0, 1)
+        cfg = self.cfg
+        if cfg.n_head % self.world or cfg.n_kv % self.world or cfg.ffn % self.world:
+            raise ConfigError(f"{cfg.n_head} heads / {cfg.n_kv} kv heads / FFN {cfg.ffn} do not split over "
+                              f"{self.world} ranks")
+        self.n_head_l, self.n_kv_l, self.ffn_l = cfg.n_head // self.world, cfg.n_kv // self.world, cfg.ffn // self.world
         self.weights = self._load()
         blocks = kv_blocks if kv_blocks is not None else max_seqs * (-(-max_ctx // KV_BLOCK))
-        self.cache = PagedKvCache(self.cfg, blocks, max_seqs, max_ctx, self.device, kv_dtype)
+        local = Qwen2Config(**{**cfg.__dict__, "n_kv": self.n_kv_l})
+        self.cache = PagedKvCache(local, blocks, max_seqs, max_ctx, self.device, kv_dtype)
         self.max_ctx = int(max_ctx)
         self.exact_linears = bool(exact_linears)
 
     # ---- load (crates/runtimed-model/src/weights/load_gguf.rs:47-120)
     FUSE = (("qkv", ("attn_q", "attn_k", "attn_v")), ("gate_up", ("ffn_gate", "ffn_up")))
 
+    def _shard(self, name: str, t) -> tuple:
+        """(raw bytes, N, K) of this rank's part of a tensor: column-parallel linears keep
+        their rows of this rank's heads / FFN rows, row-parallel ones (attn_output,
+        ffn_down) their input columns (runtimed_b200.tp, crates/runtimed-model/src/tp/*)."""
+        from . import tp
+
+        raw = self.file.tensor_bytes(t)
+        k, n = int(t.dims[0]), int(t.dims[1])
+        if self.world == 1 or not name.startswith("blk."):
+            return raw, n, k
+        kind = name.split(".")[2]
+        if kind in ("attn_q", "attn_k", "attn_v", "ffn_gate", "ffn_up"):
+            return tp.shard_rows(raw, t.dtype, n, k, self.rank, self.world), n // self.world, k
+        if kind in ("attn_output", "ffn_down"):
+            return tp.shard_cols(raw, t.dtype, n, k, self.rank, self.world), n, k // self.world
+        return raw, n, k
+
+    def _bias(self, name: str) -> Optional[np.ndarray]:
+        t = self.file.tensor(name)
+        if t is None:
+            return None
+        b = self.file.tensor_bytes(t).view(np.float32)
+        if self.world > 1:  # column-parallel bias: this rank's rows
+            per = b.size // self.world
+            b = b[self.rank * per:(self.rank + 1) * per]
+        return b
+
     def _load(self) -> Weights:
-        """Every tensor to the device.  The linears of a layer that read the same input and
-        share a format (q / k / v; gate / up) are uploaded as one row-concatenated matrix --
-        one launch serves them -- and ``q_map`` holds a row view of it under each name."""
+        """Every tensor (this rank's part of it) to the device.  The linears of a layer that
+        read the same input and share a format (q / k / v; gate / up) are uploaded as one
+        row-concatenated matrix -- one launch serves them -- and ``q_map`` holds a row view
+        of it under each name."""
         q_map: Dict[str, QMatMul] = {}
         dense: Dict[str, torch.Tensor] = {}
         infos = {t.name: t for t in self.file.tensors}
@@ -181,29 +227,30 @@ class Qwen2Model:
                     continue
                 if len({t.dtype for t in ts}) != 1 or len({int(t.dims[0]) for t in ts}) != 1:
                     continue
-                if any(int(t.dims[1]) % 16 for t in ts[:-1]):  # views start on 16-row tiles
+                shards = [self._shard(t.name, t) for t in ts]
+                if any(n % 16 for _, n, _ in shards[:-1]):  # views start on 16-row tiles
                     continue
-                n_tot, k = sum(int(t.dims[1]) for t in ts), int(ts[0].dims[0])
-                raw = np.concatenate([self.file.tensor_bytes(t) for t in ts])
-                fused = QMatMul(ts[0].dtype, raw, n_tot, k, device=self.device)
+                n_tot, k = sum(n for _, n, _ in shards), shards[0][2]
+                fused = QMatMul(ts[0].dtype, np.concatenate([r for r, _, _ in shards]), n_tot, k, device=self.device)
                 row, biases = 0, []
-                for p, t in zip(parts, ts):
-                    q_map[t.name] = fused.rows(row, int(t.dims[1]))
-                    b = infos.get(f"blk.{i}.{p}.bias")
-                    biases.append(None if b is None else self.file.tensor_bytes(b).view(np.float32))
-                    row += int(t.dims[1])
+                for p, t, (_, n, _) in zip(parts, ts, shards):
+                    q_map[t.name] = fused.rows(row, n)
+                    biases.append(self._bias(f"blk.{i}.{p}.bias"))
+                    row += n
                 bias = None
                 if all(b is not None for b in biases):
                     bias = torch.from_numpy(np.concatenate(biases)).to(self.device)
-                self.fused[(i, key)] = (fused, bias, [int(t.dims[1]) for t in ts])
+                self.fused[(i, key)] = (fused, bias, [n for _, n, _ in shards])
         for t in self.file.tensors:
             if t.name in q_map:
                 continue
-            raw = self.file.tensor_bytes(t)
             if t.dtype == 0:
-                dense[t.name] = torch.from_numpy(raw.view(np.float32).copy()).to(self.device)
+                if t.name.endswith(".bias") and t.name.split(".")[2] in ("attn_q", "attn_k", "attn_v"):
+                    dense[t.name] = torch.from_numpy(self._bias(t.name).copy()).to(self.device)
+                else:
+                    dense[t.name] = torch.from_numpy(self.file.tensor_bytes(t).view(np.float32).copy()).to(self.device)
             elif len(t.dims) == 2:
-                k, n = int(t.dims[0]), int(t.dims[1])  # GGUF [K, N] -> [N, K] (load_gguf.rs:35)
+                raw, n, k = self._shard(t.name, t)  # GGUF [K, N] -> [N, K] (load_gguf.rs:35)
                 q_map[t.name] = QMatMul(t.dtype, raw, n, k, device=self.device)
             else:
                 raise ConfigError(f"{t.name}: {len(t.dims)}-D tensor of type {t.dtype} is not on this path")
@@ -223,6 +270,20 @@ class Qwen2Model:
                                            mc, b, y[m0].data_ptr(), _lib.DT_F32, qm.n, _stream_ptr(self.device)))
         return y
 
+    def _row(self, x: torch.Tensor, ldx: int, m: int, qm: QMatMul) -> torch.Tensor:
+        """A row-parallel linear: y[m, N] summed over the ranks, on every rank (the exchange
+        fused into the GEMV up to three tokens, the GEMM + all-reduce from four)."""
+        if self.world == 1:
+            return self._lin(x, ldx, m, qm, None)
+        y = torch.empty((m, qm.n), dtype=torch.float32, device=self.device)
+        step = 3 if self.exact_linears else m
+        for m0 in range(0, m, step):
+            mc = min(step, m - m0)
+            self._check(self.L.rtd_tp_qlinear_row(self.comm.handle, qm.handle, x.data_ptr() + 4 * m0 * ldx,
+                                                  _lib.DT_F32, ldx, mc, None, y[m0].data_ptr(), _lib.DT_F32, qm.n,
+                                                  _stream_ptr(self.device)))
+        return y
+
     def _linear(self, x: torch.Tensor, name: str, bias: Optional[str] = None) -> torch.Tensor:
         qm = self.weights.q_map.get(name)
         if qm is None:
@@ -239,7 +300,8 @@ class Qwen2Model:
         h = torch.empty((T, cfg.hidden), dtype=torch.float32, device=self.device)
         self._check(L.rtd_qembed(c, emb.handle, ids.data_ptr(), T, h.data_ptr(), st))
         n = torch.empty_like(h)
-        qr = torch.empty((T, cfg.n_head * cfg.head_dim), dtype=torch.float32, device=self.device)
+        nh, nkv = self.n_head_l, self.n_kv_l  # this rank's heads
+        qr = torch.empty((T, nh * cfg.head_dim), dtype=torch.float32, device=self.device)
         att = torch.empty_like(qr)
         scale = float(np.float32(1.0) / np.sqrt(np.float32(cfg.head_dim)))
         delta = None
@@ -261,17 +323,17 @@ class Qwen2Model:
                 k = self._linear(n, f"{p}.attn_k.weight", f"{p}.attn_k.bias" if bias else None)
                 v = self._linear(n, f"{p}.attn_v.weight", f"{p}.attn_v.bias" if bias else None)
                 qp, kp, vp, ldq, ldk, ldv = q.data_ptr(), k.data_ptr(), v.data_ptr(), q.shape[1], k.shape[1], v.shape[1]
-            self._check(L.rtd_rope_kv_append(c, qp, ldq, kp, ldk, vp, ldv, T, cfg.n_head, cfg.n_kv, cfg.head_dim,
+            self._check(L.rtd_rope_kv_append(c, qp, ldq, kp, ldk, vp, ldv, T, nh, nkv, cfg.head_dim,
                                              cfg.head_dim, cfg.rope_theta, tok_seq.data_ptr(), tok_pos.data_ptr(),
                                              self.cache.table.data_ptr(), self.cache.max_blocks,
                                              self.cache.k[i].data_ptr(), self.cache.v[i].data_ptr(),
                                              self.cache.abi_dtype, qr.data_ptr(), st))
-            self._check(L.rtd_attention_paged(c, qr.data_ptr(), T, cfg.n_head, cfg.n_kv, cfg.head_dim, scale,
+            self._check(L.rtd_attention_paged(c, qr.data_ptr(), T, nh, nkv, cfg.head_dim, scale,
                                               tok_seq.data_ptr(), tok_pos.data_ptr(), self.cache.table.data_ptr(),
                                               self.cache.max_blocks, max_ctx, self.cache.k[i].data_ptr(),
                                               self.cache.v[i].data_ptr(), self.cache.abi_dtype, att.data_ptr(),
                                               _lib.DT_F32, att.shape[1], st))
-            o = self._linear(att, f"{p}.attn_output.weight")
+            o = self._row(att, att.shape[1], T, self.weights.q_map[f"{p}.attn_output.weight"])
             self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, o.data_ptr(), _lib.DT_F32, cfg.hidden,
                                       self.weights.map[f"{p}.ffn_norm.weight"].data_ptr(), cfg.eps, T, cfg.hidden,
                                       n.data_ptr(), _lib.DT_F32, cfg.hidden, st))
@@ -281,14 +343,13 @@ class Qwen2Model:
                 F, ld = fg[2][0], gu.shape[1]
                 self._check(L.rtd_silu_mul(c, gu.data_ptr(), _lib.DT_F32, ld, gu.data_ptr() + 4 * F, _lib.DT_F32, ld,
                                            T, F, gu.data_ptr(), _lib.DT_F32, ld, st))
-                down = self.weights.q_map[f"{p}.ffn_down.weight"]
-                delta = self._lin(gu, ld, T, down, None)
+                delta = self._row(gu, ld, T, self.weights.q_map[f"{p}.ffn_down.weight"])
             else:
                 g = self._linear(n, f"{p}.ffn_gate.weight")
                 u = self._linear(n, f"{p}.ffn_up.weight")
                 self._check(L.rtd_silu_mul(c, g.data_ptr(), _lib.DT_F32, g.shape[1], u.data_ptr(), _lib.DT_F32,
                                            u.shape[1], T, g.shape[1], g.data_ptr(), _lib.DT_F32, g.shape[1], st))
-                delta = self._linear(g, f"{p}.ffn_down.weight")
+                delta = self._row(g, g.shape[1], T, self.weights.q_map[f"{p}.ffn_down.weight"])
             if trace is not None:  # the residual stream after layer i (a diagnostic copy)
                 trace.append((h + delta).clone())
         self._check(L.rtd_rmsnorm(c, h.data_ptr(), cfg.hidden, delta.data_ptr(), _lib.DT_F32, cfg.hidden,

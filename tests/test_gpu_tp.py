@@ -171,3 +171,87 @@ def test_row_parallel_fused_allreduce(world):
             assert nccl_ok, (rank, key, "nccl", rn)
             assert same, (rank, key, "ranks differ")
     assert res[0]["timeout"] is True
+
+
+def _model_rank_main(rank, world, port, path, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from runtimed_b200.qwen2 import Qwen2Model, Session
+    from runtimed_b200.tp import TpComm
+    from runtimed_b200.weights import Context
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    out = {}
+    try:
+        comm = TpComm(Context.for_device(dev), rank, world, max_n=4096)
+        prompt = list(np.random.default_rng(3).integers(0, 1000, 24))
+        for exact in (True, False):  # exact: fused GEMV exchange; else a 24-token GEMM + all-reduce prefill
+            model = Qwen2Model(path, device=dev, max_ctx=128, kv_dtype=torch.float32, exact_linears=exact, comm=comm)
+            ids, per = Session(model).greedy(prompt, 8)
+            per = torch.stack(per)
+            gathered = [torch.empty_like(per) for _ in range(world)]
+            dist.all_gather(gathered, per)
+            res = {"ids": ids, "same": all(bool(torch.equal(g, gathered[0])) for g in gathered)}
+            if rank == 0:
+                single = Qwen2Model(path, device=dev, max_ctx=128, kv_dtype=torch.float32, exact_linears=exact)
+                ids1, per1 = Session(single).greedy(prompt, 8)
+                res["ids1"] = ids1
+                res["rel"] = [_rel(a.cpu().numpy(), b.cpu().numpy()) for a, b in zip(per, per1)]
+                del single
+            out[exact] = res
+            del model
+            torch.cuda.synchronize()
+            dist.barrier()
+        comm.close()
+    except BaseException as e:  # reported to the parent, which fails the test with it
+        out["error"] = f"{type(e).__name__}: {e}"
+    finally:
+        try:
+            dist.destroy_process_group()
+        finally:
+            q.put((rank, out))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_decoder(world, tmp_path):
+    # the Qwen2 decoder split over `world` GPUs (heads and FFN rows column-parallel,
+    # attn_output / ffn_down row-parallel through rtd_tp_qlinear_row) gives the logits and
+    # greedy ids of the single-GPU decoder, bit-identical on every rank
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    from runtimed_b200 import fixtures
+
+    shape = fixtures.Qwen2Shape(hidden=512, n_layer=2, n_head=8, n_kv=4, ffn=1024, vocab=1000,
+                                formats={k: 8 for k in fixtures.DEFAULT_FORMATS})
+    path = str(tmp_path / "tp.gguf")
+    fixtures.write_qwen2_gguf(path, shape, seed=4)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_model_rank_main, args=(r, world, port, path, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank, out in res.items():
+        assert "error" not in out, (rank, out.get("error"))
+        for exact in (True, False):
+            assert out[exact]["same"], (rank, exact, "ranks differ")
+            assert out[exact]["ids"] == res[0][exact]["ids"]
+    for exact, tol in ((True, 1e-5), (False, 3e-3)):
+        r0 = res[0][exact]
+        assert r0["ids"] == r0["ids1"], exact
+        assert max(r0["rel"]) <= tol, (exact, r0["rel"])

@@ -118,3 +118,39 @@ def test_fp8_scale_key_order_and_default():
     W.map["a.scale"] = torch.full((3,), 1.5)
     assert float(W.fp8_scale("a", 3)[0]) == 1.5  # ".scale" first
     assert torch.equal(W.fp8_scale("b", 4), torch.ones(4))  # none: ones of out_dim
+
+
+def test_decoder_shards_reassemble_the_full_tensors(tmp_path):
+    # Qwen2Model._shard (the TP decoder's per-rank weights): column-parallel linears keep
+    # their rows, attn_output / ffn_down their input columns, everything else is whole
+    pytest.importorskip("torch")
+    from types import SimpleNamespace
+
+    from runtimed_b200 import fixtures
+    from runtimed_b200.gguf import GgufFile
+    from runtimed_b200.qwen2 import Qwen2Model
+
+    shape = fixtures.Qwen2Shape(hidden=512, n_layer=1, n_head=8, n_kv=4, ffn=1024, vocab=300,
+                                formats={k: 8 for k in fixtures.DEFAULT_FORMATS})
+    path = str(tmp_path / "m.gguf")
+    fixtures.write_qwen2_gguf(path, shape, seed=2)
+    f = GgufFile.open(path)
+    for world in (2, 4):
+        for t in f.tensors:
+            if len(t.dims) != 2:
+                continue
+            k, n = int(t.dims[0]), int(t.dims[1])
+            rc, full = oracle.dequant_tensor(t.dtype, np.asarray(f.tensor_bytes(t)), n * k)
+            full = full.reshape(n, k)
+            parts = []
+            for r in range(world):
+                raw, ns, ks = Qwen2Model._shard(SimpleNamespace(file=f, rank=r, world=world), t.name, t)
+                rc, v = oracle.dequant_tensor(t.dtype, np.asarray(raw), ns * ks)
+                parts.append(v.reshape(ns, ks))
+            kind = t.name.split(".")[2] if t.name.startswith("blk.") else t.name
+            if kind in ("attn_q", "attn_k", "attn_v", "ffn_gate", "ffn_up"):
+                assert np.array_equal(np.concatenate(parts, axis=0), full), t.name
+            elif kind in ("attn_output", "ffn_down"):
+                assert np.array_equal(np.concatenate(parts, axis=1), full), t.name
+            else:
+                assert all(np.array_equal(p, full) for p in parts), t.name
