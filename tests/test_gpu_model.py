@@ -173,3 +173,28 @@ def test_graph_decode_matches_eager(small_model):
     torch.cuda.synchronize()
     assert [int(v) for v in out.cpu()] == ids
     del g
+
+
+def test_speculative_generate_matches_target_greedy(small_model, tmpdir_mod):
+    # greedy speculative decoding (decode/speculate.rs:17-199) reproduces the target's own
+    # greedy tokens, with a different draft (partial acceptance) and with the target
+    # as its own draft (every proposal accepted, a bonus token each round)
+    import torch
+
+    from runtimed_b200 import fixtures
+    from runtimed_b200.qwen2 import Qwen2Model, Session
+    from runtimed_b200.speculate import speculative_generate
+
+    draft_path = os.path.join(tmpdir_mod, "draft.gguf")
+    fixtures.write_qwen2_gguf(draft_path, fixtures.small_shape(n_layer=1, vocab=1000), seed=8)
+    kw = dict(max_ctx=256, kv_dtype=torch.float32, exact_linears=True)
+    target = Qwen2Model(small_model, **kw)
+    draft = Qwen2Model(draft_path, **kw)
+    prompt = list(np.random.default_rng(2).integers(0, 1000, 30))
+    want, _ = Session(target).greedy(prompt, 24)
+    st = speculative_generate(draft, target, prompt, 24, k=4)
+    assert st.tokens == want
+    assert st.proposed > 0 and st.target_forwards < 24
+    same = speculative_generate(target, Qwen2Model(small_model, **kw), prompt, 24, k=4)
+    assert same.tokens == want
+    assert same.accepted == same.proposed  # a target drafting for itself is always right
