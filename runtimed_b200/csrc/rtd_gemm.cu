@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <type_traits>
 #include <utility>
 
@@ -39,20 +40,25 @@
 namespace rtd {
 namespace {
 
-#ifndef RTD_GEMM_DECODE_WARPS
-#define RTD_GEMM_DECODE_WARPS 16
-#endif
-constexpr int kDecodeWarps = RTD_GEMM_DECODE_WARPS;  // warps 2 .. 2 + kDecodeWarps - 1
-constexpr int kGemmWarps = kDecodeWarps + 4;
-constexpr int kWarpRaw = kDecodeWarps + 2;      // packed-group producer
-constexpr int kWarpMmaOdd = kDecodeWarps + 3;   // MMA issuer of the odd k stages (warp 1: the even ones)
-constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kDecodeThreads = kDecodeWarps * 32;
-constexpr int kHalvesPerThread = 512 / kDecodeThreads;  // 16-weight halves a decode thread takes per stage
+// Warp roles of one CTA for DW decode warps (warps 2 .. 2 + DW - 1).  DW = 16: one CTA per
+// SM with the whole 227 KB; DW = 8: two CTAs per SM, each with at most 113 KB, so that two
+// independent pipelines hide each other's latencies and the grid of a skinny call fits
+// the SMs in one wave.
+template <int DW>
+struct Roles {
+  static constexpr int kDecodeWarps = DW;
+  static constexpr int kGemmWarps = DW + 4;
+  static constexpr int kWarpRaw = DW + 2;      // packed-group producer
+  static constexpr int kWarpMmaOdd = DW + 3;   // MMA issuer of the odd k stages (warp 1: the even ones)
+  static constexpr int kThreads = kGemmWarps * 32;
+  static constexpr int kDecodeThreads = DW * 32;
+  static constexpr int kHalvesPerThread = 512 / kDecodeThreads;  // 16-weight halves a thread takes per stage
+  static constexpr int kCtasPerSm = DW == 8 ? 2 : 1;
+  static constexpr int kSmem = DW == 8 ? 113 * 1024 : 227 * 1024;
+};
 constexpr int kBM = 128;             // weight rows per CTA (UMMA M)
 constexpr int kBK = 64;              // k per stage
 constexpr int kMaxStages = 8;
-constexpr int kSmemLimit = 227 * 1024;
 constexpr int kPrepThreadsG = 256;
 
 template <int FMT>
@@ -385,9 +391,9 @@ __device__ __forceinline__ void decode_q4k_pair(uint32_t raw_s, int sub, uint32_
 // (row r = 8 * (dt / 32) + dt % 8, part = (dt / 8) % 2, half h = (dt / 16) % 2); with 8
 // warps both halves of row r = 8 * (dt / 16) + dt % 8.  Eight consecutive threads
 // always hold eight consecutive rows with the same k chunk.
-template <int FMT>
+template <int FMT, int DW>
 __device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a_s, int dt) {
-  if constexpr (kHalvesPerThread == 1) {
+  if constexpr (Roles<DW>::kHalvesPerThread == 1) {
     decode_half<FMT>(raw_s, sub, a_s, 8 * (dt >> 5) + (dt & 7), (dt >> 3) & 1, (dt >> 4) & 1);
   } else {
 #pragma unroll
@@ -400,13 +406,14 @@ __device__ __forceinline__ void decode_stage(uint32_t raw_s, int sub, uint32_t a
 // groups of one k range: three for the 256-element formats, four for the 128-element
 // ones, so two groups stay in flight while one is decoded), then as many k stages
 // (decoded A tile + activation tile) as the rest of the 227 KB holds, at most 8.
-template <int FMT, int TN>
+template <int FMT, int TN, int DW>
 struct GemmSmem {
+  static constexpr int kSmemLimit = Roles<DW>::kSmem;
   static constexpr int kA = kBM * kBK * 2;                  // 16 KB
   static constexpr int kB = TN * kBK * 2;                   // TN * 128
   static constexpr int kRaw = 8 * GemmFmt<FMT>::GB;
-  static constexpr int kRawSlots = GemmFmt<FMT>::GK == 256 ? 3 : 4;
-  static constexpr int kFixed = kRawSlots * kRaw + 1024 + 512;  // + alignment slack, barriers, misc
+  static constexpr int kRawSlots = DW == 8 ? 2 : (GemmFmt<FMT>::GK == 256 ? 3 : 4);
+  static constexpr int kFixed = kRawSlots * kRaw + 1024 + 512 + TN * 4;  // + alignment slack, barriers, scales
   static constexpr int kFit = (kSmemLimit - kFixed) / (kA + kB);
   static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
   static constexpr int offA = 0;
@@ -417,13 +424,23 @@ struct GemmSmem {
   static constexpr int offMisc = offBar + nBars * 8;
   static constexpr int offScale = offMisc + 16;              // the CTA's TN token scales
   static constexpr int bytes = offScale + TN * 4 + 1024;     // + alignment slack
-  static_assert(kStages >= 3, "at least three k stages");
-  static_assert(bytes <= kSmemLimit, "shared-memory plan exceeds 227 KB");
+  static_assert(kStages >= (DW == 8 ? 2 : 3), "too few k stages");
+  static_assert(bytes <= kSmemLimit, "shared-memory plan exceeds the CTA's share");
 };
 
+// The two-CTA plan exists for tile widths whose stages fit 113 KB beside two group slots.
 template <int FMT, int TN>
-__global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a) {
-  using L = GemmSmem<FMT, TN>;
+constexpr bool two_cta_ok() {
+  constexpr int raw = 2 * 8 * GemmFmt<FMT>::GB + 1024 + 512 + TN * 4;
+  return TN <= 64 && (113 * 1024 - raw) / (kBM * kBK * 2 + TN * kBK * 2) >= 2;
+}
+
+template <int FMT, int TN, int DW>
+__global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qgemm_kernel(const GemmArgs a) {
+  using L = GemmSmem<FMT, TN, DW>;
+  using R = Roles<DW>;
+  constexpr int kDecodeWarps = R::kDecodeWarps, kWarpRaw = R::kWarpRaw, kWarpMmaOdd = R::kWarpMmaOdd;
+  constexpr int kDecodeThreads = R::kDecodeThreads;
   constexpr int SPG = GemmFmt<FMT>::GK / kBK;  // stages per group
   constexpr int GB = GemmFmt<FMT>::GB;
   // two accumulators (even / odd k stages, one MMA-issuing thread each), added in the
@@ -551,14 +568,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
       umma_commit(acc_full);  // fires once every MMA this thread issued has completed
     }
   } else {
-    // ---- decode warps 2..17 (and, afterwards, warps 4..7 run the epilogue)
-    // (the warp counts follow kDecodeWarps; 16 is the built configuration)
+    // ---- decode warps 2 .. 2 + DW - 1 (and, afterwards, warps 4..7 run the epilogue)
     const int dt = tid - 64;
-    const Q4Thread q4t = q4_thread(dt);  // used by the two-stage Q4_K decoder only
-    // With four or more stages the warps decode two consecutive stages per iteration
-    // (always within one group: SPG is 2 or 4 and kb is even), so the waits, the proxy
-    // fence and the arrivals are paid once per pair and the two decodes overlap.
-    constexpr int KPI = kStages >= 4 ? 2 : 1;
+    const Q4Thread q4t = q4_thread(dt);  // used by the Q4_K part decoder only
+    // With sixteen decode warps and four or more stages the warps decode two consecutive
+    // stages per iteration (always within one group: SPG is 2 or 4 and kb is even), so the
+    // waits, the proxy fence and the arrivals are paid once per pair and the two decodes
+    // overlap; eight decode warps take one stage per iteration.
+    constexpr int KPI = (DW == 16 && kStages >= 4) ? 2 : 1;
+    // Q4_K: one thread per (row, part) and stage -- 256 threads a stage
+    constexpr bool kQ4Parts = FMT == FMT_Q4K && kDecodeThreads == 256 * KPI;
     for (int kb = 0; kb < nkb; kb += KPI) {
       bool ok = true;
 #pragma unroll
@@ -568,7 +587,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
         if (ok && k2 >= kStages) ok = wait(&st_empty[st], (uint32_t)((k2 / kStages - 1) & 1));
       }
       if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the arrivals below are per warp
-      if constexpr (FMT == FMT_Q4K && KPI == 2 && kDecodeThreads == 512) {
+      if constexpr (kQ4Parts) {
         const int k2 = kb + (dt >> 8), s = k2 / SPG;
         decode_q4k_pair(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
                         smem_u32(sm + L::offA + (k2 % kStages) * L::kA), q4t);
@@ -576,7 +595,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const GemmArgs a
 #pragma unroll
         for (int u = 0; u < KPI; ++u) {
           const int k2 = kb + u, s = k2 / SPG;
-          decode_stage<FMT>(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
+          decode_stage<FMT, DW>(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
                             smem_u32(sm + L::offA + (k2 % kStages) * L::kA), dt);
         }
       }
@@ -854,29 +873,57 @@ cudaError_t launch_pdl(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
 }
 
-template <int FMT, int TN>
+template <int FMT, int TN, int DW>
 cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
-  using L = GemmSmem<FMT, TN>;
+  using L = GemmSmem<FMT, TN, DW>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<FMT, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::bytes);
+    cudaError_t e =
+        cudaFuncSetAttribute(qgemm_kernel<FMT, TN, DW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::bytes);
     if (e != cudaSuccess) return e;
     configured[dev & 63] = 1;
   }
   const dim3 grid((unsigned)(a.Mp / TN), (unsigned)((a.T + 7) / 8), (unsigned)a.splits);
-  return launch_pdl(qgemm_kernel<FMT, TN>, grid, dim3(kGemmThreads), (size_t)L::bytes, st, a);
+  return launch_pdl(qgemm_kernel<FMT, TN, DW>, grid, dim3(Roles<DW>::kThreads), (size_t)L::bytes, st, a);
+}
+
+template <int FMT, int TN>
+cudaError_t launch_gemm_dw(const GemmArgs& a, int dw, cudaStream_t st) {
+  if constexpr (two_cta_ok<FMT, TN>()) {
+    if (dw == 8) return launch_gemm_tn<FMT, TN, 8>(a, st);
+  }
+  return launch_gemm_tn<FMT, TN, 16>(a, st);
 }
 
 template <int FMT>
-cudaError_t launch_gemm_fmt(const GemmArgs& a, int TN, cudaStream_t st) {
+cudaError_t launch_gemm_fmt(const GemmArgs& a, int TN, int dw, cudaStream_t st) {
   switch (TN) {
-    case 16: return launch_gemm_tn<FMT, 16>(a, st);
-    case 32: return launch_gemm_tn<FMT, 32>(a, st);
-    case 64: return launch_gemm_tn<FMT, 64>(a, st);
-    case 128: return launch_gemm_tn<FMT, 128>(a, st);
-    default: return launch_gemm_tn<FMT, 256>(a, st);
+    case 16: return launch_gemm_dw<FMT, 16>(a, dw, st);
+    case 32: return launch_gemm_dw<FMT, 32>(a, dw, st);
+    case 64: return launch_gemm_dw<FMT, 64>(a, dw, st);
+    case 128: return launch_gemm_dw<FMT, 128>(a, dw, st);
+    default: return launch_gemm_dw<FMT, 256>(a, dw, st);
+  }
+}
+
+template <int FMT>
+bool two_cta_fmt(int TN) {
+  switch (TN) {
+    case 16: return two_cta_ok<FMT, 16>();
+    case 32: return two_cta_ok<FMT, 32>();
+    case 64: return two_cta_ok<FMT, 64>();
+    default: return false;
+  }
+}
+
+bool two_cta_possible(int fmt, int TN) {
+  switch (fmt) {
+    case FMT_Q4K: return two_cta_fmt<FMT_Q4K>(TN);
+    case FMT_Q6K: return two_cta_fmt<FMT_Q6K>(TN);
+    case FMT_Q80: return two_cta_fmt<FMT_Q80>(TN);
+    default: return two_cta_fmt<FMT_FP8>(TN);
   }
 }
 
@@ -887,7 +934,7 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, int TN, cudaStream_t st) {
 // adds the reduce kernel's traffic.  The candidate with the fewest estimated cycles
 // wins (ties: fewer splits, then the wider tile).
 struct GemmPlan {
-  int TN, splits;
+  int TN, splits, dw;
   int64_t Mp, kp;
   size_t xw_bytes, partial_bytes;
 };
@@ -896,8 +943,16 @@ constexpr double kDecodeStageCycles = 450.0;
 constexpr double kCtaFixedCycles = 4000.0;
 constexpr double kReduceFixedCycles = 3000.0;
 constexpr double kCyclesPerReduceByte = 1.9e9 / 3.0e12;  // ~3 TB/s at ~1.9 GHz
+// a stage of an eight-decode-warp CTA that shares its SM with a second one takes this much
+// longer than a stage of the sixteen-warp CTA alone on its SM
+constexpr double kTwoCtaStageFactor = 1.6;
 
 GemmPlan gemm_plan(const QGemvCall& c) {
+  static const int env_dw = [] {  // tuning override: RTD_GEMM_DW=8|16
+    const char* s = std::getenv("RTD_GEMM_DW");
+    const int v = s ? std::atoi(s) : 0;
+    return (v == 8 || v == 16) ? v : 0;
+  }();
   const FmtInfo f = fmt_info(c.fmt);
   const int spg = f.gk / kBK;
   const int64_t rowctas = (tiles_for(c.N) + 7) / 8;
@@ -910,17 +965,24 @@ GemmPlan gemm_plan(const QGemvCall& c) {
     if (colctas > 65535) continue;
     const int64_t Mp = colctas * TN;
     const int64_t most = std::max<int64_t>(1, std::min<int64_t>(16, c.G / 2));
-    for (int64_t s = 1; s <= most; ++s) {
-      const int64_t ctas = colctas * rowctas * s;
-      const int64_t waves = (ctas + sms - 1) / sms;
-      const int64_t stages = ((c.G + s - 1) / s) * spg;
-      double cyc = (double)waves * ((double)stages * std::max(2.0 * TN, kDecodeStageCycles) + kCtaFixedCycles);
-      if (s > 1) cyc += kReduceFixedCycles + kCyclesPerReduceByte * (double)(s * Mp * c.N * 4 + c.M * c.N * 4);
-      if (best_cyc < 0.0 || cyc < best_cyc * 0.98) {
-        best_cyc = cyc;
-        best.TN = TN;
-        best.splits = (int)s;
-        best.Mp = Mp;
+    for (int dw : {16, 8}) {
+      if (dw == 8 && !two_cta_possible(c.fmt, TN)) continue;
+      if (env_dw && dw != env_dw && !(env_dw == 8 && !two_cta_possible(c.fmt, TN))) continue;
+      const int64_t slots = sms * (dw == 8 ? 2 : 1);
+      const double stage = std::max(2.0 * TN, kDecodeStageCycles) * (dw == 8 ? kTwoCtaStageFactor : 1.0);
+      for (int64_t s = 1; s <= most; ++s) {
+        const int64_t ctas = colctas * rowctas * s;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const int64_t stages = ((c.G + s - 1) / s) * spg;
+        double cyc = (double)waves * ((double)stages * stage + kCtaFixedCycles);
+        if (s > 1) cyc += kReduceFixedCycles + kCyclesPerReduceByte * (double)(s * Mp * c.N * 4 + c.M * c.N * 4);
+        if (best_cyc < 0.0 || cyc < best_cyc * 0.98) {
+          best_cyc = cyc;
+          best.TN = TN;
+          best.splits = (int)s;
+          best.dw = dw;
+          best.Mp = Mp;
+        }
       }
     }
   }
@@ -992,10 +1054,10 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   a.splits = p.splits;
   a.partial = partial;
   switch (c.fmt) {
-    case FMT_Q4K: e = launch_gemm_fmt<FMT_Q4K>(a, TN, c.stream); break;
-    case FMT_Q6K: e = launch_gemm_fmt<FMT_Q6K>(a, TN, c.stream); break;
-    case FMT_Q80: e = launch_gemm_fmt<FMT_Q80>(a, TN, c.stream); break;
-    default: e = launch_gemm_fmt<FMT_FP8>(a, TN, c.stream); break;
+    case FMT_Q4K: e = launch_gemm_fmt<FMT_Q4K>(a, TN, p.dw, c.stream); break;
+    case FMT_Q6K: e = launch_gemm_fmt<FMT_Q6K>(a, TN, p.dw, c.stream); break;
+    case FMT_Q80: e = launch_gemm_fmt<FMT_Q80>(a, TN, p.dw, c.stream); break;
+    default: e = launch_gemm_fmt<FMT_FP8>(a, TN, p.dw, c.stream); break;
   }
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;

@@ -207,3 +207,47 @@ def test_lm_head_vocab_152064(name, t):
         want = oracle.qgemv_f64(t, sub, len(rows), K, x)
         got = y[:, torch.from_numpy(rows).cuda()].cpu().numpy()
         assert rel_l2(got, want) <= (RTOL if M >= 4 else 2e-5), M
+
+
+_TWO_CTA_CHILD = r'''
+import json, sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+import oracle
+from runtimed_b200 import synth
+from runtimed_b200.weights import Fp8Weight, QMatMul
+out = {}
+for t in (12, 14, 8, 0):
+    N, K = 1000, 2048
+    for M in (5, 17, 40, 64):
+        x = synth.bf16_round(synth.activations(M, K, seed=M, stream=t))
+        if t == 0:
+            w, s = synth.fp8_matrix(N, K, seed=M)
+            y = Fp8Weight(w, s, K, N).forward(torch.from_numpy(x).cuda()).cpu().numpy()
+            want = oracle.fp8_gemm_cpu_f64(x, w, s, N, K)
+        else:
+            raw = synth.quant_matrix(t, N, K, seed=M, stream=t)
+            y = QMatMul(t, raw, N, K).forward(torch.from_numpy(x).to(torch.bfloat16).cuda(),
+                                             out_dtype=torch.float32).cpu().numpy()
+            want = oracle.qgemv_f64(t, raw, N, K, x)
+        out[f"{t}:{M}"] = float(np.linalg.norm(y - want) / np.linalg.norm(want))
+print(json.dumps(out))
+'''
+
+
+@pytest.mark.parametrize("dw", ["8", "16"])
+def test_gemm_both_cta_configurations(dw):
+    # the GEMM's two shapes of CTA -- sixteen decode warps alone on an SM, or eight with a
+    # second CTA beside it -- forced in a child process (RTD_GEMM_DW is read once), every
+    # format at skinny token counts against the oracle
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, RTD_GEMM_DW=dw)
+    r = subprocess.run([sys.executable, "-c", _TWO_CTA_CHILD, root], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    errs = json.loads(r.stdout.strip().splitlines()[-1])
+    assert max(errs.values()) <= RTOL, errs
