@@ -606,7 +606,61 @@ def _m_sweep(dev, rank, tflops_peak):
                                 "frac": round(tf / tflops_peak, 3) if tflops_peak else None}
         out[name] = row
         del objs
+    out["FP8_W8A8"] = _fp8_w8a8_vs_cublaslt(dev, n, k, tflops_peak)
     return out
+
+
+def _fp8_w8a8_vs_cublaslt(dev, n, k, tflops_peak):
+    """FP8 W8A8 (the reference's CUDA semantics: x encoded to E4M3, E4M3 x E4M3 with f32
+    accumulation, per-channel scale after) through rtd_fp8_linear -- the kind::f8f6f4 GEMM
+    from four tokens on -- beside cuBLASLt's FP8 GEMM (torch._scaled_mm, per-tensor scales)
+    on the same shapes; each a CUDA graph of 10 calls over 3 weight copies, 5 replays."""
+    import torch
+    from runtimed_b200 import _lib, synth
+    from runtimed_b200.weights import Fp8Weight
+
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    objs, mats = [], []
+    for c in range(3):
+        w, sc = synth.fp8_matrix(n, k, seed=40 + c, stream=k)
+        objs.append(Fp8Weight(w, sc, k, n, device=dev))
+        mats.append(torch.from_numpy(w).view(torch.float8_e4m3fn).to(dev))
+    one = torch.ones((), dtype=torch.float32, device=dev)
+    row = {}
+    for m in (64, 512, 2048):
+        x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        x8 = x.to(torch.float8_e4m3fn)
+
+        def ours(o, st):
+            rc = L.rtd_fp8_linear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, y.data_ptr(),
+                                  _lib.DT_BF16, n, _lib.FP8_W8A8, st)
+            if rc != 0:
+                raise RuntimeError(f"fp8 w8a8 M={m}: status {rc}")
+
+        def lt(wm):
+            return torch._scaled_mm(x8, wm.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+        res = {}
+        for label, fn in (("ours", lambda r, st: ours(objs[r % 3], st)), ("cublaslt", lambda r, st: lt(mats[r % 3]))):
+            try:
+                for r in range(3):
+                    fn(r, stream.cuda_stream)
+                torch.cuda.synchronize(dev)
+                g = _capture(lambda st: [fn(r, st) for r in range(10)], dev)
+                g.replay()
+                us = _time_graph(g, stream, dev, 5) * 1e6 / 10
+                del g
+                tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+                res[label] = {"us": round(us, 2), "tflops": round(tf, 1),
+                              "frac_bf16_peak": round(tf / tflops_peak, 3) if tflops_peak else None}
+            except Exception as e:  # noqa: BLE001 - the comparison arm is reported, not required
+                res[label] = {"error": f"{type(e).__name__}: {e}"}
+        row[f"m{m}"] = res
+    row["note"] = "ours: rtd_fp8_linear W8A8 (E4M3 activations by the reference encoder); cublaslt: " \
+                  "torch._scaled_mm E4M3 x E4M3, per-tensor scales (timing comparison only)"
+    return row
 
 
 def _model_decode(dev, steps: int = 128, warm: int = 8):

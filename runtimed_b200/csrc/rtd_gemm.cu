@@ -61,8 +61,17 @@ constexpr int kBK = 64;              // k per stage
 constexpr int kMaxStages = 8;
 constexpr int kPrepThreadsG = 256;
 
+// FP8 weights with E4M3-encoded activations (W8A8): the E4M3 tiles enter
+// tcgen05.mma.kind::f8f6f4 as they are, so the "decode" warps only move 16-byte units
+// into the swizzled layout.  An internal id beside the layout formats of rtd_layout.h.
+constexpr int FMT_F8X = 4;
+
 template <int FMT>
 struct GemmFmt;
+template <>
+struct GemmFmt<FMT_F8X> {
+  static constexpr int GK = 128, GB = 2048;
+};
 template <>
 struct GemmFmt<FMT_Q4K> {
   static constexpr int GK = 256, GB = 2304;
@@ -85,7 +94,7 @@ struct GemmArgs {
   const float* row_scale;  // FP8
   int scale_len;
   int64_t N, T, G;         // rows, 16-row tiles, groups per row
-  int nkb;                 // 64-element k blocks
+  int nkb;                 // k stages (64 elements; 128 on the kind::f8f6f4 path)
   const __half* xw;        // staged activations [nkb][Mp / 8][1024-byte swizzled atom]
   const float* tscale;     // [Mp] per-token scale
   int64_t M, Mp;
@@ -122,6 +131,16 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+// The same with E4M3 x E4M3 operands (K = 32 per instruction): tcgen05.mma.kind::f8f6f4.
+__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
@@ -174,7 +193,8 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor: f16 x f16 -> f32, both operands K-major, UMMA M = 128.
+// Instruction descriptor: f16 x f16 -> f32 (kind::f16), or E4M3 x E4M3 -> f32
+// (kind::f8f6f4: the A / B format fields hold 0 = E4M3), both operands K-major, UMMA M = 128.
 __host__ __device__ constexpr uint32_t idesc_f16(int n) {
   return (1u << 4)                          // D format f32
          | (0u << 7) | (0u << 10)           // A, B f16
@@ -387,6 +407,20 @@ __device__ __forceinline__ void decode_q4k_pair(uint32_t raw_s, int sub, uint32_
   sts128(a_s + t.st[3], hi[4], hi[5], hi[6], hi[7]);
 }
 
+// FP8 (W8A8): the stage's eight groups move unit by unit (16 E4M3 codes = 16 bytes) from
+// the lane-owned group layout (rtd_layout.h: pass p, lane 4g + t -> row g + 8 (p >= 2),
+// codes 32t + 16 (p & 1) ..) into the 128-byte swizzled K-major tile, unchanged.
+template <int NTH>
+__device__ __forceinline__ void copy_stage_f8(uint32_t raw_s, uint32_t a_s, int dt) {
+#pragma unroll
+  for (int u = dt; u < 1024; u += NTH) {
+    const int i = u >> 7, w = u & 127, p = w >> 5, L = w & 31, g = L >> 2, t = L & 3;
+    const int r = 16 * i + g + 8 * (p >> 1), c = 2 * t + (p & 1);
+    const uint4 v = lds128(raw_s + (uint32_t)(i * 2048 + p * 512 + L * 16));
+    sts128(a_s + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4)), v.x, v.y, v.z, v.w);
+  }
+}
+
 // Thread dt of the decode warps: with 16 warps it decodes one 16-weight half of a row
 // (row r = 8 * (dt / 32) + dt % 8, part = (dt / 8) % 2, half h = (dt / 16) % 2); with 8
 // warps both halves of row r = 8 * (dt / 16) + dt % 8.  Eight consecutive threads
@@ -441,7 +475,9 @@ __global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qg
   using R = Roles<DW>;
   constexpr int kDecodeWarps = R::kDecodeWarps, kWarpRaw = R::kWarpRaw, kWarpMmaOdd = R::kWarpMmaOdd;
   constexpr int kDecodeThreads = R::kDecodeThreads;
-  constexpr int SPG = GemmFmt<FMT>::GK / kBK;  // stages per group
+  constexpr bool F8 = FMT == FMT_F8X;
+  constexpr int KST = F8 ? 128 : kBK;          // k per stage (a stage is 128 bytes of every row)
+  constexpr int SPG = GemmFmt<FMT>::GK / KST;  // stages per group
   constexpr int GB = GemmFmt<FMT>::GB;
   // two accumulators (even / odd k stages, one MMA-issuing thread each), added in the
   // epilogue in a fixed order
@@ -562,7 +598,12 @@ __global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qg
         tc_fence_after();
         const uint64_t da = da0 + (uint64_t)((st * L::kA) >> 4), db = db0 + (uint64_t)((st * L::kB) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) umma_f16(acc, da + 2 * kk, db + 2 * kk, idesc, (kb > 1 || kk) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {  // four K slices of 32 bytes
+          if constexpr (F8)
+            umma_f8(acc, da + 2 * kk, db + 2 * kk, idesc, (kb > 1 || kk) ? 1u : 0u);
+          else
+            umma_f16(acc, da + 2 * kk, db + 2 * kk, idesc, (kb > 1 || kk) ? 1u : 0u);
+        }
         umma_commit(&st_empty[st]);
       }
       umma_commit(acc_full);  // fires once every MMA this thread issued has completed
@@ -587,7 +628,14 @@ __global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qg
         if (ok && k2 >= kStages) ok = wait(&st_empty[st], (uint32_t)((k2 / kStages - 1) & 1));
       }
       if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the arrivals below are per warp
-      if constexpr (kQ4Parts) {
+      if constexpr (F8) {
+#pragma unroll
+        for (int u = 0; u < KPI; ++u) {
+          const int k2 = kb + u;
+          copy_stage_f8<kDecodeThreads>(smem_u32(sm + L::offRaw + ((k2 / SPG) % kRawSlots) * L::kRaw),
+                                        smem_u32(sm + L::offA + (k2 % kStages) * L::kA), dt);
+        }
+      } else if constexpr (kQ4Parts) {
         const int k2 = kb + (dt >> 8), s = k2 / SPG;
         decode_q4k_pair(smem_u32(sm + L::offRaw + (s % kRawSlots) * L::kRaw), k2 % SPG,
                         smem_u32(sm + L::offA + (k2 % kStages) * L::kA), q4t);
@@ -621,7 +669,7 @@ __global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qg
       const int64_t n = tile0 * 16 + r;
       float es = 1.0f, eb = 0.0f;
       if (n < a.N) {
-        if (FMT == FMT_FP8) es = a.row_scale[a.scale_len == 1 ? 0 : n];
+        if (FMT == FMT_FP8 || F8) es = a.row_scale[a.scale_len == 1 ? 0 : n];
         if (a.bias) eb = a.bias[n];
       }
 #pragma unroll 1
@@ -802,6 +850,43 @@ __global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_kernel(const void* x,
   }
 }
 
+// W8A8 staging for the kind::f8f6f4 GEMM: every activation becomes the E4M3 code of the
+// reference encoder's value (unscaled, ties toward the lower magnitude, saturating at 448:
+// fp8_gemm.rs:96-101), 16 codes a unit, in the same swizzled layout as the f16 staging
+// (128 bytes of a row per stage); the per-token scale is 1.
+template <int XDT>
+__global__ void __launch_bounds__(kPrepThreadsG) gemm_prep_f8_kernel(const void* x, int64_t ldx, int64_t M,
+                                                                     int64_t Mp, int64_t K, int64_t kp, uint8_t* xw,
+                                                                     float* tscale) {
+  pdl_trigger();
+  pdl_wait();  // x may be the previous kernel's output
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x == 0) tscale[t] = 1.0f;
+  const int64_t units = kp / 16, tg = t >> 3, r = t & 7;
+  for (int64_t u = threadIdx.x; u < units; u += kPrepThreadsG) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (t < M) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int64_t k = 16 * u + e;
+        float f = 0.0f;
+        if (k < K) {
+          if (XDT == 0)
+            f = __ldg(static_cast<const float*>(x) + t * ldx + k);
+          else {
+            const unsigned short b = __ldg(static_cast<const unsigned short*>(x) + t * ldx + k);
+            f = XDT == 1 ? __half2float(__ushort_as_half(b)) : __uint_as_float((uint32_t)b << 16);
+          }
+        }
+        w[e >> 2] |= (uint32_t)e4m3_code_of_value(e4m3_round_ref(f)) << (8 * (e & 3));
+      }
+    }
+    const int64_t kb = u / 8, c = u % 8;
+    uint8_t* dst = xw + ((size_t)kb * (Mp / 8) + (size_t)tg) * 1024 + (size_t)r * 128 + (size_t)((c ^ r) & 7) * 16;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // y[t, n] = sum over splits of the partials, scaled and biased as the GEMM epilogue
 // does; four consecutive n per thread (one 16-byte load per split) when N % 4 == 0.
 __device__ __forceinline__ void reduce_store(void* y, int y_dtype, int64_t off, float v) {
@@ -923,9 +1008,15 @@ bool two_cta_possible(int fmt, int TN) {
     case FMT_Q4K: return two_cta_fmt<FMT_Q4K>(TN);
     case FMT_Q6K: return two_cta_fmt<FMT_Q6K>(TN);
     case FMT_Q80: return two_cta_fmt<FMT_Q80>(TN);
+    case FMT_F8X: return two_cta_fmt<FMT_F8X>(TN);
     default: return two_cta_fmt<FMT_FP8>(TN);
   }
 }
+
+// The GEMM's format of a call: FP8 weights with W8A8 activations take the kind::f8f6f4 path.
+int gemm_fmt(const QGemvCall& c) { return (c.fmt == FMT_FP8 && c.w8a8) ? FMT_F8X : c.fmt; }
+// k elements of a 128-byte stage row
+int gemm_kst(int gfmt) { return gfmt == FMT_F8X ? 128 : kBK; }
 
 // Tile width and K splits from a cost model of one launch (one CTA per SM fits in
 // shared memory, so CTAs run in waves of sm_count): a k stage costs the longer of its
@@ -946,6 +1037,7 @@ constexpr double kCyclesPerReduceByte = 1.9e9 / 3.0e12;  // ~3 TB/s at ~1.9 GHz
 // a stage of an eight-decode-warp CTA that shares its SM with a second one takes this much
 // longer than a stage of the sixteen-warp CTA alone on its SM
 constexpr double kTwoCtaStageFactor = 1.6;
+constexpr double kCopyStageCycles = 150.0;
 
 GemmPlan gemm_plan(const QGemvCall& c) {
   static const int env_dw = [] {  // tuning override: RTD_GEMM_DW=8|16
@@ -954,7 +1046,8 @@ GemmPlan gemm_plan(const QGemvCall& c) {
     return (v == 8 || v == 16) ? v : 0;
   }();
   const FmtInfo f = fmt_info(c.fmt);
-  const int spg = f.gk / kBK;
+  const int gfmt = gemm_fmt(c);
+  const int spg = f.gk / gemm_kst(gfmt);
   const int64_t rowctas = (tiles_for(c.N) + 7) / 8;
   const int64_t sms = c.sm_count > 0 ? c.sm_count : 148;
   GemmPlan best{};
@@ -966,10 +1059,12 @@ GemmPlan gemm_plan(const QGemvCall& c) {
     const int64_t Mp = colctas * TN;
     const int64_t most = std::max<int64_t>(1, std::min<int64_t>(16, c.G / 2));
     for (int dw : {16, 8}) {
-      if (dw == 8 && !two_cta_possible(c.fmt, TN)) continue;
-      if (env_dw && dw != env_dw && !(env_dw == 8 && !two_cta_possible(c.fmt, TN))) continue;
+      if (dw == 8 && !two_cta_possible(gfmt, TN)) continue;
+      if (env_dw && dw != env_dw && !(env_dw == 8 && !two_cta_possible(gfmt, TN))) continue;
       const int64_t slots = sms * (dw == 8 ? 2 : 1);
-      const double stage = std::max(2.0 * TN, kDecodeStageCycles) * (dw == 8 ? kTwoCtaStageFactor : 1.0);
+      // a kind::f8f6f4 stage moves units instead of decoding them
+      const double work = gfmt == FMT_F8X ? kCopyStageCycles : kDecodeStageCycles;
+      const double stage = std::max(2.0 * TN, work) * (dw == 8 ? kTwoCtaStageFactor : 1.0);
       for (int64_t s = 1; s <= most; ++s) {
         const int64_t ctas = colctas * rowctas * s;
         const int64_t waves = (ctas + slots - 1) / slots;
@@ -987,7 +1082,7 @@ GemmPlan gemm_plan(const QGemvCall& c) {
     }
   }
   best.kp = c.G * f.gk;
-  best.xw_bytes = (size_t)best.Mp * (size_t)best.kp * 2;
+  best.xw_bytes = (size_t)best.Mp * (size_t)best.kp * (gfmt == FMT_F8X ? 1 : 2);
   best.partial_bytes = best.splits > 1 ? (size_t)best.splits * (size_t)best.Mp * (size_t)c.N * 4 : 0;
   return best;
 }
@@ -1026,7 +1121,13 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   using T2 = std::integral_constant<int, 2>;
   using Yes = std::true_type;
   using No = std::false_type;
-  if (c.fmt == FMT_Q4K) {  // Q4_K takes no W8A8 (an FP8-only mode)
+  const int gfmt = gemm_fmt(c);
+  if (gfmt == FMT_F8X) {  // E4M3 codes for the kind::f8f6f4 path
+    uint8_t* x8 = reinterpret_cast<uint8_t*>(xw);
+    e = c.x_dtype == 0   ? launch_pdl(gemm_prep_f8_kernel<0>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, x8, tscale)
+        : c.x_dtype == 1 ? launch_pdl(gemm_prep_f8_kernel<1>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, x8, tscale)
+                         : launch_pdl(gemm_prep_f8_kernel<2>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, x8, tscale);
+  } else if (c.fmt == FMT_Q4K) {  // Q4_K takes no W8A8 (an FP8-only mode)
     e = c.x_dtype == 0 ? prep(T0{}, No{}, Yes{}) : c.x_dtype == 1 ? prep(T1{}, No{}, Yes{}) : prep(T2{}, No{}, Yes{});
   } else if (c.w8a8) {
     e = c.x_dtype == 0 ? prep(T0{}, Yes{}, No{}) : c.x_dtype == 1 ? prep(T1{}, Yes{}, No{}) : prep(T2{}, Yes{}, No{});
@@ -1041,7 +1142,7 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   a.N = c.N;
   a.T = tiles_for(c.N);
   a.G = c.G;
-  a.nkb = (int)(kp / kBK);
+  a.nkb = (int)(kp / gemm_kst(gfmt));
   a.xw = xw;
   a.tscale = tscale;
   a.M = c.M;
@@ -1057,7 +1158,10 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
     case FMT_Q4K: e = launch_gemm_fmt<FMT_Q4K>(a, TN, p.dw, c.stream); break;
     case FMT_Q6K: e = launch_gemm_fmt<FMT_Q6K>(a, TN, p.dw, c.stream); break;
     case FMT_Q80: e = launch_gemm_fmt<FMT_Q80>(a, TN, p.dw, c.stream); break;
-    default: e = launch_gemm_fmt<FMT_FP8>(a, TN, p.dw, c.stream); break;
+    default:
+      e = gfmt == FMT_F8X ? launch_gemm_fmt<FMT_F8X>(a, TN, p.dw, c.stream)
+                          : launch_gemm_fmt<FMT_FP8>(a, TN, p.dw, c.stream);
+      break;
   }
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;

@@ -251,3 +251,22 @@ def test_gemm_both_cta_configurations(dw):
     assert r.returncode == 0, r.stderr[-2000:]
     errs = json.loads(r.stdout.strip().splitlines()[-1])
     assert max(errs.values()) <= RTOL, errs
+
+
+@pytest.mark.parametrize("M", [4, 40, 512])
+def test_fp8_w8a8_tensor_core_path(M):
+    # W8A8 from four tokens on runs tcgen05.mma.kind::f8f6f4 on the E4M3 codes themselves
+    # (no decode); E4M3 x E4M3 products are exact in f32, so the result sits at f32
+    # accumulation error from the restated reference semantics
+    import torch
+    from runtimed_b200.weights import Fp8Weight
+
+    N, K = 300, 1000 + 24  # ragged K: a zero-padded trailing group
+    w, s = synth.fp8_matrix(N, K, seed=M)
+    x = synth.activations(M, K, seed=M + 1)
+    fw = Fp8Weight(w, s, K, N)
+    for dt in (torch.float32, torch.bfloat16):
+        xt = torch.from_numpy(x).to(dt)
+        y = fw.forward(xt.cuda(), mode="w8a8").float().cpu().numpy()
+        want = oracle.fp8_gemm_w8a8_f64(xt.float().numpy(), w, s, N, K)
+        assert rel_l2(y, want) <= 2e-6, dt
