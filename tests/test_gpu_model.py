@@ -177,8 +177,8 @@ def test_graph_decode_matches_eager(small_model):
 
 def test_speculative_generate_matches_target_greedy(small_model, tmpdir_mod):
     # greedy speculative decoding (decode/speculate.rs:17-199) reproduces the target's own
-    # greedy tokens, with a different draft (partial acceptance) and with the target
-    # as its own draft (every proposal accepted, a bonus token each round)
+    # greedy tokens, with a different draft and with the target as its own draft (every
+    # proposal accepted, a bonus token each round)
     import torch
 
     from runtimed_b200 import fixtures
@@ -194,7 +194,10 @@ def test_speculative_generate_matches_target_greedy(small_model, tmpdir_mod):
     want, _ = Session(target).greedy(prompt, 24)
     st = speculative_generate(draft, target, prompt, 24, k=4)
     assert st.tokens == want
-    assert st.proposed > 0 and st.target_forwards < 24
+    # two unrelated random models rarely agree, so acceptance may be zero; every round
+    # still yields at least one target token
+    assert st.proposed > 0 and st.target_forwards <= len(want)
     same = speculative_generate(target, Qwen2Model(small_model, **kw), prompt, 24, k=4)
     assert same.tokens == want
     assert same.accepted == same.proposed  # a target drafting for itself is always right
+    assert same.target_forwards < len(want)  # k accepted plus a bonus token per round
