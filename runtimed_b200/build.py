@@ -22,7 +22,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libruntimed_b200.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["rtd_api.cu", "rtd_gemv.cu", "rtd_gemm.cu", "rtd_tp.cu", "rtd_model.cu", "rtd_dequant.cu", "rtd_repack.cpp"]
+SOURCES = ["rtd_api.cu", "rtd_gemv.cu", "rtd_gemm.cu", "rtd_gemm_ts.cu", "rtd_tp.cu", "rtd_model.cu", "rtd_dequant.cu", "rtd_repack.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -36,6 +36,7 @@
 
 #include "rtd_common.cuh"
 #include "rtd_kernels.h"
+#include "rtd_tcgen05.cuh"
 
 namespace rtd {
 namespace {
@@ -64,7 +65,7 @@ constexpr int kPrepThreadsG = 256;
 // FP8 weights with E4M3-encoded activations (W8A8): the E4M3 tiles enter
 // tcgen05.mma.kind::f8f6f4 as they are, so the "decode" warps only move 16-byte units
 // into the swizzled layout.  An internal id beside the layout formats of rtd_layout.h.
-constexpr int FMT_F8X = 4;
+constexpr int FMT_F8X = FMT_TS_F8X;
 
 template <int FMT>
 struct GemmFmt;
@@ -107,162 +108,10 @@ struct GemmArgs {
   float* partial;          // [splits][Mp][N] when splits > 1
 };
 
-// ---------------------------------------------------------------- tcgen05
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// D[tmem] (+)= A[smem desc] . B[smem desc]^T, both K-major f16, f32 accumulate.
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-// The same with E4M3 x E4M3 operands (K = 32 per instruction): tcgen05.mma.kind::f8f6f4.
-__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-// Sixteen accumulator columns of this warp's TMEM lane quarter: two loads, one wait;
-// the registers pass through the wait so no use is scheduled before it.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                 "=r"(r[15])
-               : "r"(taddr + 8u));
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                 "+r"(r[15])
-               :
-               : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// Programmatic dependent launch: the three kernels of a call (prep, GEMM, reduce) are
-// chained so each can start its independent work while the previous one runs.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
-__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major f16 operand in the 128-byte swizzled
-// layout: each row's 64 k (128 bytes) is one line, eight lines form a 1024-byte atom
-// (stride byte offset), and the 16-byte chunk c of row r sits at chunk c ^ (r % 8).
-// The tile base is 1024-byte aligned; the k-th K=16 slice starts 32 * k bytes in.
-// Descriptor version 1 (sm_100), layout type 2 (128-byte swizzle).
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;             // leading byte offset: unused for swizzled K-major
-  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Instruction descriptor: f16 x f16 -> f32 (kind::f16), or E4M3 x E4M3 -> f32
-// (kind::f8f6f4: the A / B format fields hold 0 = E4M3), both operands K-major, UMMA M = 128.
-__host__ __device__ constexpr uint32_t idesc_f16(int n) {
-  return (1u << 4)                          // D format f32
-         | (0u << 7) | (0u << 10)           // A, B f16
-         | ((uint32_t)(n >> 3) << 17)       // N / 8
-         | ((uint32_t)(kBM >> 4) << 24);    // M / 16
-}
-
-// Byte offset of the 8-element chunk holding (row r, k .. k+7), k % 8 == 0, in a
-// swizzled K-major tile of 64 k.
-__device__ __forceinline__ uint32_t sw_off(int r, int k) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ r) & 7) << 4));
-}
-
-__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-__device__ __forceinline__ float hbits(uint32_t b16) { return __half2float(__ushort_as_half((unsigned short)b16)); }
-
-// ---------------------------------------------------------------- shared loads
-// Explicit ld.shared on 32-bit shared addresses: the stage buffers are addressed
-// through an aligned offset of the dynamic shared array, which the compiler can no
-// longer prove to be shared memory, and generic loads cost an address-space check
-// and long-scoreboard latency on every access.
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-  unsigned short v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-  return v;
-}
-
-// Q4_K scale / min pair j (0..7) from the 12 packed scale bytes held as three words
-// (bytes 0-3, 4-7, 8-11): the same bit selection as scale_min_k4 (dequant_k.rs:8-16).
-__device__ __forceinline__ void scale_min_words(int j, uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sc,
-                                                uint32_t& m) {
-  const int sh = 8 * (j & 3);
-  const uint32_t b0 = (s0 >> sh) & 0xFFu, b1 = (s1 >> sh) & 0xFFu;
-  if (j < 4) {
-    sc = b0 & 63u;
-    m = b1 & 63u;
-  } else {
-    const uint32_t b2 = (s2 >> sh) & 0xFFu;
-    sc = (b2 & 0xFu) | ((b0 >> 6) << 4);
-    m = (b2 >> 4) | ((b1 >> 6) << 4);
-  }
-}
-
 // ---------------------------------------------------------------- stage decode
 // Codes become f16 pairs without the conversion pipe: 0x6400 | v is the f16 1024 + v
 // (v < 1024), and subtracting 1024 (+ a bias) is exact.  The weight is then one f16
 // FMA / multiply per pair with the factor (and offset) rounded once from f32.
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ __half2 h2_const(float v) { return __float2half2_rn(v); }
 
 // 16 weights of row r of the CTA tile (tile i = r / 16, row rr = r % 16 = g + 8 * hrow):
 // part and h pick its 16 of the stage's 64 k.  Eight consecutive threads share
@@ -939,25 +788,6 @@ __global__ void gemm_reduce_kernel(const float* partial, int splits, int64_t Mp,
   }
 }
 
-// Launch with programmatic stream serialization: the kernel may start before the
-// previous kernel in the stream completes; it calls griddepcontrol.wait before it reads
-// anything that kernel writes.
-template <typename... P, typename... A>
-cudaError_t launch_pdl(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  count_launch();
-  return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
-}
-
 template <int FMT, int TN, int DW>
 cudaError_t launch_gemm_tn(const GemmArgs& a, cudaStream_t st) {
   using L = GemmSmem<FMT, TN, DW>;
@@ -1026,6 +856,7 @@ int gemm_kst(int gfmt) { return gfmt == FMT_F8X ? 128 : kBK; }
 // wins (ties: fewer splits, then the wider tile).
 struct GemmPlan {
   int TN, splits, dw;
+  bool ts;  // the skinny kernel of rtd_gemm_ts.cu (decoded weights in tensor memory)
   int64_t Mp, kp;
   size_t xw_bytes, partial_bytes;
 };
@@ -1039,7 +870,53 @@ constexpr double kCyclesPerReduceByte = 1.9e9 / 3.0e12;  // ~3 TB/s at ~1.9 GHz
 constexpr double kTwoCtaStageFactor = 1.6;
 constexpr double kCopyStageCycles = 150.0;
 
+// The skinny kernel (up to 64 tokens a CTA): per weight group (GK k x 128 rows) a CTA
+// pays the longer of the group's decode into tensor memory and its MMAs; the whole call
+// cannot beat streaming its weight bytes at the HBM rate.
+constexpr double kTsDecodeGroupCycles[5] = {620.0, 740.0, 280.0, 150.0, 60.0};  // by GEMM format
+constexpr double kTsCtaFixedCycles = 3000.0;
+constexpr double kHbmBytesPerCycle = 6.5e12 / 1.9e9;
+
+GemmPlan gemm_plan_ts(const QGemvCall& c, int gfmt) {
+  const FmtInfo f = fmt_info(c.fmt);
+  const int TN = c.M <= 16 ? 16 : c.M <= 32 ? 32 : 64;
+  const int64_t rowctas = (tiles_for(c.N) + 7) / 8, colctas = (c.M + TN - 1) / TN;
+  const int64_t sms = c.sm_count > 0 ? c.sm_count : 148;
+  const int nmma = f.gk == 256 ? 16 : (gfmt == FMT_F8X ? 4 : 8);
+  const double stage = std::max(kTsDecodeGroupCycles[gfmt], (double)nmma * TN / 2.0);
+  const double hbm = (double)tiles_for(c.N) * (double)c.G * f.gb * (double)colctas / kHbmBytesPerCycle;
+  GemmPlan best{};
+  double best_cyc = -1.0;
+  const int64_t most = std::max<int64_t>(1, std::min<int64_t>(16, c.G / 2));
+  for (int64_t s = 1; s <= most; ++s) {
+    const int64_t ctas = rowctas * colctas * s;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const double cta = (double)((c.G + s - 1) / s) * stage + kTsCtaFixedCycles;
+    double cyc = std::max((double)waves * cta, hbm + kTsCtaFixedCycles);
+    if (s > 1) cyc += kReduceFixedCycles + kCyclesPerReduceByte * (double)(s * TN * colctas * c.N * 4 + c.M * c.N * 4);
+    if (best_cyc < 0.0 || cyc < best_cyc * 0.98) {
+      best_cyc = cyc;
+      best.splits = (int)s;
+    }
+  }
+  best.TN = TN;
+  best.dw = 16;
+  best.ts = true;
+  best.Mp = colctas * TN;
+  best.kp = c.G * f.gk;
+  best.xw_bytes = (size_t)best.Mp * (size_t)best.kp * (gfmt == FMT_F8X ? 1 : 2);
+  best.partial_bytes = best.splits > 1 ? (size_t)best.splits * (size_t)best.Mp * (size_t)c.N * 4 : 0;
+  return best;
+}
+
 GemmPlan gemm_plan(const QGemvCall& c) {
+  static const int env_ts = [] {  // RTD_GEMM_TS=0 keeps skinny calls on the shared-memory GEMM
+    const char* s = std::getenv("RTD_GEMM_TS");
+    return s ? std::atoi(s) : 1;
+  }();
+  // (W8A8 rounding of f16-staged activations is the shared-memory kernel's; FP8 W8A8 runs
+  // kind::f8f6f4 on either kernel)
+  if (env_ts != 0 && c.M <= 64 && (!c.w8a8 || gemm_fmt(c) == FMT_F8X)) return gemm_plan_ts(c, gemm_fmt(c));
   static const int env_dw = [] {  // tuning override: RTD_GEMM_DW=8|16
     const char* s = std::getenv("RTD_GEMM_DW");
     const int v = s ? std::atoi(s) : 0;
@@ -1122,7 +999,9 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   using Yes = std::true_type;
   using No = std::false_type;
   const int gfmt = gemm_fmt(c);
-  if (gfmt == FMT_F8X) {  // E4M3 codes for the kind::f8f6f4 path
+  if (p.ts) {  // the decoder's k order (rtd_gemm_ts.cu)
+    e = launch_ts_prep(c, gfmt, Mp, kp, xw, tscale);
+  } else if (gfmt == FMT_F8X) {  // E4M3 codes for the kind::f8f6f4 path
     uint8_t* x8 = reinterpret_cast<uint8_t*>(xw);
     e = c.x_dtype == 0   ? launch_pdl(gemm_prep_f8_kernel<0>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, x8, tscale)
         : c.x_dtype == 1 ? launch_pdl(gemm_prep_f8_kernel<1>, pg, pb, 0, c.stream, c.x, c.ldx, c.M, Mp, c.K, kp, x8, tscale)
@@ -1135,6 +1014,29 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
     e = c.x_dtype == 0 ? prep(T0{}, No{}, No{}) : c.x_dtype == 1 ? prep(T1{}, No{}, No{}) : prep(T2{}, No{}, No{});
   }
   if (e != cudaSuccess) return e;
+  if (p.ts) {
+    TsGemm g{};
+    g.fmt = gfmt;
+    g.w = c.w;
+    g.row_scale = c.fmt == FMT_FP8 ? c.row_scale : nullptr;
+    g.scale_len = c.scale_len;
+    g.N = c.N;
+    g.T = tiles_for(c.N);
+    g.G = c.G;
+    g.M = c.M;
+    g.Mp = Mp;
+    g.TN = TN;
+    g.splits = p.splits;
+    g.xw = xw;
+    g.tscale = tscale;
+    g.bias = c.bias;
+    g.y = c.y;
+    g.y_dtype = c.y_dtype;
+    g.ldy = c.ldy;
+    g.status = c.status;
+    g.partial = partial;
+    e = launch_ts_gemm(g, c.stream);
+  } else {
   GemmArgs a{};
   a.w = c.w;
   a.row_scale = c.row_scale;
@@ -1162,6 +1064,7 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
       e = gfmt == FMT_F8X ? launch_gemm_fmt<FMT_F8X>(a, TN, p.dw, c.stream)
                           : launch_gemm_fmt<FMT_FP8>(a, TN, p.dw, c.stream);
       break;
+  }
   }
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;

@@ -91,6 +91,32 @@ size_t qgemv_workspace_bytes(const QGemvCall& c);
 cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error);
 size_t qgemm_workspace_bytes(const QGemvCall& c);
 
+// The skinny tensor-core GEMM (rtd_gemm_ts.cu): decoded weights written to tensor memory,
+// 16..64 tokens a CTA.  launch_qgemm plans the call and runs the prep, this GEMM and (K
+// split over CTAs) the reduce.  fmt: FMT_* or FMT_TS_F8X (FP8 weights x E4M3 activations).
+constexpr int FMT_TS_F8X = 4;
+struct TsGemm {
+  int fmt;
+  const uint8_t* w;
+  const float* row_scale;  // FP8 only (else null)
+  int scale_len;
+  int64_t N, T, G;         // rows, 16-row tiles, groups per row
+  int64_t M, Mp;           // tokens, tokens padded to TN
+  int TN, splits;
+  const void* xw;          // staged activations (launch_ts_prep)
+  const float* tscale;     // [Mp] per-token scale
+  const float* bias;
+  void* y;
+  int y_dtype;
+  int64_t ldy;
+  int* status;
+  float* partial;          // [splits][Mp][N] when splits > 1
+};
+// k per group of the GEMM's format, activation staging in the decoder's k order, the GEMM.
+int ts_group_k(int gfmt);
+cudaError_t launch_ts_prep(const QGemvCall& c, int gfmt, int64_t Mp, int64_t kp, void* xw, float* tscale);
+cudaError_t launch_ts_gemm(const TsGemm& g, cudaStream_t st);
+
 // y[M, N] (y_dtype, rows ldy apart) = sum over ranks of partial[M, N] (f32, rows ldp
 // apart) + bias (added once), on every rank: the two-shot all-reduce over NVLink.
 // M * N must not exceed tp.ar_max_elems.
