@@ -37,6 +37,7 @@ struct rtd_qweight {
   uint8_t* dev = nullptr;
   size_t dev_bytes = 0, raw_bytes = 0;
   bool owns = true;  // false for a row view (rtd_qweight_rows): the parent owns the memory
+  float wpow2 = 0.0f;  // rtd::ts_decode_scale of the raw blocks
 };
 
 struct rtd_fp8weight {
@@ -221,6 +222,7 @@ rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host
       return fail(ctx, RTD_ERR_OOM, "rtd_qweight_upload: host staging allocation failed");
     }
     rtd::repack_host(fmt, static_cast<const uint8_t*>(host_blocks), N, K, host.data());
+    w->wpow2 = rtd::ts_decode_scale(fmt, static_cast<const uint8_t*>(host_blocks), N, K);
     DeviceGuard g(ctx->device);
     cudaError_t e = cudaMalloc(&w->dev, w->dev_bytes);
     if (e != cudaSuccess) {
@@ -309,7 +311,7 @@ rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* 
 static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N, int64_t K, int64_t G,
                            const float* row_scale, int scale_len, const void* x, uint32_t x_dtype, int64_t ldx,
                            int64_t M, int w8a8, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
-                           void* stream, const char* who) {
+                           void* stream, const char* who, float wpow2) {
   if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
   if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
   if (M == 0 || N == 0) return RTD_OK;
@@ -337,6 +339,7 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.ldx = ldx;
   c.M = M;
   c.w8a8 = w8a8;
+  c.wpow2 = wpow2;
   c.bias = bias;
   c.y = y;
   c.y_dtype = (int)y_dtype;
@@ -362,7 +365,7 @@ rtd_status rtd_qlinear(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32
                        const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
   if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qlinear: NULL ctx or weight");
   return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, nullptr, 0, x, x_dtype, ldx, M, 0, bias, y, y_dtype, ldy,
-                  stream, "rtd_qlinear");
+                  stream, "rtd_qlinear", w->wpow2);
 }
 
 rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n, float* y, void* stream) {
@@ -435,7 +438,7 @@ rtd_status rtd_fp8_linear(rtd_ctx* ctx, const rtd_fp8weight* w, const void* x, u
   if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8_linear: NULL ctx or weight");
   if (mode != RTD_FP8_W8A16 && mode != RTD_FP8_W8A8) return fail(ctx, RTD_ERR_INVALID, "rtd_fp8_linear: bad mode %u", mode);
   return run_gemv(ctx, rtd::FMT_FP8, w->dev, w->N, w->K, w->G, w->scale, (int)w->scale_len, x, x_dtype, ldx, M,
-                  mode == RTD_FP8_W8A8 ? 1 : 0, nullptr, y, y_dtype, ldy, stream, "rtd_fp8_linear");
+                  mode == RTD_FP8_W8A8 ? 1 : 0, nullptr, y, y_dtype, ldy, stream, "rtd_fp8_linear", 1.0f);
 }
 
 rtd_status rtd_fp8_encode(rtd_ctx* ctx, const float* x, int64_t n, uint8_t* out, void* stream) {
@@ -714,6 +717,7 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
   rtd::QGemvCall c{};
   c.fmt = shard->fmt;
   c.w = shard->dev;
+  c.wpow2 = shard->wpow2;
   c.N = shard->N;
   c.K = shard->K;
   c.G = shard->G;
@@ -880,6 +884,7 @@ rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_d
   rtd::QGemvCall c{};
   c.fmt = w->fmt;
   c.w = w->dev;
+  c.wpow2 = w->wpow2;
   c.N = w->N;
   c.K = w->K;
   c.G = w->G;

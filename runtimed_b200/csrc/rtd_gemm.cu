@@ -856,7 +856,8 @@ int gemm_kst(int gfmt) { return gfmt == FMT_F8X ? 128 : kBK; }
 // wins (ties: fewer splits, then the wider tile).
 struct GemmPlan {
   int TN, splits, dw;
-  bool ts;  // the skinny kernel of rtd_gemm_ts.cu (decoded weights in tensor memory)
+  bool ts;   // the skinny kernel of rtd_gemm_ts.cu (decoded weights in tensor memory)
+  int ctas;  // its persistent grid
   int64_t Mp, kp;
   size_t xw_bytes, partial_bytes;
 };
@@ -870,42 +871,25 @@ constexpr double kCyclesPerReduceByte = 1.9e9 / 3.0e12;  // ~3 TB/s at ~1.9 GHz
 constexpr double kTwoCtaStageFactor = 1.6;
 constexpr double kCopyStageCycles = 150.0;
 
-// The skinny kernel (up to 64 tokens a CTA): per weight group (GK k x 128 rows) a CTA
-// pays the longer of the group's decode into tensor memory and its MMAs; the whole call
-// cannot beat streaming its weight bytes at the HBM rate.
-constexpr double kTsDecodeGroupCycles[5] = {620.0, 740.0, 280.0, 150.0, 60.0};  // by GEMM format
-constexpr double kTsCtaFixedCycles = 3000.0;
-constexpr double kHbmBytesPerCycle = 6.5e12 / 1.9e9;
-
+// The skinny kernel (up to 64 tokens): a persistent grid of one CTA per SM shares the
+// (row tile x group) units evenly, so there is no tile, split or wave to choose.
 GemmPlan gemm_plan_ts(const QGemvCall& c, int gfmt) {
+  // persistent stream-K: one CTA per SM, each with at least kTsMinUnits groups
+  constexpr int64_t kTsMinUnits = 4;
   const FmtInfo f = fmt_info(c.fmt);
   const int TN = c.M <= 16 ? 16 : c.M <= 32 ? 32 : 64;
-  const int64_t rowctas = (tiles_for(c.N) + 7) / 8, colctas = (c.M + TN - 1) / TN;
+  const int64_t R = (tiles_for(c.N) + 7) / 8, U = R * c.G;
   const int64_t sms = c.sm_count > 0 ? c.sm_count : 148;
-  const int nmma = f.gk == 256 ? 16 : (gfmt == FMT_F8X ? 4 : 8);
-  const double stage = std::max(kTsDecodeGroupCycles[gfmt], (double)nmma * TN / 2.0);
-  const double hbm = (double)tiles_for(c.N) * (double)c.G * f.gb * (double)colctas / kHbmBytesPerCycle;
   GemmPlan best{};
-  double best_cyc = -1.0;
-  const int64_t most = std::max<int64_t>(1, std::min<int64_t>(16, c.G / 2));
-  for (int64_t s = 1; s <= most; ++s) {
-    const int64_t ctas = rowctas * colctas * s;
-    const int64_t waves = (ctas + sms - 1) / sms;
-    const double cta = (double)((c.G + s - 1) / s) * stage + kTsCtaFixedCycles;
-    double cyc = std::max((double)waves * cta, hbm + kTsCtaFixedCycles);
-    if (s > 1) cyc += kReduceFixedCycles + kCyclesPerReduceByte * (double)(s * TN * colctas * c.N * 4 + c.M * c.N * 4);
-    if (best_cyc < 0.0 || cyc < best_cyc * 0.98) {
-      best_cyc = cyc;
-      best.splits = (int)s;
-    }
-  }
   best.TN = TN;
+  best.splits = 1;
   best.dw = 16;
   best.ts = true;
-  best.Mp = colctas * TN;
+  best.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(sms, U / kTsMinUnits));
+  best.Mp = TN;
   best.kp = c.G * f.gk;
   best.xw_bytes = (size_t)best.Mp * (size_t)best.kp * (gfmt == FMT_F8X ? 1 : 2);
-  best.partial_bytes = best.splits > 1 ? (size_t)best.splits * (size_t)best.Mp * (size_t)c.N * 4 : 0;
+  best.partial_bytes = ts_partial_floats(best.ctas, TN) * 4;
   return best;
 }
 
@@ -916,7 +900,10 @@ GemmPlan gemm_plan(const QGemvCall& c) {
   }();
   // (W8A8 rounding of f16-staged activations is the shared-memory kernel's; FP8 W8A8 runs
   // kind::f8f6f4 on either kernel)
-  if (env_ts != 0 && c.M <= 64 && (!c.w8a8 || gemm_fmt(c) == FMT_F8X)) return gemm_plan_ts(c, gemm_fmt(c));
+  // (its unit indices are 32-bit)
+  if (env_ts != 0 && c.M <= 64 && (!c.w8a8 || gemm_fmt(c) == FMT_F8X) &&
+      (tiles_for(c.N) + 7) / 8 * c.G < (int64_t(1) << 30))
+    return gemm_plan_ts(c, gemm_fmt(c));
   static const int env_dw = [] {  // tuning override: RTD_GEMM_DW=8|16
     const char* s = std::getenv("RTD_GEMM_DW");
     const int v = s ? std::atoi(s) : 0;
@@ -1020,13 +1007,15 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
     g.w = c.w;
     g.row_scale = c.fmt == FMT_FP8 ? c.row_scale : nullptr;
     g.scale_len = c.scale_len;
+    g.wpow2 = c.wpow2 > 0.0f ? c.wpow2 : 16777216.0f;
     g.N = c.N;
     g.T = tiles_for(c.N);
     g.G = c.G;
+    g.R = (g.T + 7) / 8;
     g.M = c.M;
     g.Mp = Mp;
     g.TN = TN;
-    g.splits = p.splits;
+    g.ctas = p.ctas;
     g.xw = xw;
     g.tscale = tscale;
     g.bias = c.bias;

@@ -7,9 +7,11 @@
 // One CTA computes 128 weight rows (eight 16-row tiles: the UMMA M) x TN tokens (16, 32 or
 // 64: the UMMA N) with the f32 accumulator in tensor memory, one weight GROUP (GK = 256 k
 // for the K-quants, 128 for Q8_0 / FP8) per pipeline step:
-//   - warp 2 (one lane) bulk-copies the group of each of the eight tiles into a
-//     shared-memory slot (up to eight slots ahead); warp 0 (one lane) bulk-copies the
-//     group's activation tile (staged once per call by gemm_prep_ts_kernel);
+//   - each decode warp bulk-copies its own tile's groups into its part of a shared-memory
+//     slot (up to eight slots ahead, refilled as soon as it has read one); warp 0 (one
+//     lane) bulk-copies the group's activation tile, staged once per call by
+//     gemm_prep_ts_kernel (a cp.async.bulk costs its issuing thread about the same time
+//     whatever its size, so copies are few and large, and spread over threads);
 //   - sixteen decode warps in two sets take alternate groups.  In a set, the warp of
 //     tensor-memory lane quarter q and tile 2q + p decodes its tile's group: thread
 //     4g + t holds exactly the bytes the group layout gives lane 4g + t (whole
@@ -20,12 +22,14 @@
 //     ownership: registers of thread 4g + t land in lanes g and g + 8, columns 2t and
 //     2t + 1 of every 8-column repetition.  The k order inside a group is therefore the
 //     decoder's, and the activations are staged in that order (perm_* below);
-//   - one lane of warp 1 issues the group's tcgen05.mma (A from tensor memory, B from the
-//     128-byte swizzled activation tile) into the accumulator and commits them to the
-//     group's release barriers (tensor-memory slot and activation slot);
-//   - after the last group warps 4..7 read the accumulator (tcgen05.ld, one lane quarter
-//     each) and write y with the per-token activation scale, the FP8 row scale and the
-//     bias, or f32 partials when K is split over CTAs.
+//   - lane 0 of warps 1 and 3 issue the tcgen05.mma of alternate groups (A from tensor
+//     memory, B from the 128-byte swizzled activation tile), each into its own
+//     accumulator, and commit them to the group's release barriers (tensor-memory slot and
+//     activation slot);
+//   - warps 4..7 (one per lane quarter) read each finished accumulator pair (tcgen05.ld),
+//     add the two, and write y with the per-token activation scale, the FP8 row scale and
+//     the bias, or f32 partials for a row tile shared with another CTA (see the schedule
+//     below).
 // FP8 weights with E4M3 activations (W8A8) skip the decode: the E4M3 codes go to tensor
 // memory as they are and tcgen05.mma.kind::f8f6f4 multiplies them with the E4M3 codes
 // of the activations.
@@ -43,7 +47,7 @@
 namespace rtd {
 namespace {
 
-constexpr int kTsThreads = 640;     // 20 warps: 0 activations, 1 MMA, 2 weights, 3 TMEM owner, 4..19 decode
+constexpr int kTsThreads = 640;     // 20 warps: 0 activations, 1 and 3 MMA (3 owns the TMEM), 2 idle, 4..19 decode
 constexpr int kTsSmem = 227 * 1024;
 constexpr int kTsCols = 512;        // the whole tensor memory of the SM (one CTA per SM)
 constexpr int kTsMaxSlots = 8;
@@ -89,17 +93,26 @@ struct TsPlan {
   static constexpr int SB = kSbFit < 3 ? 3 : (kSbFit > kTsMaxSlots ? kTsMaxSlots : kSbFit);
   static constexpr int kFixed = 1024 + 512 + TN * 4;  // alignment slack, barriers + misc, token scales
   static constexpr int kFitR = (kTsSmem - kFixed - SB * kB) / kRaw;
-  static constexpr int SR = kFitR < kTsMaxSlots ? kFitR : kTsMaxSlots;
-  static constexpr int A0 = TN < 32 ? 32 : TN;        // first A column (the accumulator holds 0 .. TN)
+  // even: a decode warp refills the slot it has just read with the group SR later, which
+  // belongs to its own set again
+  static constexpr int SR = (kFitR < kTsMaxSlots ? kFitR : kTsMaxSlots) & ~1;
+  // Two MMA-issuing threads take alternate halves of a group's K slices into their own
+  // accumulators (summed by the epilogue); NB accumulator pairs rotate over segments
+  // (two while they fit beside three A slots, else one).
+  static constexpr int ACC = TN < 32 ? 32 : TN;       // columns per accumulator
+  static constexpr int NB = TN <= 32 ? 2 : 1;
+  static constexpr int A0 = 2 * NB * ACC;              // first A column
   static constexpr int kFitA = (kTsCols - A0) / F::ACOLS;
   static constexpr int SA = kFitA < 6 ? kFitA : 6;
   static constexpr int offB = 0;
   static constexpr int offRaw = SB * kB;
   static constexpr int offBar = offRaw + SR * kRaw;
-  static constexpr int nBars = 2 * SR + 2 * SB + 2 * SA + 1;
+  static constexpr int nBars = 8 * SR + 3 * SB + 4 * SA + 2 * NB + 1;
+  // phase index of a slot's barrier of one group parity: the slot's groups of that parity
+  // recur every lcm(slots, 2) groups
+  static constexpr int LA = SA % 2 ? 2 * SA : SA, LB = SB % 2 ? 2 * SB : SB;
   static constexpr int offMisc = offBar + nBars * 8;
-  static constexpr int offScale = offMisc + 16;
-  static constexpr int bytes = offScale + TN * 4 + 1024;
+  static constexpr int bytes = offMisc + 16 + 1024;
   static_assert(SR >= 2 && SA >= 2, "too few pipeline slots");
   static_assert(bytes <= kTsSmem, "shared-memory plan exceeds the CTA's share");
   // one CTA per SM (it allocates every tensor-memory column): launch with more than half
@@ -137,36 +150,52 @@ __host__ __device__ __forceinline__ int perm_f8x(int p) {  // E4M3 A: four codes
 }
 
 // ---------------------------------------------------------------- decoders
+// The tensor cores get A = 2^s * w in f16, w the reference's weight: every code enters
+// as an exact f16 SUBNORMAL (its bits are the code: value code * 2^-24), so a pair needs
+// one mask and one f16 FMA with the factor scaled by F = 2^(24 + s) (a power of two fixed
+// per weight at upload, the largest that keeps every scaled factor in the f16 range);
+// the epilogue multiplies by 2^-s.  Factors are computed in f32 and rounded once to f16,
+// as the products of the reference's factors with a power of two.
 // grp: shared address of this tile's group; taddr: tensor-memory address of the tile's
 // 16 lanes at the group's first A column.  Thread 4g + t (= lane) owns rows g and g + 8.
-__device__ __forceinline__ void q4k_factors(uint4 h, int t, uint32_t& dl, uint32_t& nl, uint32_t& dh,
-                                            uint32_t& nh) {
-  const float d = hbits(h.x & 0xFFFFu), dmin = hbits(h.x >> 16);
-  uint32_t sc0, m0, sc1, m1;
-  scale_min_words(2 * t, h.y, h.z, h.w, sc0, m0);
-  scale_min_words(2 * t + 1, h.y, h.z, h.w, sc1, m1);
-  dl = h2_bits(h2_const(d * (float)sc0));
-  nl = h2_bits(h2_const(-(dmin * (float)m0)));
-  dh = h2_bits(h2_const(d * (float)sc1));
-  nh = h2_bits(h2_const(-(dmin * (float)m1)));
+
+// Q4_K factor registers of one row: dl / nl for sub-block 2t (low nibbles), dh / nh for
+// sub-block 2t + 1 (high nibbles, whose codes arrive as 16 q: dh carries F / 16), each
+// duplicated into both halves.  The 6-bit scales and mins of all eight sub-blocks come
+// out of the 12 packed bytes four at a time (scale_min_k4, dequant_k.rs:8-16): bytes
+// 0-3 of the lo / hi words are sub-blocks 0-3 / 4-7; `hi` and `sel` are per-thread
+// constants, so no thread branches.
+struct Q4Fac {
+  uint32_t dl, nl, dh, nh;
+};
+__device__ __forceinline__ Q4Fac q4k_factors(uint4 h, uint32_t hmask, uint32_t sel, float F, float A) {
+  const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
+  const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+  const uint32_t scw = sc_lo ^ ((sc_lo ^ sc_hi) & hmask), mw = m_lo ^ ((m_lo ^ m_hi) & hmask);
+  const __half2 k1024 = __float2half2_rn(1024.0f);
+  // (1024 + a, 1024 + b) -> (a, b): the two sub-blocks' integers, exact in f16
+  const __half2 sc2 = __hsub2(bits_h2(prmt(scw, 0x64646464u, sel)), k1024);
+  const __half2 m2 = __hsub2(bits_h2(prmt(mw, 0x64646464u, sel)), k1024);
+  const float d = hbits(h.x & 0xFFFFu) * F, dmin = hbits(h.x >> 16) * A;
+  // d * F is an f16 value times a power of two (exact); dmin * 2^s may fall below the f16
+  // normal range, so the mins' products are formed in f32 and rounded once
+  const uint32_t df = h2_bits(__hmul2(sc2, __floats2half2_rn(d, d * 0.0625f)));
+  const float2 mf = __half22float2(m2);
+  const uint32_t nf = h2_bits(__floats2half2_rn(-(dmin * mf.x), -(dmin * mf.y)));
+  return Q4Fac{prmt(df, df, 0x1010u), prmt(nf, nf, 0x1010u), prmt(df, df, 0x3232u), prmt(nf, nf, 0x3232u)};
 }
 
-// Low nibbles at bits 0-3 / 16-19: 0x6400 | q is 1024 + q; high nibbles at bits 4-7 /
-// 20-23: 0x5400 | q << 4 is 64 + q.  The subtraction is exact, then one FMA per pair.
-__device__ __forceinline__ uint32_t q4_lo(uint32_t x, uint32_t d, uint32_t n) {
-  const __half2 v = __hsub2(bits_h2(lop_and_or(x, 0x000F000Fu, 0x64006400u)), __float2half2_rn(1024.0f));
-  return h2_bits(__hfma2(bits_h2(d), v, bits_h2(n)));
-}
-__device__ __forceinline__ uint32_t q4_hi(uint32_t x, uint32_t d, uint32_t n) {
-  const __half2 v = __hsub2(bits_h2(lop_and_or(x, 0x00F000F0u, 0x54005400u)), __float2half2_rn(64.0f));
-  return h2_bits(__hfma2(bits_h2(d), v, bits_h2(n)));
+__device__ __forceinline__ uint32_t fma_h2(uint32_t a, uint32_t b, uint32_t c) {
+  return h2_bits(__hfma2(bits_h2(a), bits_h2(b), bits_h2(c)));
 }
 
-__device__ __forceinline__ void ts_decode_q4k(uint32_t grp, uint32_t taddr, int lane) {
+__device__ __forceinline__ void ts_decode_q4k(uint32_t grp, uint32_t taddr, int lane, float F, float A) {
   const int g = lane >> 2, t = lane & 3;
-  uint32_t dl[2], nl[2], dh[2], nh[2];
-  q4k_factors(lds128(grp + 16 * g), t, dl[0], nl[0], dh[0], nh[0]);
-  q4k_factors(lds128(grp + 16 * (g + 8)), t, dl[1], nl[1], dh[1], nh[1]);
+  const uint32_t hmask = t >= 2 ? 0xFFFFFFFFu : 0u;
+  const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;  // bytes (2t) & 3 and the next, each under a 0x64
+  const Q4Fac f[2] = {q4k_factors(lds128(grp + 16 * g), hmask, sel, F, A),
+                      q4k_factors(lds128(grp + 16 * (g + 8)), hmask, sel, F, A)};
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp) {
     // 16-byte runs of the lane's chunk t: run pp of row g (pass pp), of row g + 8 (pass 2 + pp)
@@ -177,21 +206,26 @@ __device__ __forceinline__ void ts_decode_q4k(uint32_t grp, uint32_t taddr, int 
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const uint32_t x = (&u[hr].x)[w], x8 = x >> 8;
-        v[4 * (2 * w) + 0 + 2 * hr] = q4_lo(x, dl[hr], nl[hr]);       // bytes 0, 2: sub-block 2t
-        v[4 * (2 * w) + 1 + 2 * hr] = q4_lo(x8, dl[hr], nl[hr]);      // bytes 1, 3
-        v[4 * (2 * w + 1) + 0 + 2 * hr] = q4_hi(x, dh[hr], nh[hr]);   // sub-block 2t + 1
-        v[4 * (2 * w + 1) + 1 + 2 * hr] = q4_hi(x8, dh[hr], nh[hr]);
+        v[4 * (2 * w) + 0 + 2 * hr] = fma_h2(f[hr].dl, x & 0x000F000Fu, f[hr].nl);       // bytes 0, 2: sub-block 2t
+        v[4 * (2 * w) + 1 + 2 * hr] = fma_h2(f[hr].dl, x8 & 0x000F000Fu, f[hr].nl);      // bytes 1, 3
+        v[4 * (2 * w + 1) + 0 + 2 * hr] = fma_h2(f[hr].dh, x & 0x00F000F0u, f[hr].nh);   // sub-block 2t + 1
+        v[4 * (2 * w + 1) + 1 + 2 * hr] = fma_h2(f[hr].dh, x8 & 0x00F000F0u, f[hr].nh);
       }
     }
     tmem_st16x256_x8(taddr + 64u * pp, v);
+    // tcgen05.st reads its source registers asynchronously: they are not rewritten (the
+    // next half reuses them) before the store has completed
+    tmem_wait_st();
   }
 }
 
-__device__ __forceinline__ void ts_decode_q6k(uint32_t grp, uint32_t taddr, int lane) {
+// Q6_K: w = d * sc * (q - 32); with the code as a subnormal, the FMA adds -32 * F * d * sc
+// * 2^-24, which is the rounded factor times -2^-19 (exact whenever it is a normal f16).
+__device__ __forceinline__ void ts_decode_q6k(uint32_t grp, uint32_t taddr, int lane, float F) {
   const int g = lane >> 2;
-  const float d[2] = {hbits(lds16(grp + 4 * g)), hbits(lds16(grp + 4 * g + 2))};
+  const float d[2] = {hbits(lds16(grp + 4 * g)) * F, hbits(lds16(grp + 4 * g + 2)) * F};
   const uint32_t scw[2] = {lds32(grp + 32 + lane * 8), lds32(grp + 32 + lane * 8 + 4)};
-  const __half2 k1056 = __float2half2_rn(1056.0f);  // 1024 + 32
+  const __half2 k_off = __float2half2_rn(-0.0000019073486328125f);  // -2^-19
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     uint32_t wd[12];
@@ -208,7 +242,9 @@ __device__ __forceinline__ void ts_decode_q6k(uint32_t grp, uint32_t taddr, int 
     for (int tr = 0; tr < 4; ++tr) {  // (row g, 8hh+2t), (row g+8, ..), (row g, 8hh+2t+1), (row g+8, ..)
       const int hr = tr & 1, par = tr >> 1;
       const uint32_t X = wd[3 * tr], Y = wd[3 * tr + 1], Z = wd[3 * tr + 2];
-      const __half2 ds = h2_const(d[hr] * (float)(int)(int8_t)(uint8_t)(scw[hr] >> (8 * (2 * hh + par))));
+      const float ds = d[hr] * (float)(int)(int8_t)(uint8_t)(scw[hr] >> (8 * (2 * hh + par)));
+      const __half2 f2 = __floats2half2_rn(ds, ds);
+      const uint32_t fa = h2_bits(f2), fc = h2_bits(__hmul2(f2, k_off));
       const uint32_t c[8] = {X & 0x003F003Fu,
                              (X >> 6) & 0x003F003Fu,
                              Y & 0x003F003Fu,
@@ -218,22 +254,29 @@ __device__ __forceinline__ void ts_decode_q6k(uint32_t grp, uint32_t taddr, int 
                              ((X >> 12) & 0x000F000Fu) | ((Z >> 8) & 0x00300030u),
                              ((Y >> 12) & 0x000F000Fu) | ((Z >> 10) & 0x00300030u)};
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj)
-        v[4 * (4 * par + (jj >> 1)) + (jj & 1) + 2 * hr] =
-            h2_bits(__hmul2(ds, __hsub2(bits_h2(c[jj] | 0x64006400u), k1056)));
+      for (int jj = 0; jj < 8; ++jj) v[4 * (4 * par + (jj >> 1)) + (jj & 1) + 2 * hr] = fma_h2(fa, c[jj], fc);
     }
     tmem_st16x256_x8(taddr + 64u * hh, v);
+    tmem_wait_st();  // as above: the next half reuses the source registers
   }
 }
 
+// Q8_0: w = d * b; the byte b + 128 enters as a subnormal and the FMA adds -128 * F * d *
+// 2^-24 = the scaled d times -2^-17.  FP8 (W8A16): E4M3 -> f16 is exact; its row scale is
+// applied in the epilogue.
 template <bool Q8>
-__device__ __forceinline__ void ts_decode_8bit(uint32_t grp, uint32_t taddr, int lane) {
-  uint32_t dq[2] = {0u, 0u};
+__device__ __forceinline__ void ts_decode_8bit(uint32_t grp, uint32_t taddr, int lane, float F) {
+  uint32_t fa[2] = {0u, 0u}, fc[2] = {0u, 0u};
   if constexpr (Q8) {
-    dq[0] = lds16(grp + 4 * lane) * 0x10001u;
-    dq[1] = lds16(grp + 4 * lane + 2) * 0x10001u;
+    const __half2 k_off = __float2half2_rn(-0.00000762939453125f);  // -2^-17
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const float dv = hbits(lds16(grp + 4 * lane + 2 * hr)) * F;
+      const __half2 f2 = __floats2half2_rn(dv, dv);
+      fa[hr] = h2_bits(f2);
+      fc[hr] = h2_bits(__hmul2(f2, k_off));
+    }
   }
-  const __half2 k1152 = __float2half2_rn(1152.0f);  // 1024 + 128
   uint32_t v[32];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {  // pass p: row g + 8 (p >> 1), elements 16 (p & 1) ..
@@ -245,12 +288,10 @@ __device__ __forceinline__ void ts_decode_8bit(uint32_t grp, uint32_t taddr, int
 #pragma unroll
       for (int s = 0; s < 2; ++s) {  // bytes (0, 1) / (2, 3): elements 4w + 2s, 4w + 2s + 1
         uint32_t o;
-        if constexpr (Q8) {
-          const uint32_t p2 = prmt(x ^ 0x80808080u, 0x64u, s ? 0x4342u : 0x4140u);
-          o = h2_bits(__hmul2(bits_h2(dq[hr]), __hsub2(bits_h2(p2), k1152)));
-        } else {
+        if constexpr (Q8)
+          o = fma_h2(fa[hr], prmt(x ^ 0x80808080u, 0u, s ? 0x4342u : 0x4140u), fc[hr]);
+        else
           o = e4m3x2_to_f16x2((uint16_t)(s ? (x >> 16) : (x & 0xFFFFu)));
-        }
         v[4 * (4 * pp + w) + s + 2 * hr] = o;
       }
     }
@@ -274,20 +315,30 @@ __device__ __forceinline__ void ts_copy_f8x(uint32_t grp, uint32_t taddr, int la
 }
 
 template <int FMT>
-__device__ __forceinline__ void ts_decode(uint32_t grp, uint32_t taddr, int lane) {
+__device__ __forceinline__ void ts_decode(uint32_t grp, uint32_t taddr, int lane, float F, float A) {
   if constexpr (FMT == FMT_Q4K)
-    ts_decode_q4k(grp, taddr, lane);
+    ts_decode_q4k(grp, taddr, lane, F, A);
   else if constexpr (FMT == FMT_Q6K)
-    ts_decode_q6k(grp, taddr, lane);
+    ts_decode_q6k(grp, taddr, lane, F);
   else if constexpr (FMT == FMT_Q80)
-    ts_decode_8bit<true>(grp, taddr, lane);
+    ts_decode_8bit<true>(grp, taddr, lane, F);
   else if constexpr (FMT == FMT_FP8)
-    ts_decode_8bit<false>(grp, taddr, lane);
+    ts_decode_8bit<false>(grp, taddr, lane, F);
   else
     ts_copy_f8x(grp, taddr, lane);
 }
 
 // ---------------------------------------------------------------- GEMM kernel
+// Persistent stream-K schedule.  The call's work is the sequence of units (row tile rt of
+// 128 rows, group g), rt-major, U = R * G of them; CTA c of C (one per SM) takes units
+// [c U / C, (c + 1) U / C) through one pipeline, so every SM gets the same number of
+// groups whatever the shape.  A CTA's run crosses row tiles: each row tile's share (a
+// "segment") accumulates in one of two tensor-memory accumulators in turn, so the MMAs of
+// the next segment overlap the epilogue of the last.  A segment covering its whole row
+// tile writes y; the first and last segments of a CTA may cover part of one and write
+// f32 partials, which ts_fixup_kernel adds up in CTA order (deterministic).
+__host__ __device__ __forceinline__ int ts_unit0(int c, int U, int C) { return (int)((int64_t)c * U / C); }
+
 template <int FMT, int TN>
 __global__ void __launch_bounds__(kTsThreads, 1) qgemm_ts_kernel(const TsGemm a) {
   using F = TsFmt<FMT>;
@@ -298,44 +349,54 @@ __global__ void __launch_bounds__(kTsThreads, 1) qgemm_ts_kernel(const TsGemm a)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + P::offBar);
-  uint64_t* raw_full = bar;
-  uint64_t* raw_empty = raw_full + SR;
-  uint64_t* b_full = raw_empty + SR;
-  uint64_t* b_empty = b_full + SB;
-  uint64_t* a_full = b_empty + SB;
-  uint64_t* a_empty = a_full + SA;
-  uint64_t* acc_full = a_empty + SA;
+  // Barriers of the activation and A slots are split by the parity of the group (the two
+  // decode sets and the two MMA issuers take alternate groups): a slot ring of odd length
+  // alternates parities, and a thread waiting on a barrier whose previous phase is still
+  // open would read that phase's parity as done.  Split, every barrier's phases are
+  // produced and consumed in order by the same threads.
+  uint64_t* raw_full = bar;  // [SR][8]: slot x 16-row tile (one warp each)
+  uint64_t* b_full = raw_full + 8 * SR;  // [2][SB]: group parity x slot
+  uint64_t* b_empty = b_full + 2 * SB;   // [SB] (the producer waits every phase in order)
+  uint64_t* a_full = b_empty + SB;       // [2][SA]
+  uint64_t* a_empty = a_full + 2 * SA;   // [2][SA]
+  constexpr int NB = P::NB, LA = P::LA, LB = P::LB;
+  uint64_t* acc_full = a_empty + 2 * SA; // [NB]
+  uint64_t* acc_empty = acc_full + NB; // [NB]
+  uint64_t* mma_done = acc_empty + NB;
   uint32_t* misc = reinterpret_cast<uint32_t*>(sm + P::offMisc);  // [0] tensor-memory base, [1] abort flag
-  float* sscale = reinterpret_cast<float*>(sm + P::offScale);
 
-  const int64_t tile0 = (int64_t)blockIdx.y * 8;  // first 16-row tile of this CTA
-  const int64_t t0 = (int64_t)blockIdx.x * TN;    // first token
-  const int g_lo = (int)(a.G * blockIdx.z / a.splits);
-  const int g_hi = (int)(a.G * (blockIdx.z + 1) / a.splits);
-  const int ng = g_hi - g_lo;
+  // unit counts fit 32 bits (the host checks); the loops below advance (row tile, group)
+  // incrementally instead of dividing
+  const int G = (int)a.G, U = (int)(a.R * a.G);
+  const int u0 = ts_unit0(blockIdx.x, U, gridDim.x), u1 = ts_unit0(blockIdx.x + 1, U, gridDim.x);
+  const int n = u1 - u0;
+  const int rt0 = u0 / G, g0 = u0 - rt0 * G;  // first row tile of this CTA, its first group
+  const int nseg = n > 0 ? (u1 - 1) / G - rt0 + 1 : 0;
 
   if (warp == 3) {
     tmem_alloc(smem_u32(&misc[0]), kTsCols);
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int s = 0; s < SR; ++s) {
-      mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 8);  // the eight tile warps of the set that decoded it
-    }
+    for (int s = 0; s < 8 * SR; ++s) mbar_init(&raw_full[s], 1);
     for (int s = 0; s < SB; ++s) {
       mbar_init(&b_full[s], 1);
+      mbar_init(&b_full[SB + s], 1);
       mbar_init(&b_empty[s], 1);
     }
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(&a_full[s], 8);
-      mbar_init(&a_empty[s], 1);
+    for (int s = 0; s < 2 * SA; ++s) {
+      mbar_init(&a_full[s], 8);   // the eight tile warps of the set
+      mbar_init(&a_empty[s], 1);  // the commit of the thread that multiplied the group
     }
-    mbar_init(acc_full, 1);
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&acc_full[s], 2);
+      mbar_init(&acc_empty[s], 4);  // the four epilogue warps
+    }
+    mbar_init(mma_done, 2);
     misc[1] = 0;
     fence_mbar_init();
   }
-  pdl_trigger();  // the reduce kernel (or the next call) may launch; it waits for this grid
+  pdl_trigger();  // the fixup kernel (or the next call) may launch; it waits for this grid
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -356,121 +417,123 @@ __global__ void __launch_bounds__(kTsThreads, 1) qgemm_ts_kernel(const TsGemm a)
       pdl_wait();  // the staged activations are the prep kernel's output
       constexpr int kRows = F8 ? 1 : F::GK / 64;
       const uint8_t* xw = static_cast<const uint8_t*>(a.xw);
-      int issued = 0;
-      for (int gi = 0; gi < ng; ++gi) {
+      int issued = 0, g = g0;
+      for (int gi = 0; gi < n; ++gi, g = (g + 1 == G) ? 0 : g + 1) {
         const int sb = gi % SB;
         if (gi >= SB && !wait(&b_empty[sb], (uint32_t)((gi / SB - 1) & 1))) break;
-        mbar_arrive_expect_tx(&b_full[sb], (uint32_t)P::kB);
-        for (int r = 0; r < kRows; ++r) {
-          const int64_t kb = (int64_t)(g_lo + gi) * kRows + r;
-          bulk_g2s(sm + P::offB + sb * P::kB + r * TN * 128, xw + ((size_t)kb * (a.Mp / 8) + (size_t)(t0 / 8)) * 1024,
-                   TN * 128, &b_full[sb]);
-        }
+        uint64_t* bf = &b_full[(gi & 1) * SB + sb];
+        mbar_arrive_expect_tx(bf, (uint32_t)P::kB);
+        // the group's kRows 128-byte rows are contiguous in the staging buffer: one copy
+        bulk_g2s(sm + P::offB + sb * P::kB, xw + (size_t)g * P::kB, P::kB, bf);
         ++issued;
       }
       if (*abort_flag)  // no copy may still be landing when the CTA exits
         for (int gi = (issued > SB ? issued - SB : 0); gi < issued; ++gi)
-          mbar_wait_ns(&b_full[gi % SB], (uint32_t)((gi / SB) & 1), kWaitBudgetNs, a.status);
+          mbar_wait_ns(&b_full[(gi & 1) * SB + gi % SB], (uint32_t)((gi / LB) & 1), kWaitBudgetNs, a.status);
     }
-  } else if (warp == 2) {
-    // ---- packed groups of the eight tiles
+  } else if (warp == 1 || warp == 3) {
+    // ---- MMA issuers: lane 0 of warp 1 takes the even units of the CTA's run into
+    // accumulator 0 of the segment's pair, lane 0 of warp 3 the odd ones into accumulator 1.
+    // An M = 128 tcgen05.mma occupies the tensor pipe ~45 cycles however small N is, and a
+    // group needs eight or sixteen of them; while one thread waits for its next group's
+    // barriers the other keeps the pipe busy.
     if (lane == 0) {
-      const int64_t ntile = (a.T - tile0 < 8) ? a.T - tile0 : 8;
-      int issued = 0;
-      for (int gi = 0; gi < ng; ++gi) {
-        const int sr = gi % SR;
-        if (gi >= SR && !wait(&raw_empty[sr], (uint32_t)((gi / SR - 1) & 1))) break;
-        mbar_arrive_expect_tx(&raw_full[sr], (uint32_t)(ntile * F::GB));
-        for (int64_t i = 0; i < ntile; ++i)
-          bulk_g2s(sm + P::offRaw + sr * P::kRaw + i * F::GB, a.w + ((tile0 + i) * a.G + g_lo + gi) * F::GB, F::GB,
-                   &raw_full[sr]);
-        ++issued;
-      }
-      if (*abort_flag)
-        for (int gi = (issued > SR ? issued - SR : 0); gi < issued; ++gi)
-          mbar_wait_ns(&raw_full[gi % SR], (uint32_t)((gi / SR) & 1), kWaitBudgetNs, a.status);
-    }
-  } else if (warp == 1) {
-    // ---- MMA issuer
-    if (lane == 0) {
+      const int j = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc = idesc_f16(TN);  // kind::f8f6f4 reads the same fields as E4M3 x E4M3
       const uint64_t db0 = kmajor_desc(smem_u32(sm + P::offB));
-      for (int gi = 0; gi < ng; ++gi) {
-        const int sa = gi % SA, sb = gi % SB;
-        if (!wait(&a_full[sa], (uint32_t)((gi / SA) & 1)) || !wait(&b_full[sb], (uint32_t)((gi / SB) & 1))) break;
-        tc_fence_after();
-        const uint32_t a_col = tmem + (uint32_t)(P::A0 + sa * F::ACOLS);
-#pragma unroll
-        for (int i = 0; i < F::NMMA; ++i) {
-          // slice i: 8 tensor-memory columns; in the activation slot, 128-byte row i / 4 at byte 32 (i % 4)
-          const uint64_t bd = db0 + (uint64_t)((sb * P::kB + (i >> 2) * TN * 128) >> 4) + 2 * (i & 3);
-          const uint32_t acc = (gi > 0 || i > 0) ? 1u : 0u;
-          if constexpr (F8)
-            umma_f8_ts(tmem, a_col + 8u * i, bd, idesc, acc);
-          else
-            umma_f16_ts(tmem, a_col + 8u * i, bd, idesc, acc);
+      int seg = 0, g = g0;
+      bool fresh = true;  // no MMA of this thread in the current segment yet
+      for (int gi = 0; gi < n; ++gi, g = (g + 1 == G) ? 0 : g + 1) {
+        const int bf = seg % NB;
+        const bool first = gi == 0 || g == 0, last = gi == n - 1 || g == G - 1;
+        if (first) {
+          fresh = true;
+          if (seg >= NB && !wait(&acc_empty[bf], (uint32_t)((seg / NB - 1) & 1))) break;
         }
-        umma_commit(&a_empty[sa]);
-        umma_commit(&b_empty[sb]);
+        if ((gi & 1) == j) {
+          const int sa = gi % SA, sb = gi % SB;
+          if (!wait(&a_full[j * SA + sa], (uint32_t)((gi / LA) & 1)) ||
+              !wait(&b_full[j * SB + sb], (uint32_t)((gi / LB) & 1)))
+            break;
+          tc_fence_after();
+          const uint32_t acc = tmem + (uint32_t)((2 * bf + j) * P::ACC);
+          const uint32_t a_col = tmem + (uint32_t)(P::A0 + sa * F::ACOLS);
+          const uint64_t db = db0 + (uint64_t)((sb * P::kB) >> 4);
+#pragma unroll
+          for (int i = 0; i < F::NMMA; ++i) {
+            // slice i: 8 tensor-memory columns; in the activation slot, 128-byte row i / 4 at byte 32 (i % 4)
+            const uint64_t bd = db + (uint64_t)(((i >> 2) * TN * 128) >> 4) + 2 * (i & 3);
+            const uint32_t accum = (fresh && i == 0) ? 0u : 1u;
+            if constexpr (F8)
+              umma_f8_ts(acc, a_col + 8u * i, bd, idesc, accum);
+            else
+              umma_f16_ts(acc, a_col + 8u * i, bd, idesc, accum);
+          }
+          fresh = false;
+          umma_commit(&a_empty[j * SA + sa]);
+          umma_commit(&b_empty[sb]);
+        }
+        if (last) {
+          umma_commit(&acc_full[bf]);  // both threads: the segment's sums are complete
+          ++seg;
+        }
       }
-      umma_commit(acc_full);  // fires once every MMA issued has completed
+      umma_commit(mma_done);  // fires once every MMA this thread issued has completed
     }
   } else if (warp >= 4) {
     // ---- decode warps: lane quarter q = warp % 4 (tensor-memory lanes 32q ..), tile 2q + p
     const int dw = warp - 4, q = warp & 3, p = (dw >> 2) & 1, set = dw >> 3;
     const int tile = 2 * q + p;
-    const bool live = tile0 + tile < a.T;
     const uint32_t tlane = (uint32_t)(32 * q + 16 * p) << 16;
-    for (int gi = set; gi < ng; gi += 2) {
-      const int sr = gi % SR, sa = gi % SA;
-      bool ok = wait(&raw_full[sr], (uint32_t)((gi / SR) & 1));
-      if (ok && gi >= SA) ok = wait(&a_empty[sa], (uint32_t)((gi / SA - 1) & 1));
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      if (live)
-        ts_decode<FMT>(smem_u32(sm + P::offRaw + sr * P::kRaw + tile * F::GB),
-                       tmem + tlane + (uint32_t)(P::A0 + sa * F::ACOLS), lane);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[sa]);
-        mbar_arrive(&raw_empty[sr]);
+    const float wa = a.wpow2 * 5.9604644775390625e-08f;  // 2^s = F * 2^-24
+    // warps 4..7 (set 0, one per lane quarter) also run the epilogues, between their groups
+    const bool epi = warp < 8;
+    int ep = 0;           // next segment to finish
+    bool scales = false;  // the prep kernel's token scales are visible
+    auto epilogue = [&](int sg) {
+      if (!scales) {
+        pdl_wait();
+        scales = true;
       }
-    }
-    if (warp < 8) {
-      // ---- epilogue: warps 4..7, tensor-memory lanes 32q .. 32q + 31 = weight rows
-      pdl_wait();  // the token scales are the prep kernel's output
-      for (int i = tid - 128; i < TN; i += 128) sscale[i] = (t0 + i < a.M) ? a.tscale[t0 + i] : 0.0f;
-      named_sync(1, 128);
-      const bool ok = wait(acc_full, 0u);
       tc_fence_after();
+      const int rt = rt0 + sg;
+      const bool complete = u0 <= rt * G && u1 >= rt * G + G;
+      // a one-unit segment filled only the accumulator of its unit's parity
+      const int s_lo = u0 > rt * G ? u0 : rt * G, s_hi = u1 < rt * G + G ? u1 : rt * G + G;
+      const bool has0 = s_hi - s_lo >= 2 || ((s_lo - u0) & 1) == 0;
+      const bool has1 = s_hi - s_lo >= 2 || ((s_lo - u0) & 1) == 1;
       const int r = q * 32 + lane;
-      const int64_t n = tile0 * 16 + r;
-      float es = 1.0f, eb = 0.0f;
-      if (n < a.N) {
-        if (a.row_scale) es = a.row_scale[a.scale_len == 1 ? 0 : n];
-        if (a.bias) eb = a.bias[n];
+      const int64_t nrow = (int64_t)rt * 128 + r;
+      // 2^-s undoes the decoders' power of two (K-quants, Q8_0); FP8 takes its row scale
+      float es = (FMT == FMT_FP8 || F8) ? 1.0f : 16777216.0f / a.wpow2, eb = 0.0f;
+      if (nrow < a.N) {
+        if (a.row_scale) es = a.row_scale[a.scale_len == 1 ? 0 : nrow];
+        if (a.bias) eb = a.bias[nrow];
       }
+      float* part = a.partial + (size_t)(2 * blockIdx.x + (sg == 0 ? 0 : 1)) * TN * 128 + r;
 #pragma unroll 1
       for (int c0 = 0; c0 < TN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        if (!ok || n >= a.N) continue;
-        if (a.splits > 1) {  // partial sums of this k split; the reduce kernel finishes them
-          float* pp = a.partial + ((size_t)blockIdx.z * a.Mp + (size_t)(t0 + c0)) * a.N + n;
+        float v[16], v1[16];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(2 * (sg % NB) * P::ACC + c0);
+        tmem_ld16(ta, v);
+        tmem_ld16(ta + (uint32_t)P::ACC, v1);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) pp[(size_t)j * a.N] = v[j];
+        for (int jj = 0; jj < 16; ++jj)  // the two issuers' sums, in a fixed order
+          v[jj] = (has0 ? v[jj] : 0.0f) + (has1 ? v1[jj] : 0.0f);
+        if (nrow >= a.N || c0 >= a.M) continue;
+        if (!complete) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) part[(size_t)(c0 + j) * 128] = v[j];
           continue;
         }
-        const int jn = (a.M - (t0 + c0)) < 16 ? (int)(a.M - (t0 + c0)) : 16;
+        const int jn = (a.M - c0) < 16 ? (int)(a.M - c0) : 16;
         const int ysz = a.y_dtype == 0 ? 4 : 2;
-        uint8_t* yp = static_cast<uint8_t*>(a.y) + ((t0 + c0) * a.ldy + n) * ysz;
+        uint8_t* yp = static_cast<uint8_t*>(a.y) + ((int64_t)c0 * a.ldy + nrow) * ysz;
         const int64_t ystep = a.ldy * ysz;
 #pragma unroll
         for (int j = 0; j < 16; ++j, yp += ystep) {
           if (j >= jn) break;
-          const float val = v[j] * sscale[c0 + j] * es + eb;
+          const float val = v[j] * a.tscale[c0 + j] * es + eb;
           if (a.y_dtype == 0)
             *reinterpret_cast<float*>(yp) = val;
           else if (a.y_dtype == 1)
@@ -479,15 +542,155 @@ __global__ void __launch_bounds__(kTsThreads, 1) qgemm_ts_kernel(const TsGemm a)
             *reinterpret_cast<__nv_bfloat16*>(yp) = __float2bfloat16_rn(val);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[sg % NB]);
+    };
+    // Lane 0 alone polls a barrier (512 polling threads slow every barrier operation of the
+    // SM, the MMA issuers' included); once it has seen the phase complete, every lane
+    // observes it once more (an already completed phase: one try_wait) for its own acquire
+    // of the data.  On the epilogue warps the wait also runs every segment that completes
+    // meanwhile (the MMA warps may be waiting for that accumulator).  Warp-uniform.
+    auto wait_d = [&](uint64_t* b, uint32_t parity) -> bool {
+     for (;;) {
+      int r = 1;  // lane 0: 1 done, 0 failed, 2 an epilogue is due
+      if (lane == 0) {
+        if (!mbar_try_wait(b, parity)) {
+          const uint64_t t_start = global_ns();
+          for (;;) {
+            if (epi && ep < nseg && mbar_try_wait(&acc_full[ep % NB], (uint32_t)((ep / NB) & 1))) {
+              r = 2;
+              break;
+            }
+            if (mbar_try_wait_sleep(b, parity, 2000u)) break;
+            if (*abort_flag) {
+              r = 0;
+              break;
+            }
+            if (global_ns() - t_start > kWaitBudgetNs) {
+              raise_status(a.status, kDevWaitTimeout);
+              *abort_flag = 1;
+              r = 0;
+              break;
+            }
+          }
+        }
+      }
+      r = __shfl_sync(0xffffffffu, r, 0);
+      if (r == 2) {
+        mbar_try_wait(&acc_full[ep % NB], (uint32_t)((ep / NB) & 1));
+        epilogue(ep++);
+        continue;
+      }
+      if (r == 1) mbar_try_wait(b, parity);
+      return r == 1;
+     }
+    };
+    // Each decode warp streams its own 16-row tile's groups: the slot region it has just
+    // decoded is refilled at once with its tile's group SR later (bulk copies are issued
+    // by sixteen threads in parallel; one thread issuing them all is too slow), so its
+    // barrier [slot][tile] needs no release by any other warp.
+    auto issue = [&](int gi) {  // lane 0: the tile's copy of unit u0 + gi into slot gi % SR
+      const int u = u0 + gi, rt = u / G, g = u - rt * G;
+      uint64_t* b = &raw_full[(gi % SR) * 8 + tile];
+      const int64_t t16 = (int64_t)rt * 8 + tile;
+      if (t16 < a.T) {
+        mbar_arrive_expect_tx(b, (uint32_t)F::GB);
+        bulk_g2s(sm + P::offRaw + (gi % SR) * P::kRaw + tile * F::GB, a.w + (t16 * G + g) * F::GB, F::GB, b);
+      } else {
+        mbar_arrive(b);  // rows past N: no copy, but the phase advances
+      }
+    };
+    int issued = set;  // this warp issues units set, set + 2, ... in order
+    if (lane == 0)
+      for (; issued < n && issued < SR; issued += 2) issue(issued);
+    for (int gi = set; gi < n; gi += 2) {
+      const int sr = gi % SR, sa = gi % SA;
+      const bool live = (int64_t)((u0 + gi) / G) * 8 + tile < a.T;
+      bool ok = wait_d(&raw_full[sr * 8 + tile], (uint32_t)((gi / SR) & 1));
+      // the slot's previous group, gi - SA, was multiplied by the issuer of its parity
+      if (ok && gi >= SA) ok = wait_d(&a_empty[((gi - SA) & 1) * SA + sa], (uint32_t)(((gi - SA) / LA) & 1));
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      if (live)
+        ts_decode<FMT>(smem_u32(sm + P::offRaw + sr * P::kRaw + tile * F::GB),
+                       tmem + tlane + (uint32_t)(P::A0 + sa * F::ACOLS), lane, a.wpow2, wa);
+      tmem_wait_st();  // before any register the stores read can be reused
+      // the slot's bytes are in registers: order those reads before the async refill
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0 && issued < n) {
+        issue(issued);
+        issued += 2;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[set * SA + sa]);
     }
+    // no copy may still be landing when the CTA exits (only an aborted run leaves any)
+    if (lane == 0 && *abort_flag)
+      for (int gi = (issued - SR > set ? issued - SR : set); gi < issued; gi += 2)
+        mbar_wait_ns(&raw_full[(gi % SR) * 8 + tile], (uint32_t)((gi / SR) & 1), kWaitBudgetNs, a.status);
+    if (epi)
+      while (ep < nseg) {
+        const int ok = __shfl_sync(0xffffffffu, lane == 0 ? (int)wait(&acc_full[ep % NB], (uint32_t)((ep / NB) & 1)) : 0, 0);
+        if (!ok) break;
+        mbar_try_wait(&acc_full[ep % NB], (uint32_t)((ep / NB) & 1));
+        epilogue(ep++);
+      }
   }
   // teardown: outstanding MMAs must finish before the tensor memory is released
   tc_fence_before();
   __syncthreads();
-  if (warp == 1 && lane == 0 && *abort_flag) mbar_wait_ns(acc_full, 0u, kWaitBudgetNs, a.status);
+  if (warp == 1 && lane == 0) mbar_wait_ns(mma_done, 0u, kWaitBudgetNs, a.status);  // both issuers' MMAs
   __syncthreads();
   tc_fence_after();
   if (warp == 3) tmem_dealloc(tmem, kTsCols);
+}
+
+// Row tiles whose units span several CTAs: their f32 partials (slot 2c for the first
+// segment of CTA c, 2c + 1 for its last) added in CTA order, then scaled and biased as the
+// GEMM's epilogue does.  Block (row tile, chunk of 8 tokens), one thread per row.
+__global__ void __launch_bounds__(128) ts_fixup_kernel(const float* partial, int R, int G, int C, int TN, int M,
+                                                       int64_t N, const float* tscale, const float* row_scale,
+                                                       int scale_len, float escale, const float* bias, void* y,
+                                                       int y_dtype, int64_t ldy) {
+  pdl_trigger();
+  pdl_wait();  // the partials are the GEMM's output
+  const int rt = blockIdx.x, U = R * G, t0 = 8 * blockIdx.y;
+  auto cta_of = [&](int u) {  // the CTA whose units include u
+    int c = (int)((int64_t)u * C / U);
+    while (c + 1 < C && ts_unit0(c + 1, U, C) <= u) ++c;
+    while (c > 0 && ts_unit0(c, U, C) > u) --c;
+    return c;
+  };
+  const int ca = cta_of(rt * G), cb = cta_of(rt * G + G - 1);
+  const int64_t nrow = (int64_t)rt * 128 + threadIdx.x;
+  if (ca == cb || nrow >= N) return;  // one CTA covered the row tile and wrote y itself
+  const float es = row_scale ? row_scale[scale_len == 1 ? 0 : nrow] : escale;
+  const float eb = bias ? bias[nrow] : 0.0f;
+  float s[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = 0.0f;
+  for (int c = ca; c <= cb; ++c) {
+    const int which = ts_unit0(c, U, C) / G == rt ? 0 : 1;
+    const float* p = partial + ((size_t)(2 * c + which) * TN + t0) * 128 + threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] += (t0 + j < TN) ? p[(size_t)j * 128] : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int t = t0 + j;
+    if (t >= M) break;
+    const float val = s[j] * tscale[t] * es + eb;
+    const int64_t off = (int64_t)t * ldy + nrow;
+    if (y_dtype == 0)
+      static_cast<float*>(y)[off] = val;
+    else if (y_dtype == 1)
+      static_cast<__half*>(y)[off] = __float2half_rn(val);
+    else
+      static_cast<__nv_bfloat16*>(y)[off] = __float2bfloat16_rn(val);
+  }
 }
 
 // ---------------------------------------------------------------- activation staging
@@ -578,8 +781,8 @@ cudaError_t launch_ts_tn(const TsGemm& g, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured[dev & 63] = 1;
   }
-  const dim3 grid((unsigned)(g.Mp / TN), (unsigned)((g.T + 7) / 8), (unsigned)g.splits);
-  return launch_pdl(qgemm_ts_kernel<FMT, TN>, grid, dim3(kTsThreads), (size_t)P::launch_bytes, st, g);
+  return launch_pdl(qgemm_ts_kernel<FMT, TN>, dim3((unsigned)g.ctas), dim3(kTsThreads), (size_t)P::launch_bytes, st,
+                    g);
 }
 
 template <int FMT>
@@ -613,14 +816,26 @@ cudaError_t launch_ts_prep(const QGemvCall& c, int gfmt, int64_t Mp, int64_t kp,
   return launch_prep_xdt<2>(gfmt, c, Mp, kp, x8, tscale);
 }
 
+bool ts_needs_fixup(int R, int G, int C) {
+  for (int c = 1; c < C; ++c)
+    if (ts_unit0(c, R * G, C) % G != 0) return true;
+  return false;
+}
+
 cudaError_t launch_ts_gemm(const TsGemm& g, cudaStream_t st) {
+  cudaError_t e;
   switch (g.fmt) {
-    case FMT_Q4K: return launch_ts_fmt<FMT_Q4K>(g, st);
-    case FMT_Q6K: return launch_ts_fmt<FMT_Q6K>(g, st);
-    case FMT_Q80: return launch_ts_fmt<FMT_Q80>(g, st);
-    case FMT_FP8: return launch_ts_fmt<FMT_FP8>(g, st);
-    default: return launch_ts_fmt<FMT_TS_F8X>(g, st);
+    case FMT_Q4K: e = launch_ts_fmt<FMT_Q4K>(g, st); break;
+    case FMT_Q6K: e = launch_ts_fmt<FMT_Q6K>(g, st); break;
+    case FMT_Q80: e = launch_ts_fmt<FMT_Q80>(g, st); break;
+    case FMT_FP8: e = launch_ts_fmt<FMT_FP8>(g, st); break;
+    default: e = launch_ts_fmt<FMT_TS_F8X>(g, st); break;
   }
+  if (e != cudaSuccess || !ts_needs_fixup((int)g.R, (int)g.G, g.ctas)) return e;
+  const bool q = g.fmt != FMT_FP8 && g.fmt != FMT_TS_F8X;
+  return launch_pdl(ts_fixup_kernel, dim3((unsigned)g.R, (unsigned)((g.M + 7) / 8)), dim3(128), 0, st,
+                    (const float*)g.partial, (int)g.R, (int)g.G, g.ctas, g.TN, (int)g.M, g.N, g.tscale, g.row_scale,
+                    g.scale_len, q ? 16777216.0f / g.wpow2 : 1.0f, g.bias, g.y, g.y_dtype, g.ldy);
 }
 
 }  // namespace rtd

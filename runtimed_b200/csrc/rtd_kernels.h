@@ -78,6 +78,7 @@ struct QGemvCall {
   int sm_count;
   cudaStream_t stream;
   const TpReduce* tp;      // null, or the row-parallel reduction of this call
+  float wpow2;             // K-quant / Q8_0 weights: the power of two F of ts_decode_scale (0: none)
 };
 
 // Returns cudaSuccess or the launch error; *plan_error is set (non-zero) when the
@@ -100,9 +101,11 @@ struct TsGemm {
   const uint8_t* w;
   const float* row_scale;  // FP8 only (else null)
   int scale_len;
+  float wpow2;             // the decoders' factor scale F (K-quants, Q8_0)
   int64_t N, T, G;         // rows, 16-row tiles, groups per row
-  int64_t M, Mp;           // tokens, tokens padded to TN
-  int TN, splits;
+  int64_t R;               // row tiles of 128 rows
+  int64_t M, Mp;           // tokens (at most TN), Mp = TN
+  int TN, ctas;            // tokens a CTA, persistent CTAs (stream-K over row tile x group units)
   const void* xw;          // staged activations (launch_ts_prep)
   const float* tscale;     // [Mp] per-token scale
   const float* bias;
@@ -110,9 +113,14 @@ struct TsGemm {
   int y_dtype;
   int64_t ldy;
   int* status;
-  float* partial;          // [splits][Mp][N] when splits > 1
+  float* partial;          // [2 * ctas][TN][128] f32: the split row tiles' partial sums
 };
+// f32 words of the skinny GEMM's partial-sum slots.
+inline size_t ts_partial_floats(int ctas, int TN) { return (size_t)2 * ctas * TN * 128; }
 // k per group of the GEMM's format, activation staging in the decoder's k order, the GEMM.
+// The skinny GEMM's decoders feed the tensor cores f16 values 2^s * w (codes as exact f16
+// subnormals, one FMA per pair with factors scaled by F = 2^(24 + s)); F is fixed per weight
+// at upload (ts_decode_scale) so that no scaled factor exceeds the f16 range.
 int ts_group_k(int gfmt);
 cudaError_t launch_ts_prep(const QGemvCall& c, int gfmt, int64_t Mp, int64_t kp, void* xw, float* tscale);
 cudaError_t launch_ts_gemm(const TsGemm& g, cudaStream_t st);

@@ -91,6 +91,11 @@ RTD_HD inline int group_payload_offset(int fmt) {
 // (or E4M3 bytes, K per row, for FP8); `out` has tiles*groups*GB bytes.
 void repack_host(int fmt, const uint8_t* raw, int64_t N, int64_t K, uint8_t* out);
 
+// Power of two F = 2^e for the skinny GEMM's decoders: the largest with every scaled factor
+// (Q4_K d * sc and dmin * m, Q6_K d * sc, Q8_0 d, times F) inside the f16 range, from
+// the raw GGUF blocks.  1 for FP8 (its decoder needs no factor).
+float ts_decode_scale(int fmt, const uint8_t* raw, int64_t N, int64_t K);
+
 // Number of tiles / groups for a matrix.
 inline int64_t tiles_for(int64_t N) { return (N + 15) / 16; }
 inline int64_t groups_for(int fmt, int64_t K) {

@@ -3,6 +3,7 @@
 // Q8_0, FP8) or of 6-bit codes (Q6_K): no value changes, so the device decoders
 // reproduce the reference dequantization bit for bit.  Padding (rows past N, k
 // past K) is zero bytes.
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -120,6 +121,38 @@ void repack_host(int fmt, const uint8_t* raw, int64_t N, int64_t K, uint8_t* out
       }
     }
   }
+}
+
+namespace {
+float half_bits_to_float(uint16_t h) {
+  const uint32_t e = (h >> 10) & 0x1Fu, m = h & 0x3FFu;
+  const float v = e == 0 ? std::ldexp((float)m, -24) : e == 31 ? INFINITY : std::ldexp((float)(m | 0x400u), (int)e - 25);
+  return (h & 0x8000u) ? -v : v;
+}
+uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+}  // namespace
+
+float ts_decode_scale(int fmt, const uint8_t* raw, int64_t N, int64_t K) {
+  if (fmt == FMT_FP8) return 1.0f;
+  const FmtInfo f = fmt_info(fmt);
+  const int64_t blocks = N * (K / f.block_elems);
+  float mx = 0.0f;  // the largest |factor| a decoder can form
+  for (int64_t b = 0; b < blocks; ++b) {
+    const uint8_t* p = raw + (size_t)b * (size_t)f.block_bytes;
+    float v;
+    if (fmt == FMT_Q4K)
+      v = 63.0f * std::fmax(std::fabs(half_bits_to_float(rd16(p))), std::fabs(half_bits_to_float(rd16(p + 2))));
+    else if (fmt == FMT_Q6K)
+      v = 128.0f * std::fabs(half_bits_to_float(rd16(p + 208)));
+    else
+      v = std::fabs(half_bits_to_float(rd16(p)));
+    if (v > mx) mx = v;  // NaN never raises it
+  }
+  int e = 24;
+  if (mx > 0.0f && std::isfinite(mx)) e = (int)std::floor(std::log2(65504.0f / mx));
+  if (e > 100) e = 100;
+  if (e < -100) e = -100;
+  return std::ldexp(1.0f, e);
 }
 
 }  // namespace rtd
