@@ -873,9 +873,10 @@ def main() -> int:
     fmt = d["format"].lower().replace("_", "")
     step_gbs = w_bytes / (ms_max * 1e-3 / args.steps) / 1e9
     roofline = {"bound": "hbm", "achieved": d["gbs"], "peak": peak, "unit": "GB/s", "frac": d["gbs"] / peak,
-                "traffic": profile_traffic(f"qgemm_{fmt}_{d['shard_nk'][0]}x{d['shard_nk'][1]}_m{BATCH}"),
+                # up to 64 tokens run the skinny GEMM (decoded weights in tensor memory)
+                "traffic": profile_traffic(f"qgemm_ts_{fmt}_{d['shard_nk'][0]}x{d['shard_nk'][1]}_m{BATCH}"),
                 "kernel": f"{dom} ({d['format']}, rank shard {d['shard_nk'][0]}x{d['shard_nk'][1]}, M={BATCH}): "
-                          f"tensor-core GEMM (qgemm_kernel) and its prep",
+                          f"skinny tensor-core GEMM (qgemm_ts_kernel) with its prep and fixup",
                 "launch_us": d["us"], "duration_source": "CUDA events around a graph of 24 back-to-back calls over "
                                                          "3 layers' weight copies",
                 "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
