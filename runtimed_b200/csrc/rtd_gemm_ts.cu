@@ -51,7 +51,7 @@ constexpr int kTsThreads = 640;     // 20 warps: 0 activations, 1 and 3 MMA (3 o
 constexpr int kTsSmem = 227 * 1024;
 constexpr int kTsCols = 512;        // the whole tensor memory of the SM (one CTA per SM)
 constexpr int kTsMaxSlots = 8;
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 1024;  // one block per token
 
 // Per-format constants: GK k per group, GB bytes per 16-row group, ACOLS tensor-memory
 // columns of one group's A (128 rows), NMMA instructions per group (K = 16 f16 or K = 32
