@@ -607,7 +607,47 @@ def _m_sweep(dev, rank, tflops_peak):
         out[name] = row
         del objs
     out["FP8_W8A8"] = _fp8_w8a8_vs_cublaslt(dev, n, k, tflops_peak)
+    out["INT4_MARLIN"] = _marlin_points(dev, n, k)
     return out
+
+
+def _marlin_points(dev, n, k):
+    """INT4 Marlin weights (marlin_gemv.rs: 0.5 byte a weight + a f32 scale a row) at the same
+    (N, K), M = 1 and 64, in GB/s of algorithmic bytes; CUDA graph of 10 calls over 3 copies."""
+    import torch
+    from runtimed_b200 import _lib
+    from runtimed_b200.weights import MarlinWeight, repack_marlin_tiles
+
+    L = _lib.lib()
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((n, k)).astype(np.float32) * np.float32(0.02))
+    packed, s = repack_marlin_tiles(w, np.abs(w).max(axis=1) / np.float32(7.0))
+    objs = [MarlinWeight(packed, s, k, n, device=dev)]
+    objs += [objs[0].to_device(dev) for _ in range(2)]
+    stream = torch.cuda.current_stream(dev)
+    row = {"bytes_per_weight": 0.5}
+    for m in (1, 64):
+        x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+        def call(o, st):
+            rc = L.rtd_qlinear(o.ctx.handle, o.handle, x.data_ptr(), _lib.DT_BF16, k, m, None, y.data_ptr(),
+                               _lib.DT_BF16, n, st)
+            if rc != 0:
+                raise RuntimeError(f"marlin M={m}: status {rc}")
+
+        for o in objs:
+            call(o, stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+        g = _capture(lambda st: [call(objs[r % 3], st) for r in range(10)], dev)
+        for _ in range(2):
+            g.replay()
+        us = _time_graph(g, stream, dev, 5) * 1e6 / 10
+        del g
+        gbs = (n * k // 2 + 4 * n + m * k * 2 + m * n * 2) / (us * 1e-6) / 1e9
+        row[f"m{m}"] = {"us": round(us, 2), "gbs": round(gbs, 1)}
+    del objs
+    return row
 
 
 def _fp8_w8a8_vs_cublaslt(dev, n, k, tflops_peak):

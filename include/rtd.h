@@ -49,8 +49,9 @@ enum {
     RTD_ERR_WORKSPACE = 10     /* the call needs more scratch than the context reserved */
 };
 
-/* GGML type ids (crates/runtimed-gguf/src/quant/dtype.rs:27-46). */
-enum { RTD_TYPE_Q8_0 = 8, RTD_TYPE_Q4_K = 12, RTD_TYPE_Q6_K = 14 };
+/* GGML type ids (crates/runtimed-gguf/src/quant/dtype.rs:27-46), and the id this library
+ * reports for INT4 Marlin weights (rtd_marlin_upload; not a GGUF type). */
+enum { RTD_TYPE_Q8_0 = 8, RTD_TYPE_Q4_K = 12, RTD_TYPE_Q6_K = 14, RTD_TYPE_INT4_MARLIN = 1001 };
 
 /* Activation / output element types. */
 enum { RTD_DT_F32 = 0, RTD_DT_F16 = 1, RTD_DT_BF16 = 2 };
@@ -88,6 +89,16 @@ rtd_status rtd_block_geometry(uint32_t ggml_type, int64_t* elems, int64_t* bytes
 rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host_blocks,
                               size_t nbytes, int64_t N, int64_t K, rtd_qweight** out);
 rtd_status rtd_qweight_free(rtd_qweight* w);
+/* INT4 Marlin weights.  Replaces MarlinWeight::new / to the device and the sm_80 PTX GEMV
+ * behind marlin_gemv (crates/runtimed-model/src/ops/marlin_gemv.rs:20-31,122-202,
+ * ops/ptx_marlin.rs): packed = host u32 [ceil(K / 32)][N][4] (nibble i of word w of chunk c
+ * is k = 32c + 8w + i), scales = host f32 [N]; value = (q - 8) * scales[n].  The handle
+ * works with rtd_qlinear (any token count) and rtd_qdequant (bit-exact with
+ * MarlinWeight::dequantize); rtd_qembed and the row-parallel entry refuse it
+ * (RTD_ERR_UNSUPPORTED).  rtd_qweight_info reports RTD_TYPE_INT4_MARLIN and, as raw_bytes,
+ * MarlinWeight::resident_bytes. */
+rtd_status rtd_marlin_upload(rtd_ctx* ctx, const uint32_t* packed, const float* scales, int64_t N, int64_t K,
+                             rtd_qweight** out);
 /* A copy of `src` owned by `ctx` (same or another device), made on the devices without
  * a host round trip.  Replaces Weights::to_device (crates/runtimed-model/src/weights/store.rs:170-205)
  * for quantized entries, which stay quantized (the reference leaves q_map entries in place). */

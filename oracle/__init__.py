@@ -188,3 +188,57 @@ def ref_cpu_fp8_linear(x, w, scale, N, K, threads: int = 0) -> np.ndarray:
 
 def max_threads() -> int:
     return int(lib().rtdo_max_threads())
+
+
+# ---------------------------------------------------------------- INT4 Marlin
+# crates/runtimed-model/src/ops/marlin_gemv.rs: the packed layout [ceil(K/32)][N][4] u32,
+# nibble `nib` of word `w` of chunk `c` is k = 32c + 8w + nib (:47-59, :76-94).
+
+def marlin_repack(weight, scales):
+    """repack_marlin_tiles (marlin_gemv.rs:64-97): q = clamp(round(w * inv_s) + 8, 0, 15)
+    with f32 arithmetic, round half away from zero, inv_s = 1 / s unless |s| <= 1e-12."""
+    w = np.asarray(weight, dtype=np.float32)
+    n, k = w.shape
+    s = np.asarray(scales, dtype=np.float32).reshape(-1)
+    kc = (k + 31) // 32
+    packed = np.zeros((kc, n, 4), dtype=np.uint32)
+    for c in range(kc):
+        for r in range(n):
+            inv = np.float32(1.0) / s[r] if abs(float(s[r])) > 1e-12 else np.float32(1.0)
+            for wi in range(4):
+                word = 0
+                for nib in range(8):
+                    kk = c * 32 + wi * 8 + nib
+                    if kk < k:
+                        v = np.float32(w[r, kk] * inv)
+                        rv = np.floor(abs(float(v)) + 0.5) * (1.0 if v >= 0 else -1.0)
+                        q = int(min(max(rv + 8.0, 0.0), 15.0))
+                    else:
+                        q = 8
+                    word |= (q & 0xF) << (4 * nib)
+                packed[c, r, wi] = word
+    return packed
+
+
+def marlin_dequant(packed, scales, n: int, k: int) -> np.ndarray:
+    """MarlinWeight::dequantize (marlin_gemv.rs:42-60): ((q as i32 - 8) as f32) * s[n] in f32."""
+    p = np.asarray(packed, dtype=np.uint32).reshape(-1)
+    s = np.asarray(scales, dtype=np.float32).reshape(-1)
+    kc = (k + 31) // 32
+    out = np.zeros((n, k), dtype=np.float32)
+    for c in range(kc):
+        base = (c * n + np.arange(n)) * 4
+        for wi in range(4):
+            words = p[base + wi]
+            for nib in range(8):
+                kk = c * 32 + wi * 8 + nib
+                if kk < k:
+                    q = ((words >> np.uint32(4 * nib)) & np.uint32(0xF)).astype(np.int32) - 8
+                    out[:, kk] = q.astype(np.float32) * s
+    return out
+
+
+def marlin_gemv_f64(x, packed, scales, n: int, k: int) -> np.ndarray:
+    """cpu_marlin_gemv_fallback (marlin_gemv.rs:99-110) accumulated in f64."""
+    w = marlin_dequant(packed, scales, n, k).astype(np.float64)
+    return np.asarray(x, dtype=np.float64).reshape(-1, k) @ w.T

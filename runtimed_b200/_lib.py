@@ -25,6 +25,7 @@ RTD_ERR_DEVICE = 9
 RTD_ERR_WORKSPACE = 10
 
 TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 8, 12, 14
+TYPE_INT4_MARLIN = 1001  # rtd_marlin_upload handles (not a GGUF type)
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 FP8_W8A16, FP8_W8A8 = 0, 1
 
@@ -42,6 +43,7 @@ SIGNATURES = {
     "rtd_block_geometry": (_c.c_int32, [_u32, _c.POINTER(_i64), _c.POINTER(_i64)]),
     "rtd_qweight_upload": (_c.c_int32, [_vp, _u32, _vp, _c.c_size_t, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_free": (_c.c_int32, [_vp]),
+    "rtd_marlin_upload": (_c.c_int32, [_vp, _vp, _vp, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_to_device": (_c.c_int32, [_vp, _vp, _c.POINTER(_vp)]),
     "rtd_qweight_rows": (_c.c_int32, [_vp, _i64, _i64, _c.POINTER(_vp)]),
     "rtd_qweight_info": (_c.c_int32, [_vp, _c.POINTER(_u32), _c.POINTER(_i64), _c.POINTER(_i64),

@@ -38,6 +38,10 @@ struct rtd_qweight {
   size_t dev_bytes = 0, raw_bytes = 0;
   bool owns = true;  // false for a row view (rtd_qweight_rows): the parent owns the memory
   float wpow2 = 0.0f;  // rtd::ts_decode_scale of the raw blocks
+  // INT4 Marlin weights (rtd_marlin_upload): held as Q4_K groups whose codes decode to
+  // q - 8, with the per-row f32 scale applied by every kernel's epilogue
+  float* row_scale = nullptr;
+  bool owns_scale = false;
 };
 
 struct rtd_fp8weight {
@@ -190,6 +194,8 @@ rtd_status rtd_check_device_status(rtd_ctx* ctx, void* stream) {
 rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host_blocks, size_t nbytes,
                               int64_t N, int64_t K, rtd_qweight** out) {
   if (!ctx || !out) return fail(ctx, RTD_ERR_INVALID, "rtd_qweight_upload: NULL argument");
+  if (ggml_type == RTD_TYPE_INT4_MARLIN)
+    return fail(ctx, RTD_ERR_UNSUPPORTED, "rtd_qweight_upload: INT4 Marlin weights go through rtd_marlin_upload");
   *out = nullptr;
   const int fmt = fmt_of_type(ggml_type);
   if (fmt < 0) return fail(ctx, RTD_ERR_UNSUPPORTED, "rtd_qweight_upload: ggml type %u is not Q4_K/Q6_K/Q8_0", ggml_type);
@@ -239,6 +245,62 @@ rtd_status rtd_qweight_upload(rtd_ctx* ctx, uint32_t ggml_type, const void* host
   return RTD_OK;
 }
 
+// INT4 Marlin weights (marlin_gemv.rs:11-97): packed[ceil(K/32)][N][4] u32 words, nibble
+// `nib` of word `w` of chunk c holding k = 32c + 8w + nib, value (q - 8) * scales[n].  They
+// are held as Q4_K groups whose headers make every code decode to q - 8 exactly (d = 1,
+// dmin = 8, all sub-block scales and mins 1: d*sc*q - dmin*m = q - 8), so the GEMV and
+// both tensor-core GEMMs run them unchanged; the f32 row scale is applied where the FP8
+// row scale is, in every epilogue.  K is padded to 256 with code 8 (value 0).
+rtd_status rtd_marlin_upload(rtd_ctx* ctx, const uint32_t* packed, const float* scales, int64_t N, int64_t K,
+                             rtd_qweight** out) {
+  const char* who = "rtd_marlin_upload";
+  if (!ctx || !out) return fail(ctx, RTD_ERR_INVALID, "%s: NULL argument", who);
+  *out = nullptr;
+  if (N < 0 || K < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: negative shape [%lld, %lld]", who, (long long)N, (long long)K);
+  if (N > 0 && K > 0 && (!packed || !scales)) return fail(ctx, RTD_ERR_INVALID, "%s: packed or scales is NULL", who);
+  const int64_t kc = (K + 31) / 32, G = (K + 255) / 256;
+  std::vector<uint8_t> raw;
+  try {
+    raw.assign((size_t)N * (size_t)G * 144, 0);
+  } catch (...) {
+    return fail(ctx, RTD_ERR_OOM, "%s: host staging allocation failed", who);
+  }
+  static const uint8_t kHeader[16] = {0x00, 0x3C, 0x00, 0x48, 1, 1, 1, 1, 1, 1, 1, 1, 0x11, 0x11, 0x11, 0x11};
+  for (int64_t n = 0; n < N; ++n)
+    for (int64_t g = 0; g < G; ++g) {
+      uint8_t* blk = raw.data() + (size_t)(n * G + g) * 144;
+      std::memcpy(blk, kHeader, 16);
+      for (int e = 0; e < 256; ++e) {
+        const int64_t k = g * 256 + e;
+        uint32_t q = 8;
+        if (k < K) q = (packed[((k / 32) * N + n) * 4 + (k % 32) / 8] >> (4 * (k % 8))) & 0xFu;
+        // Q4_K element e: chunk e / 64, byte (e % 32), low nibble for e % 64 < 32
+        uint8_t& b = blk[16 + 32 * (e / 64) + (e % 32)];
+        b |= (uint8_t)((e % 64) < 32 ? q : (q << 4));
+      }
+    }
+  rtd_status st = rtd_qweight_upload(ctx, RTD_TYPE_Q4_K, raw.data(), raw.size(), N, G * 256, out);
+  if (st != RTD_OK) return st;
+  rtd_qweight* w = *out;
+  w->ggml_type = RTD_TYPE_INT4_MARLIN;
+  w->K = K;                                                       // x has K columns; groups past K decode to 0
+  w->raw_bytes = (size_t)kc * (size_t)N * 16 + (size_t)N * 4;     // MarlinWeight::resident_bytes
+  if (N > 0) {
+    DeviceGuard g(ctx->device);
+    cudaError_t e = cudaMalloc(&w->row_scale, (size_t)N * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(w->row_scale, scales, (size_t)N * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(w->row_scale);
+      w->row_scale = nullptr;
+      rtd_qweight_free(w);
+      *out = nullptr;
+      return fail(ctx, RTD_ERR_OOM, "%s: scales: %s", who, cudaGetErrorString(e));
+    }
+    w->owns_scale = true;
+  }
+  return RTD_OK;
+}
+
 rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweight** out) {
   const char* who = "rtd_qweight_to_device";
   if (!src || !ctx || !out) return fail(ctx, RTD_ERR_INVALID, "%s: NULL argument", who);
@@ -247,6 +309,24 @@ rtd_status rtd_qweight_to_device(const rtd_qweight* src, rtd_ctx* ctx, rtd_qweig
   if (!w) return fail(ctx, RTD_ERR_OOM, "%s: host allocation failed", who);
   w->ctx = ctx;
   w->dev = nullptr;
+  w->owns = true;
+  w->row_scale = nullptr;
+  w->owns_scale = false;
+  if (src->row_scale) {
+    DeviceGuard g(ctx->device);
+    const size_t sb = (size_t)src->N * sizeof(float);
+    cudaError_t e = cudaMalloc(&w->row_scale, sb);
+    if (e == cudaSuccess)
+      e = (src->ctx->device == ctx->device)
+              ? cudaMemcpy(w->row_scale, src->row_scale, sb, cudaMemcpyDeviceToDevice)
+              : cudaMemcpyPeer(w->row_scale, ctx->device, src->row_scale, src->ctx->device, sb);
+    if (e != cudaSuccess) {
+      cudaFree(w->row_scale);
+      delete w;
+      return cuda_fail(ctx, e, who);
+    }
+    w->owns_scale = true;
+  }
   if (w->dev_bytes > 0) {
     DeviceGuard g(ctx->device);
     cudaError_t e = cudaMalloc(&w->dev, w->dev_bytes);
@@ -283,15 +363,18 @@ rtd_status rtd_qweight_rows(const rtd_qweight* w, int64_t row0, int64_t rows, rt
   v->dev_bytes = (size_t)v->T * (size_t)w->G * (size_t)f.gb;
   v->raw_bytes = w->raw_bytes / (size_t)(w->N > 0 ? w->N : 1) * (size_t)rows;
   v->owns = false;
+  if (w->row_scale) v->row_scale = w->row_scale + row0;
+  v->owns_scale = false;
   *out = v;
   return RTD_OK;
 }
 
 rtd_status rtd_qweight_free(rtd_qweight* w) {
   if (!w) return RTD_OK;
-  if (w->dev && w->owns) {
+  if ((w->dev && w->owns) || (w->row_scale && w->owns_scale)) {
     DeviceGuard g(w->ctx->device);
-    cudaFree(w->dev);
+    if (w->dev && w->owns) cudaFree(w->dev);
+    if (w->row_scale && w->owns_scale) cudaFree(w->row_scale);
   }
   delete w;
   return RTD_OK;
@@ -364,13 +447,14 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
 rtd_status rtd_qlinear(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx, int64_t M,
                        const float* bias, void* y, uint32_t y_dtype, int64_t ldy, void* stream) {
   if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qlinear: NULL ctx or weight");
-  return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, nullptr, 0, x, x_dtype, ldx, M, 0, bias, y, y_dtype, ldy,
-                  stream, "rtd_qlinear", w->wpow2);
+  return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, w->row_scale ? (int)w->N : 0, x, x_dtype, ldx,
+                  M, 0, bias, y, y_dtype, ldy, stream, "rtd_qlinear", w->wpow2);
 }
 
 rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n, float* y, void* stream) {
   if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qembed: NULL ctx or weight");
   if (n < 0) return fail(ctx, RTD_ERR_SHAPE, "rtd_qembed: n=%lld is negative", (long long)n);
+  if (w->row_scale) return fail(ctx, RTD_ERR_UNSUPPORTED, "rtd_qembed: INT4 Marlin weights are not an embedding format");
   if (n == 0 || w->K == 0) return RTD_OK;
   if (!ids || !y) return fail(ctx, RTD_ERR_INVALID, "rtd_qembed: ids or y is NULL");
   DeviceGuard g(ctx->device);
@@ -383,7 +467,7 @@ rtd_status rtd_qdequant(rtd_ctx* ctx, const rtd_qweight* w, float* y, void* stre
   if (w->N == 0 || w->K == 0) return RTD_OK;
   if (!y) return fail(ctx, RTD_ERR_INVALID, "rtd_qdequant: y is NULL");
   DeviceGuard g(ctx->device);
-  cudaError_t e = rtd::launch_dequant(w->fmt, w->dev, w->N, w->K, w->G, y, (cudaStream_t)stream);
+  cudaError_t e = rtd::launch_dequant(w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, y, (cudaStream_t)stream);
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, "rtd_qdequant");
 }
 
@@ -702,6 +786,7 @@ rtd_status rtd_tp_qlinear_row(rtd_comm* comm, const rtd_qweight* shard, const vo
   rtd_status st = tp_check_common(comm, M, y_dtype, y, who);
   if (st != RTD_OK) return st;
   if (shard->ctx != ctx) return fail(ctx, RTD_ERR_INVALID, "%s: weight and communicator on different contexts", who);
+  if (shard->row_scale) return fail(ctx, RTD_ERR_UNSUPPORTED, "%s: INT4 Marlin weights are not sharded", who);
   if (shard->N > comm->max_n)
     return fail(ctx, RTD_ERR_SHAPE, "%s: N=%lld above the communicator's max_n=%lld", who, (long long)shard->N,
                 (long long)comm->max_n);
@@ -885,6 +970,8 @@ rtd_status rtd_qlinear_noalloc(const rtd_qweight* w, const void* x, uint32_t x_d
   c.fmt = w->fmt;
   c.w = w->dev;
   c.wpow2 = w->wpow2;
+  c.row_scale = w->row_scale;
+  c.scale_len = (int)w->N;
   c.N = w->N;
   c.K = w->K;
   c.G = w->G;

@@ -76,12 +76,17 @@ __device__ __forceinline__ float decode_row_elem(const uint8_t* w, int64_t G, in
   return decode_elem<FMT>(grp, (int)(n & 15), (int)(k - s * GK));
 }
 
+// row_scale (INT4 Marlin weights, held as Q4_K groups that decode to q - 8): the value
+// times the row's f32 scale, as marlin_gemv.rs:47-59 forms it.
 template <int FMT>
 __global__ void dequant_kernel(const uint8_t* __restrict__ w, int64_t row0, int64_t K, int64_t G,
-                               float* __restrict__ y) {
+                               const float* __restrict__ row_scale, float* __restrict__ y) {
   const int64_t n = row0 + blockIdx.y;
-  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < K; k += (int64_t)gridDim.x * blockDim.x)
-    y[n * K + k] = decode_row_elem<FMT>(w, G, n, k);
+  const float s = row_scale ? row_scale[n] : 1.0f;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < K; k += (int64_t)gridDim.x * blockDim.x) {
+    const float v = decode_row_elem<FMT>(w, G, n, k);
+    y[n * K + k] = row_scale ? __fmul_rn(v, s) : v;
+  }
 }
 
 template <int FMT>
@@ -108,17 +113,17 @@ static dim3 row_grid(int64_t K, int64_t rows) {
 }
 
 // gridDim.y is limited to 65535, so rows are walked in slabs.
-cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, float* y,
-                           cudaStream_t st) {
+cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, const float* row_scale,
+                           float* y, cudaStream_t st) {
   for (int64_t r0 = 0; r0 < N && K > 0; r0 += 65535) {
     const int64_t rows = (N - r0 < 65535) ? N - r0 : 65535;
     const dim3 grid = row_grid(K, rows);
     count_launch();
     switch (fmt) {
-      case FMT_Q4K: dequant_kernel<FMT_Q4K><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
-      case FMT_Q6K: dequant_kernel<FMT_Q6K><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
-      case FMT_Q80: dequant_kernel<FMT_Q80><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
-      default:      dequant_kernel<FMT_FP8><<<grid, 256, 0, st>>>(w, r0, K, G, y); break;
+      case FMT_Q4K: dequant_kernel<FMT_Q4K><<<grid, 256, 0, st>>>(w, r0, K, G, row_scale, y); break;
+      case FMT_Q6K: dequant_kernel<FMT_Q6K><<<grid, 256, 0, st>>>(w, r0, K, G, row_scale, y); break;
+      case FMT_Q80: dequant_kernel<FMT_Q80><<<grid, 256, 0, st>>>(w, r0, K, G, row_scale, y); break;
+      default:      dequant_kernel<FMT_FP8><<<grid, 256, 0, st>>>(w, r0, K, G, row_scale, y); break;
     }
   }
   return cudaGetLastError();

@@ -92,7 +92,7 @@ struct GemmFmt<FMT_FP8> {
 
 struct GemmArgs {
   const uint8_t* w;
-  const float* row_scale;  // FP8
+  const float* row_scale;  // per output row (FP8, INT4 Marlin weights), or null
   int scale_len;
   int64_t N, T, G;         // rows, 16-row tiles, groups per row
   int nkb;                 // k stages (64 elements; 128 on the kind::f8f6f4 path)
@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(Roles<DW>::kThreads, Roles<DW>::kCtasPerSm) qg
       const int64_t n = tile0 * 16 + r;
       float es = 1.0f, eb = 0.0f;
       if (n < a.N) {
-        if (FMT == FMT_FP8 || F8) es = a.row_scale[a.scale_len == 1 ? 0 : n];
+        if (a.row_scale) es = a.row_scale[a.scale_len == 1 ? 0 : n];
         if (a.bias) eb = a.bias[n];
       }
 #pragma unroll 1
@@ -1005,7 +1005,7 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
     TsGemm g{};
     g.fmt = gfmt;
     g.w = c.w;
-    g.row_scale = c.fmt == FMT_FP8 ? c.row_scale : nullptr;
+    g.row_scale = c.row_scale;
     g.scale_len = c.scale_len;
     g.wpow2 = c.wpow2 > 0.0f ? c.wpow2 : 16777216.0f;
     g.N = c.N;
@@ -1059,7 +1059,7 @@ cudaError_t launch_qgemm(const QGemvCall& c, int* plan_error) {
   const int64_t total = (c.N % 4 == 0) ? c.M * c.N / 4 : c.M * c.N;
   const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * (int64_t)c.sm_count));
   return launch_pdl(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, c.stream, (const float*)partial, p.splits, Mp,
-                    c.M, c.N, (const float*)tscale, (const float*)(c.fmt == FMT_FP8 ? c.row_scale : nullptr),
+                    c.M, c.N, (const float*)tscale, (const float*)c.row_scale,
                     c.scale_len, c.bias, c.y, c.y_dtype, c.ldy);
 }
 

@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) qgemm_ts_kernel(const TsGemm a)
       // 2^-s undoes the decoders' power of two (K-quants, Q8_0); FP8 takes its row scale
       float es = (FMT == FMT_FP8 || F8) ? 1.0f : 16777216.0f / a.wpow2, eb = 0.0f;
       if (nrow < a.N) {
-        if (a.row_scale) es = a.row_scale[a.scale_len == 1 ? 0 : nrow];
+        if (a.row_scale) es *= a.row_scale[a.scale_len == 1 ? 0 : nrow];
         if (a.bias) eb = a.bias[nrow];
       }
       float* part = a.partial + (size_t)(2 * blockIdx.x + (sg == 0 ? 0 : 1)) * TN * 128 + r;
@@ -658,22 +658,22 @@ __global__ void __launch_bounds__(128) ts_fixup_kernel(const float* partial, int
   pdl_trigger();
   pdl_wait();  // the partials are the GEMM's output
   const int rt = blockIdx.x, U = R * G, t0 = 8 * blockIdx.y;
-  auto cta_of = [&](int u) {  // the CTA whose units include u
-    int c = (int)((int64_t)u * C / U);
-    while (c + 1 < C && ts_unit0(c + 1, U, C) <= u) ++c;
-    while (c > 0 && ts_unit0(c, U, C) > u) --c;
-    return c;
+  // the CTA whose units include u: the last c with floor(c U / C) <= u, i.e. c U < (u + 1) C
+  auto cta_of = [&](int u) {
+    const int64_t c = ((int64_t)(u + 1) * C - 1) / U;
+    return (int)(c < C - 1 ? c : C - 1);
   };
   const int ca = cta_of(rt * G), cb = cta_of(rt * G + G - 1);
+  const int64_t tile_u0 = (int64_t)rt * G * C;  // c's first unit is in this row tile iff c U >= rt G C
   const int64_t nrow = (int64_t)rt * 128 + threadIdx.x;
   if (ca == cb || nrow >= N) return;  // one CTA covered the row tile and wrote y itself
-  const float es = row_scale ? row_scale[scale_len == 1 ? 0 : nrow] : escale;
+  const float es = row_scale ? escale * row_scale[scale_len == 1 ? 0 : nrow] : escale;
   const float eb = bias ? bias[nrow] : 0.0f;
   float s[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = 0.0f;
   for (int c = ca; c <= cb; ++c) {
-    const int which = ts_unit0(c, U, C) / G == rt ? 0 : 1;
+    const int which = (int64_t)c * U >= tile_u0 ? 0 : 1;
     const float* p = partial + ((size_t)(2 * c + which) * TN + t0) * 128 + threadIdx.x;
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j] += (t0 + j < TN) ? p[(size_t)j * 128] : 0.0f;

@@ -619,7 +619,7 @@ __device__ __forceinline__ void do_group_diag(uint32_t gs, uint32_t xs, uint32_t
 
 struct Args {
   const uint8_t* w;
-  const float* row_scale;  // FP8
+  const float* row_scale;  // per output row (FP8, INT4 Marlin), or null
   int scale_len;
   const uint8_t* cols;
   const float* tab;
@@ -931,11 +931,11 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       const int64_t n = (int64_t)tile * 16 + (whole ? g : lane), n2 = n + 8;
       if (n < a.N) {
         if (a.bias) eb = __ldg(a.bias + n);
-        if constexpr (FMT == FMT_FP8) es = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n));
+        if (a.row_scale) es = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n));
       }
       if (whole && n2 < a.N) {
         if (a.bias) eb2 = __ldg(a.bias + n2);
-        if constexpr (FMT == FMT_FP8) es2 = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n2));
+        if (a.row_scale) es2 = __ldg(a.row_scale + (a.scale_len == 1 ? 0 : n2));
       }
     }
     for (int k = 0; k < per_tile; ++k, ++i) {

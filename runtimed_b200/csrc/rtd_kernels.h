@@ -18,9 +18,10 @@ inline std::atomic<uint64_t>& launch_counter() {
 }
 inline void count_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
 
-// Decode all N rows of an uploaded weight to f32 [N, K] (bit-exact).
-cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, float* y,
-                           cudaStream_t st);
+// Decode all N rows of an uploaded weight to f32 [N, K] (bit-exact); row_scale (or null)
+// multiplies row n's values by row_scale[n].
+cudaError_t launch_dequant(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, const float* row_scale,
+                           float* y, cudaStream_t st);
 // Gather + decode rows ids[0..n) to f32 [n, K]; out-of-range ids raise the status word.
 cudaError_t launch_embed(int fmt, const uint8_t* w, int64_t N, int64_t K, int64_t G, const uint32_t* ids,
                          int64_t n, float* y, int* status, cudaStream_t st);
@@ -61,7 +62,7 @@ struct QGemvCall {
   int fmt;
   const uint8_t* w;
   int64_t N, K, G;
-  const float* row_scale;  // FP8 only
+  const float* row_scale;  // per output row: FP8 and INT4 Marlin weights (null otherwise)
   int scale_len;           // FP8 only: 1 or N
   const void* x;
   int x_dtype;             // RTD_DT_*
@@ -99,7 +100,7 @@ constexpr int FMT_TS_F8X = 4;
 struct TsGemm {
   int fmt;
   const uint8_t* w;
-  const float* row_scale;  // FP8 only (else null)
+  const float* row_scale;  // per output row, or null
   int scale_len;
   float wpow2;             // the decoders' factor scale F (K-quants, Q8_0)
   int64_t N, T, G;         // rows, 16-row tiles, groups per row

@@ -259,6 +259,93 @@ class Fp8Weight:
             pass
 
 
+def _round_half_away(v: np.ndarray) -> np.ndarray:
+    """f32::round: halves go away from zero (numpy's round goes to even)."""
+    return (np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))).astype(np.float32)
+
+
+def repack_marlin_tiles(weight, scales):
+    """Dense [out, in] weight and per-row scales -> (packed u32 [ceil(in / 32), out, 4],
+    scales), as repack_marlin_tiles does (crates/runtimed-model/src/ops/marlin_gemv.rs:64-97):
+    q = clamp(round(w / s) + 8, 0, 15) in f32 (1 / s taken as 1 when |s| <= 1e-12), eight
+    nibbles to a word, k past `in` padded with 8.  Host-side packing, as in the reference."""
+    w = np.asarray(weight, dtype=np.float32)
+    if w.ndim != 2:
+        raise ConfigError(f"weight must be 2D, got {list(w.shape)}")
+    out_dim, in_dim = w.shape
+    s = np.asarray(scales, dtype=np.float32).reshape(-1)
+    if s.size != out_dim:
+        raise ShapeError("scales", [out_dim], [int(s.size)])
+    inv = np.where(np.abs(s) > np.float32(1e-12), np.float32(1.0) / s, np.float32(1.0)).astype(np.float32)
+    kc = (in_dim + 31) // 32
+    q = np.full((out_dim, kc * 32), 8, dtype=np.uint32)
+    if in_dim:
+        q[:, :in_dim] = np.clip(_round_half_away(w * inv[:, None]) + np.float32(8.0), 0.0, 15.0).astype(np.uint32)
+    nib = q.reshape(out_dim, kc, 4, 8)
+    words = np.zeros((out_dim, kc, 4), dtype=np.uint32)
+    for i in range(8):
+        words |= nib[..., i] << np.uint32(4 * i)
+    return np.ascontiguousarray(words.transpose(1, 0, 2)), s
+
+
+class MarlinWeight(QMatMul):
+    """INT4 Marlin weight (crates/runtimed-model/src/ops/marlin_gemv.rs:11-62): packed u32
+    [ceil(in / 32), out, 4] and f32 scales [out] (or [out, 1]); value (q - 8) * s[n].
+    forward runs the library's tensor-core paths (rtd_qlinear on an rtd_marlin_upload
+    handle) for any token count; dequantize is bit-exact with MarlinWeight::dequantize."""
+
+    def __init__(self, packed, scales, in_dim: int, out_dim: int, device="cuda:0"):
+        p = np.asarray(packed)
+        if p.dtype != np.uint32:
+            raise ConfigError(f"marlin packed must be U32, got {p.dtype}")
+        s = np.asarray(scales, dtype=np.float32)
+        if list(s.shape) not in ([out_dim], [out_dim, 1]):
+            raise ShapeError("marlin_scales", [out_dim], list(s.shape))
+        kc = (int(in_dim) + 31) // 32
+        if p.size < kc * out_dim * 4:
+            raise ShapeError("marlin_packed", [kc, out_dim, 4], list(p.shape))
+        self.ctx = Context.for_device(device)
+        self.ggml_type = _lib.TYPE_INT4_MARLIN
+        self.n, self.k = int(out_dim), int(in_dim)
+        p = np.ascontiguousarray(p.reshape(-1)[: kc * out_dim * 4])
+        s = np.ascontiguousarray(s.reshape(-1))
+        h = ctypes.c_void_p()
+        _raise(_lib.lib().rtd_marlin_upload(self.ctx.handle, p.ctypes.data_as(ctypes.c_void_p),
+                                            s.ctypes.data_as(ctypes.c_void_p), self.n, self.k, ctypes.byref(h)),
+               self.ctx.handle)
+        self.handle = h
+        raw_b, dev_b = ctypes.c_size_t(), ctypes.c_size_t()
+        check(_lib.lib().rtd_qweight_info(h, None, None, None, ctypes.byref(raw_b), ctypes.byref(dev_b)))
+        self._raw_bytes, self._dev_bytes = raw_b.value, dev_b.value
+
+    @property
+    def in_dim(self) -> int:
+        return self.k
+
+    @property
+    def out_dim(self) -> int:
+        return self.n
+
+    def resident_bytes(self) -> int:
+        return self._raw_bytes
+
+    def forward(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        if x.shape[-1] != self.k:
+            raise ShapeError("marlin_gemv", [self.k], list(x.shape))
+        return super().forward(x, bias, out_dtype)
+
+    __call__ = forward
+
+    def embedding(self, ids: torch.Tensor) -> torch.Tensor:
+        raise ConfigError("INT4 Marlin weights are not an embedding format")
+
+
+def marlin_gemv(x: torch.Tensor, w: MarlinWeight) -> torch.Tensor:
+    """y = x @ (w * scale)^T (marlin_gemv.rs:112-119), in x's dtype."""
+    return w.forward(x)
+
+
 def fp8_encode(x: torch.Tensor) -> torch.Tensor:
     """Device E4M3 encoding of f32 x with the reference rounding (uint8 codes)."""
     x = x.to(torch.float32).contiguous()
