@@ -80,7 +80,7 @@ struct TsFmt<FMT_TS_F8X> {
 };
 
 // Shared-memory and tensor-memory plan: SB activation slots (TN * BTOK bytes), SR
-// weight slots (8 * GB bytes), SA tensor-memory A slots after the accumulator.
+// weight slots (8 * GB bytes), SA tensor-memory A slots after the accumulators.
 template <int FMT, int TN>
 struct TsPlan {
   using F = TsFmt<FMT>;
@@ -91,14 +91,14 @@ struct TsPlan {
   // round trip: up to 96 KB of slots, at least three, at most eight.
   static constexpr int kSbFit = (96 * 1024) / kB;
   static constexpr int SB = kSbFit < 3 ? 3 : (kSbFit > kTsMaxSlots ? kTsMaxSlots : kSbFit);
-  static constexpr int kFixed = 1024 + 512 + TN * 4;  // alignment slack, barriers + misc, token scales
+  static constexpr int kFixed = 1024 + 1024;  // alignment slack, barriers + misc
   static constexpr int kFitR = (kTsSmem - kFixed - SB * kB) / kRaw;
   // even: a decode warp refills the slot it has just read with the group SR later, which
   // belongs to its own set again
   static constexpr int SR = (kFitR < kTsMaxSlots ? kFitR : kTsMaxSlots) & ~1;
-  // Two MMA-issuing threads take alternate halves of a group's K slices into their own
-  // accumulators (summed by the epilogue); NB accumulator pairs rotate over segments
-  // (two while they fit beside three A slots, else one).
+  // Two MMA-issuing threads take alternate groups into their own accumulators (summed by
+  // the epilogue); NB accumulator pairs rotate over segments (two while they fit beside
+  // three A slots, else one).
   static constexpr int ACC = TN < 32 ? 32 : TN;       // columns per accumulator
   static constexpr int NB = TN <= 32 ? 2 : 1;
   static constexpr int A0 = 2 * NB * ACC;              // first A column
