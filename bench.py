@@ -546,6 +546,9 @@ def _gemv_sweep(dev, stream, rank, peak):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": profile_traffic(f"qgemv_{dit['name'].lower()}_{dit['n']}x{dit['k']}_m1")},
             "per_gemv_gbs": {k2: round(v, 1) for k2, v in per.items()},
+            # the layer-shaped GEMVs beside the LM head: the fractions a Q4_K_M decode lives on
+            "layer_frac": {k2: round(per[k2] / peak, 3) for k2 in ("Q4_K:4096x4096", "Q4_K:14336x4096",
+                                                                   "Q6_K:4096x14336") if k2 in per},
             "timing": "CUDA graph of the 14-GEMV pass (20 replays); per GEMV a graph of 24 launches over 3 "
                       "device copies, CUDA events"}
 

@@ -270,3 +270,39 @@ def test_fp8_w8a8_tensor_core_path(M):
         y = fw.forward(xt.cuda(), mode="w8a8").float().cpu().numpy()
         want = oracle.fp8_gemm_w8a8_f64(xt.float().numpy(), w, s, N, K)
         assert rel_l2(y, want) <= 2e-6, dt
+
+
+# The rank shards of the config-3 (70B-shaped) decoder's linears at 2, 4 and 8 GPUs:
+# column-parallel attn_q+k / attn_v / ffn_gate+up split N, row-parallel attn_output /
+# ffn_down split K.  The 8-GPU shards are the smallest shapes the tensor-parallel step runs
+# (a 128-row attn_v shard is one row tile shared by eight CTAs of the skinny GEMM).
+_TP_SHARDS = sorted({
+    (name, t, n, k)
+    for w in (2, 4, 8)
+    for name, t, n, k in [("attn_qk", 12, (8192 + 1024) // w, 8192), ("attn_v", 14, 1024 // w, 8192),
+                          ("ffn_gate_up", 12, 2 * 28672 // w, 8192), ("attn_output", 12, 8192, 8192 // w),
+                          ("ffn_down", 14, 8192, 28672 // w)]
+})
+
+
+@pytest.mark.parametrize("M", [1, 64])
+@pytest.mark.parametrize("name,t,N,K", _TP_SHARDS)
+def test_config3_tp_shard_shapes(name, t, N, K, M):
+    import torch
+    from runtimed_b200.weights import QMatMul
+
+    key = ("tp", t, N, K)
+    if key not in _SWEEP_CACHE:
+        _SWEEP_CACHE.clear()  # one shard resident at a time
+        raw = synth.quant_matrix(t, N, K, seed=N + K, stream=t)
+        _SWEEP_CACHE[key] = (QMatMul(t, raw, N, K), raw)
+    qm, raw = _SWEEP_CACHE[key]
+    x = synth.bf16_round(synth.activations(M, K, seed=M, stream=K))
+    y = qm.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), out_dtype=torch.float32)
+    rows = _sampled_rows(N, 64)
+    elems, bb = synth.BLOCK[t]
+    sub = np.ascontiguousarray(raw.reshape(N, (K // elems) * bb)[rows]).reshape(-1)
+    want = oracle.qgemv_f64(t, sub, len(rows), K, x)
+    got = y[:, torch.from_numpy(rows).cuda()].cpu().numpy()
+    assert np.isfinite(y.cpu().numpy()).all()
+    assert rel_l2(got, want) <= (2e-5 if M == 1 else RTOL)
