@@ -199,6 +199,19 @@ rtd_status rtd_silu_mul(rtd_ctx* ctx, const void* gate, uint32_t gate_dtype, int
  * SubstratePort::argmax behind greedy sampling (crates/runtimed-model/src/decode/sample.rs:11-18). */
 rtd_status rtd_argmax(rtd_ctx* ctx, const float* x, int64_t ldx, int64_t T, int64_t V, int32_t* out, void* stream);
 
+/* The LM head and the greedy pick in one call: ids[t] = argmax over n of the f32 value of
+ * y[t, n] = x[t] . W[n] (+ bias[n]), ties to the lowest row, NaN never chosen (0 when every
+ * value is NaN) -- qwen2::forward's `linear(h, "output.weight")` followed by
+ * SubstratePort::argmax (crates/runtimed-model/src/arch/qwen2.rs:224-228,
+ * crates/runtimed-model/src/decode/sample.rs:11-18).  Fewer than four tokens (decode): the
+ * argmax runs in the GEMV's epilogue, so no logits need to exist -- y may be NULL; when
+ * given, the logits are written too, in y_dtype.  Four or more tokens: y (f32) is required
+ * and rtd_argmax follows the linear.  ids is a device array of M int32.  The context holds
+ * the epilogue's key state: calls of one context must not overlap on different streams. */
+rtd_status rtd_qlinear_argmax(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype,
+                              int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype,
+                              int64_t ldy, int32_t* ids, void* stream);
+
 /* ---- tensor-parallel row reduction -----------------------------------------
  * Replaces RowParallelLinear::forward + ring_all_reduce
  * (crates/runtimed-model/src/tp/row_linear.rs:20-66, crates/runtimed-model/src/tp/ring_reduce.rs:7-65)

@@ -26,6 +26,8 @@ struct rtd_ctx {
   float* ws = nullptr;
   size_t ws_bytes = 0;
   int* status = nullptr;
+  // rtd_qlinear_argmax's epilogue state: [4] packed keys and a CTA count, zero between calls
+  unsigned long long* amax = nullptr;
   std::string err;
 };
 
@@ -60,6 +62,7 @@ constexpr size_t kWorkspaceBytes = 64ull << 20;  // activation staging (GEMV pre
 // the four-column GEMV pass is slower than one TN = 16 GEMM tile from M = 4 on, and
 // faster up to M = 3
 constexpr int64_t kGemmMinTokens = 4;
+constexpr size_t kAmaxBytes = 64;  // rtd_ctx::amax: 4 keys of 8 bytes, the count, padding
 
 thread_local std::string g_thread_err;
 
@@ -153,9 +156,11 @@ rtd_status rtd_init(int device, rtd_ctx** out) {
   cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
   if ((e = cudaMalloc(&c->ws, kWorkspaceBytes)) != cudaSuccess ||
       (e = cudaMalloc(&c->status, sizeof(int))) != cudaSuccess ||
-      (e = cudaMemset(c->status, 0, sizeof(int))) != cudaSuccess) {
+      (e = cudaMemset(c->status, 0, sizeof(int))) != cudaSuccess ||
+      (e = cudaMalloc(&c->amax, kAmaxBytes)) != cudaSuccess || (e = cudaMemset(c->amax, 0, kAmaxBytes)) != cudaSuccess) {
     cudaFree(c->ws);
     cudaFree(c->status);
+    cudaFree(c->amax);
     delete c;
     return fail(nullptr, RTD_ERR_OOM, "rtd_init: workspace allocation failed: %s", cudaGetErrorString(e));
   }
@@ -169,6 +174,7 @@ rtd_status rtd_destroy(rtd_ctx* ctx) {
   DeviceGuard g(ctx->device);
   cudaFree(ctx->ws);
   cudaFree(ctx->status);
+  cudaFree(ctx->amax);
   delete ctx;
   return RTD_OK;
 }
@@ -394,12 +400,12 @@ rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* 
 static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N, int64_t K, int64_t G,
                            const float* row_scale, int scale_len, const void* x, uint32_t x_dtype, int64_t ldx,
                            int64_t M, int w8a8, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
-                           void* stream, const char* who, float wpow2) {
+                           void* stream, const char* who, float wpow2, int32_t* ids = nullptr) {
   if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
   if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
   if (M == 0 || N == 0) return RTD_OK;
-  if ((K > 0 && !x) || !y) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
-  if (ldx < K || ldy < N)
+  if ((K > 0 && !x) || (!y && !ids)) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if (ldx < K || (y && ldy < N))
     return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who, (long long)ldx,
                 (long long)ldy, (long long)K, (long long)N);
   DeviceGuard g(ctx->device);
@@ -432,10 +438,12 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.status = ctx->status;
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
+  c.ids = ids;
+  c.amax = ids ? ctx->amax : nullptr;
   int plan_err = 0;
   // four or more tokens go to the tensor-core GEMM when its staged activations fit
-  // the workspace
-  if (M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
+  // the workspace (the argmax epilogue is the GEMV's: its callers pass fewer)
+  if (!ids && M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
     e = rtd::launch_qgemm(c, &plan_err);
   else
     e = rtd::launch_qgemv(c, &plan_err);
@@ -449,6 +457,32 @@ rtd_status rtd_qlinear(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32
   if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "rtd_qlinear: NULL ctx or weight");
   return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, w->row_scale ? (int)w->N : 0, x, x_dtype, ldx,
                   M, 0, bias, y, y_dtype, ldy, stream, "rtd_qlinear", w->wpow2);
+}
+
+rtd_status rtd_qlinear_argmax(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype, int64_t ldx,
+                              int64_t M, const float* bias, void* y, uint32_t y_dtype, int64_t ldy, int32_t* ids,
+                              void* stream) {
+  const char* who = "rtd_qlinear_argmax";
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "%s: NULL ctx or weight", who);
+  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (M == 0) return RTD_OK;
+  if (!ids) return fail(ctx, RTD_ERR_INVALID, "%s: ids is NULL", who);
+  if (w->N <= 0 || w->N > INT32_MAX || w->K <= 0)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: [%lld x %lld] (1 .. 2^31 - 1 rows, K > 0)", who, (long long)w->N,
+                (long long)w->K);
+  const int scale_len = w->row_scale ? (int)w->N : 0;
+  if (M < kGemmMinTokens)  // decode: the argmax runs in the GEMV's epilogue, y is optional
+    return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, scale_len, x, x_dtype, ldx, M, 0, bias, y,
+                    y_dtype, ldy, stream, who, w->wpow2, ids);
+  // prompt-sized calls: the logits, then the argmax kernel over them
+  if (!y || y_dtype != RTD_DT_F32)
+    return fail(ctx, RTD_ERR_INVALID, "%s: %lld tokens need f32 logits in y", who, (long long)M);
+  rtd_status s = run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, scale_len, x, x_dtype, ldx, M, 0, bias,
+                          y, y_dtype, ldy, stream, who, w->wpow2);
+  if (s != RTD_OK) return s;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = rtd::launch_argmax(static_cast<const float*>(y), ldy, M, w->N, ids, (cudaStream_t)stream);
+  return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
 }
 
 rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n, float* y, void* stream) {

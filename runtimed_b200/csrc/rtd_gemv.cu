@@ -648,8 +648,31 @@ struct Args {
   uint64_t* tp_ll[kMaxTpWorld];
   int64_t tp_max_n;
   uint32_t* tp_ctrl;  // [0] epoch, [1] finished-CTA count (device)
+  // greedy argmax of the outputs (qgemv_kernel<..., true>): the launch's tokens' ids,
+  // the [4] packed keys and the finished-CTA count (both zero between launches)
+  int* ids;
+  unsigned long long* amax_key;
+  unsigned int* amax_ctl;
   int* status;
 };
+
+// Packed argmax key of output v of row n: the high word maps the float order onto
+// unsigned order (+0 and -0 equal, every value above the empty key 0), the low word
+// prefers the lower row among equal values.  NaN is never packed.
+__device__ __forceinline__ unsigned long long amax_pack(float v, int64_t n) {
+  uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+}
+
+template <int NK>
+__device__ __forceinline__ void amax_fold(unsigned long long (&key)[NK], int t, float v, int64_t n) {
+  if (v != v) return;  // NaN never wins
+  const unsigned long long k = amax_pack(v, n);
+#pragma unroll
+  for (int u = 0; u < NK; ++u)
+    if (u == t && k > key[u]) key[u] = k;
+}
 
 __device__ __forceinline__ void store_y(const Args& a, int t, int64_t n, float v) {
   const int64_t off = (int64_t)t * a.ldy + n;
@@ -817,7 +840,9 @@ __device__ __forceinline__ void stage_local_diag(const Args& a, uint8_t* sm, boo
 // item sequence through a private ring of NS shared-memory stages, so warps only
 // meet once per tile: to add their partial sums in shared memory (double
 // buffered), after which one warp (tile index mod 8) writes the tile's outputs.
-template <int FMT, int NT>
+// AMAX: the greedy argmax of every token's outputs is folded into the epilogue (the
+// outputs themselves are written only when a.y is set).
+template <int FMT, int NT, bool AMAX>
 __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(const Args a) {
   using F = FmtC<FMT>;
   constexpr int CSB = col_stride_bytes(F::GK);
@@ -917,6 +942,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+  unsigned long long akey[4] = {0ull, 0ull, 0ull, 0ull};  // AMAX: this lane's best key per token
   int i = 0;
   int slot_i = 0;         // ring slot of item i
   uint32_t phase = 0;     // its mbarrier phase parity
@@ -994,10 +1020,15 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
           for (int c = 0; c < NT; ++c) {
             if (a.P == 2) {
               const int t = c >> 1;
-              if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N)
-                store_y(a, t, n, (acc[c][rr] + acc[c + 1][rr]) * cs + bias);
+              if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N) {
+                const float v = (acc[c][rr] + acc[c + 1][rr]) * cs + bias;
+                if (!AMAX || a.y) store_y(a, t, n, v);
+                if (AMAX) amax_fold(akey, t, v, n);
+              }
             } else if (tq == c && c < a.M && n < a.N) {
-              store_y(a, c, n, acc[c][rr] * cs + bias);
+              const float v = acc[c][rr] * cs + bias;
+              if (!AMAX || a.y) store_y(a, c, n, v);
+              if (AMAX) amax_fold(akey, c, v, n);
             }
           }
         }
@@ -1047,7 +1078,11 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
 #pragma unroll
           for (int w = 0; w < kWarps; ++w)
             for (int p = 0; p < a.P; ++p) sum += rb[((size_t)w * 16 + r) * a.ncol8 + t * a.P + p];
-          if (n < a.N) store_y(a, t, n, sum * ep[16 + r] + ep[r]);
+          if (n < a.N) {
+            const float v = sum * ep[16 + r] + ep[r];
+            if (!AMAX || a.y) store_y(a, t, n, v);
+            if (AMAX) amax_fold(akey, t, v, n);
+          }
         }
       }
       __syncwarp();
@@ -1075,6 +1110,28 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         a.tp_ctrl[0] = tp_epoch;
         __threadfence();
       }
+    }
+  }
+  if constexpr (AMAX) {  // one atomic per warp and token; the launch's last CTA reads the ids
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      unsigned long long k = akey[u];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+        k = k2 > k ? k2 : k;
+      }
+      if (lane == 0 && u < a.M && k != 0ull) atomicMax(a.amax_key + u, k);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0 && atomicAdd(a.amax_ctl, 1u) == gridDim.x - 1) {
+      __threadfence();
+      for (int t = 0; t < a.M; ++t) {
+        const unsigned long long k = atomicExch(a.amax_key + t, 0ull);
+        a.ids[t] = k != 0ull ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
+      }
+      atomicExch(a.amax_ctl, 0u);
     }
   }
 }
@@ -1184,14 +1241,16 @@ int gemv_occupancy(size_t smem) {
   cudaGetDevice(&dev);
   dev &= 63;
   if (!configured[dev]) {
-    cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    cudaFuncSetAttribute(qgemv_kernel<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxGemvSmem);
+    cudaFuncSetAttribute(qgemv_kernel<FMT, NT, false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(qgemv_kernel<FMT, NT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxGemvSmem);
+    cudaFuncSetAttribute(qgemv_kernel<FMT, NT, true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(qgemv_kernel<FMT, NT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxGemvSmem);
     configured[dev] = true;
   }
   for (int i = 0; i < kCache; ++i)
     if (cached_occ[dev][i] > 0 && cached_smem[dev][i] == smem) return cached_occ[dev][i];
   int occ = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qgemv_kernel<FMT, NT>, kThreads, smem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qgemv_kernel<FMT, NT, false>, kThreads, smem) != cudaSuccess ||
       occ < 1)
     occ = 1;
   const int slot = next_slot[dev]++ % kCache;
@@ -1232,7 +1291,8 @@ cudaError_t launch_gemv(const Args& a, unsigned nctas, size_t smem, cudaStream_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   count_launch();
-  return cudaLaunchKernelEx(&cfg, qgemv_kernel<FMT, NT>, a);
+  if (a.amax_key) return cudaLaunchKernelEx(&cfg, qgemv_kernel<FMT, NT, true>, a);
+  return cudaLaunchKernelEx(&cfg, qgemv_kernel<FMT, NT, false>, a);
 }
 
 template <int FMT>
@@ -1398,7 +1458,7 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.ncol8 = ncol8;
     a.bias = c.bias;
     const size_t ysz = (c.y_dtype == 0) ? 4 : 2;
-    a.y = static_cast<uint8_t*>(c.y) + (size_t)(m0 * c.ldy) * ysz;
+    a.y = c.y ? static_cast<uint8_t*>(c.y) + (size_t)(m0 * c.ldy) * ysz : nullptr;
     a.ldy = c.ldy;
     a.y_dtype = c.y_dtype;
     a.N = c.N;
@@ -1428,10 +1488,13 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_tabloc = pl.off_tabloc;
     a.tabw = ncol * (f.gk / f.sbe + 4);
     a.off_zero = pl.off_zero;
+    a.ids = c.ids ? c.ids + m0 : nullptr;
+    a.amax_key = c.ids ? c.amax : nullptr;  // every launch of the call starts from clear keys
+    a.amax_ctl = c.ids ? reinterpret_cast<unsigned int*>(c.amax + 4) : nullptr;
     a.tp_world = 1;
     if (c.tp && c.tp->world > 1) {
       const TpReduce& tp = *c.tp;
-      if (c.N > tp.max_n || Mt > 4) {
+      if (c.N > tp.max_n || Mt > 4 || c.ids) {  // (no argmax over a rank's partial sums)
         *plan_error = 1;
         return cudaSuccess;
       }

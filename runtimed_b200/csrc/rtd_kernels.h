@@ -80,6 +80,13 @@ struct QGemvCall {
   cudaStream_t stream;
   const TpReduce* tp;      // null, or the row-parallel reduction of this call
   float wpow2;             // K-quant / Q8_0 weights: the power of two F of ts_decode_scale (0: none)
+  // greedy argmax in the GEMV's epilogue (launch_qgemv only; null: none).  ids[t] = the
+  // row of token t's largest f32 output (lowest row among equal maxima, NaN never wins,
+  // 0 when every output is NaN); y may then be null.  amax: the context's [4] packed
+  // keys and a finished-CTA count (word 4), zero between launches -- the last CTA of
+  // each launch reads them and clears them again.
+  int* ids;
+  unsigned long long* amax;
 };
 
 // Returns cudaSuccess or the launch error; *plan_error is set (non-zero) when the

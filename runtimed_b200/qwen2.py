@@ -292,7 +292,11 @@ class Qwen2Model:
 
     # ---- one call over T tokens, each with its own (sequence, position)
     def _run(self, ids: torch.Tensor, tok_seq: torch.Tensor, tok_pos: torch.Tensor, max_ctx: int,
-             logits_rows: Optional[torch.Tensor] = None, trace: Optional[list] = None) -> torch.Tensor:
+             logits_rows: Optional[torch.Tensor] = None, trace: Optional[list] = None,
+             head_ids: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        """Logits of the call's tokens (rows `logits_rows` only, when given); with `head_ids`
+        (int32 [rows]) the greedy ids are written there instead, the pick fused into the LM
+        head (rtd_qlinear_argmax: no logits written below four rows), and None is returned."""
         cfg, L, st = self.cfg, self.L, _stream_ptr(self.device)
         T = int(ids.shape[0])
         c = self.ctx.handle
@@ -356,6 +360,16 @@ class Qwen2Model:
                                   self.weights.map["output_norm.weight"].data_ptr(), cfg.eps, T, cfg.hidden,
                                   n.data_ptr(), _lib.DT_F32, cfg.hidden, st))
         rows = n if logits_rows is None else n.index_select(0, logits_rows)
+        if head_ids is not None:
+            qm = self.weights.q_map.get("output.weight")
+            if qm is None:
+                raise MissingWeight("output.weight")
+            m = int(rows.shape[0])
+            lg = None if m < 4 else torch.empty((m, qm.n), dtype=torch.float32, device=self.device)
+            self._check(L.rtd_qlinear_argmax(c, qm.handle, rows.data_ptr(), _lib.DT_F32, cfg.hidden, m, None,
+                                             None if lg is None else lg.data_ptr(), _lib.DT_F32, qm.n,
+                                             head_ids.data_ptr(), st))
+            return None
         return self._linear(rows, "output.weight")
 
     def _tokens(self, values: Sequence[int]) -> torch.Tensor:
@@ -386,8 +400,9 @@ class Qwen2Model:
     def greedy_graph(self, prompt: Sequence[int], steps: int, seq: int = 0):
         """Greedy decode of `steps` tokens after the prompt with one decode step captured as
         a CUDA graph: the step reads its token and position from device tensors, and its
-        last kernel (the argmax) writes the next token where the next replay reads it, so
-        no step waits for the host.  Returns (ids on the device [steps], the graph, a
+        last kernel (the LM head with the greedy pick in its epilogue, rtd_qlinear_argmax:
+        no logits are written) puts the next token where the next replay reads it, so no
+        step waits for the host.  Returns (ids on the device [steps], the graph, a
         replay function) -- the timing target of the bench's decode figure."""
         logits = self.forward(list(prompt), 0, seq=seq, last_only=True)
         total = len(prompt) + steps
@@ -399,9 +414,7 @@ class Qwen2Model:
         out = torch.empty((steps,), dtype=torch.int32, device=self.device)
 
         def step():
-            lg = self._run(tok, seq_d, pos, total)
-            self._check(self.L.rtd_argmax(self.ctx.handle, lg.data_ptr(), lg.shape[1], 1, lg.shape[1],
-                                          tok.data_ptr(), _stream_ptr(self.device)))
+            self._run(tok, seq_d, pos, total, head_ids=tok)
             pos.add_(1)
 
         # one eager step first (kernel attributes are configured outside capture); the

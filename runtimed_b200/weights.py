@@ -146,6 +146,34 @@ class QMatMul:
 
     __call__ = forward
 
+    def greedy(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
+               logits: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """int32 ids [m] of the largest output of each row of x: the LM head followed by
+        the greedy pick (qwen2.rs:224-228, sample.rs:11-18) in one call.  Below four rows
+        the pick runs in the GEMV's epilogue and the logits are written only into
+        `logits` ([m, N] f32) when it is given; from four rows they are required."""
+        if x.dim() != 2 or x.shape[1] != self.k:
+            raise ShapeError("qmatmul_greedy", [-1, self.k], list(x.shape))
+        if x.dtype not in _DT:
+            x = x.to(torch.float32)
+        x2 = x.to(self.device).contiguous()
+        m = x2.shape[0]
+        if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (m, self.n)
+                                   or not logits.is_contiguous()):
+            raise ShapeError("logits", [m, self.n], list(logits.shape))
+        b = None
+        if bias is not None:
+            b = bias.to(device=self.device, dtype=torch.float32).contiguous()
+            if b.numel() != self.n:
+                raise ShapeError("bias", [self.n], list(bias.shape))
+        ids = torch.empty((m,), dtype=torch.int32, device=self.device)
+        st = _lib.lib().rtd_qlinear_argmax(self.ctx.handle, self.handle, x2.data_ptr(), _DT[x2.dtype], self.k, m,
+                                           None if b is None else b.data_ptr(),
+                                           None if logits is None else logits.data_ptr(), _lib.DT_F32, self.n,
+                                           ids.data_ptr(), _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return ids
+
     def embedding(self, ids: torch.Tensor) -> torch.Tensor:
         """f32 rows ids of the dequantized matrix (QMatMul::embedding)."""
         ids_d = ids.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous()
