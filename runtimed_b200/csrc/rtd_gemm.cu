@@ -1,5 +1,8 @@
 // rtd_gemm.cu -- tcgen05 / TMEM tensor-core GEMM for token counts past the decode
-// GEMV's sweet spot (prefill, batched decode, speculative verify).
+// GEMV's sweet spot, and the planner of every call of four or more tokens: up to 64
+// tokens (batched decode, speculative verify) run the skinny kernel of rtd_gemm_ts.cu
+// (decoded weights in tensor memory) unless RTD_GEMM_TS=0; prefill sizes run the
+// kernel below (decoded weights in shared memory).
 //
 //   y[M, N] = x[M, K] . W^T (+ bias)      W in Q4_K / Q6_K / Q8_0 / FP8-E4M3 groups
 //
@@ -17,7 +20,7 @@
 //     stage's "empty" barrier, which releases both buffers;
 //   - after the last stage warps 4..7 read both accumulators (tcgen05.ld, one TMEM
 //     lane quarter each), add them, and write y with the per-token activation scale,
-//     the FP8 row scale and the bias.
+//     the row scale (FP8, INT4 Marlin) and the bias.
 // The activations are staged once per call by gemm_prep_kernel: power-of-two-scaled
 // f16 per token, already in the swizzled layout, so one bulk copy moves a tile.  The
 // prep, GEMM and (split-K) reduce kernels are chained with programmatic dependent

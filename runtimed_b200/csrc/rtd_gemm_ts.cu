@@ -16,8 +16,10 @@
 //     tensor-memory lane quarter q and tile 2q + p decodes its tile's group: thread
 //     4g + t holds exactly the bytes the group layout gives lane 4g + t (whole
 //     sub-blocks of rows g and g + 8, conflict-free 16-byte shared loads), turns them
-//     into f16 pairs (codes exact in f16 through an exponent-bias constant, the
-//     reference's per-sub-block factors rounded once to f16, one f16 FMA per pair) and
+//     into f16 pairs -- the codes masked in place are exact f16 subnormals (code * 2^-24),
+//     multiplied by the reference's per-sub-block factor times the weight's power of two
+//     F (ts_decode_scale at upload, so the products are normal f16) and rounded once, one
+//     f16 FMA per pair; the epilogue divides F out -- and
 //     stores them with tcgen05.st.16x256b, whose thread pattern is that same lane
 //     ownership: registers of thread 4g + t land in lanes g and g + 8, columns 2t and
 //     2t + 1 of every 8-column repetition.  The k order inside a group is therefore the
@@ -27,9 +29,9 @@
 //     accumulator, and commit them to the group's release barriers (tensor-memory slot and
 //     activation slot);
 //   - warps 4..7 (one per lane quarter) read each finished accumulator pair (tcgen05.ld),
-//     add the two, and write y with the per-token activation scale, the FP8 row scale and
-//     the bias, or f32 partials for a row tile shared with another CTA (see the schedule
-//     below).
+//     add the two, and write y with the per-token activation scale, 1 / F, the row scale
+//     (FP8, INT4 Marlin) and the bias, or f32 partials for a row tile shared with another
+//     CTA (see the schedule below).
 // FP8 weights with E4M3 activations (W8A8) skip the decode: the E4M3 codes go to tensor
 // memory as they are and tcgen05.mma.kind::f8f6f4 multiplies them with the E4M3 codes
 // of the activations.

@@ -1,10 +1,11 @@
-// rtd_gemv.cu -- decode GEMV / skinny GEMM on quantized weights, sm_100a.
+// rtd_gemv.cu -- decode GEMV on quantized weights, sm_100a.
 //
 //   y[M, N] = x[M, K] . W^T (+ bias)     W in Q4_K / Q6_K / Q8_0 / FP8-E4M3 blocks
 //
 // Replaces QMatMul::forward behind Weights::linear
-// (crates/runtimed-model/src/weights/linear_layer.rs:45-52) for decode-sized M,
-// and the per-call cuBLASLt FP8 GEMM of crates/runtimed-model/src/ops/fp8_gemm.rs:88-191.
+// (crates/runtimed-model/src/weights/linear_layer.rs:45-52) for decode-sized M (up to
+// three tokens a call; more run the tensor-core GEMMs), and the per-call cuBLASLt FP8
+// GEMM of crates/runtimed-model/src/ops/fp8_gemm.rs:88-191 at those sizes.
 //
 // Every weight byte is read from HBM exactly once per call; the kernels are built
 // to keep HBM busy with as little synchronisation as possible:
@@ -43,6 +44,9 @@
 //    partial into every rank's exchange buffer over NVLink as LL words (value and
 //    epoch in one 8-byte store); after the CTA's last tile it waits (bounded) for
 //    every rank's words of its tiles and writes their rank-ordered sum.
+//  * Greedy pick (qgemv_kernel<..., true>, the LM head of greedy decode): every output
+//    is folded into a packed (value, row) key per token; one atomicMax per warp and
+//    token, and the launch's last CTA writes the ids (the logits need not be written).
 
 #include <algorithm>
 #include <cstdlib>
