@@ -202,10 +202,12 @@ def _cpu_sample(t, k, m):
 
 
 def cpu_baseline(budget_s: float = 20.0, batch: int = BATCH):
-    """The restated reference CPU path (oracle/: bit-exact block decode + f32 dots, OpenMP
-    over all host threads) on a row sample of each of the seven layer linears at full K
-    and M = batch; the measured seconds per row, times the rows of all 80 layers, give the
-    step's CPU time and tokens/s.  Only the oracle calls are timed."""
+    """The reference's CPU quantized matmul restated (oracle/rtd_cpu_qmatmul.c: candle's
+    QMatMul algorithm -- activations quantized to Q8_K / Q8_0 blocks, integer dots with
+    AVX2, f32 accumulation; OpenMP over all host threads) on a row sample of each of the
+    seven layer linears at full K and M = batch; the measured seconds per row, times the
+    rows of all 80 layers, give the step's CPU time and tokens/s.  Only the oracle calls
+    are timed."""
     import oracle
 
     threads = os.cpu_count() or 1
@@ -218,7 +220,10 @@ def cpu_baseline(budget_s: float = 20.0, batch: int = BATCH):
         rows, spent, done = 8, 0.0, 0
         while spent < per:
             t0 = time.perf_counter()
-            oracle.ref_cpu_linear(t, raw[: rows * row_b], rows, k, x, threads=threads)
+            if t in (oracle.Q4_K, oracle.Q6_K, oracle.Q8_0):
+                oracle.cpu_qmatmul(t, raw[: rows * row_b], rows, k, x, threads=threads)
+            else:
+                oracle.ref_cpu_linear(t, raw[: rows * row_b], rows, k, x, threads=threads)
             dt = time.perf_counter() - t0
             spent += dt
             done += rows
@@ -228,8 +233,9 @@ def cpu_baseline(budget_s: float = 20.0, batch: int = BATCH):
         rows_used[name] = done
     return {"value": batch / step_s, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"row samples of the 7 config-3 layer linears at full K and M={batch} "
-                      f"(~{budget_s:.0f} s of CPU work), scaled to the 80-layer step; oracle/rtd_oracle.c "
-                      f"restating the reference block decoders + f32 dots, OpenMP {threads} threads"}
+                      f"(~{budget_s:.0f} s of CPU work), scaled to the 80-layer step; oracle/rtd_cpu_qmatmul.c "
+                      f"restating candle-core 0.11 QMatMul's CPU algorithm (x -> Q8_K blocks, AVX2 integer "
+                      f"dots, f32 accumulation), OpenMP {threads} threads"}
 
 
 def run_reference(args) -> None:

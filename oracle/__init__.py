@@ -6,8 +6,9 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 
 It wraps ``oracle/liboracle.so``, a C restatement of the reference's own CPU
 arithmetic (every function in ``rtd_oracle.c`` cites the reference file:line it
-follows).  The library is built by ``make -C oracle`` (``__graft_entry__.build()``
-runs that).
+follows), and ``rtd_cpu_qmatmul.c``, the reference's CPU quantized matmul (candle's
+8-bit activation blocks and integer dots) restated as the timed CPU baseline.  The
+library is built by ``make -C oracle`` (``__graft_entry__.build()`` runs that).
 """
 from __future__ import annotations
 
@@ -35,8 +36,9 @@ def build() -> str:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH) or (
-            os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "rtd_oracle.c"))
+        if not os.path.exists(_LIB_PATH) or any(
+            os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, src))
+            for src in ("rtd_oracle.c", "rtd_cpu_qmatmul.c")
         ):
             build()
         L = ctypes.CDLL(_LIB_PATH)
@@ -74,6 +76,12 @@ def lib() -> ctypes.CDLL:
         L.rtdo_ref_cpu_fp8_linear.restype = None
         L.rtdo_max_threads.argtypes = []
         L.rtdo_max_threads.restype = ctypes.c_int
+        L.rtdo_cpu_qmatmul.argtypes = [ctypes.c_uint32, c_u8p, ctypes.c_int64, ctypes.c_int64, c_fp,
+                                       ctypes.c_int64, c_fp, ctypes.c_int, ctypes.c_int]
+        L.rtdo_cpu_qmatmul.restype = ctypes.c_int
+        L.rtdo_cpu_quantize_x.argtypes = [ctypes.c_uint32, c_fp, ctypes.c_int64, ctypes.POINTER(ctypes.c_int8),
+                                          c_fp, ctypes.POINTER(ctypes.c_int16)]
+        L.rtdo_cpu_quantize_x.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -138,6 +146,36 @@ def ref_cpu_linear(ggml_type: int, raw: np.ndarray, N: int, K: int, x: np.ndarra
     y = np.zeros((x.shape[0], N), dtype=np.float32)
     lib().rtdo_ref_cpu_linear(ggml_type, _u8(raw), N, K, _f32(x), x.shape[0], _f32(y), threads)
     return y
+
+
+def cpu_qmatmul(ggml_type: int, raw: np.ndarray, N: int, K: int, x: np.ndarray, threads: int = 0,
+                simd: bool = True) -> np.ndarray:
+    """The reference's CPU quantized matmul (candle-core 0.11 QMatMul::forward behind
+    linear_layer.rs:45-52): x quantized to Q8_K blocks (Q8_0 for Q8_0 weights), integer
+    dots per block, f32 accumulation.  The timed CPU baseline of the bench."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K)
+    y = np.zeros((x.shape[0], N), dtype=np.float32)
+    rc = lib().rtdo_cpu_qmatmul(ggml_type, _u8(raw), N, K, _f32(x), x.shape[0], _f32(y), threads, int(simd))
+    if rc != 0:
+        raise ValueError(f"rtdo_cpu_qmatmul: status {rc} (type {ggml_type}, K {K})")
+    return y
+
+
+def cpu_quantize_x(ggml_type: int, x: np.ndarray):
+    """(codes int8 [K], scales f32 [K / QK], bsums int16 [K / 16] or None) of the
+    activation blocks rtdo_cpu_qmatmul builds for x[K]."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    qk = 32 if ggml_type == Q8_0 else 256
+    codes = np.zeros(x.size, dtype=np.int8)
+    scales = np.zeros(x.size // qk, dtype=np.float32)
+    bsums = None if ggml_type == Q8_0 else np.zeros(x.size // 16, dtype=np.int16)
+    rc = lib().rtdo_cpu_quantize_x(ggml_type, _f32(x), x.size, codes.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)),
+                                   _f32(scales),
+                                   None if bsums is None else bsums.ctypes.data_as(ctypes.POINTER(ctypes.c_int16)))
+    if rc != 0:
+        raise ValueError(f"rtdo_cpu_quantize_x: status {rc}")
+    return codes, scales, bsums
 
 
 def fp8_to_f32(b: int) -> float:
