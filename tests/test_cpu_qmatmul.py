@@ -53,7 +53,7 @@ def test_activation_quantizers_follow_the_published_rules():
         assert np.array_equal(codes[256 * b:256 * (b + 1)], q), b
         assert scales[b] == d, b
     assert np.array_equal(bsums, codes.reshape(-1, 16).astype(np.int32).sum(1))
-    assert codes[300] == -128 and scales[1] > 0  # d = max / -128: its sign follows that value
+    assert codes[300] == -128 and scales[1] > 0  # d = max / -128, of the opposite sign to max
     codes, scales, _ = oracle.cpu_quantize_x(oracle.Q8_0, x)
     for b in range(32):
         q, d = _q8_0_numpy(x[32 * b:32 * (b + 1)])
