@@ -212,6 +212,17 @@ rtd_status rtd_qlinear_argmax(rtd_ctx* ctx, const rtd_qweight* w, const void* x,
                               int64_t ldx, int64_t M, const float* bias, void* y, uint32_t y_dtype,
                               int64_t ldy, int32_t* ids, void* stream);
 
+/* The same pick for one shard of a vocabulary-parallel LM head (the column-parallel head
+ * with a distributed argmax: each rank holds rows [row0, row0 + N) of output.weight).
+ * keys[t] (device u64) = (f32 order mapped onto unsigned, -0 as +0) << 32 | (0xFFFFFFFF -
+ * (row0 + n)) of token t's largest output, 0 when every output is NaN: the unsigned maximum
+ * of the ranks' keys is the key of the whole head's greedy pick, whose row is 0xFFFFFFFF
+ * minus its low word (0 for the key 0).  Any M, in GEMV launches of up to four tokens; rows
+ * below 2^32. */
+rtd_status rtd_qlinear_argmax_keys(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype,
+                                   int64_t ldx, int64_t M, const float* bias, int64_t row0, uint64_t* keys,
+                                   void* stream);
+
 /* ---- tensor-parallel row reduction -----------------------------------------
  * Replaces RowParallelLinear::forward + ring_all_reduce
  * (crates/runtimed-model/src/tp/row_linear.rs:20-66, crates/runtimed-model/src/tp/ring_reduce.rs:7-65)

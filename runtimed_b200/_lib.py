@@ -66,6 +66,7 @@ SIGNATURES = {
     "rtd_silu_mul": (_c.c_int32, [_vp, _vp, _u32, _i64, _vp, _u32, _i64, _i64, _i64, _vp, _u32, _i64, _vp]),
     "rtd_argmax": (_c.c_int32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "rtd_qlinear_argmax": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _vp, _u32, _i64, _vp, _vp]),
+    "rtd_qlinear_argmax_keys": (_c.c_int32, [_vp, _vp, _vp, _u32, _i64, _i64, _vp, _i64, _vp, _vp]),
     "rtd_qembed": (_c.c_int32, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "rtd_qdequant": (_c.c_int32, [_vp, _vp, _vp, _vp]),
     "rtd_fp8weight_upload": (_c.c_int32, [_vp, _vp, _vp, _i64, _i64, _i64, _c.POINTER(_vp)]),

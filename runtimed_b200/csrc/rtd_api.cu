@@ -400,11 +400,12 @@ rtd_status rtd_qweight_info(const rtd_qweight* w, uint32_t* ggml_type, int64_t* 
 static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N, int64_t K, int64_t G,
                            const float* row_scale, int scale_len, const void* x, uint32_t x_dtype, int64_t ldx,
                            int64_t M, int w8a8, const float* bias, void* y, uint32_t y_dtype, int64_t ldy,
-                           void* stream, const char* who, float wpow2, int32_t* ids = nullptr) {
+                           void* stream, const char* who, float wpow2, int32_t* ids = nullptr,
+                           uint64_t* keys = nullptr, int64_t row0 = 0) {
   if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
   if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ctx, RTD_ERR_INVALID, "%s: bad dtype", who);
   if (M == 0 || N == 0) return RTD_OK;
-  if ((K > 0 && !x) || (!y && !ids)) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
+  if ((K > 0 && !x) || (!y && !ids && !keys)) return fail(ctx, RTD_ERR_INVALID, "%s: x or y is NULL", who);
   if (ldx < K || (y && ldy < N))
     return fail(ctx, RTD_ERR_SHAPE, "%s: row strides ldx=%lld ldy=%lld below K=%lld N=%lld", who, (long long)ldx,
                 (long long)ldy, (long long)K, (long long)N);
@@ -439,11 +440,13 @@ static rtd_status run_gemv(rtd_ctx* ctx, int fmt, const uint8_t* wdev, int64_t N
   c.sm_count = ctx->sm_count;
   c.stream = (cudaStream_t)stream;
   c.ids = ids;
-  c.amax = ids ? ctx->amax : nullptr;
+  c.amax_out = reinterpret_cast<unsigned long long*>(keys);
+  c.amax_row0 = row0;
+  c.amax = (ids || keys) ? ctx->amax : nullptr;
   int plan_err = 0;
   // four or more tokens go to the tensor-core GEMM when its staged activations fit
-  // the workspace (the argmax epilogue is the GEMV's: its callers pass fewer)
-  if (!ids && M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
+  // the workspace (the argmax epilogue is the GEMV's, in launches of up to four tokens)
+  if (!ids && !keys && M >= kGemmMinTokens && rtd::qgemm_workspace_bytes(c) <= c.ws_bytes)
     e = rtd::launch_qgemm(c, &plan_err);
   else
     e = rtd::launch_qgemv(c, &plan_err);
@@ -483,6 +486,21 @@ rtd_status rtd_qlinear_argmax(rtd_ctx* ctx, const rtd_qweight* w, const void* x,
   DeviceGuard g(ctx->device);
   cudaError_t e = rtd::launch_argmax(static_cast<const float*>(y), ldy, M, w->N, ids, (cudaStream_t)stream);
   return e == cudaSuccess ? RTD_OK : cuda_fail(ctx, e, who);
+}
+
+rtd_status rtd_qlinear_argmax_keys(rtd_ctx* ctx, const rtd_qweight* w, const void* x, uint32_t x_dtype,
+                                   int64_t ldx, int64_t M, const float* bias, int64_t row0, uint64_t* keys,
+                                   void* stream) {
+  const char* who = "rtd_qlinear_argmax_keys";
+  if (!ctx || !w) return fail(ctx, RTD_ERR_INVALID, "%s: NULL ctx or weight", who);
+  if (M < 0) return fail(ctx, RTD_ERR_SHAPE, "%s: M=%lld is negative", who, (long long)M);
+  if (M == 0) return RTD_OK;
+  if (!keys) return fail(ctx, RTD_ERR_INVALID, "%s: keys is NULL", who);
+  if (w->N <= 0 || w->K <= 0 || row0 < 0 || row0 + w->N > (int64_t)UINT32_MAX)
+    return fail(ctx, RTD_ERR_SHAPE, "%s: rows [%lld, %lld) (below 2^32, K > 0)", who, (long long)row0,
+                (long long)(row0 + w->N));
+  return run_gemv(ctx, w->fmt, w->dev, w->N, w->K, w->G, w->row_scale, w->row_scale ? (int)w->N : 0, x, x_dtype, ldx,
+                  M, 0, bias, nullptr, RTD_DT_F32, w->N, stream, who, w->wpow2, nullptr, keys, row0);
 }
 
 rtd_status rtd_qembed(rtd_ctx* ctx, const rtd_qweight* w, const uint32_t* ids, int64_t n, float* y, void* stream) {

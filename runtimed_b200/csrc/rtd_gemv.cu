@@ -657,6 +657,8 @@ struct Args {
   int* ids;
   unsigned long long* amax_key;
   unsigned int* amax_ctl;
+  int64_t amax_row0;               // added to the row in every key (a vocabulary shard's first row)
+  unsigned long long* amax_out;    // non-null: the launch's tokens' keys are written here, not ids
   int* status;
 };
 
@@ -1027,12 +1029,12 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
               if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N) {
                 const float v = (acc[c][rr] + acc[c + 1][rr]) * cs + bias;
                 if (!AMAX || a.y) store_y(a, t, n, v);
-                if (AMAX) amax_fold(akey, t, v, n);
+                if (AMAX) amax_fold(akey, t, v, n + a.amax_row0);
               }
             } else if (tq == c && c < a.M && n < a.N) {
               const float v = acc[c][rr] * cs + bias;
               if (!AMAX || a.y) store_y(a, c, n, v);
-              if (AMAX) amax_fold(akey, c, v, n);
+              if (AMAX) amax_fold(akey, c, v, n + a.amax_row0);
             }
           }
         }
@@ -1085,7 +1087,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
           if (n < a.N) {
             const float v = sum * ep[16 + r] + ep[r];
             if (!AMAX || a.y) store_y(a, t, n, v);
-            if (AMAX) amax_fold(akey, t, v, n);
+            if (AMAX) amax_fold(akey, t, v, n + a.amax_row0);
           }
         }
       }
@@ -1133,7 +1135,10 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       __threadfence();
       for (int t = 0; t < a.M; ++t) {
         const unsigned long long k = atomicExch(a.amax_key + t, 0ull);
-        a.ids[t] = k != 0ull ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
+        if (a.amax_out)
+          a.amax_out[t] = k;
+        else
+          a.ids[t] = k != 0ull ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
       }
       atomicExch(a.amax_ctl, 0u);
     }
@@ -1492,13 +1497,16 @@ cudaError_t launch_qgemv(const QGemvCall& c, int* plan_error) {
     a.off_tabloc = pl.off_tabloc;
     a.tabw = ncol * (f.gk / f.sbe + 4);
     a.off_zero = pl.off_zero;
+    const bool amax = c.ids || c.amax_out;
     a.ids = c.ids ? c.ids + m0 : nullptr;
-    a.amax_key = c.ids ? c.amax : nullptr;  // every launch of the call starts from clear keys
-    a.amax_ctl = c.ids ? reinterpret_cast<unsigned int*>(c.amax + 4) : nullptr;
+    a.amax_out = c.amax_out ? c.amax_out + m0 : nullptr;
+    a.amax_row0 = c.amax_row0;
+    a.amax_key = amax ? c.amax : nullptr;  // every launch of the call starts from clear keys
+    a.amax_ctl = amax ? reinterpret_cast<unsigned int*>(c.amax + 4) : nullptr;
     a.tp_world = 1;
     if (c.tp && c.tp->world > 1) {
       const TpReduce& tp = *c.tp;
-      if (c.N > tp.max_n || Mt > 4 || c.ids) {  // (no argmax over a rank's partial sums)
+      if (c.N > tp.max_n || Mt > 4 || c.ids || c.amax_out) {  // (no argmax over a rank's partial sums)
         *plan_error = 1;
         return cudaSuccess;
       }

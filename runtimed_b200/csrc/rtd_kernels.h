@@ -87,6 +87,11 @@ struct QGemvCall {
   // each launch reads them and clears them again.
   int* ids;
   unsigned long long* amax;
+  // the same epilogue, writing each token's packed key ((order-mapped f32) << 32 |
+  // 0xFFFFFFFF - row) instead of its id, the rows counted from amax_row0: keys of
+  // vocabulary shards combine by an unsigned max (null: ids)
+  unsigned long long* amax_out;
+  int64_t amax_row0;
 };
 
 // Returns cudaSuccess or the launch error; *plan_error is set (non-zero) when the

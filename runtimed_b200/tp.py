@@ -14,6 +14,11 @@ Mirrors the reference's Megatron-style layers:
 
 `forward_nccl` computes the same result with an NCCL all-reduce, as the measured
 comparison; `forward_ar` runs the unfused GEMV followed by this library's all-reduce.
+
+- `VocabParallelHead`: the LM head (qwen2.rs:224-228) split by vocabulary rows, with the
+  greedy pick (decode/sample.rs:11-18) distributed: every rank picks in its GEMV epilogue
+  and outputs one packed 8-byte key per token, and the keys of all ranks are gathered and
+  combined by an unsigned maximum (`combine_keys`), so no logits cross NVLink.
 The shard helpers work on raw GGUF bytes and are plain numpy, so the host side can be
 tested without a GPU.
 """
@@ -219,3 +224,70 @@ class RowParallelLinear:
         if self.bias is not None:
             y = y + self.bias
         return y.to(x.dtype) if x.dtype in (torch.float16, torch.bfloat16) else y
+
+
+# ---- the vocabulary-parallel LM head and its distributed greedy pick
+_TOP = -(1 << 63)  # XOR with this maps unsigned 64-bit order onto signed order
+
+
+def pack_key(value: float, row: int) -> int:
+    """The packed key of output `value` at global row `row`, as the GEMV epilogue forms it
+    (u64 as a Python int): the f32 order mapped onto unsigned order (-0 as +0) in the high
+    word, 0xFFFFFFFF - row in the low word, so the larger key is the larger value and,
+    among equal values, the lower row.  NaN has no key (0)."""
+    v = np.float32(value)
+    if np.isnan(v):
+        return 0
+    u = int(np.float32(0.0 if v == 0 else v).view(np.uint32))
+    u = (~u & 0xFFFFFFFF) if u & 0x80000000 else (u | 0x80000000)
+    return (u << 32) | (0xFFFFFFFF - int(row))
+
+
+def combine_keys(keys):
+    """Greedy ids (int32 [M]) from every rank's keys ([world, M] int64 holding u64 bit
+    patterns): the unsigned maximum per token, its row decoded; 0 where every key is 0."""
+    import torch
+
+    k = torch.as_tensor(keys, dtype=torch.int64)
+    if k.dim() == 1:
+        k = k[None, :]
+    best = (k ^ _TOP).max(dim=0).values ^ _TOP
+    ids = torch.where(best == 0, torch.zeros_like(best), 0xFFFFFFFF - (best & 0xFFFFFFFF))
+    return ids.to(torch.int32)
+
+
+class VocabParallelHead:
+    """output.weight split by vocabulary rows: rank r holds rows [r V / world, (r + 1) V /
+    world).  `greedy` returns the whole head's greedy ids on every rank: the local pick as
+    keys (rtd_qlinear_argmax_keys), an all-gather of M keys per rank, `combine_keys`."""
+
+    def __init__(self, weight, row0: int, rank: int, tp_size: int, group=None):
+        self.weight, self.row0, self.rank, self.tp_size, self.group = weight, int(row0), rank, tp_size, group
+
+    @classmethod
+    def from_full_weight(cls, raw, ggml_type: int, n: int, k: int, rank: int, tp_size: int, device="cuda:0",
+                         group=None) -> "VocabParallelHead":
+        from .weights import QMatMul
+
+        shard = shard_rows(raw, ggml_type, n, k, rank, tp_size)
+        rows = n // tp_size
+        return cls(QMatMul(ggml_type, shard, rows, k, device=device), rank * rows, rank, tp_size, group)
+
+    def local_keys(self, x):
+        return self.weight.greedy_keys(x, row0=self.row0)
+
+    def greedy(self, x):
+        return gather_greedy(self.local_keys(x), self.tp_size, self.group)
+
+
+def gather_greedy(keys, tp_size: int, group=None):
+    """Every rank's keys [M] gathered (torch.distributed, M int64 a rank) and combined:
+    the whole head's greedy ids on every rank."""
+    if tp_size == 1:
+        return combine_keys(keys)
+    import torch
+    import torch.distributed as dist
+
+    everyone = [torch.empty_like(keys) for _ in range(tp_size)]
+    dist.all_gather(everyone, keys.contiguous(), group=group)
+    return combine_keys(torch.stack(everyone))

@@ -174,6 +174,27 @@ class QMatMul:
         _raise(st, self.ctx.handle)
         return ids
 
+    def greedy_keys(self, x: torch.Tensor, row0: int = 0, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Packed greedy keys [m] (int64 holding the u64 bit patterns) of the rows of x against
+        this matrix, its rows numbered from `row0` -- one vocabulary shard's share of a
+        distributed greedy pick (rtd_qlinear_argmax_keys; combine with tp.combine_keys)."""
+        if x.dim() != 2 or x.shape[1] != self.k:
+            raise ShapeError("qmatmul_greedy", [-1, self.k], list(x.shape))
+        if x.dtype not in _DT:
+            x = x.to(torch.float32)
+        x2 = x.to(self.device).contiguous()
+        b = None
+        if bias is not None:
+            b = bias.to(device=self.device, dtype=torch.float32).contiguous()
+            if b.numel() != self.n:
+                raise ShapeError("bias", [self.n], list(bias.shape))
+        keys = torch.empty((x2.shape[0],), dtype=torch.int64, device=self.device)
+        st = _lib.lib().rtd_qlinear_argmax_keys(self.ctx.handle, self.handle, x2.data_ptr(), _DT[x2.dtype], self.k,
+                                                x2.shape[0], None if b is None else b.data_ptr(), int(row0),
+                                                keys.data_ptr(), _stream_ptr(self.device))
+        _raise(st, self.ctx.handle)
+        return keys
+
     def embedding(self, ids: torch.Tensor) -> torch.Tensor:
         """f32 rows ids of the dequantized matrix (QMatMul::embedding)."""
         ids_d = ids.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous()

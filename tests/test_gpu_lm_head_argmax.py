@@ -133,3 +133,35 @@ def test_fused_argmax_prompt_sizes_and_errors():
     assert ids == _argmax_rows(y)
     with pytest.raises(ConfigError):
         qm.greedy(xd)  # four or more tokens need the logits
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_vocab_parallel_shards_combine_to_the_unsharded_pick(world):
+    # config 0's head split by vocabulary rows over `world` ranks (151936 / 8 = 18992 rows a
+    # shard), each shard uploaded on its own with its first row as row0: the shards' keys,
+    # combined by an unsigned maximum, give the unsharded head's ids -- five f32 tokens,
+    # so three GEMV launches of at most two tokens each, and a tie across shards
+    import torch
+    from runtimed_b200.tp import VocabParallelHead, combine_keys
+
+    t, N, K, M = synth.Q8_0, 151936, 896, 5
+    nb = K // 32
+    raw = synth.quant_matrix(t, N, K, seed=61, stream=8).reshape(N, nb * 34).copy()
+    _, xd = _x(M, K, torch.float32, seed=62)
+    full = _qm(t, raw.reshape(-1), N, K)
+    want = full.greedy(xd[:3]).cpu().tolist() + full.greedy(xd[3:]).cpu().tolist()
+
+    def sharded(w):
+        keys = [VocabParallelHead.from_full_weight(w.reshape(-1), t, N, K, r, world).local_keys(xd)
+                for r in range(world)]
+        return combine_keys(torch.stack(keys).cpu()).tolist()
+
+    assert sharded(raw) == want
+    r = want[0]
+    lo = 1 if r != 1 else 2
+    tied = raw.copy()
+    tied[lo] = raw[r]  # token 0's winner also in shard 0's row lo: the lower row wins
+    full = _qm(t, tied.reshape(-1), N, K)
+    want_t = full.greedy(xd[:3]).cpu().tolist() + full.greedy(xd[3:]).cpu().tolist()
+    assert want_t[0] == min(lo, r)
+    assert sharded(tied) == want_t

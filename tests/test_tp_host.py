@@ -154,3 +154,100 @@ def test_decoder_shards_reassemble_the_full_tensors(tmp_path):
                 assert np.array_equal(np.concatenate(parts, axis=1), full), t.name
             else:
                 assert all(np.array_equal(p, full) for p in parts), t.name
+
+
+def _np_greedy(v):
+    """The greedy pick over f32 values as the reference's argmax makes it: the largest
+    value, the lowest row among equal ones (-0 == +0), NaN never chosen, 0 if all are NaN."""
+    v = np.asarray(v, np.float32)
+    if np.isnan(v).all():
+        return 0
+    return int(np.nanargmax(v))
+
+
+def _shard_keys(v, world):
+    import ctypes
+
+    from runtimed_b200.tp import pack_key
+
+    rows = len(v) // world
+    out = []
+    for r in range(world):
+        part = v[r * rows:(r + 1) * rows]
+        best = max([pack_key(x, r * rows + i) for i, x in enumerate(part)] + [0])
+        out.append(ctypes.c_int64(best).value)  # the u64 bit pattern, as int64
+    return out
+
+
+def test_vocab_parallel_keys_combine_to_the_greedy_pick():
+    import torch
+
+    from runtimed_b200.tp import combine_keys, pack_key
+
+    # the packing orders values, then prefers the lower row; -0 equals +0; NaN has no key
+    assert pack_key(1.0, 5) > pack_key(0.5, 0) > pack_key(0.0, 9) > pack_key(-1.0, 0) > pack_key(-np.inf, 0) > 0
+    assert pack_key(2.0, 3) > pack_key(2.0, 4)
+    assert pack_key(-0.0, 7) == pack_key(0.0, 7)
+    assert pack_key(float("nan"), 1) == 0
+    rng = np.random.default_rng(3)
+    cases = []
+    v = rng.normal(0, 1, 4096).astype(np.float32)
+    cases.append(v)
+    t = v.copy()
+    t[[100, 3000]] = 9.0  # a tie across shards: the lower global row
+    cases.append(t)
+    n = v.copy()
+    n[::3] = np.nan
+    n[2] = np.nan
+    cases.append(n)
+    cases.append(np.full(4096, np.nan, np.float32))  # every value NaN: row 0
+    z = np.zeros(4096, np.float32)
+    z[::2] = -0.0
+    cases.append(z)  # all zeros of either sign: row 0
+    neg = -np.abs(v) - 1.0
+    neg[2049] = -0.5
+    cases.append(neg)
+    for world in (1, 2, 4, 8):
+        keys = torch.tensor([_shard_keys(c, world) for c in cases], dtype=torch.int64).T  # [world, cases]
+        got = combine_keys(keys).tolist()
+        assert got == [_np_greedy(c) for c in cases], world
+
+
+def _gloo_vocab_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from runtimed_b200.tp import gather_greedy
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        logits = rng.normal(0, 1, (3, 1200)).astype(np.float32)  # 3 tokens, vocabulary 1200
+        logits[1, [40, 900]] = 7.0
+        mine = torch.tensor([_shard_keys(row, world)[rank] for row in logits], dtype=torch.int64)
+        ids = gather_greedy(mine, world)
+        q.put((rank, ids.tolist() == [_np_greedy(r) for r in logits]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_parallel_greedy_over_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_vocab_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(r for r, _ in res) == [0, 1]
+    assert all(ok for _, ok in res)
