@@ -13,7 +13,9 @@ words, and the launch's last CTA writes the ids and clears the keys.  Checked on
     accepts at a divergence);
   * ties go to the lowest row (duplicated weight rows give bit-identical outputs), NaN
     rows never win, all-zero outputs give row 0, a bias alone decides when x is zero;
-  * from four tokens the call writes f32 logits and runs rtd_argmax after them.
+  * from four tokens the call writes f32 logits and runs rtd_argmax after them;
+  * rtd_qlinear_argmax_keys on vocabulary shards (rows numbered from the shard's first
+    row): the shards' keys combined by an unsigned maximum give the unsharded ids.
 """
 import numpy as np
 import pytest
