@@ -167,3 +167,24 @@ def test_vocab_parallel_shards_combine_to_the_unsharded_pick(world):
     want_t = full.greedy(xd[:3]).cpu().tolist() + full.greedy(xd[3:]).cpu().tolist()
     assert want_t[0] == min(lo, r)
     assert sharded(tied) == want_t
+
+
+def test_reference_greedy_known_answers():
+    # decode/sample.rs:173-195: greedy([0.1, 5.0, 2.0]) = 1, and 151646 zeros with 100.0 at
+    # row 19 give 19 (the reference's multi-device case; here on cuda:0).  Through
+    # rtd_argmax on the logits, and through the fused pick of a head whose outputs are
+    # those values (zero activations, the values as the bias; 151646 rows end in a ragged
+    # tile of 14), one to three tokens a call
+    import torch
+
+    big = np.zeros(151646, np.float32)
+    big[19] = 100.0
+    for vals, want in ((np.array([0.1, 5.0, 2.0], np.float32), 1), (big, 19)):
+        logits = torch.from_numpy(vals[None, :]).cuda()
+        assert _argmax_rows(logits) == [want]
+        N, K = vals.size, 256
+        qm = _qm(synth.Q8_0, synth.quant_matrix(synth.Q8_0, N, K, seed=71), N, K)
+        bias = torch.from_numpy(vals).cuda()
+        for M in (1, 2, 3):
+            z = torch.zeros((M, K), dtype=torch.bfloat16, device="cuda")
+            assert qm.greedy(z, bias=bias).cpu().tolist() == [want] * M
