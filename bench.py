@@ -19,8 +19,9 @@ value = B * steps / device time of the step's CUDA graph (max over ranks, strong
 scaling: the same model and batch at every N).  e2e = the same through the public API
 with the step's hidden states copied in from pinned host memory and its outputs read
 back every step.  The line also carries the batch-1 step, the roofline of the step's
-dominant kernel and of the whole step, the CPU baseline (the restated reference CPU path
-on the host cores, scaled to the step), the SM clocks of the timed window, and:
+dominant kernel and of the whole step, the CPU baseline (the reference's CPU quantized
+matmul restated -- 8-bit activation blocks, AVX2 integer dots -- on the host cores, scaled
+to the step), the SM clocks of the timed window, and:
   tp          N > 1: the config-3 row-parallel linears (attn_output, ffn_down) fused vs the
               library's all-reduce vs NCCL, at M = 1 and 64, each checked against the
               unsharded single-GPU result (rel_l2);
@@ -28,7 +29,8 @@ on the host cores, scaled to the step), the SM clocks of the timed window, and:
               GB/s of algorithmic bytes) with the roofline of its longest GEMV;
   m_sweep     N = 1: the config-1 token counts M = 4..2048 at (14336, 4096);
   model_decode  N = 1: config 0 end to end (GGUF load, 128-token prompt, greedy decode
-              steps as a CUDA graph) in tokens/s, beside the restated reference forward.
+              steps as a CUDA graph, the pick in the LM head's epilogue) in tokens/s,
+              beside the restated reference forward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     python bench.py --profile-one FMT:N:K[:M] | sweep | tpstep[:B]   (ncu target, no JSON line)
