@@ -33,7 +33,8 @@ to the step), the SM clocks of the timed window, and:
               beside the restated reference forward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-    python bench.py --profile-one FMT:N:K[:M] | sweep | tpstep[:B]   (ncu target, no JSON line)
+    python bench.py --profile-one FMT:N:K[:M] | sweep | tpstep[:B] | greedy:FMT:N:K
+                                                                     (ncu target, no JSON line)
 """
 from __future__ import annotations
 
@@ -786,6 +787,27 @@ def profile_tpstep(b: int, calls: int, layers: int = 4) -> int:
     return 0
 
 
+def profile_greedy(spec: str, calls: int) -> int:
+    """`calls` pairs of one-token LM-head calls (FMT:N:K, bf16 x): the plain GEMV writing the
+    logits, then the same GEMV with the greedy pick in its epilogue and no logits."""
+    import torch
+    from runtimed_b200 import synth
+    from runtimed_b200.weights import QMatMul
+
+    name, n, k = spec.split(":")
+    t, n, k = dict(FORMATS)[name], int(n), int(k)
+    dev = torch.device("cuda", 0)
+    qm = QMatMul(t, synth.quant_matrix(t, n, k, seed=0, stream=k), n, k, device=dev)
+    x = torch.from_numpy(synth.bf16_round(synth.activations(1, k, seed=0))).to(torch.bfloat16).to(dev)
+    for _ in range(calls):
+        y = qm.forward(x, out_dtype=torch.float32)
+        ids = qm.greedy(x)
+    torch.cuda.synchronize(dev)
+    assert int(ids[0]) == int(torch.argmax(y[0]))
+    print(f"profile-one greedy:{spec}: {calls} pairs ok")
+    return 0
+
+
 def profile_one(spec: str, calls: int) -> int:
     """Run `calls` bf16 calls of one linear (FMT:N:K, or FMT:N:K:M for M tokens; M = 1 by
     default), or of every config-1 sweep GEMV in order ("sweep"), eagerly, and exit: the
@@ -797,6 +819,8 @@ def profile_one(spec: str, calls: int) -> int:
     m = 1
     if spec.startswith("tpstep"):
         return profile_tpstep(int(spec.split(":")[1]) if ":" in spec else BATCH, calls)
+    if spec.startswith("greedy:"):
+        return profile_greedy(spec[len("greedy:"):], calls)
     if spec == "sweep":
         todo = [(t, n, k) for _, t, n, k in sweep()]
     else:
@@ -838,7 +862,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep|tpstep[:B]",
+    ap.add_argument("--profile-one", default=None, metavar="FMT:N:K[:M]|sweep|tpstep[:B]|greedy:FMT:N:K",
                     help="only run a few eager calls of one linear or of the config-1 sweep (ncu target), "
                          "no JSON line")
     ap.add_argument("--calls", type=int, default=4)

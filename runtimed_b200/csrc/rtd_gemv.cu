@@ -45,7 +45,7 @@
 //    epoch in one 8-byte store); after the CTA's last tile it waits (bounded) for
 //    every rank's words of its tiles and writes their rank-ordered sum.
 //  * Greedy pick (qgemv_kernel<..., true>, the LM head of greedy decode): every output
-//    is folded into a packed (value, row) key per token; one atomicMax per warp and
+//    is folded into a packed (value, row) key per token; one atomicMax per CTA and
 //    token, and the launch's last CTA writes the ids (the logits need not be written).
 
 #include <algorithm>
@@ -1118,7 +1118,10 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       }
     }
   }
-  if constexpr (AMAX) {  // one atomic per warp and token; the launch's last CTA reads the ids
+  if constexpr (AMAX) {  // the CTA's best key per token: one atomic per CTA and token; the
+                         // launch's last CTA reads the ids
+    // each warp's keys go to its epilogue scratch (idle once its tiles are written)
+    unsigned long long* wk = reinterpret_cast<unsigned long long*>(tblw);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       unsigned long long k = akey[u];
@@ -1127,20 +1130,31 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
         const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
         k = k2 > k ? k2 : k;
       }
-      if (lane == 0 && u < a.M && k != 0ull) atomicMax(a.amax_key + u, k);
+      if (lane == 0) wk[u] = k;
     }
-    __threadfence();
     __syncthreads();
-    if (tid == 0 && atomicAdd(a.amax_ctl, 1u) == gridDim.x - 1) {
-      __threadfence();
-      for (int t = 0; t < a.M; ++t) {
-        const unsigned long long k = atomicExch(a.amax_key + t, 0ull);
-        if (a.amax_out)
-          a.amax_out[t] = k;
-        else
-          a.ids[t] = k != 0ull ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
+    if (tid == 0) {
+      for (int u = 0; u < a.M; ++u) {
+        unsigned long long k = 0ull;
+        for (int w = 0; w < kWarps; ++w) {
+          const unsigned long long kw =
+              reinterpret_cast<const unsigned long long*>(sm + (size_t)w * a.warp_bytes + a.off_tbl)[u];
+          k = kw > k ? kw : k;
+        }
+        if (k != 0ull) atomicMax(a.amax_key + u, k);
       }
-      atomicExch(a.amax_ctl, 0u);
+      __threadfence();
+      if (atomicAdd(a.amax_ctl, 1u) == gridDim.x - 1) {
+        __threadfence();
+        for (int t = 0; t < a.M; ++t) {
+          const unsigned long long k = atomicExch(a.amax_key + t, 0ull);
+          if (a.amax_out)
+            a.amax_out[t] = k;
+          else
+            a.ids[t] = k != 0ull ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
+        }
+        atomicExch(a.amax_ctl, 0u);
+      }
     }
   }
 }
