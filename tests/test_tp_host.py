@@ -251,3 +251,25 @@ def test_vocab_parallel_greedy_over_gloo():
         p.join(timeout=60)
     assert sorted(r for r, _ in res) == [0, 1]
     assert all(ok for _, ok in res)
+
+
+def test_vocab_keys_property_random_values():
+    # any f32 values (NaN, infinities, signed zeros, subnormals, duplicates) split into any
+    # number of equal shards: the combined keys pick what the reference's argmax picks
+    import torch
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from runtimed_b200.tp import combine_keys
+
+    special = st.sampled_from([0.0, -0.0, float("inf"), float("-inf"), float("nan"), 1e-45, -1e-45, 3.0, -3.0])
+    value = st.one_of(special, st.floats(width=32, allow_nan=True, allow_infinity=True))
+
+    @settings(max_examples=200, deadline=None)
+    @given(st.lists(value, min_size=1, max_size=12), st.sampled_from([1, 2, 3, 4]))
+    def check(vals, world):
+        v = np.array(vals * world, dtype=np.float32)  # length divisible by world, duplicates
+        keys = torch.tensor([_shard_keys(v, world)], dtype=torch.int64).T
+        assert combine_keys(keys).tolist() == [_np_greedy(v)]
+
+    check()
