@@ -671,13 +671,24 @@ __device__ __forceinline__ unsigned long long amax_pack(float v, int64_t n) {
   return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
 }
 
-template <int NK>
-__device__ __forceinline__ void amax_fold(unsigned long long (&key)[NK], int t, float v, int64_t n) {
-  if (v != v) return;  // NaN never wins
-  const unsigned long long k = amax_pack(v, n);
+// The larger of key k and the key of output v at row n (NaN never wins).
+__device__ __forceinline__ unsigned long long amax_take(unsigned long long k, float v, int64_t n) {
+  if (v != v) return k;
+  const unsigned long long c = amax_pack(v, n);
+  return c > k ? c : k;
+}
+
+// The largest of k over the lanes xor distances first_xor .. 16 apart: first_xor = 4 joins
+// the lanes of one token in whole mode (lane t of every group of four holds token t), 1
+// joins the whole warp (split mode, one token at a time).
+__device__ __forceinline__ unsigned long long amax_warp_max(unsigned long long k, int first_xor) {
 #pragma unroll
-  for (int u = 0; u < NK; ++u)
-    if (u == t && k > key[u]) key[u] = k;
+  for (int o = 16; o >= 1; o >>= 1)
+    if (o >= first_xor) {
+      const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+      k = k2 > k ? k2 : k;
+    }
+  return k;
 }
 
 __device__ __forceinline__ void store_y(const Args& a, int t, int64_t n, float v) {
@@ -934,6 +945,11 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   }
   // the zero page idle B-fragment lanes read (published by the barrier below)
   for (int i = tid; i < kZeroPage / 4; i += kThreads) reinterpret_cast<uint32_t*>(sm + a.off_zero)[i] = 0u;
+  // AMAX: the CTA's best key per token, in the 128 spare bytes after the split-mode
+  // reduction buffer (published by the barrier below)
+  unsigned long long* cta_keys =
+      reinterpret_cast<unsigned long long*>(sm + a.off_red + (size_t)2 * kWarps * 16 * a.ncol8 * 4);
+  if (AMAX && tid < 4) cta_keys[tid] = 0ull;
   if (local_x) {
     stage_local_diag<FMT>(a, sm, whole, &a.status[0]);
   } else {
@@ -948,7 +964,6 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
-  unsigned long long akey[4] = {0ull, 0ull, 0ull, 0ull};  // AMAX: this lane's best key per token
   int i = 0;
   int slot_i = 0;         // ring slot of item i
   uint32_t phase = 0;     // its mbarrier phase parity
@@ -1018,6 +1033,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
           acc[c][r] = v;
         }
       if (whole) {  // lane t writes token t of rows g and g+8
+        unsigned long long tkey = 0ull;  // AMAX: this lane's best key of the tile (token tq)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int64_t n = (int64_t)tile * 16 + g + 8 * rr;
@@ -1029,14 +1045,18 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
               if ((c & 1) == 0 && c + 1 < NT && tq == t && t < a.M && n < a.N) {
                 const float v = (acc[c][rr] + acc[c + 1][rr]) * cs + bias;
                 if (!AMAX || a.y) store_y(a, t, n, v);
-                if (AMAX) amax_fold(akey, t, v, n + a.amax_row0);
+                if (AMAX) tkey = amax_take(tkey, v, n + a.amax_row0);
               }
             } else if (tq == c && c < a.M && n < a.N) {
               const float v = acc[c][rr] * cs + bias;
               if (!AMAX || a.y) store_y(a, c, n, v);
-              if (AMAX) amax_fold(akey, c, v, n + a.amax_row0);
+              if (AMAX) tkey = amax_take(tkey, v, n + a.amax_row0);
             }
           }
+        }
+        if constexpr (AMAX) {  // lanes of one tq hold one token: reduce over g, lanes 0..3 publish
+          tkey = amax_warp_max(tkey, 4);
+          if (g == 0 && tq < a.M && tkey != 0ull) atomicMax(cta_keys + tq, tkey);
         }
 #pragma unroll
         for (int c = 0; c < NT; ++c) acc[c][0] = acc[c][1] = 0.0f;
@@ -1077,6 +1097,7 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       if (a.tp_world > 1) {
         tp_publish_tile(a, tile, rb, ep, lane, tp_epoch);  // finished after the last tile
       } else {
+        unsigned long long tk[4] = {0ull, 0ull, 0ull, 0ull};  // AMAX: this lane's best key per token
         for (int o = lane; o < 16 * a.M; o += 32) {
           const int r = o / a.M, t = o - r * a.M;
           const int64_t n = (int64_t)tile * 16 + r;
@@ -1087,7 +1108,18 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
           if (n < a.N) {
             const float v = sum * ep[16 + r] + ep[r];
             if (!AMAX || a.y) store_y(a, t, n, v);
-            if (AMAX) amax_fold(akey, t, v, n + a.amax_row0);
+            if constexpr (AMAX) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (u == t) tk[u] = amax_take(tk[u], v, n + a.amax_row0);
+            }
+          }
+        }
+        if constexpr (AMAX) {  // the writer warp's keys of this tile, per token
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const unsigned long long k = amax_warp_max(tk[u], 1);
+            if (lane == 0 && u < a.M && k != 0ull) atomicMax(cta_keys + u, k);
           }
         }
       }
@@ -1118,31 +1150,12 @@ __global__ void __launch_bounds__(kThreads, (NT <= 2 ? 2 : 1)) qgemv_kernel(cons
       }
     }
   }
-  if constexpr (AMAX) {  // the CTA's best key per token: one atomic per CTA and token; the
-                         // launch's last CTA reads the ids
-    // each warp's keys go to its epilogue scratch (idle once its tiles are written)
-    unsigned long long* wk = reinterpret_cast<unsigned long long*>(tblw);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      unsigned long long k = akey[u];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
-        k = k2 > k ? k2 : k;
-      }
-      if (lane == 0) wk[u] = k;
-    }
+  if constexpr (AMAX) {  // the CTA's best key per token, one atomic each; the launch's last
+                         // CTA reads the ids
     __syncthreads();
     if (tid == 0) {
-      for (int u = 0; u < a.M; ++u) {
-        unsigned long long k = 0ull;
-        for (int w = 0; w < kWarps; ++w) {
-          const unsigned long long kw =
-              reinterpret_cast<const unsigned long long*>(sm + (size_t)w * a.warp_bytes + a.off_tbl)[u];
-          k = kw > k ? kw : k;
-        }
-        if (k != 0ull) atomicMax(a.amax_key + u, k);
-      }
+      for (int u = 0; u < a.M; ++u)
+        if (cta_keys[u] != 0ull) atomicMax(a.amax_key + u, cta_keys[u]);
       __threadfence();
       if (atomicAdd(a.amax_ctl, 1u) == gridDim.x - 1) {
         __threadfence();
