@@ -366,6 +366,7 @@ class MarlinWeight(QMatMul):
         raw_b, dev_b = ctypes.c_size_t(), ctypes.c_size_t()
         check(_lib.lib().rtd_qweight_info(h, None, None, None, ctypes.byref(raw_b), ctypes.byref(dev_b)))
         self._raw_bytes, self._dev_bytes = raw_b.value, dev_b.value
+        self.packed, self.scales = p.reshape(kc, self.n, 4), s  # the struct's host tensors
 
     @property
     def in_dim(self) -> int:
@@ -405,6 +406,10 @@ def fp8_encode(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def _is_u32(t) -> bool:
+    return (torch.is_tensor(t) and t.dtype == torch.uint32) or (isinstance(t, np.ndarray) and t.dtype == np.uint32)
+
+
 class Weights:
     """The reference's weight store: dense tensors in ``map``, quantized in ``q_map``."""
 
@@ -442,12 +447,77 @@ class Weights:
         qm = self.q_map.get(name)
         if qm is not None:
             return qm.forward(x)
+        if self.find_marlin(name) is not None:
+            return self._marlin_linear(x, name)
         fw = self.fp8_map.get(name)
         if fw is not None:
             return fw.forward(x).to(x.dtype)
         if name in self.map:
             return self.linear_dense(x, name)
         raise MissingWeight(name)
+
+    # -- INT4 Marlin entries (linear_layer.rs:17-66): packed / scales tensors in ``map``
+    MARLIN_PACKED_KEYS = ("{name}.marlin_packed", "{stem}.marlin_packed", "{name}.packed", "{stem}.packed")
+    MARLIN_SCALE_KEYS = ("{name}.marlin_scales", "{stem}.marlin_scales", "{name}.scales", "{stem}.scales",
+                         "{name}.scale", "{stem}.scale", "{name}.weight.scale", "{stem}.weight.scale")
+
+    def insert_marlin(self, name: str, mw: "MarlinWeight") -> None:
+        """Weights::insert_marlin (linear_layer.rs:17-22): the packed words under ``name``
+        and ``{stem}.marlin_packed``, the scales under ``{stem}.marlin_scales``; the device
+        handle is kept for the linears that use it."""
+        stem = name[:-len(".weight")] if name.endswith(".weight") else name
+        packed = torch.from_numpy(np.ascontiguousarray(mw.packed, dtype=np.uint32))
+        self.map[name] = packed
+        self.map[f"{stem}.marlin_packed"] = packed
+        self.map[f"{stem}.marlin_scales"] = torch.from_numpy(np.asarray(mw.scales, dtype=np.float32).copy())
+        self.__dict__.setdefault("_marlin_dev", {})[(stem, mw.in_dim)] = mw
+
+    def find_marlin(self, name: str):
+        """(packed, scales) of a Marlin entry, found as Weights::find_marlin does
+        (linear_layer.rs:24-43): the suffixed keys first, then a U32 tensor under the name or
+        its stem; None when either half is missing."""
+        stem = name[:-len(".weight")] if name.endswith(".weight") else name
+        packed = None
+        for key in self.MARLIN_PACKED_KEYS:
+            packed = self.map.get(key.format(name=name, stem=stem))
+            if packed is not None:
+                break
+        if packed is None:
+            for key in (name, stem):
+                t = self.map.get(key)
+                if t is not None and _is_u32(t):
+                    packed = t
+                    break
+        if packed is None:
+            return None
+        for key in self.MARLIN_SCALE_KEYS:
+            scales = self.map.get(key.format(name=name, stem=stem))
+            if scales is not None:
+                return packed, scales
+        return None
+
+    def _marlin_linear(self, x: torch.Tensor, name: str, check: bool = True) -> torch.Tensor:
+        """The Marlin branch of Weights::linear (linear_layer.rs:53-63): in_dim from x, the
+        packed chunk count bounding it (`check`; linear_dense's branch, :69-74, skips the
+        bound), then marlin_gemv."""
+        packed, scales = self.find_marlin(name)
+        x_in = int(x.shape[-1]) if x.dim() else 0
+        out_dim = int(scales.numel()) if torch.is_tensor(scales) else int(np.asarray(scales).size)
+        ndim = packed.dim() if torch.is_tensor(packed) else np.asarray(packed).ndim
+        kc = int(packed.shape[0]) if ndim >= 2 else (x_in + 31) // 32
+        max_k, min_k = kc * 32, ((kc - 1) * 32 if kc > 1 else 0)
+        if check and (x_in > max_k or (kc > 1 and x_in <= min_k)):
+            raise ShapeError(name, [max_k], list(x.shape))
+        stem = name[:-len(".weight")] if name.endswith(".weight") else name
+        cache = self.__dict__.setdefault("_marlin_dev", {})
+        mw = cache.get((stem, x_in))
+        if mw is None:
+            p = packed.cpu().numpy() if torch.is_tensor(packed) else np.asarray(packed)
+            sc = scales.cpu().numpy() if torch.is_tensor(scales) else np.asarray(scales)
+            mw = MarlinWeight(p.astype(np.uint32, copy=False), sc.astype(np.float32).reshape(-1), x_in, out_dim,
+                              device=self.dev)
+            cache[(stem, x_in)] = mw
+        return mw.forward(x)
 
     FP8_SCALE_SUFFIXES = (".scale", "_scale", ".weight_scale_inv")
 
@@ -466,6 +536,8 @@ class Weights:
         (torch.float8_e4m3fn, [out, in]): the scale by key lookup, then the FP8 linear
         with the reference CUDA semantics (W8A8: x encoded to E4M3 first,
         fp8_gemm.rs:96-101); the device weight is built once per entry."""
+        if self.find_marlin(name) is not None:  # linear_layer.rs:68-75: Marlin entries first
+            return self._marlin_linear(x, name, check=False)
         w = self.map.get(name)
         if w is None:
             raise MissingWeight(name)

@@ -97,3 +97,59 @@ def test_marlin_shape_errors_and_refusals():
     with pytest.raises(ConfigError):
         mw.embedding(torch.zeros(1, dtype=torch.int32))
     assert mw.forward(torch.zeros(0, 64, device="cuda")).shape == (0, 16)
+
+
+def test_weights_find_marlin_keys_and_bounds_on_cpu():
+    # Weights::find_marlin's key order (linear_layer.rs:24-43) and Weights::linear's bound on
+    # the activation width (:55-59), both decided before any device work
+    import torch
+
+    from runtimed_b200.errors import ShapeError
+    from runtimed_b200.weights import Weights, repack_marlin_tiles
+
+    w, s = _case(2, 4, 3)
+    p, s = repack_marlin_tiles(w, s)
+    pt, st = torch.from_numpy(p), torch.from_numpy(s)
+    W = Weights(device="cuda:0", map={"a.weight": pt, "a.scale": st})
+    assert W.find_marlin("a.weight") is not None  # a U32 tensor under the name, ".scale" of the stem
+    W = Weights(device="cuda:0", map={"b.weight": pt.to(torch.int64), "b.scales": st})
+    assert W.find_marlin("b.weight") is None  # not U32, no packed key
+    W = Weights(device="cuda:0", map={"c.packed": pt, "c.weight.marlin_scales": st, "c.scales": st * 2})
+    got = W.find_marlin("c.weight")
+    assert got is not None and got[1] is W.map["c.weight.marlin_scales"]  # "{name}.marlin_scales" first
+    W = Weights(device="cuda:0", map={"d.marlin_packed": pt})
+    assert W.find_marlin("d.weight") is None  # scales missing
+    # one 32-wide chunk: any in_dim up to 32; more than 32 is a shape error
+    W = Weights(device="cuda:0", map={"e.marlin_packed": pt, "e.marlin_scales": st})
+    with pytest.raises(ShapeError):
+        W.linear(torch.zeros(1, 80), "e.weight")
+    # two chunks: in_dim must exceed 32 (the first chunk alone would do)
+    w2, s2 = _case(2, 40, 4)
+    p2, s2 = repack_marlin_tiles(w2, s2)
+    W = Weights(device="cuda:0", map={"f.marlin_packed": torch.from_numpy(p2), "f.marlin_scales": torch.from_numpy(s2)})
+    with pytest.raises(ShapeError):
+        W.linear(torch.zeros(1, 32), "f.weight")
+    with pytest.raises(ShapeError):
+        W.linear(torch.zeros(1, 65), "f.weight")
+
+
+@pytest.mark.gpu
+def test_weights_linear_marlin_reference_known_answer():
+    # linear_layer.rs:142-158 (linear_marlin_cpu): W = [[1, 2, 3, 4], [2, 3, 4, 5]], scales 1,
+    # repacked, inserted under blk.0.attn_q; x = ones(4) gives [10, 14]; an 80-wide x is an error
+    import torch
+
+    from runtimed_b200.errors import ShapeError
+    from runtimed_b200.weights import MarlinWeight, Weights, repack_marlin_tiles
+
+    w = np.array([[1.0, 2.0, 3.0, 4.0], [2.0, 3.0, 4.0, 5.0]], np.float32)
+    p, s = repack_marlin_tiles(w, np.ones(2, np.float32))
+    W = Weights(device="cuda:0")
+    W.insert_marlin("blk.0.attn_q", MarlinWeight(p, s, 4, 2))
+    y = W.linear(torch.ones(1, 4, device="cuda"), "blk.0.attn_q.weight")
+    assert tuple(y.shape) == (1, 2)
+    assert y.flatten().cpu().tolist() == [10.0, 14.0]
+    with pytest.raises(ShapeError):
+        W.linear(torch.ones(1, 80, device="cuda"), "blk.0.attn_q.weight")
+    # linear_dense reaches the same entry first
+    assert W.linear_dense(torch.ones(1, 4, device="cuda"), "blk.0.attn_q.weight").flatten().cpu().tolist() == [10.0, 14.0]
