@@ -443,6 +443,42 @@ class Weights:
             return self.q_map[name].dequantize()
         raise MissingWeight(name)
 
+    def get_raw(self, name: str) -> torch.Tensor:
+        """The dense entry itself (store.rs:103-107)."""
+        t = self.map.get(name)
+        if t is None:
+            raise MissingWeight(name)
+        return t
+
+    def contains_key(self, name: str) -> bool:
+        return name in self.map or name in self.q_map
+
+    def replace(self, name: str, tensor: torch.Tensor) -> None:
+        """Weights::replace (store.rs:147-162): a dense entry is overwritten; a quantized
+        one is dropped from q_map and the dense tensor takes its name; else MissingWeight."""
+        if name in self.map:
+            self.map[name] = tensor
+            return
+        if self.q_map.pop(name, None) is not None:
+            self.map[name] = tensor
+            return
+        raise MissingWeight(name)
+
+    def candidate_weights(self, name: str, ids) -> torch.Tensor:
+        """Rows `ids` of a vocabulary matrix, [len(ids), hidden] (embed_layer.rs:59-82): f32
+        dequantized rows of a q_map entry (rtd_qembed), else rows of the dense entry in its
+        own dtype."""
+        ids_t = torch.as_tensor(np.asarray(ids, dtype=np.int64) if not torch.is_tensor(ids) else ids).reshape(-1)
+        qm = self.q_map.get(name)
+        if qm is not None:
+            if ids_t.numel() == 0:
+                return torch.zeros((0, qm.k), dtype=torch.float32, device=qm.device)
+            return qm.embedding(ids_t)
+        w = self.get_raw(name)
+        if ids_t.numel() == 0:
+            return torch.zeros((0, int(w.shape[1])), dtype=torch.float32, device=w.device)
+        return w.index_select(0, ids_t.to(device=w.device, dtype=torch.int64))
+
     def linear(self, x: torch.Tensor, name: str) -> torch.Tensor:
         qm = self.q_map.get(name)
         if qm is not None:

@@ -199,6 +199,11 @@ def test_embed_rows_bit_exact(name, t):
     want = full.reshape(N, K)[ids]
     assert np.array_equal(y[0].cpu().numpy().view(np.uint32), want.view(np.uint32))
     assert tuple(w.embed("token_embd.weight", []).shape) == (1, 0, K)
+    # Weights::candidate_weights (embed_layer.rs:59-82): the same rows, [n, K]
+    cw = w.candidate_weights("token_embd.weight", ids)
+    assert tuple(cw.shape) == (len(ids), K)
+    assert np.array_equal(cw.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert tuple(w.candidate_weights("token_embd.weight", []).shape) == (0, K)
 
 
 def test_embed_out_of_range_raises_status():

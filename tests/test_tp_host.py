@@ -273,3 +273,28 @@ def test_vocab_keys_property_random_values():
         assert combine_keys(keys).tolist() == [_np_greedy(v)]
 
     check()
+
+
+def test_weights_store_helpers_on_dense_entries():
+    # store.rs:103-107,147-168 and embed_layer.rs:74-81 on dense entries (no device work)
+    import torch
+
+    from runtimed_b200.errors import MissingWeight
+    from runtimed_b200.weights import Weights
+
+    emb = torch.arange(12, dtype=torch.float32).reshape(4, 3)
+    W = Weights(device="cuda:0", map={"tok.weight": emb}, q_map={"q.weight": object()})
+    assert W.get_raw("tok.weight") is emb
+    with pytest.raises(MissingWeight):
+        W.get_raw("nope")
+    assert W.contains_key("tok.weight") and W.contains_key("q.weight") and not W.contains_key("nope")
+    assert W.candidate_weights("tok.weight", [3, 0, 3]).tolist() == [[9, 10, 11], [0, 1, 2], [9, 10, 11]]
+    assert tuple(W.candidate_weights("tok.weight", []).shape) == (0, 3)
+    with pytest.raises(MissingWeight):
+        W.candidate_weights("nope", [0])
+    W.replace("tok.weight", emb * 2)
+    assert W.get_raw("tok.weight")[1, 1] == 8
+    W.replace("q.weight", emb)  # a quantized entry gives way to the dense tensor
+    assert "q.weight" not in W.q_map and W.get_raw("q.weight") is emb
+    with pytest.raises(MissingWeight):
+        W.replace("nope", emb)
