@@ -420,8 +420,23 @@ class Weights:
         self.q_map: Dict[str, QMatMul] = dict(q_map or {})
         self.fp8_map: Dict[str, Fp8Weight] = dict(fp8_map or {})
 
+    @classmethod
+    def from_parts(cls, device, map: dict) -> "Weights":
+        """Weights::from_parts (store.rs:22-29): dense tensors only."""
+        return cls(device=device, map=map)
+
+    @classmethod
+    def from_quantized(cls, device, map: dict, q_map: dict) -> "Weights":
+        """Weights::from_quantized (store.rs:31-43): dense and quantized entries."""
+        return cls(device=device, map=map, q_map=q_map)
+
     def device(self) -> torch.device:
         return self.dev
+
+    @staticmethod
+    def cuda_available(ordinal: int) -> bool:
+        """Weights::cuda_available (store.rs:116-126)."""
+        return torch.cuda.is_available() and 0 <= int(ordinal) < torch.cuda.device_count()
 
     def q_matmul(self, name: str) -> Optional[QMatMul]:
         return self.q_map.get(name)

@@ -298,3 +298,8 @@ def test_weights_store_helpers_on_dense_entries():
     assert "q.weight" not in W.q_map and W.get_raw("q.weight") is emb
     with pytest.raises(MissingWeight):
         W.replace("nope", emb)
+    W2 = Weights.from_quantized("cuda:0", {"a": emb}, {"b.weight": object()})
+    assert W2.contains_key("a") and W2.contains_key("b.weight")
+    assert Weights.from_parts("cuda:0", {"a": emb}).q_map == {}
+    assert Weights.cuda_available(0) == torch.cuda.is_available()
+    assert not Weights.cuda_available(1 << 20)
