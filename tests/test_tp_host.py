@@ -303,3 +303,23 @@ def test_weights_store_helpers_on_dense_entries():
     assert Weights.from_parts("cuda:0", {"a": emb}).q_map == {}
     assert Weights.cuda_available(0) == torch.cuda.is_available()
     assert not Weights.cuda_available(1 << 20)
+
+
+def test_reference_tensor_parallel_known_answer():
+    # tp/mod.rs:18-38: W = [[1, 2], [3, 4]] split by output rows over two ranks; x = [1, 1]
+    # gives [3] and [7], concatenated [3, 7].  Here W is a Q8_0 matrix (d = 1, the codes the
+    # values, K padded to one 32-wide block with zeros) and each rank's shard is its byte
+    # slice; the partial outputs come from the oracle.
+    from runtimed_b200.tp import shard_rows
+
+    blocks = np.zeros((2, 34), np.uint8)
+    blocks[:, 0:2] = np.array([0x3C00], np.uint16).view(np.uint8)  # d = 1.0 (f16)
+    blocks[0, 2:4] = [1, 2]
+    blocks[1, 2:4] = [3, 4]
+    raw = blocks.reshape(-1)
+    x = np.zeros((1, 32), np.float32)
+    x[0, :2] = 1.0
+    ys = [oracle.qgemv_f64(8, shard_rows(raw, 8, 2, 32, r, 2), 1, 32, x) for r in range(2)]
+    assert np.concatenate(ys, axis=1).tolist() == [[3.0, 7.0]]
+    # the reduction of two equal partials (ring_all_reduce over [y0, y0]): every rank gets 2 y0
+    assert (ys[0] + ys[0]).tolist() == [[6.0]]
