@@ -619,10 +619,19 @@ class Weights:
         return y + b.to(device=y.device, dtype=y.dtype)
 
     def embed(self, name: str, ids) -> torch.Tensor:
+        """Weights::embed (embed_layer.rs:16-57): rows `ids` as f32 [1, len(ids), hidden] --
+        dequantized rows of a q_map entry (rtd_qembed), else rows of the dense entry."""
         qm = self.q_map.get(name)
+        ids_t = torch.as_tensor(np.asarray(ids, dtype=np.int64) if not torch.is_tensor(ids) else ids).reshape(-1)
         if qm is None:
-            raise MissingWeight(name)
-        ids_t = torch.as_tensor(np.asarray(ids, dtype=np.int64) if not torch.is_tensor(ids) else ids)
+            w = self.map.get(name)
+            if w is None:
+                raise MissingWeight(name)
+            if ids_t.numel() == 0:
+                return torch.zeros((1, 0, int(w.shape[1])), dtype=torch.float32, device=w.device)
+            if int(ids_t.max()) >= int(w.shape[0]) or int(ids_t.min()) < 0:
+                raise ConfigError(f"embedding id out of range for {name} with {int(w.shape[0])} rows")
+            return w.index_select(0, ids_t.to(device=w.device, dtype=torch.int64)).unsqueeze(0).to(torch.float32)
         if ids_t.numel() == 0:
             return torch.zeros((1, 0, qm.k), dtype=torch.float32, device=qm.device)
         if int(ids_t.max()) >= qm.n or int(ids_t.min()) < 0:

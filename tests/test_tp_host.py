@@ -323,3 +323,26 @@ def test_reference_tensor_parallel_known_answer():
     assert np.concatenate(ys, axis=1).tolist() == [[3.0, 7.0]]
     # the reduction of two equal partials (ring_all_reduce over [y0, y0]): every rank gets 2 y0
     assert (ys[0] + ys[0]).tolist() == [[6.0]]
+
+
+def test_reference_embed_dense_known_answer():
+    # embed_layer.rs:90-124 (embed_dense_and_quantized), the dense half: a 4 x 3 table,
+    # ids [1, 3] -> [1, 2, 3] rows [3, 4, 5] and [9, 10, 11]; candidate_weights -> [2, 3]
+    # (the quantized half runs rtd_qembed and is checked bit-exact on the GPU)
+    import torch
+
+    from runtimed_b200.errors import ConfigError, MissingWeight
+    from runtimed_b200.weights import Weights
+
+    table = torch.arange(12, dtype=torch.float32).reshape(4, 3)
+    W = Weights.from_parts("cuda:0", {"dense_embd": table})
+    out = W.embed("dense_embd", [1, 3])
+    assert tuple(out.shape) == (1, 2, 3)
+    assert out.flatten().tolist() == [3.0, 4.0, 5.0, 9.0, 10.0, 11.0]
+    assert tuple(W.candidate_weights("dense_embd", [1, 3]).shape) == (2, 3)
+    assert tuple(W.embed("dense_embd", []).shape) == (1, 0, 3)
+    assert W.embed("dense_embd", [2]).dtype == torch.float32
+    with pytest.raises(ConfigError):
+        W.embed("dense_embd", [4])
+    with pytest.raises(MissingWeight):
+        W.embed("nope", [0])
