@@ -346,3 +346,61 @@ def test_reference_embed_dense_known_answer():
         W.embed("dense_embd", [4])
     with pytest.raises(MissingWeight):
         W.embed("nope", [0])
+
+
+def _gloo_mlp_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        h, inter = 256, 512
+        gate = synth.quant_matrix(12, inter, h, seed=31)
+        up = synth.quant_matrix(12, inter, h, seed=32)
+        down = synth.quant_matrix(14, h, inter, seed=33)
+        x = synth.activations(2, h, seed=34).astype(np.float64)
+        # this rank: gate / up rows (column parallel), down columns (row parallel)
+        fr = inter // world
+        g = oracle.qgemv_f64(12, shard_rows(gate, 12, inter, h, rank, world), fr, h, x)
+        u = oracle.qgemv_f64(12, shard_rows(up, 12, inter, h, rank, world), fr, h, x)
+        act = g / (1.0 + np.exp(-g)) * u
+        part = oracle.qgemv_f64(14, shard_cols(down, 14, h, inter, rank, world), h, fr, act)
+        y = torch.from_numpy(part)
+        dist.all_reduce(y)
+        # the unsharded MLP
+        G = oracle.qgemv_f64(12, gate, inter, h, x)
+        U = oracle.qgemv_f64(12, up, inter, h, x)
+        full = oracle.qgemv_f64(14, down, h, inter, G / (1.0 + np.exp(-G)) * U)
+        mine = y.numpy().copy()
+        got = [torch.zeros_like(y) for _ in range(world)]
+        dist.all_gather(got, y)
+        q.put((rank, float(np.abs(mine - full).max() / np.abs(full).max()),
+               all(torch.equal(got[0], t) for t in got)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_mlp_ranks_agree_over_gloo():
+    # tp/dual_gpu.rs:192-205 (test_dual_gpu_mlp_and_block, the MLP half) with quantized
+    # shards: gate / up split by rows, down by columns, SwiGLU on each rank's slice, the
+    # partial outputs summed over two gloo ranks; every rank holds the same y, equal to
+    # the unsharded MLP (the reference's bar: ranks within 1e-4)
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_mlp_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(r for r, _, _ in res) == [0, 1]
+    assert all(err < 1e-12 and same for _, err, same in res)
