@@ -81,3 +81,15 @@ def test_noalloc_status_reader_reports_without_a_device():
     assert L.rtd_noalloc_check_status(0, None) == _lib.RTD_ERR_CUDA
     assert L.rtd_last_error(None)
     assert L.rtd_noalloc_check_status(-1, None) == _lib.RTD_ERR_INVALID
+
+
+def test_entry_points_refuse_null_handles_without_a_device():
+    # every compute entry point checks its handles before touching a device: NULL context or
+    # weight is RTD_ERR_INVALID with a message, on any host
+    L = _lib.lib()
+    assert L.rtd_qlinear(None, None, None, 0, 1, 1, None, None, 0, 1, None) == _lib.RTD_ERR_INVALID
+    assert L.rtd_qlinear_argmax(None, None, None, 0, 1, 1, None, None, 0, 1, None, None) == _lib.RTD_ERR_INVALID
+    assert L.rtd_qlinear_argmax_keys(None, None, None, 0, 1, 1, None, 0, None, None) == _lib.RTD_ERR_INVALID
+    assert L.rtd_argmax(None, None, 1, 1, 1, None, None) == _lib.RTD_ERR_INVALID
+    assert L.rtd_qembed(None, None, None, 1, None, None) == _lib.RTD_ERR_INVALID
+    assert L.rtd_last_error(None)
