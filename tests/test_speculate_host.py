@@ -6,6 +6,10 @@ that insists every forward start exactly where the cache ends -- so each rollbac
 (truncate) and each re-feed of a correction, bonus or unseen proposal is checked, as the
 reference checks its decode loop with canned-logit stubs (decode/generate.rs:130-151).
 The speculative tokens must equal the target's own greedy decode for any draft.
+
+The paged KV cache's block bookkeeping (PagedKvCache, after cache/paged/table.rs:57-145)
+is checked on the CPU too: blocks spanned, rollback returning blocks to the pool, the
+block table, and the limits.
 """
 import numpy as np
 import pytest
@@ -89,3 +93,50 @@ def test_speculative_stops_at_eos():
     eos = want[17]
     st = speculative_generate(_Stub(_target_rule), _Stub(_target_rule), prompt, 60, k=4, eos=[eos])
     assert st.tokens == want[:want.index(eos) + 1]
+
+
+def _cache(num_blocks=8, max_seqs=3, max_ctx=128):
+    from runtimed_b200.qwen2 import PagedKvCache, Qwen2Config
+
+    cfg = Qwen2Config(n_layer=1, hidden=64, n_head=2, n_kv=2, head_dim=4, ffn=128, vocab=V, eps=1e-6,
+                      rope_theta=1e6, has_qkv_bias=False)
+    return PagedKvCache(cfg, num_blocks, max_seqs, max_ctx, "cpu", dtype=torch.float32)
+
+
+def test_paged_cache_spans_blocks_and_rolls_back():
+    # cache/paged/table.rs:169-215: 25 tokens span two 16-token blocks and one more token
+    # stays in the second; 35 tokens take three, a rollback to 20 keeps two, and two more
+    # tokens after it make 22 in the same two blocks
+    from runtimed_b200.errors import ConfigError
+
+    c = _cache()
+    c.reserve(0, 25)
+    assert len(c._blocks[0]) == 2 and c.lengths[0] == 25
+    c.reserve(0, 26)
+    assert len(c._blocks[0]) == 2 and c.lengths[0] == 26
+    c.reserve(1, 35)
+    assert len(c._blocks[1]) == 3
+    third = c._blocks[1][2]
+    c.truncate(1, 20)
+    assert len(c._blocks[1]) == 2 and c.lengths[1] == 20
+    assert third in c._free  # the rolled-back block returns to the pool
+    c.reserve(1, 22)
+    assert len(c._blocks[1]) == 2 and c.lengths[1] == 22
+    # the device table holds each sequence's blocks in order, after sync
+    c.sync_table()
+    assert c.table[0, :2].tolist() == c._blocks[0] and c.table[1, :2].tolist() == c._blocks[1]
+    # no block is owned twice; release returns them all
+    owned = c._blocks[0] + c._blocks[1]
+    assert len(set(owned)) == len(owned) and not set(owned) & set(c._free)
+    c.release(0)
+    c.release(1)
+    assert sorted(c._free) == list(range(8))
+    # limits: the pool, the context length, the sequence slots
+    c.reserve(2, 8 * 16)
+    with pytest.raises(ConfigError):
+        c.reserve(0, 1)  # out of blocks
+    c.release(2)
+    with pytest.raises(ConfigError):
+        c.reserve(0, 129)  # past max_ctx
+    with pytest.raises(ConfigError):
+        c.reserve(3, 1)  # no such sequence slot
