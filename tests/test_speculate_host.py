@@ -140,3 +140,20 @@ def test_paged_cache_spans_blocks_and_rolls_back():
         c.reserve(0, 129)  # past max_ctx
     with pytest.raises(ConfigError):
         c.reserve(3, 1)  # no such sequence slot
+
+
+def test_session_greedy_and_truncate_on_a_stub():
+    # Session (decode/session.rs:157-166): prefill, one forward per step at the next
+    # position, and truncate to roll back -- on the stub, every forward starts where the
+    # cache ends
+    from runtimed_b200.qwen2 import Session
+
+    prompt = [7, 11, 13]
+    stub = _Stub(_target_rule)
+    s = Session(stub, seq=0)
+    ids, rows = s.greedy(prompt, 12)
+    assert ids == _greedy(_target_rule, prompt, 12)
+    assert len(rows) == 13 and s.pos == len(prompt) + 12
+    s.truncate(len(prompt) + 4)  # keep four generated tokens
+    logits = s.step(ids[4])
+    assert int(torch.argmax(logits)) == ids[5]
