@@ -458,6 +458,25 @@ class Weights:
             return self.q_map[name].dequantize()
         raise MissingWeight(name)
 
+    def to_device(self, target) -> int:
+        """Weights::to_device (store.rs:170-205): dense entries move to `target` in its store
+        dtype (f16 on a GPU, f32 on the CPU; E4M3 stays E4M3 on a GPU); quantized entries stay
+        where they are, as the reference leaves its QTensors.  Integer entries (Marlin's
+        packed words) keep their dtype here -- a cast would change the words.  Returns the
+        resident bytes."""
+        dev = torch.device(target)
+        store = torch.float16 if dev.type == "cuda" else torch.float32
+        for name, t in list(self.map.items()):
+            t = t.to(dev)
+            if t.dtype == torch.float8_e4m3fn:
+                if dev.type != "cuda":
+                    t = t.to(store)
+            elif t.dtype != store and t.dtype.is_floating_point:
+                t = t.to(store)
+            self.map[name] = t
+        self.dev = dev
+        return self.resident_bytes()
+
     def get_raw(self, name: str) -> torch.Tensor:
         """The dense entry itself (store.rs:103-107)."""
         t = self.map.get(name)

@@ -404,3 +404,20 @@ def test_tensor_parallel_mlp_ranks_agree_over_gloo():
         p.join(timeout=60)
     assert sorted(r for r, _, _ in res) == [0, 1]
     assert all(err < 1e-12 and same for _, err, same in res)
+
+
+def test_weights_to_device_store_dtypes():
+    # store.rs:170-205 toward the CPU: dense entries become f32 (E4M3 included), integer
+    # entries keep their dtype, and the resident bytes follow
+    import torch
+
+    from runtimed_b200.weights import Weights
+
+    W = Weights.from_parts("cuda:0", {"a": torch.ones(4, 3, dtype=torch.float16),
+                                      "e": torch.ones(2, 2).to(torch.float8_e4m3fn),
+                                      "packed": torch.zeros(3, dtype=torch.uint32)})
+    n = W.to_device("cpu")
+    assert W.map["a"].dtype == torch.float32 and W.map["e"].dtype == torch.float32
+    assert W.map["packed"].dtype == torch.uint32
+    assert W.device() == torch.device("cpu")
+    assert n == 4 * 3 * 4 + 2 * 2 * 4 + 3 * 4
